@@ -1,0 +1,181 @@
+/*
+ * mdsoap -- B200 (sm_100a) SOAP engine behind a plain C ABI.
+ *
+ * The engine computes MDescriptor's GTO SOAP power spectrum (compression
+ * "off", average off / inner / outer, optional per-species weights) on the
+ * GPU: cell-binned periodic/isolated neighbour search, per-centre spherical
+ * expansion c_{nlm}, power spectrum p_{nn'l}.  No torch types, no C++ in the
+ * signatures: plain pointers and sizes.  All arithmetic is IEEE fp64; the
+ * result is rounded once, to fp32 or fp64, when it is stored.
+ *
+ * Every function returns an mdsoap_status; on failure mdsoap_last_error()
+ * gives a message for the calling thread.
+ */
+#ifndef MDSOAP_H
+#define MDSOAP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MDSOAP_ABI_VERSION 1
+
+/* Status codes.  They mirror the reference plugin's error classes
+ * (cpp/cuda/include/mdescriptor/cuda/error.hpp:15-28 and
+ * src/mdescriptor/core/errors.py:83-113): INVALID_ARGUMENT -> ValueError,
+ * DEVICE_UNAVAILABLE -> CudaUnavailable (ImportError), OUT_OF_MEMORY ->
+ * CudaOutOfMemory (MemoryError), CANCELLED -> CudaCancelledError. */
+typedef enum {
+    MDSOAP_OK = 0,
+    MDSOAP_INVALID_ARGUMENT = 1,
+    MDSOAP_DEVICE_UNAVAILABLE = 2,
+    MDSOAP_OUT_OF_MEMORY = 3,
+    MDSOAP_CANCELLED = 4,
+    MDSOAP_CAPACITY_OVERFLOW = 5,
+    MDSOAP_INTERNAL = 6
+} mdsoap_status;
+
+typedef enum { MDSOAP_FLOAT32 = 0, MDSOAP_FLOAT64 = 1 } mdsoap_dtype;
+
+typedef enum { MDSOAP_AVERAGE_OFF = 0, MDSOAP_AVERAGE_INNER = 1, MDSOAP_AVERAGE_OUTER = 2 } mdsoap_average;
+
+/* Descriptor parameters; the fields of the reference's SoapOptions that the
+ * GTO / compression-off path reads (cpp/include/mdescriptor/descriptor.hpp:17-43,
+ * filled by SoapKernel._ensure_native, _kernels/core.py:207-258). */
+typedef struct {
+    int32_t n_species;
+    const int32_t* species;        /* atomic numbers in declared order (feature order follows it) */
+    const double* species_weights; /* n_species entries, or NULL for 1.0 each */
+    double r_cut;                  /* > 1 for the GTO basis */
+    double sigma;                  /* Gaussian width; graph cutoff = r_cut + sigma*sqrt(-2 ln 1e-3) */
+    int32_t n_max;                 /* 1..32 */
+    int32_t l_max;                 /* 0..20 */
+    const double* alphas;          /* (l_max+1)*n_max, index l*n_max + k */
+    const double* betas;           /* (l_max+1)*n_max*n_max, index (l*n_max + n)*n_max + k */
+    int32_t average;               /* mdsoap_average */
+    int32_t output_dtype;          /* mdsoap_dtype */
+} mdsoap_params;
+
+/* A flat batch with StructureBatch's layout (src/mdescriptor/core/input.py:20-131):
+ * numbers int32[atoms], positions float64[atoms*3], cells float64[structures*9]
+ * (lattice vectors as rows), pbc int32[structures*3] (all 0 or all 1 per
+ * structure), offsets int64[structures+1]. */
+typedef struct {
+    const int32_t* numbers;
+    const double* positions;
+    const double* cells;
+    const int32_t* pbc;
+    const int64_t* offsets;
+    int64_t structures;
+    int64_t atoms;
+} mdsoap_batch;
+
+typedef struct mdsoap_plan mdsoap_plan;
+typedef struct mdsoap_graph mdsoap_graph;
+
+/* Cooperative cancellation probe; non-zero means "stop".  Polled between
+ * blocks of work, never inside a kernel. */
+typedef int (*mdsoap_cancel_fn)(void* context);
+
+/* Thread-local message of the last failing call ("" if none). */
+const char* mdsoap_last_error(void);
+
+int32_t mdsoap_abi_version(void);
+
+/* Number of CUDA devices visible to this process (0 when there is no usable
+ * driver/device; never fails). */
+int32_t mdsoap_device_count(void);
+
+/* Build a plan: validates the parameters and precomputes the radial and
+ * harmonic tables.  Touches no GPU (device state is created lazily, per
+ * device, on the first compute there).
+ * Replaces: the SOAP option parsing and constant upload of
+ * compute_soap_descriptor (cpp/cuda/src/extended_descriptors_soap.cuh:806-906)
+ * behind Backend::Backend (cpp/cuda/src/backend.cu:296-332); CPU counterpart
+ * SoapCalculator::SoapCalculator / prepare_soap (cpp/src/standalone/soap.cpp:1248, 507-572). */
+int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan);
+
+/* Release the plan and every device buffer it holds (idempotent on NULL).
+ * Replaces: Backend::close (cpp/cuda/src/backend.cu:720-744). */
+void mdsoap_plan_destroy(mdsoap_plan* plan);
+
+/* Features per output row: (S n)(S n + 1)/2 (L + 1)
+ * (SoapKernel.feature_count, src/mdescriptor/descriptors/_kernels/core.py:272-284). */
+int64_t mdsoap_plan_feature_count(const mdsoap_plan* plan);
+
+/* Output rows for a batch: atoms (average off) or structures (inner/outer). */
+int64_t mdsoap_plan_rows(const mdsoap_plan* plan, const mdsoap_batch* batch);
+
+/* End-to-end compute from HOST memory into HOST memory: validates the batch
+ * on the host, uploads it, runs the GPU pipeline and copies the rows into
+ * `out` (rows * feature_count elements of params.output_dtype, C order).
+ * The batch is split into structure blocks that are computed and copied back
+ * with the copies overlapping the next block's kernels.  `devices` lists the
+ * CUDA devices to shard structures across (NULL / 0 means device 0); each
+ * device fills a disjoint row range of `out`.  `cancel` (may be NULL) is
+ * polled between blocks.
+ * Replaces: Backend::compute -> compute_extended_descriptor ->
+ * compute_soap_descriptor (cpp/cuda/src/backend.cu:338-356,570-588;
+ * cpp/cuda/src/extended_descriptors_soap.cuh:799-1125) and the upload /
+ * download path (cpp/cuda/src/batch.cu, context.cu:111-138). */
+int mdsoap_compute(mdsoap_plan* plan, const mdsoap_batch* batch, void* out,
+                   const int32_t* devices, int32_t n_devices, mdsoap_cancel_fn cancel,
+                   void* cancel_context);
+
+/* Device-resident compute on one device: every pointer of `batch` and `out`
+ * is device memory on `device`; work is enqueued on `stream` (a cudaStream_t,
+ * NULL for the legacy default stream) and the call returns without waiting.
+ * Errors detected on the device (unknown species, int32 image overflow) are
+ * reported by mdsoap_plan_check(), which synchronises the stream.
+ * Replaces: the device part of compute_soap_descriptor
+ * (extended_descriptors_soap.cuh:888-1114: build_dpa, expansion, power). */
+int mdsoap_compute_device(mdsoap_plan* plan, const mdsoap_batch* batch, void* out, int32_t device,
+                          void* stream);
+
+/* Wait for `stream` and report any error flagged by kernels of this plan on
+ * `device` since the last check (and clear it). */
+int mdsoap_plan_check(mdsoap_plan* plan, int32_t device, void* stream);
+
+/* Per-kernel CUDA-event timing of mdsoap_compute_device calls (measurement
+ * support; no counterpart in the reference).  While enabled, each device call
+ * records events around its binning, centre and structure kernels on the
+ * caller's stream; mdsoap_plan_last_timing waits for them and returns the
+ * milliseconds of the last call on `device`. */
+int mdsoap_plan_set_timing(mdsoap_plan* plan, int32_t enable);
+int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, double* center_ms,
+                            double* structure_ms);
+
+/* Measured fp64 FMA throughput of `device` in TFLOP/s (2 flops per FMA) from a
+ * register-resident FMA chain kernel over every SM (measurement support; no
+ * counterpart in the reference).  Used as the roofline denominator of the
+ * fp64-bound centre kernel. */
+int mdsoap_probe_fp64_fma(int32_t device, double* tflops);
+
+/* Neighbour graph of a host batch on `device` with an explicit cutoff:
+ * inclusive boundary, exact self pair kept, periodic images as integer
+ * shifts of the unwrapped positions.  The pair SET and the fp64
+ * displacement / squared-distance bits equal the reference CPU graph's; pairs
+ * of one centre come in the engine's (deterministic) cell order.
+ * Replaces: DeviceNeighborGraph::build_dpa (cpp/cuda/src/neighbor_graph.cu:1106-1363);
+ * CPU counterpart build_neighbor_graph (cpp/src/common/neighbor.cpp:703-768). */
+int mdsoap_graph_build(const mdsoap_batch* batch, double cutoff, int32_t device,
+                       mdsoap_graph** graph);
+
+int64_t mdsoap_graph_pairs(const mdsoap_graph* graph);
+
+/* Copy the CSR out: offsets int64[atoms+1], atoms int32[pairs] (batch-global
+ * indices), shifts int32[pairs*3], displacements float64[pairs*3],
+ * distance2 float64[pairs].  Any pointer may be NULL to skip that array. */
+int mdsoap_graph_copy(const mdsoap_graph* graph, int64_t* offsets, int32_t* atoms, int32_t* shifts,
+                      double* displacements, double* distance2);
+
+void mdsoap_graph_destroy(mdsoap_graph* graph);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MDSOAP_H */

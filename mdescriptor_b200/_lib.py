@@ -1,0 +1,154 @@
+"""ctypes binding of ``libmdsoap.so`` (the C ABI declared in include/mdsoap.h).
+
+The library is built in-tree by ``mdescriptor_b200/build.py`` into
+``mdescriptor_b200/lib/``.  There is no fallback: if the library is missing,
+importing this module raises ImportError, so nothing can silently run a CPU
+path in its place.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmdsoap.so"
+
+OK = 0
+INVALID_ARGUMENT = 1
+DEVICE_UNAVAILABLE = 2
+OUT_OF_MEMORY = 3
+CANCELLED = 4
+CAPACITY_OVERFLOW = 5
+INTERNAL = 6
+
+FLOAT32 = 0
+FLOAT64 = 1
+AVERAGE = {"off": 0, "inner": 1, "outer": 2}
+
+_P = ctypes.c_void_p
+CancelFn = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+
+
+class Params(ctypes.Structure):
+    _fields_ = [
+        ("n_species", ctypes.c_int32),
+        ("species", _P),
+        ("species_weights", _P),
+        ("r_cut", ctypes.c_double),
+        ("sigma", ctypes.c_double),
+        ("n_max", ctypes.c_int32),
+        ("l_max", ctypes.c_int32),
+        ("alphas", _P),
+        ("betas", _P),
+        ("average", ctypes.c_int32),
+        ("output_dtype", ctypes.c_int32),
+    ]
+
+
+class BatchView(ctypes.Structure):
+    _fields_ = [
+        ("numbers", _P),
+        ("positions", _P),
+        ("cells", _P),
+        ("pbc", _P),
+        ("offsets", _P),
+        ("structures", ctypes.c_int64),
+        ("atoms", ctypes.c_int64),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.is_file():
+        raise ImportError(
+            f"mdsoap CUDA library not built ({LIB_PATH}); run `python -m mdescriptor_b200.build`"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    lib.mdsoap_last_error.restype = ctypes.c_char_p
+    lib.mdsoap_abi_version.restype = ctypes.c_int32
+    lib.mdsoap_device_count.restype = ctypes.c_int32
+    lib.mdsoap_plan_create.argtypes = [ctypes.POINTER(Params), ctypes.POINTER(_P)]
+    lib.mdsoap_plan_create.restype = ctypes.c_int
+    lib.mdsoap_plan_destroy.argtypes = [_P]
+    lib.mdsoap_plan_destroy.restype = None
+    lib.mdsoap_plan_feature_count.argtypes = [_P]
+    lib.mdsoap_plan_feature_count.restype = ctypes.c_int64
+    lib.mdsoap_plan_rows.argtypes = [_P, ctypes.POINTER(BatchView)]
+    lib.mdsoap_plan_rows.restype = ctypes.c_int64
+    lib.mdsoap_compute.argtypes = [_P, ctypes.POINTER(BatchView), _P, _P, ctypes.c_int32, _P, _P]
+    lib.mdsoap_compute.restype = ctypes.c_int
+    lib.mdsoap_compute_device.argtypes = [_P, ctypes.POINTER(BatchView), _P, ctypes.c_int32, _P]
+    lib.mdsoap_compute_device.restype = ctypes.c_int
+    lib.mdsoap_plan_check.argtypes = [_P, ctypes.c_int32, _P]
+    lib.mdsoap_plan_check.restype = ctypes.c_int
+    lib.mdsoap_plan_set_timing.argtypes = [_P, ctypes.c_int32]
+    lib.mdsoap_plan_set_timing.restype = ctypes.c_int
+    lib.mdsoap_plan_last_timing.argtypes = [_P, ctypes.c_int32, _P, _P, _P]
+    lib.mdsoap_plan_last_timing.restype = ctypes.c_int
+    lib.mdsoap_probe_fp64_fma.argtypes = [ctypes.c_int32, _P]
+    lib.mdsoap_probe_fp64_fma.restype = ctypes.c_int
+    lib.mdsoap_graph_build.argtypes = [ctypes.POINTER(BatchView), ctypes.c_double, ctypes.c_int32, ctypes.POINTER(_P)]
+    lib.mdsoap_graph_build.restype = ctypes.c_int
+    lib.mdsoap_graph_pairs.argtypes = [_P]
+    lib.mdsoap_graph_pairs.restype = ctypes.c_int64
+    lib.mdsoap_graph_copy.argtypes = [_P, _P, _P, _P, _P, _P]
+    lib.mdsoap_graph_copy.restype = ctypes.c_int
+    lib.mdsoap_graph_destroy.argtypes = [_P]
+    lib.mdsoap_graph_destroy.restype = None
+    return lib
+
+
+lib = _load()
+
+# Every symbol the header declares (checked by the CPU test suite).
+EXPORTED = (
+    "mdsoap_last_error",
+    "mdsoap_abi_version",
+    "mdsoap_device_count",
+    "mdsoap_plan_create",
+    "mdsoap_plan_destroy",
+    "mdsoap_plan_feature_count",
+    "mdsoap_plan_rows",
+    "mdsoap_compute",
+    "mdsoap_compute_device",
+    "mdsoap_plan_check",
+    "mdsoap_plan_set_timing",
+    "mdsoap_plan_last_timing",
+    "mdsoap_probe_fp64_fma",
+    "mdsoap_graph_build",
+    "mdsoap_graph_pairs",
+    "mdsoap_graph_copy",
+    "mdsoap_graph_destroy",
+)
+
+
+class CudaUnavailable(ImportError):
+    """No usable CUDA device or driver (maps to the reference's CudaUnavailable)."""
+
+
+class CudaOutOfMemory(MemoryError):
+    """Device allocation failed (maps to the reference's CudaOutOfMemory)."""
+
+
+class CudaCancelledError(RuntimeError):
+    """The computation was cancelled cooperatively."""
+
+
+def last_error() -> str:
+    return lib.mdsoap_last_error().decode()
+
+
+def raise_for(status: int) -> None:
+    """Map a status onto the reference plugin's exception classes
+    (cpp/cuda/src/bindings.cu:18-20, src/mdescriptor/core/errors.py:83-113)."""
+    if status == OK:
+        return
+    message = last_error()
+    if status == INVALID_ARGUMENT:
+        raise ValueError(message)
+    if status == DEVICE_UNAVAILABLE:
+        raise CudaUnavailable(message)
+    if status == OUT_OF_MEMORY:
+        raise CudaOutOfMemory(message)
+    if status == CANCELLED:
+        raise CudaCancelledError(message)
+    raise RuntimeError(message)

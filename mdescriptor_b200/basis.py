@@ -1,0 +1,67 @@
+"""GTO radial basis and feature layout of MDescriptor's SOAP, restated.
+
+The drop-in plugin never calls these: MDescriptor's adapter hands the plugin
+the basis it built itself (``_cuda_payload``).  They exist so that the C ABI
+can be driven without MDescriptor installed (benchmarks, GPU tests).
+"""
+
+from __future__ import annotations
+
+from math import gamma, log, sqrt
+
+import numpy as np
+
+
+def basis_gto(r_cut: float, n_max: int, l_max: int) -> tuple[np.ndarray, np.ndarray]:
+    """Orthonormalised GTO radial basis (alphas (L+1, n), betas (L+1, n, n)).
+
+    Restates ``_basis_gto`` (src/mdescriptor/descriptors/_kernels/core.py:60-76):
+    r_k = linspace(1, r_cut, n); alpha_{lk} = -ln(1e-3 / r_k^l) / r_k^2; the
+    Gaussian overlap S_l = 0.5 Gamma(l + 3/2) (alpha_k + alpha_k')^(-l-3/2) is
+    inverted-square-rooted through its eigendecomposition, beta_l = S_l^(-1/2).
+    """
+    radii = np.linspace(1.0, r_cut, n_max)
+    alphas = np.empty((l_max + 1, n_max), dtype=np.float64)
+    betas = np.empty((l_max + 1, n_max, n_max), dtype=np.float64)
+    for degree in range(l_max + 1):
+        alpha = -np.log(1e-3 / radii**degree) / radii**2
+        overlap = 0.5 * gamma(degree + 1.5) * (alpha[:, None] + alpha[None, :]) ** (-degree - 1.5)
+        values, vectors = np.linalg.eigh(overlap)
+        if np.any(values <= 0):
+            raise ValueError("could not normalize the SOAP GTO radial basis")
+        betas[degree] = (vectors * (1.0 / np.sqrt(values))) @ vectors.T
+        alphas[degree] = alpha
+    return alphas, betas
+
+
+def feature_count(n_species: int, n_max: int, l_max: int) -> int:
+    """Features for compression "off": (S n)(S n + 1)/2 (L + 1) (_kernels/core.py:272-284)."""
+    width = n_species * n_max
+    return width * (width + 1) // 2 * (l_max + 1)
+
+
+def labels(species, n_max: int, l_max: int) -> tuple[str, ...]:
+    """Feature labels in output order (_kernels/core.py:306-329, compression off).
+
+    Species pairs follow the declared (not sorted) species order, z1 <= z2 by
+    position; then l, then n1, then n2 (n2 >= n1 within a species).
+    """
+    species = list(species)
+    out = []
+    for i, first in enumerate(species):
+        for second in species[i:]:
+            for degree in range(l_max + 1):
+                for n1 in range(n_max):
+                    for n2 in range(n1 if first == second else 0, n_max):
+                        out.append(f"soap:z1={first},z2={second},l={degree},n1={n1},n2={n2}")
+    return tuple(out)
+
+
+def graph_cutoff(r_cut: float, sigma: float) -> float:
+    """Neighbour cutoff of the GTO SOAP: r_cut + sigma sqrt(-2 ln 1e-3) (soap.cpp:1214,1234).
+
+    Evaluated with the C library's log/sqrt (as the reference's C++ does), not
+    numpy's vectorised ones, so the last bit of the cutoff matches.  The C ABI
+    computes the same value itself; this copy is for reporting only.
+    """
+    return r_cut + sigma * sqrt(-2.0 * log(1e-3))

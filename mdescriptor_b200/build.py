@@ -1,0 +1,86 @@
+"""In-tree build of the engine: ``python -m mdescriptor_b200.build``.
+
+* ``lib/libmdsoap.so``  -- the CUDA engine + C ABI, nvcc for sm_100a only;
+* ``plugin/_cuda<EXT_SUFFIX>`` -- the pybind11 ``mdescriptor._cuda`` drop-in
+  (point ``MDESCRIPTOR_CUDA_PLUGIN_DIR`` at ``plugin/``), linked to
+  ``libmdsoap.so`` through an $ORIGIN rpath.
+
+Both are written next to the sources so that they travel with the
+repository; nothing is installed into site-packages.
+"""
+
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+import sysconfig
+from pathlib import Path
+
+PACKAGE = Path(__file__).resolve().parent
+CSRC = PACKAGE / "csrc"
+INCLUDE = PACKAGE.parent / "include"
+LIB = PACKAGE / "lib" / "libmdsoap.so"
+PLUGIN_DIR = PACKAGE / "plugin"
+PLUGIN = PLUGIN_DIR / f"_cuda{sysconfig.get_config_var('EXT_SUFFIX')}"
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",
+]
+
+
+def _nvcc() -> str:
+    home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    candidate = Path(home) / "bin" / "nvcc"
+    return str(candidate) if candidate.is_file() else "nvcc"
+
+
+def _run(cmd: list[str]) -> str:
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        raise RuntimeError(f"build failed: {' '.join(cmd)}\n{result.stdout}\n{result.stderr}")
+    return result.stdout + result.stderr
+
+
+def _stale(target: Path, sources: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    mtime = target.stat().st_mtime
+    return any(s.stat().st_mtime > mtime for s in sources)
+
+
+def build_library(force: bool = False, verbose: bool = False) -> Path:
+    sources = [CSRC / "mdsoap.cu", CSRC / "soap.cuh", CSRC / "neighbors.cuh", CSRC / "common.cuh",
+               INCLUDE / "mdsoap.h"]
+    if force or _stale(LIB, sources):
+        LIB.parent.mkdir(parents=True, exist_ok=True)
+        extra = ["-Xptxas", "-v"] if verbose else []
+        log = _run([_nvcc(), *NVCC_FLAGS, *extra, "-shared", str(CSRC / "mdsoap.cu"), "-o", str(LIB)])
+        if verbose:
+            print(log)
+    return LIB
+
+
+def build_plugin(force: bool = False) -> Path:
+    import pybind11
+
+    sources = [CSRC / "cuda_plugin.cpp", INCLUDE / "mdsoap.h", LIB]
+    if force or _stale(PLUGIN, sources):
+        PLUGIN_DIR.mkdir(parents=True, exist_ok=True)
+        _run(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+              f"-I{pybind11.get_include()}", f"-I{sysconfig.get_paths()['include']}",
+              str(CSRC / "cuda_plugin.cpp"), f"-L{LIB.parent}", "-lmdsoap",
+              "-Wl,-rpath,$ORIGIN/../lib", "-o", str(PLUGIN)])
+    return PLUGIN
+
+
+def build_all(force: bool = False, verbose: bool = False) -> None:
+    build_library(force, verbose)
+    build_plugin(force)
+
+
+if __name__ == "__main__":
+    build_all(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print(f"built {LIB} and {PLUGIN}")

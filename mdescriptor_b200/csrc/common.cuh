@@ -1,0 +1,69 @@
+// Shared device-side definitions of the mdsoap engine (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mdsoap {
+
+constexpr int kMaxSpecies = 64;
+constexpr int kMaxL = 20;
+constexpr int kMaxN = 32;
+constexpr int kWarps = 4;             // warps per CTA of the centre kernel
+constexpr int kPending = 64;          // accepted-edge queue per warp (>= 2 * 32)
+constexpr int kTri = (kMaxL + 1) * (kMaxL + 2) / 2;
+
+// Bits of the per-device error word that kernels raise instead of trapping.
+enum DeviceError : unsigned {
+    kErrUnknownSpecies = 1u,   // an atomic number outside the plan's species
+    kErrWrapRange = 2u,        // fractional coordinate beyond the int32 image range
+    kErrMixedPbc = 4u,         // pbc neither all 0 nor all 1
+    kErrSingularCell = 8u,     // |det(cell)| < 1e-14 for a periodic structure
+    kErrPairCapacity = 16u,    // neighbour CSR fill overran its counted capacity
+};
+
+// Per-structure geometry and binning plan, written by bin_structures_kernel.
+// Periodic structures are binned in lattice (fractional) coordinates, isolated
+// ones in their bounding box; bins of one structure are numbered
+// x + Mx (y + My z) and their atom lists are contiguous in `sorted`.
+struct StructInfo {
+    double cell[9];      // lattice vectors as rows
+    double inv[9];       // inverse cell (math3.hpp:52-68 arithmetic)
+    double origin[3];    // isolated: bounding-box minimum
+    double extent[3];    // isolated: bounding-box extent
+    int32_t periodic;
+    int32_t bounds[3];   // periodic image range [-b, b] (neighbor.cpp:459-467)
+    int32_t M[3];        // bins per axis
+    int32_t K[3];        // bin search half-width per axis
+    int64_t atom_begin;
+    int32_t atom_count;
+    int32_t pad_;
+    int64_t bin_base;    // first bin_start entry of this structure
+};
+
+struct BinView {
+    StructInfo* info;        // [structures]
+    int32_t* struct_of;      // [atoms]
+    int32_t* type;           // [atoms] species index, -1 if unknown
+    int32_t* bin_of;         // [atoms] bin index within the structure
+    int32_t* wrap;           // [atoms*3] floor of the fractional coordinates (periodic)
+    int32_t* sorted;         // [atoms] structure-local atom ids grouped by bin
+    int32_t* bin_start;      // [2*atoms + 8*structures] bin offsets (+1 sentinel per structure)
+    int32_t* bin_cursor;     // same size, scatter cursors
+    unsigned* error;         // device error word
+};
+
+// Capacity of the bin table of a structure with `atoms` atoms: its bin count
+// is capped at 2*atoms + 7 so that bin_base has the closed form below.
+__host__ __device__ inline int64_t bin_base_of(int64_t atom_begin, int64_t structure) {
+    return 2 * atom_begin + 8 * structure;
+}
+__host__ __device__ inline int64_t bin_capacity(int64_t atoms) { return 2 * atoms + 7; }
+
+__device__ __forceinline__ int floor_div(int a, int b) {
+    const int q = a / b;
+    return (a % b != 0 && ((a < 0) != (b < 0))) ? q - 1 : q;
+}
+
+}  // namespace mdsoap

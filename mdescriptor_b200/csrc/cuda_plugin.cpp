@@ -1,0 +1,338 @@
+// `mdescriptor._cuda` drop-in plugin: the Python-visible ABI that MDescriptor's
+// lazy CUDA seam loads (src/mdescriptor/_runtime.py:78-125 via
+// MDESCRIPTOR_CUDA_PLUGIN_DIR, src/mdescriptor/_cuda_loader.py), implemented as
+// a thin pybind11 layer over the C ABI of libmdsoap (include/mdsoap.h).
+//
+// Mirrors cpp/cuda/src/bindings.cu:15-57 (module attributes, exception
+// registration, create_backend) and the SOAP parts of Backend
+// (cpp/cuda/src/backend.cu:296-356, 570-588, 720-744) and
+// compute_soap_descriptor's option parsing and result dictionary
+// (cpp/cuda/src/extended_descriptors_soap.cuh:806-906, 1115-1124).
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <cstdlib>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/mdsoap.h"
+
+namespace py = pybind11;
+
+namespace {
+
+struct CudaCancelledError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+struct CudaUnavailable : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+struct CudaOutOfMemory : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+[[noreturn]] void throw_status(int status) {
+    const std::string message = mdsoap_last_error();
+    switch (status) {
+        case MDSOAP_INVALID_ARGUMENT:
+            throw std::invalid_argument(message);
+        case MDSOAP_DEVICE_UNAVAILABLE:
+            throw CudaUnavailable(message);
+        case MDSOAP_OUT_OF_MEMORY:
+            throw CudaOutOfMemory(message);
+        case MDSOAP_CANCELLED:
+            throw CudaCancelledError(message);
+        default:
+            throw std::runtime_error(message);
+    }
+}
+
+template <class T>
+T option(const py::dict& options, const char* key, T fallback) {
+    const py::str name(key);
+    if (!options.contains(name) || options[name].is_none()) return fallback;
+    return py::cast<T>(options[name]);
+}
+
+py::dict child_dict(const py::dict& options, const char* key) {
+    const py::str name(key);
+    if (!options.contains(name) || options[name].is_none()) return py::dict();
+    return py::cast<py::dict>(options[name]);
+}
+
+std::vector<double> flat_doubles(const py::dict& d, const char* key) {
+    const py::str name(key);
+    if (!d.contains(name) || d[name].is_none()) return {};
+    auto array = py::array_t<double, py::array::c_style | py::array::forcecast>::ensure(d[name]);
+    if (!array) throw std::invalid_argument(std::string("CUDA SOAP payload entry is not numeric: ") + key);
+    return std::vector<double>(array.data(), array.data() + array.size());
+}
+
+std::vector<int32_t> device_list() {
+    // Private selector: the public ExecutionOptions device token cannot carry
+    // an index (src/mdescriptor/core/options.py:48-54).
+    std::vector<int32_t> ids;
+    const char* env = std::getenv("MDSOAP_DEVICES");
+    if (!env || !*env) return {0};
+    const std::string text(env);
+    if (text == "all") {
+        const int count = mdsoap_device_count();
+        for (int i = 0; i < count; ++i) ids.push_back(i);
+        if (ids.empty()) ids.push_back(0);
+        return ids;
+    }
+    size_t start = 0;
+    while (start < text.size()) {
+        size_t end = text.find(',', start);
+        if (end == std::string::npos) end = text.size();
+        const std::string token = text.substr(start, end - start);
+        if (!token.empty()) ids.push_back((int32_t)std::stoi(token));
+        start = end + 1;
+    }
+    if (ids.empty()) ids.push_back(0);
+    return ids;
+}
+
+struct CancelContext {
+    py::object control;
+};
+
+int cancel_probe(void* context) {
+    py::gil_scoped_acquire gil;
+    auto* ctx = static_cast<CancelContext*>(context);
+    try {
+        return py::cast<bool>(ctx->control.attr("cancelled")()) ? 1 : 0;
+    } catch (py::error_already_set& error) {
+        error.discard_as_unraisable("mdsoap cancellation probe");
+        return 1;
+    }
+}
+
+class Backend {
+public:
+    Backend(std::string name, py::dict options) : name_(std::move(name)), options_(std::move(options)) {
+        if (name_ != "SOAP")
+            throw CudaUnavailable("this CUDA plugin implements SOAP only; '" + name_ + "' has no CUDA backend here");
+        species_ = option(options_, "species", std::vector<int32_t>{});
+        if (species_.empty()) throw std::invalid_argument("SOAP species must not be empty");
+        n_max_ = option(options_, "n_max", 8);
+        l_max_ = option(options_, "l_max", 6);
+        r_cut_ = option(options_, "r_cut", 6.0);
+        sigma_ = option(options_, "sigma", 1.0);
+        if (n_max_ < 1 || n_max_ > 32 || l_max_ < 0 || l_max_ > 20 || r_cut_ <= 0.0 || sigma_ <= 0.0)
+            throw std::invalid_argument("invalid CUDA SOAP parameters");
+        if (option(options_, "rbf", std::string("gto")) != "gto")
+            throw std::invalid_argument("unsupported CUDA SOAP radial basis");
+        const py::dict compression = child_dict(options_, "compression");
+        if (option(compression, "mode", std::string("off")) != "off")
+            throw std::invalid_argument("unsupported CUDA SOAP compression");
+        const std::string average = option(options_, "average", std::string("inner"));
+        if (average != "off" && average != "inner" && average != "outer")
+            throw std::invalid_argument("unsupported CUDA SOAP average mode");
+        average_ = average == "off" ? MDSOAP_AVERAGE_OFF : average == "inner" ? MDSOAP_AVERAGE_INNER : MDSOAP_AVERAGE_OUTER;
+        const py::dict weighting = child_dict(options_, "weighting");
+        if (option(weighting, "function", std::string()) != "" || weighting.contains("w0"))
+            throw std::invalid_argument("unsupported CUDA SOAP weighting");
+        weights_.assign(species_.size(), 1.0);
+        if (compression.contains("species_weighting") && !compression["species_weighting"].is_none()) {
+            const py::dict map = py::cast<py::dict>(compression["species_weighting"]);
+            for (size_t i = 0; i < species_.size(); ++i) {
+                const py::int_ key(species_[i]);
+                if (!map.contains(key))
+                    throw std::invalid_argument("species_weighting must contain exactly the configured species");
+                weights_[i] = py::cast<double>(map[key]);
+            }
+        }
+        const py::dict output = child_dict(options_, "output");
+        const std::string dtype = option(output, "dtype", std::string("float64"));
+        if (dtype != "float32" && dtype != "float64") throw std::invalid_argument("CUDA SOAP output dtype must be float32 or float64");
+        f64_ = dtype == "float64";
+        const py::dict payload = child_dict(options_, "_cuda_payload");
+        const py::dict radial = child_dict(payload, "radial_basis");
+        alphas_ = flat_doubles(radial, "alphas");
+        betas_ = flat_doubles(radial, "betas");
+        const size_t W = (size_t)l_max_ + 1;
+        if (alphas_.size() != W * n_max_ || betas_.size() != W * n_max_ * n_max_)
+            throw std::invalid_argument("CUDA SOAP GTO payload has an invalid shape");
+        mdsoap_params params{};
+        params.n_species = (int32_t)species_.size();
+        params.species = species_.data();
+        params.species_weights = weights_.data();
+        params.r_cut = r_cut_;
+        params.sigma = sigma_;
+        params.n_max = n_max_;
+        params.l_max = l_max_;
+        params.alphas = alphas_.data();
+        params.betas = betas_.data();
+        params.average = average_;
+        params.output_dtype = f64_ ? MDSOAP_FLOAT64 : MDSOAP_FLOAT32;
+        mdsoap_plan* plan = nullptr;
+        const int status = mdsoap_plan_create(&params, &plan);
+        if (status != MDSOAP_OK) throw_status(status);
+        plan_ = plan;
+        features_ = mdsoap_plan_feature_count(plan_);
+        const py::str fc_key("_cuda_feature_count");
+        if (options_.contains(fc_key) && !options_[fc_key].is_none()) {
+            const auto configured = py::cast<int64_t>(options_[fc_key]);
+            if (configured > 0 && configured != features_)
+                throw std::invalid_argument("CUDA SOAP feature count does not match its layout");
+        }
+        labels_ = labels_option();
+        devices_ = device_list();
+    }
+
+    ~Backend() { close(); }
+
+    int64_t feature_count() const { return features_; }
+
+    py::object compute(py::object batch, py::object control) {
+        std::unique_lock<std::mutex> guard(mutex_, std::defer_lock);
+        {
+            // Never wait for the instance lock while holding the GIL
+            // (cpp/cuda/src/backend.cu:339-345).
+            py::gil_scoped_release release;
+            guard.lock();
+        }
+        if (closed_ || plan_ == nullptr) throw std::runtime_error("CUDA backend is closed");
+        auto numbers = py::array_t<int32_t, py::array::c_style | py::array::forcecast>::ensure(batch.attr("numbers"));
+        auto positions = py::array_t<double, py::array::c_style | py::array::forcecast>::ensure(batch.attr("positions"));
+        auto cells = py::array_t<double, py::array::c_style | py::array::forcecast>::ensure(batch.attr("cells"));
+        auto pbc = py::array_t<int32_t, py::array::c_style | py::array::forcecast>::ensure(batch.attr("pbc"));
+        auto offsets = py::array_t<int64_t, py::array::c_style | py::array::forcecast>::ensure(batch.attr("offsets"));
+        if (!numbers || !positions || !cells || !pbc || !offsets)
+            throw std::invalid_argument("structure batch arrays have unsupported types");
+        const int64_t structures = (int64_t)offsets.size() - 1;
+        if (structures < 0) throw std::invalid_argument("invalid structure batch");
+        const int64_t atoms = (int64_t)numbers.size();
+        if (positions.size() != 3 * atoms || cells.size() != 9 * structures || pbc.size() != 3 * structures)
+            throw std::invalid_argument("structure batch arrays have inconsistent shapes");
+        if (!control.is_none()) {
+            if (py::hasattr(control, "reset")) control.attr("reset")(structures);
+            if (py::cast<bool>(control.attr("cancelled")()))
+                throw CudaCancelledError("descriptor computation was cancelled");
+        }
+        mdsoap_batch view{numbers.data(), positions.data(), cells.data(), pbc.data(), offsets.data(), structures, atoms};
+        const int64_t rows = average_ == MDSOAP_AVERAGE_OFF ? atoms : structures;
+        py::array values = f64_ ? py::array(py::array_t<double>({(py::ssize_t)rows, (py::ssize_t)features_}))
+                                : py::array(py::array_t<float>({(py::ssize_t)rows, (py::ssize_t)features_}));
+        void* out = values.mutable_data();
+        CancelContext context{control};
+        int status;
+        {
+            py::gil_scoped_release release;
+            status = mdsoap_compute(plan_, &view, rows > 0 ? out : nullptr, devices_.data(), (int32_t)devices_.size(),
+                                    control.is_none() ? nullptr : &cancel_probe, &context);
+        }
+        if (status != MDSOAP_OK) throw_status(status);
+        if (!control.is_none() && py::hasattr(control, "mark_completed")) {
+            for (int64_t s = 0; s < structures; ++s) control.attr("mark_completed")();
+        }
+        py::dict result;
+        result["values"] = values;
+        result["_mdescriptor_owned_values"] = true;
+        result["level"] = average_ == MDSOAP_AVERAGE_OFF ? "atom" : "structure";
+        if (average_ == MDSOAP_AVERAGE_OFF) {
+            py::array_t<int64_t> row_offsets(structures + 1);
+            std::copy(offsets.data(), offsets.data() + structures + 1, row_offsets.mutable_data());
+            result["row_offsets"] = row_offsets;
+        }
+        result["labels"] = labels_;
+        result["metadata"] = metadata();
+        return std::move(result);
+    }
+
+    py::object predict(py::object, py::object) {
+        throw std::invalid_argument("CUDA prediction supports NEP and DPA4C only");
+    }
+
+    py::dict metadata() const {
+        py::dict result;
+        result["descriptor"] = name_;
+        result["backend"] = "mdescriptor-cuda";
+        py::dict execution;
+        execution["device"] = "cuda";
+        const py::dict configured = child_dict(options_, "execution");
+        execution["num_threads"] = configured.contains("num_threads") ? configured["num_threads"] : py::none();
+        result["execution"] = execution;
+        return result;
+    }
+
+    void close() noexcept {
+        std::unique_lock<std::mutex> guard(mutex_, std::defer_lock);
+        if (PyGILState_Check()) {
+            py::gil_scoped_release release;
+            guard.lock();
+        } else {
+            guard.lock();
+        }
+        if (!closed_) {
+            closed_ = true;
+            if (plan_) mdsoap_plan_destroy(plan_);
+            plan_ = nullptr;
+        }
+    }
+
+private:
+    py::list labels_option() const {
+        const py::str key("_cuda_labels");
+        if (options_.contains(key) && !options_[key].is_none()) {
+            py::list configured = py::list(options_[key]);
+            if ((int64_t)py::len(configured) == features_) return configured;
+        }
+        py::list out;
+        for (int64_t i = 0; i < features_; ++i) out.append(name_ + ":" + std::to_string(i));
+        return out;
+    }
+
+    std::string name_;
+    py::dict options_;
+    std::vector<int32_t> species_;
+    std::vector<double> weights_, alphas_, betas_;
+    int n_max_ = 8, l_max_ = 6, average_ = MDSOAP_AVERAGE_INNER;
+    double r_cut_ = 6.0, sigma_ = 1.0;
+    bool f64_ = true;
+    int64_t features_ = 0;
+    py::list labels_;
+    std::vector<int32_t> devices_;
+    mdsoap_plan* plan_ = nullptr;
+    bool closed_ = false;
+    std::mutex mutex_;
+};
+
+}  // namespace
+
+PYBIND11_MODULE(_cuda, module) {
+    module.doc() = "MDescriptor CUDA plugin: B200 SOAP engine (mdsoap)";
+    module.attr("MODEL_SNAPSHOT_ABI") = 1;
+    module.attr("MDSOAP_ABI_VERSION") = mdsoap_abi_version();
+    py::register_exception<CudaCancelledError>(module, "CudaCancelledError", PyExc_RuntimeError);
+    py::register_exception<CudaUnavailable>(module, "CudaUnavailable", PyExc_ImportError);
+    py::register_exception<CudaOutOfMemory>(module, "CudaOutOfMemory", PyExc_MemoryError);
+
+    py::class_<Backend, std::shared_ptr<Backend>>(module, "CudaBackend")
+        .def(py::init<std::string, py::dict>())
+        .def_property_readonly("feature_count", &Backend::feature_count)
+        .def("compute", &Backend::compute, py::arg("batch"), py::arg("control") = py::none())
+        .def("predict", &Backend::predict, py::arg("batch"), py::arg("control") = py::none())
+        .def("metadata", &Backend::metadata)
+        .def("close", &Backend::close);
+
+    module.def("create_backend", [](const std::string& name, const py::dict& options) {
+        try {
+            return std::make_shared<Backend>(name, options);
+        } catch (const CudaUnavailable& error) {
+            PyErr_SetString(PyExc_ImportError, error.what());
+            throw py::error_already_set();
+        } catch (const CudaOutOfMemory& error) {
+            PyErr_SetString(PyExc_MemoryError, error.what());
+            throw py::error_already_set();
+        }
+    });
+    module.def("create_predictor", [](const std::string&, const py::dict&) -> py::object {
+        throw std::invalid_argument("CUDA prediction supports NEP and DPA4C only");
+    });
+}

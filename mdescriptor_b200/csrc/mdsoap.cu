@@ -1,0 +1,1046 @@
+// mdsoap: host side of the B200 SOAP engine and its C ABI (include/mdsoap.h).
+//
+// One plan = one SOAP configuration.  Device state (constants, workspaces,
+// streams, pinned staging) is created lazily per device on the first compute
+// there, so building a plan touches no GPU (the reference's construction-time
+// contract, tests/test_cuda_backend.py:266-279).
+#include "../../include/mdsoap.h"
+#include "soap.cuh"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+using namespace mdsoap;
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int status, const std::string& message) {
+    g_error = message;
+    return status;
+}
+
+struct Failure {
+    int status;
+    std::string message;
+};
+
+[[noreturn]] void raise(int status, const std::string& message) { throw Failure{status, message}; }
+
+void check(cudaError_t err, const char* what) {
+    if (err == cudaSuccess) return;
+    const std::string text = std::string(what) + ": " + cudaGetErrorString(err);
+    if (err == cudaErrorMemoryAllocation) raise(MDSOAP_OUT_OF_MEMORY, text);
+    if (err == cudaErrorNoDevice || err == cudaErrorInsufficientDriver || err == cudaErrorInvalidDevice ||
+        err == cudaErrorDevicesUnavailable || err == cudaErrorInitializationError)
+        raise(MDSOAP_DEVICE_UNAVAILABLE, text);
+    raise(MDSOAP_INTERNAL, text);
+}
+
+std::string device_error_text(unsigned bits) {
+    if (bits & kErrUnknownSpecies) return "batch contains an atomic number outside calculator species";
+    if (bits & kErrMixedPbc) return "mixed periodicity is not supported; use all-zero or all-one pbc";
+    if (bits & kErrSingularCell) return "cells must be nonsingular";
+    if (bits & kErrWrapRange) return "periodic image range exceeds integer range";
+    if (bits & kErrPairCapacity) return "neighbour graph fill exceeded its counted capacity";
+    return "device error";
+}
+
+// Grow-only device buffer.
+struct DeviceBytes {
+    void* ptr = nullptr;
+    size_t size = 0;
+    void reserve(size_t bytes, const char* what) {
+        if (bytes <= size) return;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        size = 0;
+        const size_t rounded = std::max<size_t>(bytes + bytes / 8, 256);
+        check(cudaMalloc(&ptr, rounded), what);
+        size = rounded;
+    }
+    template <class T>
+    T* as() const { return static_cast<T*>(ptr); }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        size = 0;
+    }
+};
+
+struct PinnedBytes {
+    void* ptr = nullptr;
+    size_t size = 0;
+    void reserve(size_t bytes) {
+        if (bytes <= size) return;
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        size = 0;
+        check(cudaMallocHost(&ptr, bytes), "pinned staging allocation");
+        size = bytes;
+    }
+    void release() {
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        size = 0;
+    }
+};
+
+// Device workspace for one batch (or one shard of one).
+struct Workspace {
+    DeviceBytes numbers, positions, cells, pbc, offsets;
+    DeviceBytes info, struct_of, type, bin_of, wrap, sorted, bin_start, bin_cursor;
+    DeviceBytes cbuf, pbuf, rbuf;
+    void release() {
+        for (DeviceBytes* b : {&numbers, &positions, &cells, &pbc, &offsets, &info, &struct_of, &type, &bin_of,
+                               &wrap, &sorted, &bin_start, &bin_cursor, &cbuf, &pbuf, &rbuf})
+            b->release();
+    }
+    BinView bins(unsigned* error) {
+        BinView v;
+        v.info = info.as<StructInfo>();
+        v.struct_of = struct_of.as<int32_t>();
+        v.type = type.as<int32_t>();
+        v.bin_of = bin_of.as<int32_t>();
+        v.wrap = wrap.as<int32_t>();
+        v.sorted = sorted.as<int32_t>();
+        v.bin_start = bin_start.as<int32_t>();
+        v.bin_cursor = bin_cursor.as<int32_t>();
+        v.error = error;
+        return v;
+    }
+    void reserve_bins(int64_t atoms, int64_t structures) {
+        const size_t a = (size_t)std::max<int64_t>(atoms, 1);
+        info.reserve(sizeof(StructInfo) * (size_t)std::max<int64_t>(structures, 1), "bin info");
+        struct_of.reserve(4 * a, "bin struct_of");
+        type.reserve(4 * a, "bin type");
+        bin_of.reserve(4 * a, "bin bin_of");
+        wrap.reserve(12 * a, "bin wrap");
+        sorted.reserve(4 * a, "bin sorted");
+        const size_t bins = (size_t)(2 * atoms + 8 * structures + 8);
+        bin_start.reserve(4 * bins, "bin starts");
+        bin_cursor.reserve(4 * bins, "bin cursors");
+    }
+};
+
+using CenterLauncher = void (*)(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);
+using StructureLauncher = void (*)(dim3, size_t, cudaStream_t, const SoapTables&, const int64_t*, int64_t, int64_t,
+                                   const double*, const double*, void*, int64_t);
+
+template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX>
+void launch_center(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX>
+const void* center_symbol() {
+    return reinterpret_cast<const void*>(&soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX>);
+}
+template <int LMAX>
+void launch_structure(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const int64_t* offsets,
+                      int64_t s0, int64_t s1, const double* cbuf, const double* pbuf, void* out, int64_t row0) {
+    soap_structure_kernel<LMAX><<<grid, kWarps * 32, smem, stream>>>(tab, offsets, s0, s1, cbuf, pbuf, out, row0);
+}
+template <int LMAX>
+const void* structure_symbol() {
+    return reinterpret_cast<const void*>(&soap_structure_kernel<LMAX>);
+}
+
+// Kernel variants.  Slot lengths bound 2l+1 of the channels a lane owns per
+// pass: channels are sorted by l descending, 32 per slot, and with n_max <= 8
+// the channels ranked 32s.. have l <= l_max - 4s.
+struct Variant {
+    int maxt, l0, l1, l2, nmax, lmax;
+    CenterLauncher center;
+    const void* (*center_sym)();
+    StructureLauncher structure;
+    const void* (*structure_sym)();
+};
+
+#define MDSOAP_VARIANT(T, A, B, C, N, L)                                                              \
+    Variant {                                                                                          \
+        T, A, B, C, N, L, &launch_center<T, A, B, C, N, L>, &center_symbol<T, A, B, C, N, L>,          \
+            &launch_structure<L>, &structure_symbol<L>                                                 \
+    }
+
+const Variant kVariants[] = {
+    MDSOAP_VARIANT(8, 7, 0, 0, 8, 3),    // n <= 8, l <= 3
+    MDSOAP_VARIANT(6, 9, 1, 0, 8, 4),    // n <= 8, l == 4
+    MDSOAP_VARIANT(4, 13, 5, 0, 8, 6),   // n <= 8, l in 5..6
+    MDSOAP_VARIANT(2, 17, 9, 1, 8, 8),   // n <= 8, l in 7..8
+    MDSOAP_VARIANT(1, 41, 0, 0, 32, 20), // any n <= 32, l <= 20
+};
+
+const Variant& pick_variant(int n_max, int l_max) {
+    if (n_max <= 8) {
+        if (l_max <= 3) return kVariants[0];
+        if (l_max == 4) return kVariants[1];
+        if (l_max <= 6) return kVariants[2];
+        if (l_max <= 8) return kVariants[3];
+    }
+    return kVariants[4];
+}
+
+// fp64 FMA throughput probe: kProbeChains independent dependent-FMA chains per
+// thread, all in registers, result kept live through a store.
+constexpr int kProbeChains = 8;
+__global__ void fma_probe_kernel(double* sink, int iters) {
+    double v[kProbeChains];
+    const double a = 1.0 + 1e-9 * threadIdx.x, b = 1e-12;
+#pragma unroll
+    for (int c = 0; c < kProbeChains; ++c) v[c] = 0.5 + c;
+    for (int i = 0; i < iters; ++i) {
+#pragma unroll
+        for (int c = 0; c < kProbeChains; ++c) v[c] = fma(v[c], a, b);
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int c = 0; c < kProbeChains; ++c) s += v[c];
+    sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+
+struct DeviceState {
+    int device = -1;
+    cudaStream_t compute = nullptr;
+    cudaStream_t copy = nullptr;
+    cudaEvent_t computed[2] = {nullptr, nullptr};
+    cudaEvent_t copied[2] = {nullptr, nullptr};
+    DeviceBytes items, betas, species, error;
+    Workspace work;
+    DeviceBytes out[2];
+    PinnedBytes staging[2];
+    bool smem_configured = false;
+    cudaEvent_t timing[4] = {nullptr, nullptr, nullptr, nullptr};
+    bool timed = false;  // the last device call recorded the timing events
+    std::mutex mutex;
+
+    ~DeviceState() {
+        if (device < 0) return;
+        int previous = 0;
+        cudaGetDevice(&previous);
+        cudaSetDevice(device);
+        if (compute) cudaStreamSynchronize(compute);
+        if (copy) cudaStreamSynchronize(copy);
+        work.release();
+        for (auto& b : out) b.release();
+        for (auto& b : staging) b.release();
+        items.release();
+        betas.release();
+        species.release();
+        error.release();
+        for (auto& e : computed)
+            if (e) cudaEventDestroy(e);
+        for (auto& e : copied)
+            if (e) cudaEventDestroy(e);
+        for (auto& e : timing)
+            if (e) cudaEventDestroy(e);
+        if (compute) cudaStreamDestroy(compute);
+        if (copy) cudaStreamDestroy(copy);
+        cudaSetDevice(previous);
+    }
+};
+
+struct mdsoap_plan {
+    int n_species = 0, n_max = 0, l_max = 0, average = 0, out_dtype = 0;
+    double r_cut = 0, sigma = 0, cutoff = 0;
+    std::vector<int32_t> species;
+    std::vector<double> weights, alphas, betas;
+    std::vector<RadialItem> items;
+    SoapTables tab{};
+    const Variant* variant = nullptr;
+    size_t center_smem = 0;
+    size_t structure_smem = 0;
+    int64_t features = 0;
+    bool timing = false;
+    std::mutex devices_mutex;
+    std::vector<std::unique_ptr<DeviceState>> devices;
+
+    size_t out_elem() const { return out_dtype == MDSOAP_FLOAT64 ? 8 : 4; }
+
+    DeviceState& state(int device);
+    void configure_smem(DeviceState& st);
+    void bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream, unsigned* error);
+    void run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, int64_t s1, int64_t a0, int64_t a1,
+                   void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center = nullptr);
+    void shard_compute(int device, const mdsoap_batch& batch, int64_t s0, int64_t s1, char* out,
+                       mdsoap_cancel_fn cancel, void* ctx, std::atomic<bool>& stop);
+};
+
+DeviceState& mdsoap_plan::state(int device) {
+    std::lock_guard<std::mutex> lock(devices_mutex);
+    for (auto& st : devices)
+        if (st->device == device) return *st;
+    int count = 0;
+    const cudaError_t probe = cudaGetDeviceCount(&count);
+    if (probe != cudaSuccess || count == 0)
+        raise(MDSOAP_DEVICE_UNAVAILABLE,
+              std::string("no CUDA device available: ") + cudaGetErrorString(probe));
+    if (device < 0 || device >= count) raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device index out of range");
+    auto st = std::make_unique<DeviceState>();
+    check(cudaSetDevice(device), "cudaSetDevice");
+    st->device = device;
+    check(cudaStreamCreateWithFlags(&st->compute, cudaStreamNonBlocking), "stream");
+    check(cudaStreamCreateWithFlags(&st->copy, cudaStreamNonBlocking), "stream");
+    for (int i = 0; i < 2; ++i) {
+        check(cudaEventCreateWithFlags(&st->computed[i], cudaEventDisableTiming), "event");
+        check(cudaEventCreateWithFlags(&st->copied[i], cudaEventDisableTiming), "event");
+    }
+    st->items.reserve(sizeof(RadialItem) * items.size(), "radial items");
+    check(cudaMemcpy(st->items.ptr, items.data(), sizeof(RadialItem) * items.size(), cudaMemcpyHostToDevice),
+          "upload radial items");
+    st->betas.reserve(8 * betas.size(), "betas");
+    check(cudaMemcpy(st->betas.ptr, betas.data(), 8 * betas.size(), cudaMemcpyHostToDevice), "upload betas");
+    st->species.reserve(4 * species.size(), "species");
+    check(cudaMemcpy(st->species.ptr, species.data(), 4 * species.size(), cudaMemcpyHostToDevice), "upload species");
+    st->error.reserve(64, "error word");
+    check(cudaMemset(st->error.ptr, 0, 64), "clear error word");
+    configure_smem(*st);
+    devices.push_back(std::move(st));
+    return *devices.back();
+}
+
+void mdsoap_plan::configure_smem(DeviceState& st) {
+    int optin = 0;
+    check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, st.device), "smem attribute");
+    if (center_smem > (size_t)optin || structure_smem > (size_t)optin)
+        raise(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
+    // The attribute is a per-kernel ceiling shared by every plan using the same
+    // instantiation, so raise it to the device maximum rather than this plan's need.
+    check(cudaFuncSetAttribute(variant->center_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+          "center kernel smem");
+    check(cudaFuncSetAttribute(variant->structure_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+          "structure kernel smem");
+    st.smem_configured = true;
+}
+
+void mdsoap_plan::bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream, unsigned* error) {
+    if (b.structures == 0) return;
+    st.work.reserve_bins(b.atoms, b.structures);
+    bin_structures_kernel<<<(unsigned)b.structures, 256, 0, stream>>>(b, st.work.bins(error), cutoff,
+                                                                       st.species.as<int32_t>(), n_species);
+    check(cudaGetLastError(), "bin kernel launch");
+}
+
+// Centres [a0, a1) = atoms of structures [s0, s1); rows go to `out` starting
+// at the block's first row.
+void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, int64_t s1, int64_t a0, int64_t a1,
+                            void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center) {
+    const int64_t centers = a1 - a0;
+    const int64_t csize = (int64_t)n_species * n_max * tab.H;
+    SoapPointers p{};
+    p.positions = b.positions;
+    p.bins = st.work.bins(error);
+    p.items = st.items.as<RadialItem>();
+    p.betas = st.betas.as<double>();
+    p.out = out;
+    p.out_row_begin = a0;
+    p.center_begin = a0;
+    p.center_end = a1;
+    if (average == MDSOAP_AVERAGE_INNER) {
+        st.work.cbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * csize, "inner-average scratch");
+        p.cbuf = st.work.cbuf.as<double>();
+    } else if (average == MDSOAP_AVERAGE_OUTER) {
+        st.work.pbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * features, "outer-average scratch");
+        p.pbuf = st.work.pbuf.as<double>();
+    }
+    if (tab.r_global) {
+        st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * csize, "coefficient scratch");
+        p.rbuf = st.work.rbuf.as<double>();
+    }
+    if (centers > 0) {
+        const int64_t grid = (centers + kWarps - 1) / kWarps;
+        variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
+        check(cudaGetLastError(), "centre kernel launch");
+    }
+    if (after_center) check(cudaEventRecord(after_center, stream), "timing event");
+    if (average != MDSOAP_AVERAGE_OFF && s1 > s0) {
+        variant->structure(dim3((unsigned)(s1 - s0)), structure_smem, stream, tab, b.offsets, s0, s1, p.cbuf, p.pbuf,
+                           out, s0);
+        check(cudaGetLastError(), "structure kernel launch");
+    }
+}
+
+namespace {
+
+void validate_host_batch(const mdsoap_plan* plan, const mdsoap_batch& b) {
+    // detail/batch.hpp:19-80 (validate_batch) and species.hpp:55-69 (validate_species).
+    if (b.structures < 0 || b.atoms < 0 || b.offsets == nullptr) raise(MDSOAP_INVALID_ARGUMENT, "invalid structure batch");
+    if (b.structures == 0) {
+        if (b.atoms != 0 || b.offsets[0] != 0)
+            raise(MDSOAP_INVALID_ARGUMENT, "empty structure batch has non-empty atom data");
+        return;
+    }
+    if (!b.numbers || !b.positions || !b.cells || !b.pbc)
+        raise(MDSOAP_INVALID_ARGUMENT, "structure batch contains null arrays");
+    if (b.offsets[0] != 0 || b.offsets[b.structures] != b.atoms)
+        raise(MDSOAP_INVALID_ARGUMENT, "offsets do not describe the flattened arrays");
+    if (b.atoms > 2147483647LL) raise(MDSOAP_INVALID_ARGUMENT, "neighbor atom index exceeds int32 range");
+    for (int64_t s = 0; s < b.structures; ++s) {
+        if (b.offsets[s] < 0 || b.offsets[s] > b.offsets[s + 1] || b.offsets[s + 1] > b.atoms)
+            raise(MDSOAP_INVALID_ARGUMENT, "offsets must be monotonic");
+        bool periodic = true, isolated = true;
+        for (int a = 0; a < 3; ++a) {
+            const int32_t f = b.pbc[3 * s + a];
+            if (f != 0 && f != 1) raise(MDSOAP_INVALID_ARGUMENT, "pbc must contain only 0 or 1");
+            periodic = periodic && f == 1;
+            isolated = isolated && f == 0;
+        }
+        if (!periodic && !isolated)
+            raise(MDSOAP_INVALID_ARGUMENT, "mixed periodicity is not supported; use all-zero or all-one pbc");
+        const double* c = b.cells + 9 * s;
+        for (int k = 0; k < 9; ++k)
+            if (!std::isfinite(c[k])) raise(MDSOAP_INVALID_ARGUMENT, "cells must be finite");
+        const double det = c[0] * (c[4] * c[8] - c[5] * c[7]) - c[1] * (c[3] * c[8] - c[5] * c[6]) +
+                           c[2] * (c[3] * c[7] - c[4] * c[6]);
+        if (periodic && (!std::isfinite(det) || std::abs(det) < 1e-14))
+            raise(MDSOAP_INVALID_ARGUMENT, "cells must be nonsingular");
+    }
+    for (int64_t a = 0; a < b.atoms; ++a) {
+        if (b.numbers[a] <= 0) raise(MDSOAP_INVALID_ARGUMENT, "atomic numbers must be positive");
+        for (int c = 0; c < 3; ++c)
+            if (!std::isfinite(b.positions[3 * a + c])) raise(MDSOAP_INVALID_ARGUMENT, "positions must be finite");
+        if (!plan) continue;
+        bool known = false;
+        for (int32_t z : plan->species) known = known || z == b.numbers[a];
+        if (!known) raise(MDSOAP_INVALID_ARGUMENT, "batch contains an atomic number outside calculator species");
+    }
+}
+
+// Host copy with several threads (pinned staging -> caller memory).
+void parallel_copy(char* dst, const char* src, size_t bytes) {
+    const size_t grain = (size_t)32 << 20;
+    const unsigned hw = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+    const size_t parts = std::min<size_t>(hw, (bytes + grain - 1) / grain);
+    if (parts <= 1) {
+        std::memcpy(dst, src, bytes);
+        return;
+    }
+    std::vector<std::thread> threads;
+    const size_t step = (bytes + parts - 1) / parts;
+    for (size_t i = 0; i < parts; ++i) {
+        const size_t begin = i * step;
+        const size_t end = std::min(bytes, begin + step);
+        if (begin >= end) break;
+        threads.emplace_back([=] { std::memcpy(dst + begin, src + begin, end - begin); });
+    }
+    for (auto& t : threads) t.join();
+}
+
+bool is_pinned(const void* ptr) {
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, ptr) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeHost;
+}
+
+int64_t block_bytes_target() {
+    const char* env = std::getenv("MDSOAP_BLOCK_BYTES");
+    if (env) {
+        const long long v = std::atoll(env);
+        if (v > 0) return v;
+    }
+    return (int64_t)64 << 20;
+}
+
+}  // namespace
+
+// One device's share [s0, s1) of a host batch, copied into `out` (rows of the shard).
+void mdsoap_plan::shard_compute(int device, const mdsoap_batch& batch, int64_t s0, int64_t s1, char* out,
+                                mdsoap_cancel_fn cancel, void* ctx, std::atomic<bool>& stop) {
+    DeviceState& st = state(device);
+    std::lock_guard<std::mutex> lock(st.mutex);
+    check(cudaSetDevice(device), "cudaSetDevice");
+    const int64_t a_begin = batch.offsets[s0];
+    const int64_t structures = s1 - s0;
+    const int64_t atoms = batch.offsets[s1] - a_begin;
+    const bool by_structure = average != MDSOAP_AVERAGE_OFF;
+    const size_t row_bytes = (size_t)features * out_elem();
+    // Upload the shard (offsets rebased to the shard).
+    Workspace& w = st.work;
+    w.numbers.reserve(4 * (size_t)std::max<int64_t>(atoms, 1), "numbers");
+    w.positions.reserve(24 * (size_t)std::max<int64_t>(atoms, 1), "positions");
+    w.cells.reserve(72 * (size_t)std::max<int64_t>(structures, 1), "cells");
+    w.pbc.reserve(12 * (size_t)std::max<int64_t>(structures, 1), "pbc");
+    w.offsets.reserve(8 * (size_t)(structures + 1), "offsets");
+    std::vector<int64_t> offsets(structures + 1);
+    for (int64_t s = 0; s <= structures; ++s) offsets[s] = batch.offsets[s0 + s] - a_begin;
+    cudaStream_t cs = st.compute;
+    if (atoms > 0) {
+        check(cudaMemcpyAsync(w.numbers.ptr, batch.numbers + a_begin, 4 * atoms, cudaMemcpyHostToDevice, cs), "H2D numbers");
+        check(cudaMemcpyAsync(w.positions.ptr, batch.positions + 3 * a_begin, 24 * atoms, cudaMemcpyHostToDevice, cs),
+              "H2D positions");
+    }
+    check(cudaMemcpyAsync(w.cells.ptr, batch.cells + 9 * s0, 72 * structures, cudaMemcpyHostToDevice, cs), "H2D cells");
+    check(cudaMemcpyAsync(w.pbc.ptr, batch.pbc + 3 * s0, 12 * structures, cudaMemcpyHostToDevice, cs), "H2D pbc");
+    check(cudaMemcpyAsync(w.offsets.ptr, offsets.data(), 8 * (structures + 1), cudaMemcpyHostToDevice, cs),
+          "H2D offsets");
+    DeviceBatch db{w.numbers.as<int32_t>(), w.positions.as<double>(), w.cells.as<double>(), w.pbc.as<int32_t>(),
+                   w.offsets.as<int64_t>(), structures, atoms};
+    unsigned* error = st.error.as<unsigned>();
+    check(cudaMemsetAsync(error, 0, sizeof(unsigned), cs), "clear error word");
+    bin(st, db, cs, error);
+
+    // Blocks of whole structures, about block_bytes_target() of output each.
+    const int64_t target = std::max<int64_t>(1, block_bytes_target() / (int64_t)std::max<size_t>(row_bytes, 1));
+    std::vector<int64_t> cuts{0};
+    {
+        int64_t rows = 0;
+        for (int64_t s = 0; s < structures; ++s) {
+            rows += by_structure ? 1 : offsets[s + 1] - offsets[s];
+            if (rows >= target) {
+                cuts.push_back(s + 1);
+                rows = 0;
+            }
+        }
+        if (cuts.back() != structures) cuts.push_back(structures);
+    }
+    const bool direct = is_pinned(out);
+    size_t max_block_bytes = 0;
+    for (size_t i = 0; i + 1 < cuts.size(); ++i) {
+        const int64_t rows = by_structure ? cuts[i + 1] - cuts[i] : offsets[cuts[i + 1]] - offsets[cuts[i]];
+        max_block_bytes = std::max(max_block_bytes, (size_t)rows * row_bytes);
+    }
+    for (int i = 0; i < 2; ++i) {
+        st.out[i].reserve(std::max<size_t>(max_block_bytes, 16), "output block");
+        if (!direct) st.staging[i].reserve(std::max<size_t>(max_block_bytes, 16));
+    }
+    const size_t blocks = cuts.size() - 1;
+    struct Pending {
+        size_t bytes;
+        char* dst;
+    };
+    std::vector<Pending> pending(blocks);
+    auto finish = [&](size_t i) {
+        check(cudaEventSynchronize(st.copied[i % 2]), "D2H wait");
+        if (!direct && pending[i].bytes) parallel_copy(pending[i].dst, static_cast<char*>(st.staging[i % 2].ptr), pending[i].bytes);
+    };
+    for (size_t i = 0; i < blocks; ++i) {
+        if (stop.load() || (cancel && cancel(ctx))) {
+            stop.store(true);
+            if (i > 0) finish(i - 1);
+            check(cudaStreamSynchronize(cs), "cancel sync");
+            raise(MDSOAP_CANCELLED, "descriptor computation was cancelled");
+        }
+        const int64_t bs0 = cuts[i], bs1 = cuts[i + 1];
+        const int64_t rows = by_structure ? bs1 - bs0 : offsets[bs1] - offsets[bs0];
+        const int64_t row0 = by_structure ? bs0 : offsets[bs0];
+        const size_t bytes = (size_t)rows * row_bytes;
+        char* dst = out + (size_t)row0 * row_bytes;
+        if (i >= 2) check(cudaStreamWaitEvent(cs, st.copied[i % 2], 0), "wait output buffer");
+        run_block(st, db, bs0, bs1, offsets[bs0], offsets[bs1], st.out[i % 2].ptr, cs, error);
+        check(cudaEventRecord(st.computed[i % 2], cs), "record compute");
+        if (i >= 1) finish(i - 1);
+        check(cudaStreamWaitEvent(st.copy, st.computed[i % 2], 0), "wait compute");
+        if (bytes)
+            check(cudaMemcpyAsync(direct ? dst : st.staging[i % 2].ptr, st.out[i % 2].ptr, bytes, cudaMemcpyDeviceToHost,
+                                  st.copy),
+                  "D2H output");
+        check(cudaEventRecord(st.copied[i % 2], st.copy), "record copy");
+        pending[i] = {bytes, dst};
+    }
+    if (blocks) finish(blocks - 1);
+    check(cudaStreamSynchronize(cs), "compute sync");
+    unsigned bits = 0;
+    check(cudaMemcpy(&bits, error, sizeof(unsigned), cudaMemcpyDeviceToHost), "read error word");
+    if (bits) raise(bits & kErrUnknownSpecies || bits & kErrMixedPbc || bits & kErrSingularCell ? MDSOAP_INVALID_ARGUMENT
+                                                                                                : MDSOAP_INTERNAL,
+                    device_error_text(bits));
+}
+
+struct mdsoap_graph {
+    int64_t atoms = 0;
+    std::vector<int64_t> offsets;
+    std::vector<int32_t> atom_ids, shifts;
+    std::vector<double> displacements, distance2;
+};
+
+// ---------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+const char* mdsoap_last_error(void) { return g_error.c_str(); }
+
+int32_t mdsoap_abi_version(void) { return MDSOAP_ABI_VERSION; }
+
+int32_t mdsoap_device_count(void) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return count;
+}
+
+int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
+    if (!params || !plan_out) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    *plan_out = nullptr;
+    const mdsoap_params& q = *params;
+    // soap.cpp:1149-1176 parameter checks; n_max <= 32 is the reference CUDA
+    // plugin's limit (extended_descriptors_soap.cuh:812-815).
+    if (q.n_species < 1 || q.n_species > kMaxSpecies || !q.species)
+        return fail(MDSOAP_INVALID_ARGUMENT, "SOAP species must contain 1..64 atomic numbers");
+    if (!std::isfinite(q.r_cut) || !std::isfinite(q.sigma) || q.r_cut <= 0.0 || q.sigma <= 0.0 || q.n_max < 1 ||
+        q.l_max < 0 || q.l_max > kMaxL)
+        return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP parameters");
+    if (q.n_max > kMaxN) return fail(MDSOAP_INVALID_ARGUMENT, "invalid CUDA SOAP parameters (n_max > 32)");
+    if (q.average < 0 || q.average > 2) return fail(MDSOAP_INVALID_ARGUMENT, "unsupported CUDA SOAP average mode");
+    if (q.output_dtype != MDSOAP_FLOAT32 && q.output_dtype != MDSOAP_FLOAT64)
+        return fail(MDSOAP_INVALID_ARGUMENT, "output dtype must be float32 or float64");
+    if (!q.alphas || !q.betas) return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP radial basis size");
+    for (int i = 0; i < q.n_species; ++i) {
+        if (q.species[i] <= 0) return fail(MDSOAP_INVALID_ARGUMENT, "species must be positive atomic numbers");
+        for (int j = 0; j < i; ++j)
+            if (q.species[j] == q.species[i]) return fail(MDSOAP_INVALID_ARGUMENT, "species must be unique");
+    }
+    try {
+        auto plan = std::make_unique<mdsoap_plan>();
+        plan->n_species = q.n_species;
+        plan->n_max = q.n_max;
+        plan->l_max = q.l_max;
+        plan->average = q.average;
+        plan->out_dtype = q.output_dtype;
+        plan->r_cut = q.r_cut;
+        plan->sigma = q.sigma;
+        plan->species.assign(q.species, q.species + q.n_species);
+        plan->weights.assign(q.n_species, 1.0);
+        if (q.species_weights) {
+            for (int i = 0; i < q.n_species; ++i) {
+                if (!std::isfinite(q.species_weights[i]))
+                    return fail(MDSOAP_INVALID_ARGUMENT, "SOAP species weights must be finite");
+                plan->weights[i] = q.species_weights[i];
+            }
+        }
+        const int L = q.l_max, n = q.n_max, W = L + 1;
+        plan->alphas.assign(q.alphas, q.alphas + W * n);
+        plan->betas.assign(q.betas, q.betas + W * n * n);
+        for (double v : plan->alphas)
+            if (!std::isfinite(v)) return fail(MDSOAP_INVALID_ARGUMENT, "SOAP radial basis must be finite");
+        for (double v : plan->betas)
+            if (!std::isfinite(v)) return fail(MDSOAP_INVALID_ARGUMENT, "SOAP radial basis must be finite");
+        // soap.cpp:1214 + neighbor.cpp:552 (host double arithmetic, same order).
+        const double padding = q.sigma * std::sqrt(-2.0 * std::log(1e-3));
+        plan->cutoff = q.r_cut + padding;
+        // prepare_soap (soap.cpp:507-534).
+        const double eta = 1.0 / (2.0 * q.sigma * q.sigma);
+        std::vector<double> eta_powers(W, 1.0);
+        for (int l = 1; l <= L; ++l) eta_powers[l] = eta_powers[l - 1] * eta;
+        for (int l = L; l >= 0; --l) {
+            for (int k = 0; k < n; ++k) {
+                const double alpha = plan->alphas[l * n + k];
+                const double denominator = alpha + eta;
+                RadialItem it;
+                it.prefactor = eta_powers[l] * std::pow(denominator, -l - 1.5);
+                it.exponent = alpha * eta / denominator;
+                it.l = l;
+                it.k = k;
+                plan->items.push_back(it);
+            }
+        }
+        SoapTables& t = plan->tab;
+        std::memset(&t, 0, sizeof(t));
+        t.n_species = q.n_species;
+        t.n_max = n;
+        t.l_max = L;
+        t.H = W * W;
+        t.items = W * n;
+        t.rows = q.n_species * n;
+        const int64_t width = (int64_t)q.n_species * n;
+        plan->features = width * (width + 1) / 2 * W;
+        t.features = plan->features;
+        t.average = q.average;
+        t.out_f64 = q.output_dtype == MDSOAP_FLOAT64;
+        t.cutoff2 = plan->cutoff * plan->cutoff;
+        const double pi = 3.141592653589793238462643383279502884;
+        t.soap_scale = pi * std::sqrt(pi);
+        for (int l = 0; l <= L; ++l) {
+            t.power_pref[l] = pi * std::sqrt(8.0 / (2.0 * l + 1.0));
+            for (int m = 0; m <= l; ++m) {
+                const int i = l * (l + 1) / 2 + m;
+                // solid_harmonic_normalization (soap.cpp:26-38), sqrt 2 folded in for m > 0.
+                const double norm =
+                    std::sqrt((2.0 * l + 1.0) / (4.0 * pi) * std::exp(std::lgamma(l - m + 1.0) - std::lgamma(l + m + 1.0)));
+                t.ynorm[i] = m == 0 ? norm : norm * 1.414213562373095048801688724209698079;
+                t.yra[i] = l > m ? (2.0 * l - 1.0) / (l - m) : 0.0;
+                t.yrb[i] = l > m ? (l + m - 1.0) / (l - m) : 0.0;
+            }
+        }
+        for (int i = 0; i < q.n_species; ++i) t.species_weight[i] = plan->weights[i];
+        const Variant& v = pick_variant(n, L);
+        plan->variant = &v;
+        const int ns = (v.l0 > 0) + (v.l1 > 0) + (v.l2 > 0);
+        const int slots = (t.items + 31) / 32;
+        t.slot_groups = (slots + ns - 1) / ns;
+        t.type_groups = (q.n_species + v.maxt - 1) / v.maxt;
+        const bool single_pass = t.slot_groups == 1 && t.type_groups == 1;
+        const size_t beta_bytes = (size_t)W * n * n * 8;
+        t.beta_in_smem = beta_bytes <= 32768;
+        const size_t beta_smem = t.beta_in_smem ? ((beta_bytes + 15) & ~(size_t)15) : 0;
+        const size_t r_bytes = (size_t)q.n_species * n * t.H * 8;
+        const size_t pend = (size_t)kPending * 36;
+        auto region_a = [&](int chunk) { return pend + ((size_t)chunk * t.H + 48) * 8; };
+        auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+        auto per_warp = [&](int chunk, bool r_in_smem) {
+            if (!r_in_smem) return align16(region_a(chunk));
+            if (single_pass) return align16(std::max(region_a(chunk), r_bytes));
+            return align16(region_a(chunk)) + align16(r_bytes);
+        };
+        // Largest chunk (<= 32) that keeps >= 2 CTAs of kWarps warps on an SM
+        // (about 113 KB each); else the smallest footprint that fits at all.
+        const size_t budget2 = 113 * 1024, budget1 = 227 * 1024;
+        int chunk = 32;
+        bool r_smem = true;
+        while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, true) > budget2) chunk -= 8;
+        if (beta_smem + kWarps * per_warp(chunk, true) > budget1) {
+            r_smem = false;
+            chunk = 32;
+            while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, false) > budget2) chunk -= 8;
+        }
+        t.chunk = chunk;
+        t.r_global = r_smem ? 0 : 1;
+        t.warp_bytes = (int32_t)per_warp(chunk, r_smem);
+        t.r_offset = (r_smem && !single_pass) ? (int32_t)align16(region_a(chunk)) : 0;
+        plan->center_smem = beta_smem + kWarps * (size_t)t.warp_bytes;
+        plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? r_bytes : 0;
+        if (plan->center_smem > budget1 || plan->structure_smem > budget1)
+            return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
+        *plan_out = plan.release();
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
+
+void mdsoap_plan_destroy(mdsoap_plan* plan) { delete plan; }
+
+int64_t mdsoap_plan_feature_count(const mdsoap_plan* plan) { return plan ? plan->features : 0; }
+
+int64_t mdsoap_plan_rows(const mdsoap_plan* plan, const mdsoap_batch* batch) {
+    if (!plan || !batch) return 0;
+    return plan->average == MDSOAP_AVERAGE_OFF ? batch->atoms : batch->structures;
+}
+
+int mdsoap_compute(mdsoap_plan* plan, const mdsoap_batch* batch, void* out, const int32_t* devices,
+                   int32_t n_devices, mdsoap_cancel_fn cancel, void* cancel_context) {
+    if (!plan || !batch) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        validate_host_batch(plan, *batch);
+        const int64_t rows = mdsoap_plan_rows(plan, batch);
+        if (rows > 0 && !out) return fail(MDSOAP_INVALID_ARGUMENT, "null output buffer");
+        if (cancel && cancel(cancel_context)) return fail(MDSOAP_CANCELLED, "descriptor computation was cancelled");
+        std::vector<int> ids;
+        if (devices && n_devices > 0)
+            ids.assign(devices, devices + n_devices);
+        else
+            ids.push_back(0);
+        if (batch->structures == 0 || rows == 0) {
+            // Still resolve the device so a missing GPU fails loudly.
+            plan->state(ids[0]);
+            return MDSOAP_OK;
+        }
+        // Contiguous structure shards balanced by atom count.
+        const int64_t S = batch->structures;
+        const int parts = (int)std::min<int64_t>((int64_t)ids.size(), S);
+        std::vector<int64_t> cuts{0};
+        for (int i = 1; i < parts; ++i) {
+            const int64_t goal = batch->atoms * i / parts;
+            int64_t s = std::upper_bound(batch->offsets, batch->offsets + S + 1, goal) - batch->offsets - 1;
+            s = std::max<int64_t>(s, cuts.back() + 1);
+            s = std::min<int64_t>(s, S - (parts - i));
+            cuts.push_back(s);
+        }
+        cuts.push_back(S);
+        std::atomic<bool> stop{false};
+        const size_t row_bytes = (size_t)plan->features * plan->out_elem();
+        const bool by_structure = plan->average != MDSOAP_AVERAGE_OFF;
+        std::vector<Failure> failures(parts);
+        std::vector<bool> failed(parts, false);
+        auto work = [&](int i) {
+            try {
+                const int64_t row0 = by_structure ? cuts[i] : batch->offsets[cuts[i]];
+                plan->shard_compute(ids[i], *batch, cuts[i], cuts[i + 1], static_cast<char*>(out) + row0 * row_bytes,
+                                    cancel, cancel_context, stop);
+            } catch (const Failure& f) {
+                failures[i] = f;
+                failed[i] = true;
+                stop.store(true);
+            } catch (const std::exception& e) {
+                failures[i] = Failure{MDSOAP_INTERNAL, e.what()};
+                failed[i] = true;
+                stop.store(true);
+            }
+        };
+        if (parts == 1) {
+            work(0);
+        } else {
+            std::vector<std::thread> threads;
+            for (int i = 0; i < parts; ++i) threads.emplace_back(work, i);
+            for (auto& t : threads) t.join();
+        }
+        // Report the first real failure ahead of secondary cancellations.
+        for (int i = 0; i < parts; ++i)
+            if (failed[i] && failures[i].status != MDSOAP_CANCELLED) return fail(failures[i].status, failures[i].message);
+        for (int i = 0; i < parts; ++i)
+            if (failed[i]) return fail(failures[i].status, failures[i].message);
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
+
+int mdsoap_compute_device(mdsoap_plan* plan, const mdsoap_batch* batch, void* out, int32_t device, void* stream) {
+    if (!plan || !batch) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    if (batch->structures < 0 || batch->atoms < 0) return fail(MDSOAP_INVALID_ARGUMENT, "invalid structure batch");
+    try {
+        DeviceState& st = plan->state(device);
+        std::lock_guard<std::mutex> lock(st.mutex);
+        check(cudaSetDevice(device), "cudaSetDevice");
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        DeviceBatch db{batch->numbers, batch->positions, batch->cells, batch->pbc, batch->offsets, batch->structures,
+                       batch->atoms};
+        unsigned* error = st.error.as<unsigned>();
+        const bool timed = plan->timing;
+        if (timed && !st.timing[0])
+            for (auto& e : st.timing) check(cudaEventCreate(&e), "timing event");
+        if (timed) check(cudaEventRecord(st.timing[0], s), "timing event");
+        plan->bin(st, db, s, error);
+        if (timed) check(cudaEventRecord(st.timing[1], s), "timing event");
+        // Structure ranges are only needed for the averages; the device batch
+        // is one block.
+        plan->run_block(st, db, 0, batch->structures, 0, batch->atoms, out, s, error, timed ? st.timing[2] : nullptr);
+        if (timed) check(cudaEventRecord(st.timing[3], s), "timing event");
+        st.timed = timed;
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
+
+int mdsoap_plan_check(mdsoap_plan* plan, int32_t device, void* stream) {
+    if (!plan) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        DeviceState& st = plan->state(device);
+        check(cudaSetDevice(device), "cudaSetDevice");
+        check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "stream sync");
+        unsigned bits = 0;
+        check(cudaMemcpy(&bits, st.error.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "read error word");
+        check(cudaMemset(st.error.ptr, 0, sizeof(unsigned)), "clear error word");
+        if (bits)
+            return fail(bits & (kErrUnknownSpecies | kErrMixedPbc | kErrSingularCell) ? MDSOAP_INVALID_ARGUMENT
+                                                                                      : MDSOAP_INTERNAL,
+                        device_error_text(bits));
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    }
+}
+
+int mdsoap_plan_set_timing(mdsoap_plan* plan, int32_t enable) {
+    if (!plan) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    plan->timing = enable != 0;
+    return MDSOAP_OK;
+}
+
+int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, double* center_ms,
+                            double* structure_ms) {
+    if (!plan) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        DeviceState& st = plan->state(device);
+        if (!st.timed) return fail(MDSOAP_INVALID_ARGUMENT, "no timed device call on this device");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        check(cudaEventSynchronize(st.timing[3]), "timing sync");
+        float a = 0, b = 0, c = 0;
+        check(cudaEventElapsedTime(&a, st.timing[0], st.timing[1]), "elapsed");
+        check(cudaEventElapsedTime(&b, st.timing[1], st.timing[2]), "elapsed");
+        check(cudaEventElapsedTime(&c, st.timing[2], st.timing[3]), "elapsed");
+        if (bin_ms) *bin_ms = a;
+        if (center_ms) *center_ms = b;
+        if (structure_ms) *structure_ms = c;
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    }
+}
+
+int mdsoap_probe_fp64_fma(int32_t device, double* tflops) {
+    if (!tflops) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        int count = 0;
+        if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count)
+            raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device unavailable");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        int sms = 0;
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "SM count");
+        DeviceBytes sink;
+        const int blocks = sms * 8, threads = 256;
+        sink.reserve(8 * (size_t)blocks * threads, "probe sink");
+        cudaEvent_t e0, e1;
+        check(cudaEventCreate(&e0), "event");
+        check(cudaEventCreate(&e1), "event");
+        const int iters = 4096;
+        fma_probe_kernel<<<blocks, threads>>>(sink.as<double>(), iters);  // warm-up
+        check(cudaEventRecord(e0), "event");
+        const int reps = 8;
+        for (int r = 0; r < reps; ++r) fma_probe_kernel<<<blocks, threads>>>(sink.as<double>(), iters);
+        check(cudaEventRecord(e1), "event");
+        check(cudaEventSynchronize(e1), "probe sync");
+        float ms = 0;
+        check(cudaEventElapsedTime(&ms, e0, e1), "elapsed");
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        sink.release();
+        const double flops = 2.0 * kProbeChains * (double)iters * blocks * threads * reps;
+        *tflops = flops / (ms * 1e-3) / 1e12;
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    }
+}
+
+int mdsoap_graph_build(const mdsoap_batch* batch, double cutoff, int32_t device, mdsoap_graph** graph_out) {
+    if (!batch || !graph_out) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    *graph_out = nullptr;
+    if (!std::isfinite(cutoff) || cutoff <= 0.0)
+        return fail(MDSOAP_INVALID_ARGUMENT, "neighbor cutoff must be finite and positive");
+    try {
+        validate_host_batch(nullptr, *batch);
+        int count = 0;
+        const cudaError_t probe_err = cudaGetDeviceCount(&count);
+        if (probe_err != cudaSuccess || count == 0)
+            raise(MDSOAP_DEVICE_UNAVAILABLE, std::string("no CUDA device available: ") + cudaGetErrorString(probe_err));
+        if (device < 0 || device >= count) raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device index out of range");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        auto g = std::make_unique<mdsoap_graph>();
+        const int64_t atoms = batch->atoms, S = batch->structures;
+        g->atoms = atoms;
+        g->offsets.assign(atoms + 1, 0);
+        if (atoms == 0 || S == 0) {
+            *graph_out = g.release();
+            return MDSOAP_OK;
+        }
+        cudaStream_t stream = nullptr;
+        check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+        struct StreamGuard {
+            cudaStream_t s;
+            ~StreamGuard() { cudaStreamDestroy(s); }
+        } guard{stream};
+        Workspace w;
+        struct WorkGuard {
+            Workspace& w;
+            ~WorkGuard() { w.release(); }
+        } wguard{w};
+        DeviceBytes error, counts, offsets_d, atoms_d, shifts_d, disp_d, d2_d;
+        struct BytesGuard {
+            std::vector<DeviceBytes*> list;
+            ~BytesGuard() {
+                for (auto* b : list) b->release();
+            }
+        } bguard{{&error, &counts, &offsets_d, &atoms_d, &shifts_d, &disp_d, &d2_d}};
+        w.numbers.reserve(4 * atoms, "numbers");
+        w.positions.reserve(24 * atoms, "positions");
+        w.cells.reserve(72 * S, "cells");
+        w.pbc.reserve(12 * S, "pbc");
+        w.offsets.reserve(8 * (S + 1), "offsets");
+        check(cudaMemcpyAsync(w.numbers.ptr, batch->numbers, 4 * atoms, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.positions.ptr, batch->positions, 24 * atoms, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.cells.ptr, batch->cells, 72 * S, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.pbc.ptr, batch->pbc, 12 * S, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.offsets.ptr, batch->offsets, 8 * (S + 1), cudaMemcpyHostToDevice, stream), "H2D");
+        error.reserve(64, "error");
+        check(cudaMemsetAsync(error.ptr, 0, 64, stream), "memset");
+        w.reserve_bins(atoms, S);
+        DeviceBatch db{w.numbers.as<int32_t>(), w.positions.as<double>(), w.cells.as<double>(), w.pbc.as<int32_t>(),
+                       w.offsets.as<int64_t>(), S, atoms};
+        // Species lookup is irrelevant here: pass an empty list (types -> -1,
+        // the unknown-species bit is ignored below).
+        bin_structures_kernel<<<(unsigned)S, 256, 0, stream>>>(db, w.bins(error.as<unsigned>()), cutoff, nullptr, 0);
+        check(cudaGetLastError(), "bin kernel");
+        counts.reserve(8 * atoms, "counts");
+        const double cutoff2 = cutoff * cutoff;
+        const unsigned grid = (unsigned)((atoms + 7) / 8);
+        graph_count_kernel<<<grid, 256, 0, stream>>>(db.positions, w.bins(error.as<unsigned>()), atoms, cutoff2,
+                                                     counts.as<int64_t>());
+        check(cudaGetLastError(), "count kernel");
+        std::vector<int64_t> host_counts(atoms);
+        check(cudaMemcpyAsync(host_counts.data(), counts.ptr, 8 * atoms, cudaMemcpyDeviceToHost, stream), "D2H counts");
+        check(cudaStreamSynchronize(stream), "sync");
+        unsigned bits = 0;
+        check(cudaMemcpy(&bits, error.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "error word");
+        bits &= ~kErrUnknownSpecies;
+        if (bits) raise(bits & (kErrMixedPbc | kErrSingularCell) ? MDSOAP_INVALID_ARGUMENT : MDSOAP_INTERNAL,
+                        device_error_text(bits));
+        for (int64_t a = 0; a < atoms; ++a) g->offsets[a + 1] = g->offsets[a] + host_counts[a];
+        const int64_t pairs = g->offsets[atoms];
+        offsets_d.reserve(8 * (atoms + 1), "offsets");
+        atoms_d.reserve(4 * std::max<int64_t>(pairs, 1), "pair atoms");
+        shifts_d.reserve(12 * std::max<int64_t>(pairs, 1), "pair shifts");
+        disp_d.reserve(24 * std::max<int64_t>(pairs, 1), "pair displacements");
+        d2_d.reserve(8 * std::max<int64_t>(pairs, 1), "pair distances");
+        check(cudaMemcpyAsync(offsets_d.ptr, g->offsets.data(), 8 * (atoms + 1), cudaMemcpyHostToDevice, stream), "H2D");
+        graph_fill_kernel<<<grid, 256, 0, stream>>>(db.positions, w.bins(error.as<unsigned>()), atoms, cutoff2,
+                                                    offsets_d.as<int64_t>(), atoms_d.as<int32_t>(),
+                                                    shifts_d.as<int32_t>(), disp_d.as<double>(), d2_d.as<double>());
+        check(cudaGetLastError(), "fill kernel");
+        g->atom_ids.resize(pairs);
+        g->shifts.resize(3 * pairs);
+        g->displacements.resize(3 * pairs);
+        g->distance2.resize(pairs);
+        if (pairs) {
+            check(cudaMemcpyAsync(g->atom_ids.data(), atoms_d.ptr, 4 * pairs, cudaMemcpyDeviceToHost, stream), "D2H");
+            check(cudaMemcpyAsync(g->shifts.data(), shifts_d.ptr, 12 * pairs, cudaMemcpyDeviceToHost, stream), "D2H");
+            check(cudaMemcpyAsync(g->displacements.data(), disp_d.ptr, 24 * pairs, cudaMemcpyDeviceToHost, stream), "D2H");
+            check(cudaMemcpyAsync(g->distance2.data(), d2_d.ptr, 8 * pairs, cudaMemcpyDeviceToHost, stream), "D2H");
+        }
+        check(cudaStreamSynchronize(stream), "sync");
+        check(cudaMemcpy(&bits, error.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "error word");
+        bits &= ~kErrUnknownSpecies;
+        if (bits) raise(MDSOAP_INTERNAL, device_error_text(bits));
+        *graph_out = g.release();
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
+
+int64_t mdsoap_graph_pairs(const mdsoap_graph* graph) { return graph ? (int64_t)graph->atom_ids.size() : 0; }
+
+int mdsoap_graph_copy(const mdsoap_graph* graph, int64_t* offsets, int32_t* atoms, int32_t* shifts,
+                      double* displacements, double* distance2) {
+    if (!graph) return fail(MDSOAP_INVALID_ARGUMENT, "null graph");
+    if (offsets) std::memcpy(offsets, graph->offsets.data(), 8 * graph->offsets.size());
+    if (atoms && !graph->atom_ids.empty()) std::memcpy(atoms, graph->atom_ids.data(), 4 * graph->atom_ids.size());
+    if (shifts && !graph->shifts.empty()) std::memcpy(shifts, graph->shifts.data(), 4 * graph->shifts.size());
+    if (displacements && !graph->displacements.empty())
+        std::memcpy(displacements, graph->displacements.data(), 8 * graph->displacements.size());
+    if (distance2 && !graph->distance2.empty())
+        std::memcpy(distance2, graph->distance2.data(), 8 * graph->distance2.size());
+    return MDSOAP_OK;
+}
+
+void mdsoap_graph_destroy(mdsoap_graph* graph) { delete graph; }
+
+}  // extern "C"

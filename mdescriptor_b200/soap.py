@@ -1,0 +1,198 @@
+"""Python front-end of the B200 SOAP engine (over the C ABI in include/mdsoap.h).
+
+``Soap`` mirrors the constructor arguments and output layout of MDescriptor's
+``SoapKernel`` (src/mdescriptor/descriptors/_kernels/core.py:156-304) for the
+GTO / compression-off path: ``compute(batch)`` returns the (rows, F) matrix
+that ``SoapKernel.compute(...).values`` holds, in the requested dtype.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Any, Callable, Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import BatchView, CancelFn, Params, lib, raise_for
+from .basis import basis_gto, feature_count, graph_cutoff, labels
+
+
+def _contiguous(batch) -> tuple[np.ndarray, ...]:
+    numbers = np.ascontiguousarray(batch.numbers, dtype=np.int32)
+    positions = np.ascontiguousarray(batch.positions, dtype=np.float64).reshape(-1, 3)
+    cells = np.ascontiguousarray(batch.cells, dtype=np.float64).reshape(-1, 3, 3)
+    pbc = np.ascontiguousarray(batch.pbc, dtype=np.int32).reshape(-1, 3)
+    offsets = np.ascontiguousarray(batch.offsets, dtype=np.int64)
+    return numbers, positions, cells, pbc, offsets
+
+
+def host_view(arrays: Sequence[np.ndarray]) -> BatchView:
+    numbers, positions, cells, pbc, offsets = arrays
+    return BatchView(numbers.ctypes.data, positions.ctypes.data, cells.ctypes.data, pbc.ctypes.data,
+                     offsets.ctypes.data, int(offsets.shape[0]) - 1, int(numbers.shape[0]))
+
+
+def device_view(numbers: int, positions: int, cells: int, pbc: int, offsets: int, structures: int,
+                atoms: int) -> BatchView:
+    """Batch view over device pointers (e.g. ``tensor.data_ptr()``)."""
+    return BatchView(numbers, positions, cells, pbc, offsets, structures, atoms)
+
+
+class Soap:
+    """GTO SOAP power spectrum (compression off) computed on B200 GPUs.
+
+    Parameters follow ``SoapKernel``: species (declared order), r_cut, n_max,
+    l_max, sigma, average ("off" | "inner" | "outer"), dtype ("float32" |
+    "float64"), species_weights (the ``compression["species_weighting"]``
+    mapping, optional).  ``alphas``/``betas`` default to the reference basis
+    construction (``basis_gto``); the plugin passes the adapter's payload.
+    """
+
+    def __init__(self, species: Sequence[int], r_cut: float = 6.0, n_max: int = 8, l_max: int = 6,
+                 sigma: float = 1.0, average: str = "inner", dtype: str = "float64",
+                 species_weights: dict | Sequence[float] | None = None,
+                 alphas: np.ndarray | None = None, betas: np.ndarray | None = None) -> None:
+        self.species = tuple(int(z) for z in species)
+        self.r_cut = float(r_cut)
+        self.n_max = int(n_max)
+        self.l_max = int(l_max)
+        self.sigma = float(sigma)
+        if average not in _lib.AVERAGE:
+            raise ValueError("average must be 'off', 'inner', or 'outer'")
+        self.average = average
+        if dtype not in ("float32", "float64"):
+            raise ValueError("dtype must be 'float32' or 'float64'")
+        self.dtype = np.dtype(dtype)
+        if alphas is None or betas is None:
+            alphas, betas = basis_gto(self.r_cut, self.n_max, self.l_max)
+        self._alphas = np.ascontiguousarray(alphas, dtype=np.float64).ravel()
+        self._betas = np.ascontiguousarray(betas, dtype=np.float64).ravel()
+        self._species = np.asarray(self.species, dtype=np.int32)
+        if species_weights is None:
+            self._weights = None
+        elif isinstance(species_weights, dict):
+            if set(species_weights) != set(self.species):
+                raise ValueError("species_weighting must contain exactly the configured species")
+            self._weights = np.asarray([float(species_weights[z]) for z in self.species], np.float64)
+        else:
+            self._weights = np.ascontiguousarray(species_weights, dtype=np.float64)
+        params = Params(
+            len(self.species), self._species.ctypes.data,
+            None if self._weights is None else self._weights.ctypes.data,
+            self.r_cut, self.sigma, self.n_max, self.l_max, self._alphas.ctypes.data,
+            self._betas.ctypes.data, _lib.AVERAGE[average],
+            _lib.FLOAT64 if self.dtype == np.float64 else _lib.FLOAT32)
+        handle = ctypes.c_void_p()
+        raise_for(lib.mdsoap_plan_create(ctypes.byref(params), ctypes.byref(handle)))
+        self._plan = handle
+        self.feature_count = int(lib.mdsoap_plan_feature_count(self._plan))
+        assert self.feature_count == feature_count(len(self.species), self.n_max, self.l_max)
+
+    @property
+    def cutoff(self) -> float:
+        return graph_cutoff(self.r_cut, self.sigma)
+
+    def labels(self) -> tuple[str, ...]:
+        return labels(self.species, self.n_max, self.l_max)
+
+    def rows(self, batch) -> int:
+        return int(batch.offsets.shape[0]) - 1 if self.average != "off" else int(batch.offsets[-1])
+
+    def compute(self, batch, devices: Sequence[int] | None = None, out: np.ndarray | None = None,
+                cancelled: Callable[[], bool] | None = None) -> np.ndarray:
+        """End to end: host batch in, host (rows, F) matrix out (C ABI ``mdsoap_compute``)."""
+        arrays = _contiguous(batch)
+        view = host_view(arrays)
+        rows = self.rows(batch)
+        if out is None:
+            out = np.empty((rows, self.feature_count), dtype=self.dtype)
+        elif out.shape != (rows, self.feature_count) or out.dtype != self.dtype or not out.flags.c_contiguous:
+            raise ValueError("out has the wrong shape, dtype or layout")
+        ids = None
+        count = 0
+        if devices:
+            ids = np.ascontiguousarray(devices, dtype=np.int32)
+            count = len(ids)
+        callback = None if cancelled is None else CancelFn(lambda _ctx: 1 if cancelled() else 0)
+        status = lib.mdsoap_compute(self._plan, ctypes.byref(view), out.ctypes.data if out.size else None,
+                                    None if ids is None else ids.ctypes.data, count,
+                                    ctypes.cast(callback, ctypes.c_void_p) if callback else None, None)
+        raise_for(status)
+        return out
+
+    def compute_device(self, view: BatchView, out_ptr: int, device: int = 0, stream: int = 0) -> None:
+        """Enqueue the pipeline on device memory (C ABI ``mdsoap_compute_device``)."""
+        raise_for(lib.mdsoap_compute_device(self._plan, ctypes.byref(view), out_ptr or None, int(device),
+                                            stream or None))
+
+    def set_timing(self, enable: bool) -> None:
+        raise_for(lib.mdsoap_plan_set_timing(self._plan, 1 if enable else 0))
+
+    def last_timing(self, device: int = 0) -> tuple[float, float, float]:
+        """(bin_ms, center_ms, structure_ms) of the last timed ``compute_device`` call."""
+        values = (ctypes.c_double * 3)()
+        raise_for(lib.mdsoap_plan_last_timing(self._plan, int(device), ctypes.byref(values, 0),
+                                              ctypes.byref(values, 8), ctypes.byref(values, 16)))
+        return values[0], values[1], values[2]
+
+    def check(self, device: int = 0, stream: int = 0) -> None:
+        raise_for(lib.mdsoap_plan_check(self._plan, int(device), stream or None))
+
+    def close(self) -> None:
+        if getattr(self, "_plan", None):
+            lib.mdsoap_plan_destroy(self._plan)
+            self._plan = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def neighbor_graph(batch, cutoff: float, device: int = 0):
+    """GPU neighbour graph (C ABI ``mdsoap_graph_build``):
+    (offsets, atoms, shifts, displacements, distance2) like the reference's
+    ``build_neighbor_graph`` over the whole batch (cpp/src/common/neighbor.cpp:703-768)."""
+    arrays = _contiguous(batch)
+    view = host_view(arrays)
+    handle = ctypes.c_void_p()
+    raise_for(lib.mdsoap_graph_build(ctypes.byref(view), float(cutoff), int(device), ctypes.byref(handle)))
+    try:
+        pairs = int(lib.mdsoap_graph_pairs(handle))
+        atoms_total = int(arrays[4][-1])
+        offsets = np.zeros(atoms_total + 1, np.int64)
+        atoms = np.zeros(pairs, np.int32)
+        shifts = np.zeros((pairs, 3), np.int32)
+        displacements = np.zeros((pairs, 3), np.float64)
+        distance2 = np.zeros(pairs, np.float64)
+        raise_for(lib.mdsoap_graph_copy(handle, offsets.ctypes.data, atoms.ctypes.data, shifts.ctypes.data,
+                                        displacements.ctypes.data, distance2.ctypes.data))
+    finally:
+        lib.mdsoap_graph_destroy(handle)
+    return offsets, atoms, shifts, displacements, distance2
+
+
+def probe_fp64_fma(device: int = 0) -> float:
+    """Measured fp64 FMA throughput of one device, TFLOP/s."""
+    value = ctypes.c_double()
+    raise_for(lib.mdsoap_probe_fp64_fma(int(device), ctypes.byref(value)))
+    return float(value.value)
+
+
+def device_count() -> int:
+    return int(lib.mdsoap_device_count())
+
+
+def options_from_payload(options: dict[str, Any]) -> dict[str, Any]:
+    """Decode the adapter's backend options (src/mdescriptor/core/adapter.py:529-603)
+    into ``Soap`` keyword arguments; used by tests that mimic the plugin seam."""
+    payload = options["_cuda_payload"]["radial_basis"]
+    output = options.get("output") or {}
+    compression = options.get("compression") or {}
+    return dict(species=options["species"], r_cut=options.get("r_cut", 6.0), n_max=options.get("n_max", 8),
+                l_max=options.get("l_max", 6), sigma=options.get("sigma", 1.0),
+                average=options.get("average", "inner"), dtype=output.get("dtype", "float64"),
+                species_weights=compression.get("species_weighting"),
+                alphas=payload["alphas"], betas=payload["betas"])

@@ -1,0 +1,196 @@
+"""TEST INFRASTRUCTURE ONLY -- ctypes front-end for the CPU checkers.
+
+``OracleLib`` wraps ``oracle/liboracle_soap.so`` (the plain-C restatement in
+``soap_oracle.c``); ``RefLib`` wraps ``oracle/_ref/libref_soap.so`` (the
+reference's own ``compute_soap`` / ``build_neighbor_graph`` compiled from its
+sources, see ``build_oracle.py``).  Both expose the same two calls:
+
+* ``graph(batch, cutoff)`` -> ``(offsets, atoms, shifts, displacements, distance2)``
+  with global atom indices, like ``build_neighbor_graph`` over a whole batch
+  (cpp/src/common/neighbor.cpp:703-768);
+* ``soap(batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average)``
+  -> fp64 ``(rows, F)`` features, like ``compute_soap``
+  (cpp/src/standalone/soap.cpp:1149-1246).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg import this module.  The product package never does.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+ORACLE_DIR = Path(__file__).resolve().parent
+_P = ctypes.c_void_p
+_AVERAGE = {"off": 0, "inner": 1, "outer": 2}
+
+
+def _ptr(array: np.ndarray) -> ctypes.c_void_p:
+    return ctypes.c_void_p(array.ctypes.data)
+
+
+def _batch_arrays(batch):
+    numbers = np.ascontiguousarray(batch.numbers, dtype=np.int32)
+    positions = np.ascontiguousarray(batch.positions, dtype=np.float64)
+    cells = np.ascontiguousarray(batch.cells, dtype=np.float64)
+    pbc = np.ascontiguousarray(batch.pbc, dtype=np.int32)
+    offsets = np.ascontiguousarray(batch.offsets, dtype=np.int64)
+    return numbers, positions, cells, pbc, offsets
+
+
+def feature_count(n_species: int, n_max: int, l_max: int) -> int:
+    width = n_species * n_max
+    return width * (width + 1) // 2 * (l_max + 1)
+
+
+class _Checker:
+    prefix = ""
+
+    def __init__(self, path: Path) -> None:
+        if not path.is_file():
+            raise FileNotFoundError(f"checker library {path} is not built")
+        self.lib = ctypes.CDLL(str(path))
+        p = self.prefix
+        self._last_error = getattr(self.lib, f"{p}_last_error")
+        self._last_error.restype = ctypes.c_char_p
+        self._build = getattr(self.lib, f"{p}_graph_build")
+        self._pairs = getattr(self.lib, f"{p}_graph_pairs")
+        self._pairs.restype = ctypes.c_int64
+        self._pairs.argtypes = [_P]
+        self._copy = getattr(self.lib, f"{p}_graph_copy")
+        self._copy.argtypes = [_P] * 6
+        self._free = getattr(self.lib, f"{p}_graph_free")
+        self._free.argtypes = [_P]
+        self._soap = getattr(self.lib, f"{p}_soap_compute")
+
+    def error(self) -> str:
+        return self._last_error().decode()
+
+    def _graph_handle(self, arrays, structures: int, cutoff: float):
+        raise NotImplementedError
+
+    def graph(self, batch, cutoff: float):
+        arrays = _batch_arrays(batch)
+        structures = len(arrays[4]) - 1
+        handle = self._graph_handle(arrays, structures, cutoff)
+        if not handle:
+            raise ValueError(self.error())
+        try:
+            pairs = self._pairs(handle)
+            atoms_total = int(arrays[4][-1])
+            offsets = np.zeros(atoms_total + 1, np.int64)
+            atoms = np.zeros(pairs, np.int32)
+            shifts = np.zeros((pairs, 3), np.int32)
+            displacements = np.zeros((pairs, 3), np.float64)
+            distance2 = np.zeros(pairs, np.float64)
+            self._copy(handle, _ptr(offsets), _ptr(atoms), _ptr(shifts), _ptr(displacements),
+                       _ptr(distance2))
+        finally:
+            self._free(handle)
+        return offsets, atoms, shifts, displacements, distance2
+
+
+class OracleLib(_Checker):
+    """The plain-C restatement (soap_oracle.c)."""
+
+    prefix = "oracle"
+
+    def __init__(self, path: Path | None = None) -> None:
+        super().__init__(path or ORACLE_DIR / "liboracle_soap.so")
+        self._build.restype = _P
+        self._build.argtypes = [_P] * 5 + [ctypes.c_int64, ctypes.c_double]
+        self._soap.restype = ctypes.c_int
+        self._soap.argtypes = ([_P] * 5 + [ctypes.c_int64, _P, ctypes.c_int, _P, ctypes.c_double,
+                                ctypes.c_int, ctypes.c_int, ctypes.c_double, _P, _P, ctypes.c_int,
+                                ctypes.c_int, _P])
+
+        self._rows = self.lib.oracle_soap_rows
+        self._rows.restype = ctypes.c_int
+        self._rows.argtypes = ([_P] * 5 + [ctypes.c_int64, _P, ctypes.c_int, _P, ctypes.c_double,
+                                ctypes.c_int, ctypes.c_int, ctypes.c_double, _P, _P, _P, ctypes.c_int64, _P])
+
+    def _graph_handle(self, arrays, structures, cutoff):
+        return self._build(*map(_ptr, arrays), structures, cutoff)
+
+    def soap_rows(self, batch, rows, species, r_cut, n_max, l_max, sigma, alphas, betas, species_weights=None):
+        """Average-off feature rows of the selected atoms only (global indices)."""
+        arrays = _batch_arrays(batch)
+        structures = len(arrays[4]) - 1
+        species = np.ascontiguousarray(species, dtype=np.int32)
+        rows = np.ascontiguousarray(rows, dtype=np.int64)
+        out = np.zeros((len(rows), feature_count(len(species), n_max, l_max)), np.float64)
+        weights = None if species_weights is None else np.ascontiguousarray(species_weights, np.float64)
+        alphas = np.ascontiguousarray(alphas, np.float64)
+        betas = np.ascontiguousarray(betas, np.float64)
+        status = self._rows(*map(_ptr, arrays), structures, _ptr(species), len(species),
+                            None if weights is None else _ptr(weights), float(r_cut), int(n_max), int(l_max),
+                            float(sigma), _ptr(alphas), _ptr(betas), _ptr(rows), len(rows), _ptr(out))
+        if status:
+            raise ValueError(self.error())
+        return out
+
+    def soap(self, batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average="off",
+             species_weights=None, num_threads=0):
+        arrays = _batch_arrays(batch)
+        structures = len(arrays[4]) - 1
+        species = np.ascontiguousarray(species, dtype=np.int32)
+        rows = structures if average != "off" else int(arrays[4][-1])
+        out = np.zeros((rows, feature_count(len(species), n_max, l_max)), np.float64)
+        weights = None if species_weights is None else np.ascontiguousarray(species_weights, np.float64)
+        alphas = np.ascontiguousarray(alphas, np.float64)
+        betas = np.ascontiguousarray(betas, np.float64)
+        status = self._soap(*map(_ptr, arrays), structures, _ptr(species), len(species),
+                            None if weights is None else _ptr(weights), float(r_cut), int(n_max),
+                            int(l_max), float(sigma), _ptr(alphas), _ptr(betas), _AVERAGE[average],
+                            int(num_threads), _ptr(out))
+        if status:
+            raise ValueError(self.error())
+        return out
+
+
+class RefLib(_Checker):
+    """The reference's own CPU path, compiled from its sources into oracle/_ref."""
+
+    prefix = "ref"
+
+    def __init__(self, path: Path | None = None) -> None:
+        super().__init__(path or ORACLE_DIR / "_ref" / "libref_soap.so")
+        self._build.restype = _P
+        self._build.argtypes = [_P] * 5 + [ctypes.c_int64, ctypes.c_double, ctypes.c_int]
+        self._soap.restype = ctypes.c_int
+        self._soap.argtypes = ([_P] * 5 + [ctypes.c_int64, _P, ctypes.c_int, ctypes.c_double,
+                                ctypes.c_int, ctypes.c_int, ctypes.c_double, _P, _P, ctypes.c_int,
+                                ctypes.c_int, _P])
+
+    def _graph_handle(self, arrays, structures, cutoff):
+        return self._build(*map(_ptr, arrays), structures, cutoff, 1)
+
+    def soap(self, batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average="off",
+             species_weights=None, num_threads=0):
+        if species_weights is not None:
+            raise ValueError("the reference entry layer runs with unit species weights")
+        arrays = _batch_arrays(batch)
+        structures = len(arrays[4]) - 1
+        species = np.ascontiguousarray(species, dtype=np.int32)
+        rows = structures if average != "off" else int(arrays[4][-1])
+        out = np.zeros((rows, feature_count(len(species), n_max, l_max)), np.float64)
+        alphas = np.ascontiguousarray(alphas, np.float64)
+        betas = np.ascontiguousarray(betas, np.float64)
+        status = self._soap(*map(_ptr, arrays), structures, _ptr(species), len(species),
+                            float(r_cut), int(n_max), int(l_max), float(sigma), _ptr(alphas),
+                            _ptr(betas), _AVERAGE[average], int(num_threads), _ptr(out))
+        if status:
+            raise ValueError(self.error())
+        return out
+
+
+def reference_available() -> bool:
+    return (ORACLE_DIR / "_ref" / "libref_soap.so").is_file()
+
+
+def cpu_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)

@@ -1,0 +1,111 @@
+// Test infrastructure only: a C entry layer over the reference's own CPU SOAP
+// and neighbour-graph code, compiled from the reference sources in place by
+// oracle/build_oracle.py into oracle/_ref/.  Nothing in the product links or
+// calls this file.  It is the "reference" CPU baseline that bench.py times and
+// the checker that pins the plain-C restatement in oracle/soap_oracle.c.
+//
+// Wrapped reference entry points:
+//   mdescriptor::compute_soap            cpp/src/standalone/soap.cpp:1149
+//   mdescriptor::build_neighbor_graph    cpp/src/common/neighbor.cpp:703
+#include "mdescriptor/descriptor.hpp"
+#include "mdescriptor/neighbor.hpp"
+
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+namespace {
+thread_local std::string g_error;
+
+mdescriptor::StructureBatchView make_view(
+    const int32_t* numbers, const double* positions, const double* cells,
+    const int32_t* pbc, const int64_t* offsets, int64_t structures) {
+    mdescriptor::StructureBatchView view;
+    view.numbers = numbers;
+    view.positions = positions;
+    view.cells = cells;
+    view.pbc = pbc;
+    view.offsets = offsets;
+    view.structures = structures;
+    view.atoms = offsets[structures];
+    return view;
+}
+
+struct GraphHandle {
+    mdescriptor::NeighborGraph graph;
+};
+}  // namespace
+
+extern "C" {
+
+const char* ref_last_error(void) { return g_error.c_str(); }
+
+// average: 0 off, 1 inner, 2 outer.  Output is fp64 (rows, features).
+int ref_soap_compute(
+    const int32_t* numbers, const double* positions, const double* cells,
+    const int32_t* pbc, const int64_t* offsets, int64_t structures,
+    const int32_t* species, int n_species, double r_cut, int n_max, int l_max,
+    double sigma, const double* alphas, const double* betas, int average,
+    int num_threads, double* out) {
+    try {
+        mdescriptor::SoapOptions options;
+        options.species.assign(species, species + n_species);
+        options.r_cut = r_cut;
+        options.n_max = n_max;
+        options.l_max = l_max;
+        options.sigma = sigma;
+        options.radial_basis = 0;
+        const size_t count = static_cast<size_t>((l_max + 1) * n_max);
+        options.alphas.assign(alphas, alphas + count);
+        options.betas.assign(betas, betas + count * n_max);
+        options.species_weights.assign(static_cast<size_t>(n_species), 1.0);
+        options.compression = 0;
+        options.inner_average = average == 1;
+        options.outer_average = average == 2;
+        options.num_threads = num_threads;
+        mdescriptor::compute_soap(
+            make_view(numbers, positions, cells, pbc, offsets, structures), options, out, nullptr);
+        return 0;
+    } catch (const std::exception& error) {
+        g_error = error.what();
+        return 1;
+    }
+}
+
+void* ref_graph_build(
+    const int32_t* numbers, const double* positions, const double* cells,
+    const int32_t* pbc, const int64_t* offsets, int64_t structures, double cutoff,
+    int num_threads) {
+    try {
+        auto* handle = new GraphHandle;
+        handle->graph = mdescriptor::build_neighbor_graph(
+            make_view(numbers, positions, cells, pbc, offsets, structures), cutoff, nullptr,
+            num_threads);
+        return handle;
+    } catch (const std::exception& error) {
+        g_error = error.what();
+        return nullptr;
+    }
+}
+
+int64_t ref_graph_pairs(void* handle) {
+    return static_cast<int64_t>(static_cast<GraphHandle*>(handle)->graph.atoms_data().size());
+}
+
+void ref_graph_copy(
+    void* handle, int64_t* offsets, int32_t* atoms, int32_t* shifts, double* displacements,
+    double* distance2) {
+    const auto& graph = static_cast<GraphHandle*>(handle)->graph;
+    std::memcpy(offsets, graph.offsets().data(), graph.offsets().size() * sizeof(int64_t));
+    std::memcpy(atoms, graph.atoms_data().data(), graph.atoms_data().size() * sizeof(int32_t));
+    std::memcpy(shifts, graph.shifts().data(), graph.shifts().size() * sizeof(int32_t));
+    std::memcpy(displacements, graph.displacements().data(),
+                graph.displacements().size() * sizeof(double));
+    std::memcpy(distance2, graph.distance2().data(), graph.distance2().size() * sizeof(double));
+}
+
+void ref_graph_free(void* handle) { delete static_cast<GraphHandle*>(handle); }
+
+}  // extern "C"

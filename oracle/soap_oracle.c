@@ -1,0 +1,703 @@
+/*
+ * TEST INFRASTRUCTURE ONLY -- the CPU checker for the SOAP hot path.
+ *
+ * A plain-C restatement of MDescriptor's CPU SOAP path (GTO radial basis,
+ * compression off, average off/inner/outer, optional species weights):
+ *   - neighbour graph: cpp/src/common/neighbor.cpp:423-679 (build_structure_graph,
+ *     store_shifts=true, include_boundary=true, unscaled images), build_grid
+ *     :135-194, CellGrid::coordinate :122-132, inverse/bounds math3.hpp:52-68 and
+ *     neighbor.cpp:455-468, image order :519-528, query :558-574, serial append
+ *     :579-608, batch concatenation :742-767;
+ *   - SOAP: cpp/src/standalone/soap.cpp:1149-1246 (compute_soap), prepare_soap
+ *     :507-572, solid harmonics :101-216 (the Cartesian recurrence, used here for
+ *     every l; the reference's literal l<=4 / l=6 tables and l>6 Legendre form
+ *     are the same functions), species-sorted accumulation :737-760 and
+ *     :881-929, power spectrum :997-1012, inner/outer averages :1019-1120.
+ *
+ * Floating-point order follows the reference expressions (no FMA contraction:
+ * the build passes -ffp-contract=off), so the neighbour graph is bit-identical
+ * to the reference's and the features agree to rounding.  Only tests/,
+ * __graft_entry__.smoke() and bench.py's CPU-baseline leg load this library;
+ * the product never does.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define OR_PI 3.141592653589793238462643383279502884
+#define OR_SQRT2 1.414213562373095048801688724209698079
+
+static _Thread_local char g_error[256];
+
+static int fail(const char* message) {
+    strncpy(g_error, message, sizeof(g_error) - 1);
+    g_error[sizeof(g_error) - 1] = '\0';
+    return 1;
+}
+
+const char* oracle_last_error(void) { return g_error; }
+
+/* ---------------------------------------------------------------- graph -- */
+
+typedef struct {
+    int64_t count, capacity;
+    int32_t* atoms;
+    int32_t* shifts;
+    double* displacements;
+    double* distance2;
+} pair_list;
+
+static int pair_push(pair_list* list, int32_t atom, const int32_t shift[3], const double d[3],
+                     double distance2) {
+    if (list->count == list->capacity) {
+        int64_t capacity = list->capacity ? list->capacity * 2 : 1024;
+        int32_t* atoms = realloc(list->atoms, (size_t)capacity * sizeof(int32_t));
+        if (!atoms) return 1;
+        list->atoms = atoms;
+        int32_t* shifts = realloc(list->shifts, (size_t)capacity * 3 * sizeof(int32_t));
+        if (!shifts) return 1;
+        list->shifts = shifts;
+        double* displacements = realloc(list->displacements, (size_t)capacity * 3 * sizeof(double));
+        if (!displacements) return 1;
+        list->displacements = displacements;
+        double* d2 = realloc(list->distance2, (size_t)capacity * sizeof(double));
+        if (!d2) return 1;
+        list->distance2 = d2;
+        list->capacity = capacity;
+    }
+    int64_t i = list->count++;
+    list->atoms[i] = atom;
+    memcpy(list->shifts + 3 * i, shift, 3 * sizeof(int32_t));
+    memcpy(list->displacements + 3 * i, d, 3 * sizeof(double));
+    list->distance2[i] = distance2;
+    return 0;
+}
+
+static void pair_free(pair_list* list) {
+    free(list->atoms);
+    free(list->shifts);
+    free(list->displacements);
+    free(list->distance2);
+    memset(list, 0, sizeof(*list));
+}
+
+typedef struct {
+    int32_t atom;
+    int32_t shift[3];
+    double position[3];
+} extended_atom;
+
+/* CellGrid::coordinate, neighbor.cpp:122-132 */
+static int grid_coordinate(double value, double origin, double width, int dimension) {
+    const double scaled = (value - origin) / width;
+    if (!(scaled > 0.0)) return 0;
+    if (!isfinite(scaled) || scaled >= (double)dimension) return dimension - 1;
+    return (int)scaled;
+}
+
+/* math3.hpp:44-68 (determinant, inverse) */
+static int inverse3(const double m[9], double r[9]) {
+    const double det = m[0] * (m[4] * m[8] - m[5] * m[7]) - m[1] * (m[3] * m[8] - m[5] * m[6])
+                       + m[2] * (m[3] * m[7] - m[4] * m[6]);
+    if (!isfinite(det) || fabs(det) < 1e-14) return 1;
+    r[0] = (m[4] * m[8] - m[5] * m[7]) / det;
+    r[1] = (m[2] * m[7] - m[1] * m[8]) / det;
+    r[2] = (m[1] * m[5] - m[2] * m[4]) / det;
+    r[3] = (m[5] * m[6] - m[3] * m[8]) / det;
+    r[4] = (m[0] * m[8] - m[2] * m[6]) / det;
+    r[5] = (m[2] * m[3] - m[0] * m[5]) / det;
+    r[6] = (m[3] * m[7] - m[4] * m[6]) / det;
+    r[7] = (m[1] * m[6] - m[0] * m[7]) / det;
+    r[8] = (m[0] * m[4] - m[1] * m[3]) / det;
+    return 0;
+}
+
+/*
+ * One structure's graph (neighbor.cpp:423-679).  `begin`/`end` index the batch;
+ * emitted atom indices are `index_base + local` with local in [0, end-begin).
+ * counts has end-begin+1 entries, relative to the list's size on entry.
+ */
+static int structure_graph(const double* positions, const double* cell, const int32_t* pbc,
+                           int64_t begin, int64_t end, double cutoff, int64_t index_base,
+                           const int64_t* subset, int64_t subset_count, pair_list* out, int64_t* counts) {
+    const int periodic = pbc[0] == 1 && pbc[1] == 1 && pbc[2] == 1;
+    const int isolated = pbc[0] == 0 && pbc[1] == 0 && pbc[2] == 0;
+    if (!periodic && !isolated) return fail("mixed periodicity is not supported; use all-zero or all-one pbc");
+    const int64_t atom_count = end - begin;
+    int bounds[3] = {0, 0, 0};
+    if (periodic) {
+        double inv[9];
+        if (inverse3(cell, inv)) return fail("cell matrix is singular");
+        for (int a = 0; a < 3; ++a) {
+            const double b = floor(cutoff * sqrt(inv[0 * 3 + a] * inv[0 * 3 + a] + inv[1 * 3 + a] * inv[1 * 3 + a]
+                                                 + inv[2 * 3 + a] * inv[2 * 3 + a]) + 1.0);
+            if (!isfinite(b) || b < 0.0 || b > 2147483647.0) return fail("periodic image range exceeds integer range");
+            bounds[a] = (int)b;
+        }
+    }
+    const int64_t images = (int64_t)(2 * bounds[0] + 1) * (2 * bounds[1] + 1) * (2 * bounds[2] + 1);
+    const int64_t extended_count = images * atom_count;
+    extended_atom* extended = malloc((size_t)(extended_count ? extended_count : 1) * sizeof(extended_atom));
+    if (!extended) return fail("out of memory");
+    int64_t e = 0;
+    /* image order n0 -> n1 -> n2, then atoms (neighbor.cpp:519-528, 471-498) */
+    for (int n0 = -bounds[0]; n0 <= bounds[0]; ++n0) {
+        for (int n1 = -bounds[1]; n1 <= bounds[1]; ++n1) {
+            for (int n2 = -bounds[2]; n2 <= bounds[2]; ++n2) {
+                double shift[3];
+                for (int c = 0; c < 3; ++c) {
+                    const double t0 = (double)n0 * cell[0 * 3 + c];
+                    const double t1 = (double)n1 * cell[1 * 3 + c];
+                    const double t2 = (double)n2 * cell[2 * 3 + c];
+                    shift[c] = (t0 + t1) + t2;
+                }
+                for (int64_t atom = begin; atom < end; ++atom) {
+                    extended_atom* x = &extended[e++];
+                    x->atom = (int32_t)(index_base + (atom - begin));
+                    x->shift[0] = n0;
+                    x->shift[1] = n1;
+                    x->shift[2] = n2;
+                    /* isolated structures keep the original position (neighbor.cpp:499-502) */
+                    for (int c = 0; c < 3; ++c)
+                        x->position[c] = periodic ? positions[3 * atom + c] + shift[c] : positions[3 * atom + c];
+                }
+            }
+        }
+    }
+    /* build_grid, neighbor.cpp:135-194 */
+    double minimum[3] = {0, 0, 0}, maximum[3] = {0, 0, 0}, spacing[3] = {0, 0, 0};
+    int dims[3] = {1, 1, 1};
+    int64_t* cell_offsets = NULL;
+    int32_t* cell_atoms = NULL;
+    if (extended_count > 0) {
+        for (int c = 0; c < 3; ++c) minimum[c] = maximum[c] = extended[0].position[c];
+        for (int64_t i = 0; i < extended_count; ++i) {
+            for (int c = 0; c < 3; ++c) {
+                const double v = extended[i].position[c];
+                if (v < minimum[c]) minimum[c] = v;
+                if (v > maximum[c]) maximum[c] = v;
+            }
+        }
+        for (int c = 0; c < 3; ++c) {
+            minimum[c] -= 1e-10;
+            maximum[c] += 1e-10;
+            const double range = maximum[c] - minimum[c];
+            const double cells = range / cutoff;
+            if (!isfinite(range) || range < 0.0 || !isfinite(cells) || cells > 2147483647.0) {
+                free(extended);
+                return fail("neighbor cell-grid dimension exceeds integer range");
+            }
+            dims[c] = (int)cells > 1 ? (int)cells : 1;
+            const double width = range / dims[c];
+            spacing[c] = cutoff > width ? cutoff : width;
+        }
+        const int64_t cell_count = (int64_t)dims[0] * dims[1] * dims[2];
+        cell_offsets = calloc((size_t)cell_count + 1, sizeof(int64_t));
+        int64_t* fill = calloc((size_t)cell_count, sizeof(int64_t));
+        int32_t* cell_of = malloc((size_t)extended_count * sizeof(int32_t));
+        cell_atoms = malloc((size_t)extended_count * sizeof(int32_t));
+        if (!cell_offsets || !fill || !cell_of || !cell_atoms) {
+            free(extended); free(cell_offsets); free(fill); free(cell_of); free(cell_atoms);
+            return fail("out of memory");
+        }
+        for (int64_t i = 0; i < extended_count; ++i) {
+            const int x = grid_coordinate(extended[i].position[0], minimum[0], spacing[0], dims[0]);
+            const int y = grid_coordinate(extended[i].position[1], minimum[1], spacing[1], dims[1]);
+            const int z = grid_coordinate(extended[i].position[2], minimum[2], spacing[2], dims[2]);
+            cell_of[i] = (int32_t)(x + (int64_t)dims[0] * (y + (int64_t)dims[1] * z));
+            ++cell_offsets[cell_of[i] + 1];
+        }
+        for (int64_t c = 0; c < cell_count; ++c) cell_offsets[c + 1] += cell_offsets[c];
+        for (int64_t i = 0; i < extended_count; ++i) {
+            const int32_t c = cell_of[i];
+            cell_atoms[cell_offsets[c] + fill[c]++] = (int32_t)i;
+        }
+        free(fill);
+        free(cell_of);
+    }
+    /* query + serial append, neighbor.cpp:552-608 */
+    const double cutoff2 = cutoff * cutoff;
+    const int64_t base = out->count;
+    const int64_t queries = subset ? subset_count : atom_count;
+    for (int64_t q = 0; q < queries; ++q) {
+        const int64_t local = subset ? subset[q] : q;
+        counts[q] = out->count - base;
+        if (extended_count == 0) continue;
+        const double* center = positions + 3 * (begin + local);
+        const int ix = grid_coordinate(center[0], minimum[0], spacing[0], dims[0]);
+        const int iy = grid_coordinate(center[1], minimum[1], spacing[1], dims[1]);
+        const int iz = grid_coordinate(center[2], minimum[2], spacing[2], dims[2]);
+        for (int z = iz - 1 > 0 ? iz - 1 : 0; z <= (iz + 1 < dims[2] - 1 ? iz + 1 : dims[2] - 1); ++z) {
+            for (int y = iy - 1 > 0 ? iy - 1 : 0; y <= (iy + 1 < dims[1] - 1 ? iy + 1 : dims[1] - 1); ++y) {
+                for (int x = ix - 1 > 0 ? ix - 1 : 0; x <= (ix + 1 < dims[0] - 1 ? ix + 1 : dims[0] - 1); ++x) {
+                    const int64_t c = x + (int64_t)dims[0] * (y + (int64_t)dims[1] * z);
+                    for (int64_t o = cell_offsets[c]; o < cell_offsets[c + 1]; ++o) {
+                        const extended_atom* n = &extended[cell_atoms[o]];
+                        const double d[3] = {n->position[0] - center[0], n->position[1] - center[1],
+                                             n->position[2] - center[2]};
+                        const double distance2 = d[0] * d[0] + d[1] * d[1] + d[2] * d[2];
+                        if (!(distance2 <= cutoff2)) continue;
+                        if (pair_push(out, n->atom, n->shift, d, distance2)) {
+                            free(extended); free(cell_offsets); free(cell_atoms);
+                            return fail("out of memory");
+                        }
+                    }
+                }
+            }
+        }
+    }
+    counts[queries] = out->count - base;
+    free(extended);
+    free(cell_offsets);
+    free(cell_atoms);
+    return 0;
+}
+
+typedef struct {
+    int64_t atoms;
+    int64_t* offsets;
+    pair_list pairs;
+} oracle_graph;
+
+static int validate_batch(const int32_t* numbers, const double* positions, const double* cells,
+                          const int32_t* pbc, const int64_t* offsets, int64_t structures) {
+    if (structures < 0 || !offsets) return fail("invalid structure batch");
+    if (offsets[0] != 0) return fail("offsets do not describe the flattened arrays");
+    for (int64_t s = 0; s < structures; ++s) {
+        if (offsets[s + 1] < offsets[s]) return fail("offsets must be monotonic");
+        int periodic = 1, isolated = 1;
+        for (int a = 0; a < 3; ++a) {
+            if (pbc[3 * s + a] != 0 && pbc[3 * s + a] != 1) return fail("pbc must contain only 0 or 1");
+            periodic = periodic && pbc[3 * s + a] == 1;
+            isolated = isolated && pbc[3 * s + a] == 0;
+        }
+        if (!periodic && !isolated) return fail("mixed periodicity is not supported; use all-zero or all-one pbc");
+        for (int k = 0; k < 9; ++k)
+            if (!isfinite(cells[9 * s + k])) return fail("cells must be finite");
+    }
+    for (int64_t i = 0; i < offsets[structures]; ++i) {
+        if (numbers[i] <= 0) return fail("atomic numbers must be positive");
+        for (int a = 0; a < 3; ++a)
+            if (!isfinite(positions[3 * i + a])) return fail("positions must be finite");
+    }
+    return 0;
+}
+
+/* build_neighbor_graph over a whole batch (neighbor.cpp:703-768): global atom
+ * indices, structures concatenated in order. */
+void* oracle_graph_build(const int32_t* numbers, const double* positions, const double* cells,
+                         const int32_t* pbc, const int64_t* offsets, int64_t structures,
+                         double cutoff) {
+    if (!isfinite(cutoff) || cutoff <= 0.0) {
+        fail("neighbor cutoff must be finite and positive");
+        return NULL;
+    }
+    if (validate_batch(numbers, positions, cells, pbc, offsets, structures)) return NULL;
+    oracle_graph* g = calloc(1, sizeof(oracle_graph));
+    const int64_t atoms = offsets[structures];
+    g->atoms = atoms;
+    g->offsets = calloc((size_t)atoms + 2, sizeof(int64_t));
+    int64_t* counts = malloc(((size_t)atoms + 2) * sizeof(int64_t));
+    for (int64_t s = 0; s < structures; ++s) {
+        const int64_t begin = offsets[s], end = offsets[s + 1];
+        const int64_t before = g->pairs.count;
+        if (structure_graph(positions, cells + 9 * s, pbc + 3 * s, begin, end, cutoff, begin, NULL, 0,
+                            &g->pairs, counts)) {
+            free(counts);
+            pair_free(&g->pairs);
+            free(g->offsets);
+            free(g);
+            return NULL;
+        }
+        for (int64_t local = 0; local <= end - begin; ++local) g->offsets[begin + local] = before + counts[local];
+    }
+    if (structures == 0) g->offsets[0] = 0;
+    free(counts);
+    return g;
+}
+
+int64_t oracle_graph_pairs(void* handle) { return ((oracle_graph*)handle)->pairs.count; }
+
+void oracle_graph_copy(void* handle, int64_t* offsets, int32_t* atoms, int32_t* shifts,
+                       double* displacements, double* distance2) {
+    oracle_graph* g = handle;
+    const int64_t p = g->pairs.count;
+    memcpy(offsets, g->offsets, ((size_t)g->atoms + 1) * sizeof(int64_t));
+    if (p) {
+        memcpy(atoms, g->pairs.atoms, (size_t)p * sizeof(int32_t));
+        memcpy(shifts, g->pairs.shifts, (size_t)p * 3 * sizeof(int32_t));
+        memcpy(displacements, g->pairs.displacements, (size_t)p * 3 * sizeof(double));
+        memcpy(distance2, g->pairs.distance2, (size_t)p * sizeof(double));
+    }
+}
+
+void oracle_graph_free(void* handle) {
+    oracle_graph* g = handle;
+    if (!g) return;
+    pair_free(&g->pairs);
+    free(g->offsets);
+    free(g);
+}
+
+/* ----------------------------------------------------------------- SOAP -- */
+
+typedef struct {
+    int n_species, n_max, l_max, width, harmonics;
+    const int32_t* species;
+    const double* species_weights;
+    const double* betas;
+    double soap_scale;
+    double* power_prefactors;   /* [L+1] */
+    double* normalization;      /* [(L+1)^2], l*width+m */
+    double* radial_prefactors;  /* [(L+1)*n] */
+    double* radial_exponents;   /* [(L+1)*n] */
+} soap_plan;
+
+/* Real regular solid harmonics r^l Y_lm, layout l^2 + (l-m) = cos m, l^2 + l = m0,
+ * l^2 + (l+m) = sin m (soap.cpp:101-216, generic Cartesian recurrence). */
+static void solid_harmonics(const soap_plan* plan, double x, double y, double z, double r2,
+                            double* real, double* imag, double* result) {
+    const int L = plan->l_max, w = plan->width;
+    for (int i = 0; i < w * w; ++i) real[i] = imag[i] = 0.0;
+    real[0] = 1.0;
+    for (int m = 0; m <= L; ++m) {
+        if (m > 0) {
+            const double factor = -(2.0 * m - 1.0);
+            const double pr = real[(m - 1) * w + (m - 1)], pi = imag[(m - 1) * w + (m - 1)];
+            real[m * w + m] = factor * (x * pr - y * pi);
+            imag[m * w + m] = factor * (x * pi + y * pr);
+        }
+        if (m == 0) {
+            if (L >= 1) real[1 * w + 0] = z;
+            for (int l = 2; l <= L; ++l)
+                real[l * w] = ((2.0 * l - 1.0) * z * real[(l - 1) * w] - (l - 1.0) * r2 * real[(l - 2) * w]) / l;
+        } else {
+            if (m < L) {
+                real[(m + 1) * w + m] = (2.0 * m + 1.0) * z * real[m * w + m];
+                imag[(m + 1) * w + m] = (2.0 * m + 1.0) * z * imag[m * w + m];
+            }
+            for (int l = m + 2; l <= L; ++l) {
+                real[l * w + m] = ((2.0 * l - 1.0) * z * real[(l - 1) * w + m]
+                                   - (l + m - 1.0) * r2 * real[(l - 2) * w + m]) / (l - m);
+                imag[l * w + m] = ((2.0 * l - 1.0) * z * imag[(l - 1) * w + m]
+                                   - (l + m - 1.0) * r2 * imag[(l - 2) * w + m]) / (l - m);
+            }
+        }
+    }
+    for (int l = 0; l <= L; ++l) {
+        result[l * l + l] = plan->normalization[l * w] * real[l * w];
+        for (int m = 1; m <= l; ++m) {
+            const double factor = OR_SQRT2 * plan->normalization[l * w + m];
+            result[l * l + (l - m)] = factor * real[l * w + m];
+            result[l * l + (l + m)] = factor * imag[l * w + m];
+        }
+    }
+}
+
+static int species_type(const soap_plan* plan, int32_t z) {
+    for (int t = 0; t < plan->n_species; ++t)
+        if (plan->species[t] == z) return t;
+    return -1;
+}
+
+/* calculate_coefficients (soap.cpp:701-931) for one centre of one structure. */
+static void center_coefficients(const soap_plan* plan, const int* atom_types, int64_t local,
+                                const pair_list* pairs, int64_t pair_begin, int64_t pair_end,
+                                int64_t structure_begin_index, double* coefficients,
+                                double* scratch) {
+    const int S = plan->n_species, n = plan->n_max, L = plan->l_max, H = plan->harmonics;
+    const int w = plan->width;
+    const int64_t count = pair_end - pair_begin;
+    memset(coefficients, 0, sizeof(double) * (size_t)S * n * H);
+    /* scratch layout */
+    int64_t* order = (int64_t*)scratch;
+    double* harm = scratch + count;                 /* [count][H] */
+    double* weight = harm + count * H;              /* [count] */
+    double* real = weight + count;
+    double* imag = real + w * w;
+    double* hs = imag + w * w;                      /* [2L+1] */
+    int64_t type_offsets[65];
+    int64_t cursor[64];
+    for (int t = 0; t <= S; ++t) type_offsets[t] = 0;
+    for (int64_t i = 0; i < count; ++i)
+        ++type_offsets[atom_types[pairs->atoms[pair_begin + i] - structure_begin_index] + 1];
+    for (int t = 0; t < S; ++t) type_offsets[t + 1] += type_offsets[t];
+    for (int t = 0; t < S; ++t) cursor[t] = type_offsets[t];
+    for (int64_t i = 0; i < count; ++i) {
+        const int t = atom_types[pairs->atoms[pair_begin + i] - structure_begin_index];
+        order[cursor[t]++] = pair_begin + i;
+    }
+    for (int64_t j = 0; j < count; ++j) {
+        const int64_t p = order[j];
+        const double* d = pairs->displacements + 3 * p;
+        solid_harmonics(plan, d[0], d[1], d[2], d[0] * d[0] + d[1] * d[1] + d[2] * d[2], real, imag,
+                        harm + j * H);
+    }
+    for (int t = 0; t < S; ++t)
+        for (int64_t j = type_offsets[t]; j < type_offsets[t + 1]; ++j) weight[j] = plan->species_weights[t];
+    (void)local;
+    for (int t = 0; t < S; ++t) {
+        for (int l = 0; l <= L; ++l) {
+            const int off = l * l, mc = 2 * l + 1;
+            for (int k = 0; k < n; ++k) {
+                const int ri = l * n + k;
+                for (int m = 0; m < mc; ++m) hs[m] = 0.0;
+                for (int64_t j = type_offsets[t]; j < type_offsets[t + 1]; ++j) {
+                    const double radial = plan->radial_prefactors[ri]
+                                          * exp(-plan->radial_exponents[ri] * pairs->distance2[order[j]]);
+                    for (int m = 0; m < mc; ++m) hs[m] += radial * harm[j * H + off + m] * weight[j];
+                }
+                for (int nn = 0; nn < n; ++nn) {
+                    const double beta = plan->betas[(l * n + nn) * n + k];
+                    double* dest = coefficients + (t * n + nn) * H + off;
+                    for (int m = 0; m < mc; ++m) dest[m] += plan->soap_scale * beta * hs[m];
+                }
+            }
+        }
+    }
+}
+
+/* power spectrum, compression off (soap.cpp:997-1012) */
+static void power_spectrum(const soap_plan* plan, const double* c, double* out) {
+    const int S = plan->n_species, n = plan->n_max, L = plan->l_max, H = plan->harmonics;
+    int64_t f = 0;
+    for (int t1 = 0; t1 < S; ++t1)
+        for (int t2 = t1; t2 < S; ++t2)
+            for (int l = 0; l <= L; ++l) {
+                const double pref = plan->power_prefactors[l];
+                for (int n1 = 0; n1 < n; ++n1)
+                    for (int n2 = (t1 == t2 ? n1 : 0); n2 < n; ++n2) {
+                        const double* a = c + (t1 * n + n1) * H + l * l;
+                        const double* b = c + (t2 * n + n2) * H + l * l;
+                        double sum = 0.0;
+                        for (int m = 0; m < 2 * l + 1; ++m) sum += a[m] * b[m];
+                        out[f++] = pref * sum;
+                    }
+            }
+}
+
+int64_t oracle_soap_feature_count(int n_species, int n_max, int l_max) {
+    const int64_t width = (int64_t)n_species * n_max;
+    return width * (width + 1) / 2 * (l_max + 1);
+}
+
+/*
+ * compute_soap (soap.cpp:1149-1246), GTO basis, compression off.
+ * average: 0 off (rows = atoms), 1 inner, 2 outer (rows = structures).
+ * species_weights may be NULL (all 1.0).  out is fp64 (rows, F).
+ */
+int oracle_soap_compute(const int32_t* numbers, const double* positions, const double* cells,
+                        const int32_t* pbc, const int64_t* offsets, int64_t structures,
+                        const int32_t* species, int n_species, const double* species_weights,
+                        double r_cut, int n_max, int l_max, double sigma, const double* alphas,
+                        const double* betas, int average, int num_threads, double* out) {
+    if (validate_batch(numbers, positions, cells, pbc, offsets, structures)) return 1;
+    if (!isfinite(r_cut) || !isfinite(sigma) || r_cut <= 0.0 || sigma <= 0.0 || n_max < 1 || l_max < 0
+        || l_max > 20 || n_species < 1 || n_species > 64 || average < 0 || average > 2)
+        return fail("invalid SOAP parameters");
+    soap_plan plan;
+    plan.n_species = n_species;
+    plan.n_max = n_max;
+    plan.l_max = l_max;
+    plan.width = l_max + 1;
+    plan.harmonics = (l_max + 1) * (l_max + 1);
+    plan.species = species;
+    double* ones = malloc(sizeof(double) * (size_t)n_species);
+    for (int t = 0; t < n_species; ++t) ones[t] = species_weights ? species_weights[t] : 1.0;
+    plan.species_weights = ones;
+    plan.betas = betas;
+    plan.soap_scale = OR_PI * sqrt(OR_PI);
+    const int w = l_max + 1;
+    plan.power_prefactors = malloc(sizeof(double) * w);
+    plan.normalization = calloc((size_t)w * w, sizeof(double));
+    plan.radial_prefactors = malloc(sizeof(double) * w * n_max);
+    plan.radial_exponents = malloc(sizeof(double) * w * n_max);
+    for (int l = 0; l <= l_max; ++l) {
+        plan.power_prefactors[l] = OR_PI * sqrt(8.0 / (2.0 * l + 1.0));
+        for (int m = 0; m <= l; ++m)
+            plan.normalization[l * w + m] =
+                sqrt((2.0 * l + 1.0) / (4.0 * OR_PI) * exp(lgamma(l - m + 1.0) - lgamma(l + m + 1.0)));
+    }
+    const double eta = 1.0 / (2.0 * sigma * sigma);
+    double eta_power = 1.0;
+    for (int l = 0; l <= l_max; ++l) {
+        if (l > 0) eta_power *= eta;
+        for (int k = 0; k < n_max; ++k) {
+            const int i = l * n_max + k;
+            const double alpha = alphas[i];
+            const double denominator = alpha + eta;
+            plan.radial_prefactors[i] = eta_power * pow(denominator, -l - 1.5);
+            plan.radial_exponents[i] = alpha * eta / denominator;
+        }
+    }
+    const double cutoff = r_cut + sigma * sqrt(-2.0 * log(1e-3));
+    const int64_t F = oracle_soap_feature_count(n_species, n_max, l_max);
+    const int64_t csize = (int64_t)n_species * n_max * plan.harmonics;
+    int status = 0;
+#ifdef _OPENMP
+    const int threads = num_threads > 0 ? num_threads : omp_get_max_threads();
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads) reduction(| : status)
+#endif
+    for (int64_t s = 0; s < structures; ++s) {
+        if (status) continue;
+        const int64_t begin = offsets[s], end = offsets[s + 1], atoms = end - begin;
+        pair_list pairs = {0};
+        int64_t* counts = malloc(sizeof(int64_t) * ((size_t)atoms + 1));
+        int* types = malloc(sizeof(int) * ((size_t)atoms + 1));
+        double* coefficients = malloc(sizeof(double) * (size_t)csize);
+        double* accumulated = calloc((size_t)csize, sizeof(double));
+        double* power = malloc(sizeof(double) * (size_t)F);
+        double* power_sum = calloc((size_t)F, sizeof(double));
+        int local_status = structure_graph(positions, cells + 9 * s, pbc + 3 * s, begin, end, cutoff,
+                                           0, NULL, 0, &pairs, counts);
+        for (int64_t i = 0; i < atoms && !local_status; ++i) {
+            types[i] = species_type(&plan, numbers[begin + i]);
+            if (types[i] < 0) local_status = fail("batch contains an atomic number outside calculator species");
+        }
+        int64_t max_count = 0;
+        for (int64_t i = 0; i < atoms && !local_status; ++i)
+            if (counts[i + 1] - counts[i] > max_count) max_count = counts[i + 1] - counts[i];
+        double* scratch = malloc(sizeof(double) * (size_t)(max_count * (plan.harmonics + 3) + 4 * w * w + 64));
+        for (int64_t i = 0; i < atoms && !local_status; ++i) {
+            center_coefficients(&plan, types, i, &pairs, counts[i], counts[i + 1], 0, coefficients, scratch);
+            if (average == 0) {
+                power_spectrum(&plan, coefficients, out + (begin + i) * F);
+            } else if (average == 1) {
+                for (int64_t k = 0; k < csize; ++k) accumulated[k] += coefficients[k];
+            } else {
+                power_spectrum(&plan, coefficients, power);
+                for (int64_t k = 0; k < F; ++k) power_sum[k] += power[k];
+            }
+        }
+        if (!local_status && average == 1) {
+            if (atoms > 0) {
+                const double inverse = 1.0 / (double)atoms;
+                for (int64_t k = 0; k < csize; ++k) accumulated[k] *= inverse;
+            }
+            power_spectrum(&plan, accumulated, out + s * F);
+        } else if (!local_status && average == 2) {
+            for (int64_t k = 0; k < F; ++k) out[s * F + k] = atoms > 0 ? power_sum[k] / (double)atoms : 0.0;
+        }
+        free(scratch);
+        free(counts);
+        free(types);
+        free(coefficients);
+        free(accumulated);
+        free(power);
+        free(power_sum);
+        pair_free(&pairs);
+        status |= local_status;
+    }
+    free(ones);
+    free(plan.power_prefactors);
+    free(plan.normalization);
+    free(plan.radial_prefactors);
+    free(plan.radial_exponents);
+    return status;
+}
+
+/*
+ * Rows of the average-"off" feature matrix for selected atoms only (global
+ * indices `rows`, any order): the same per-centre arithmetic as
+ * oracle_soap_compute, with the neighbour query restricted to the requested
+ * centres.  Lets tests check sampled rows of full-size structures.
+ */
+int oracle_soap_rows(const int32_t* numbers, const double* positions, const double* cells,
+                     const int32_t* pbc, const int64_t* offsets, int64_t structures,
+                     const int32_t* species, int n_species, const double* species_weights,
+                     double r_cut, int n_max, int l_max, double sigma, const double* alphas,
+                     const double* betas, const int64_t* rows, int64_t n_rows, double* out) {
+    if (validate_batch(numbers, positions, cells, pbc, offsets, structures)) return 1;
+    if (!isfinite(r_cut) || !isfinite(sigma) || r_cut <= 0.0 || sigma <= 0.0 || n_max < 1 || l_max < 0
+        || l_max > 20 || n_species < 1 || n_species > 64)
+        return fail("invalid SOAP parameters");
+    soap_plan plan;
+    plan.n_species = n_species;
+    plan.n_max = n_max;
+    plan.l_max = l_max;
+    plan.width = l_max + 1;
+    plan.harmonics = (l_max + 1) * (l_max + 1);
+    plan.species = species;
+    double* weights = malloc(sizeof(double) * (size_t)n_species);
+    for (int t = 0; t < n_species; ++t) weights[t] = species_weights ? species_weights[t] : 1.0;
+    plan.species_weights = weights;
+    plan.betas = betas;
+    plan.soap_scale = OR_PI * sqrt(OR_PI);
+    const int w = l_max + 1;
+    plan.power_prefactors = malloc(sizeof(double) * w);
+    plan.normalization = calloc((size_t)w * w, sizeof(double));
+    plan.radial_prefactors = malloc(sizeof(double) * w * n_max);
+    plan.radial_exponents = malloc(sizeof(double) * w * n_max);
+    for (int l = 0; l <= l_max; ++l) {
+        plan.power_prefactors[l] = OR_PI * sqrt(8.0 / (2.0 * l + 1.0));
+        for (int m = 0; m <= l; ++m)
+            plan.normalization[l * w + m] =
+                sqrt((2.0 * l + 1.0) / (4.0 * OR_PI) * exp(lgamma(l - m + 1.0) - lgamma(l + m + 1.0)));
+    }
+    const double eta = 1.0 / (2.0 * sigma * sigma);
+    double eta_power = 1.0;
+    for (int l = 0; l <= l_max; ++l) {
+        if (l > 0) eta_power *= eta;
+        for (int k = 0; k < n_max; ++k) {
+            const int i = l * n_max + k;
+            const double denominator = alphas[i] + eta;
+            plan.radial_prefactors[i] = eta_power * pow(denominator, -l - 1.5);
+            plan.radial_exponents[i] = alphas[i] * eta / denominator;
+        }
+    }
+    const double cutoff = r_cut + sigma * sqrt(-2.0 * log(1e-3));
+    const int64_t F = oracle_soap_feature_count(n_species, n_max, l_max);
+    const int64_t csize = (int64_t)n_species * n_max * plan.harmonics;
+    int status = 0;
+    for (int64_t s = 0; s < structures && !status; ++s) {
+        const int64_t begin = offsets[s], end = offsets[s + 1], atoms = end - begin;
+        int64_t wanted = 0;
+        for (int64_t r = 0; r < n_rows; ++r) wanted += rows[r] >= begin && rows[r] < end;
+        if (!wanted) continue;
+        int64_t* subset = malloc(sizeof(int64_t) * (size_t)wanted);
+        int64_t* slot = malloc(sizeof(int64_t) * (size_t)wanted);
+        int64_t q = 0;
+        for (int64_t r = 0; r < n_rows; ++r)
+            if (rows[r] >= begin && rows[r] < end) {
+                subset[q] = rows[r] - begin;
+                slot[q++] = r;
+            }
+        int* types = malloc(sizeof(int) * ((size_t)atoms + 1));
+        for (int64_t i = 0; i < atoms && !status; ++i) {
+            types[i] = species_type(&plan, numbers[begin + i]);
+            if (types[i] < 0) status = fail("batch contains an atomic number outside calculator species");
+        }
+        pair_list pairs = {0};
+        int64_t* counts = malloc(sizeof(int64_t) * ((size_t)wanted + 1));
+        if (!status)
+            status = structure_graph(positions, cells + 9 * s, pbc + 3 * s, begin, end, cutoff, 0, subset, wanted,
+                                     &pairs, counts);
+        int64_t max_count = 0;
+        for (int64_t i = 0; i < wanted && !status; ++i)
+            if (counts[i + 1] - counts[i] > max_count) max_count = counts[i + 1] - counts[i];
+        double* coefficients = malloc(sizeof(double) * (size_t)csize);
+        double* scratch = malloc(sizeof(double) * (size_t)(max_count * (plan.harmonics + 3) + 4 * w * w + 64));
+        for (int64_t i = 0; i < wanted && !status; ++i) {
+            center_coefficients(&plan, types, subset[i], &pairs, counts[i], counts[i + 1], 0, coefficients, scratch);
+            power_spectrum(&plan, coefficients, out + slot[i] * F);
+        }
+        free(scratch);
+        free(coefficients);
+        free(counts);
+        pair_free(&pairs);
+        free(types);
+        free(subset);
+        free(slot);
+    }
+    free(weights);
+    free(plan.power_prefactors);
+    free(plan.normalization);
+    free(plan.radial_prefactors);
+    free(plan.radial_exponents);
+    return status;
+}

@@ -1,0 +1,196 @@
+"""Pin the CPU checker (oracle/soap_oracle.c) before trusting it.
+
+* the reference's own committed goldens: tests/golden/soap (project golden,
+  average inner, 2 structures incl. isolated), the DScribe 2.1.2 static golden
+  (average off, sigma 0.5) and tests/golden/neighborlist (448 pairs);
+* the reference neighbour-graph known-answer test (tests/test_neighbor_graph.py:38-79):
+  a triclinic two-atom cell against a brute-force image sum;
+* seeded slices of the five benchmark configs, generated through the
+  reference's public API (tests/golden/make_golden.py): features, graph digest,
+  basis and labels;
+* when the reference library compiled from its sources is present
+  (oracle/_ref), bit-for-bit graph equality on extra random cases.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from _util import (AGREE_FLOOR, AGREE_TOL, F32_FLOOR, F32_TOL, F64_FLOOR, F64_TOL, assert_graph_bit_exact,
+                   max_rel_err)
+from mdescriptor_b200 import workloads
+from mdescriptor_b200.basis import basis_gto, feature_count, graph_cutoff, labels
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+REF = np.load(GOLDEN / "reference_goldens.npz")
+REF_META = json.loads((GOLDEN / "reference_goldens.json").read_text())
+CFG = np.load(GOLDEN / "config_goldens.npz")
+CFG_META = json.loads((GOLDEN / "config_goldens.json").read_text())
+
+
+def batch_from(arrays, prefix):
+    return workloads.Batch(*(arrays[f"{prefix}/{key}"] for key in ("numbers", "positions", "cells", "pbc", "offsets")))
+
+
+def graph_digest(graph):
+    offsets, atoms, shifts, disp, d2 = graph
+    centers = np.repeat(np.arange(len(offsets) - 1, dtype=np.int64), np.diff(offsets))
+    order = np.lexsort((shifts[:, 2], shifts[:, 1], shifts[:, 0], atoms, centers))
+    h = hashlib.sha256()
+    for array in (centers[order], atoms[order].astype(np.int64), shifts[order].astype(np.int64),
+                  np.ascontiguousarray(disp[order]), np.ascontiguousarray(d2[order])):
+        h.update(np.ascontiguousarray(array).tobytes())
+    return h.hexdigest()
+
+
+def test_oracle_matches_reference_soap_golden(oracle):
+    meta = REF_META["soap"]
+    p = meta["parameters"]
+    batch = batch_from(REF, "soap/input")
+    alphas, betas = basis_gto(p["r_cut"], p["n_max"], p["l_max"])
+    values = oracle.soap(batch, p["species"], p["r_cut"], p["n_max"], p["l_max"], p["sigma"], alphas, betas,
+                         p["average"])
+    expected = REF["soap/expected/values"]
+    tol = meta["tolerance"]
+    np.testing.assert_allclose(values, expected, rtol=tol["rtol"], atol=tol["atol"])
+    assert values.shape[1] == meta["feature_count"] == feature_count(len(p["species"]), p["n_max"], p["l_max"])
+
+
+def test_oracle_matches_dscribe_static_golden(oracle):
+    meta = REF_META["soap_dscribe"]
+    p = meta["parameters"]
+    batch = batch_from(REF, "soap_dscribe/input")
+    alphas, betas = basis_gto(p["r_cut"], p["n_max"], p["l_max"])
+    values = oracle.soap(batch, p["species"], p["r_cut"], p["n_max"], p["l_max"], p["sigma"], alphas, betas,
+                         p["average"])
+    tol = meta["tolerance"]
+    np.testing.assert_allclose(values, REF["soap_dscribe/expected/values"], rtol=tol["rtol"], atol=tol["atol"])
+
+
+def test_oracle_graph_matches_neighborlist_golden(oracle):
+    meta = REF_META["neighborlist"]
+    batch = batch_from(REF, "neighborlist/input")
+    offsets, atoms, shifts, disp, d2 = oracle.graph(batch, meta["parameters"]["cutoff"])
+    centers = np.repeat(np.arange(len(offsets) - 1), np.diff(offsets))
+    structure_of = np.searchsorted(batch.offsets, np.arange(batch.atoms), side="right") - 1
+    keep = ~((atoms == centers) & (shifts == 0).all(axis=1))  # NeighborList drops the exact self pair
+    base = batch.offsets[structure_of[centers[keep]]]
+    ours = {
+        (int(structure_of[c]), int(c - b), int(a - b), *map(int, s)): (dv, np.sqrt(q))
+        for c, a, s, dv, q, b in zip(centers[keep], atoms[keep], shifts[keep], disp[keep], d2[keep], base)
+    }
+    samples = REF["neighborlist/expected/samples"]
+    values = REF["neighborlist/expected/values"]
+    expected = {tuple(int(v) for v in row): (val[:3], val[3]) for row, val in zip(samples, values)}
+    assert set(ours) == set(expected)
+    tol = meta["tolerance"]
+    for key, (vector, distance) in ours.items():
+        np.testing.assert_allclose(vector, expected[key][0], rtol=tol["rtol"], atol=tol["atol"])
+        np.testing.assert_allclose(distance, expected[key][1], rtol=tol["rtol"], atol=tol["atol"])
+
+
+def triclinic_pair():
+    cell = np.array([[1.8, 0.0, 0.0], [0.25, 1.7, 0.0], [0.1, 0.2, 1.9]])
+    positions = np.array([[0.18, 0.29, 0.41], [0.96, 0.85, 1.12]])
+    return workloads.Batch(np.array([8, 14], np.int32), positions, cell[None], np.ones((1, 3), np.int32),
+                           np.array([0, 2], np.int64))
+
+
+def brute_force_graph(batch, cutoff, span=4):
+    """All images |n_i| <= span, reference arithmetic order (neighbor.cpp:472-474, 552-555)."""
+    result = {}
+    cell = batch.cells[0]
+    for center in range(batch.atoms):
+        for atom in range(batch.atoms):
+            for n0 in range(-span, span + 1):
+                for n1 in range(-span, span + 1):
+                    for n2 in range(-span, span + 1):
+                        shift = (n0 * cell[0] + n1 * cell[1]) + n2 * cell[2]
+                        d = (batch.positions[atom] + shift) - batch.positions[center]
+                        q = (d[0] * d[0] + d[1] * d[1]) + d[2] * d[2]
+                        if q <= cutoff * cutoff:
+                            result[(center, atom, n0, n1, n2)] = (d, q)
+    return result
+
+
+def test_oracle_graph_triclinic_known_answer(oracle):
+    batch = triclinic_pair()
+    offsets, atoms, shifts, disp, d2 = oracle.graph(batch, 2.3)
+    ours = {}
+    for c in range(batch.atoms):
+        for i in range(offsets[c], offsets[c + 1]):
+            ours[(c, int(atoms[i]), *map(int, shifts[i]))] = (disp[i], d2[i])
+    expected = brute_force_graph(batch, 2.3)
+    assert set(ours) == set(expected)
+    for key, (vector, q) in ours.items():
+        np.testing.assert_allclose(vector, expected[key][0], rtol=0, atol=1e-12)
+        np.testing.assert_allclose(q, expected[key][1], rtol=0, atol=1e-12)
+    assert (0, 0, 0, 0, 0) in ours  # exact self kept
+    assert any(k[:2] == (0, 0) and k[2:] != (0, 0, 0) for k in ours)
+
+
+@pytest.mark.parametrize("name", sorted(CFG_META))
+def test_oracle_matches_reference_config_slices(oracle, name):
+    meta = CFG_META[name]
+    batch = batch_from(CFG, f"{name}/input")
+    alphas, betas = basis_gto(meta["r_cut"], meta["n_max"], meta["l_max"])
+    np.testing.assert_allclose(alphas, CFG[f"{name}/alphas"], rtol=1e-14, atol=0)
+    np.testing.assert_allclose(betas, CFG[f"{name}/betas"], rtol=1e-12, atol=1e-12)
+    for average, info in meta["outputs"].items():
+        got = oracle.soap(batch, meta["species"], meta["r_cut"], meta["n_max"], meta["l_max"], meta["sigma"],
+                          CFG[f"{name}/alphas"], CFG[f"{name}/betas"], average)
+        rows = CFG[f"{name}/{average}/rows"]
+        assert got.shape[0] == info["rows_total"]
+        err = max_rel_err(got[rows], CFG[f"{name}/{average}/values"], AGREE_FLOOR)
+        assert err <= AGREE_TOL, f"{name}/{average}: {err:.3e}"
+        if meta["dtype"] == "float64":
+            # the float64-output config must hold the stated 1e-10 bound
+            err = max_rel_err(got[rows], CFG[f"{name}/{average}/values"], F64_FLOOR)
+            assert err <= F64_TOL, f"{name}/{average}: {err:.3e}"
+        names = labels(meta["species"], meta["n_max"], meta["l_max"])
+        assert len(names) == info["labels_count"]
+        assert hashlib.sha256("\n".join(names).encode()).hexdigest() == info["labels_sha256"]
+    graph = oracle.graph(batch, graph_cutoff(meta["r_cut"], meta["sigma"]))
+    assert len(graph[1]) == meta["graph_pairs"]
+    assert graph_digest(graph) == meta["graph_sha256"]
+
+
+def test_graph_cutoff_matches_reference_padding():
+    for name, meta in CFG_META.items():
+        assert graph_cutoff(meta["r_cut"], meta["sigma"]) == meta["graph_cutoff"], name
+
+
+@pytest.mark.skipif(not (Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libref_soap.so").is_file(),
+                    reason="reference library not built in this tree")
+@pytest.mark.parametrize("seed", range(4))
+def test_oracle_graph_bit_exact_vs_reference_library(oracle, seed):
+    from oracle import RefLib
+
+    ref = RefLib()
+    rng = np.random.default_rng(seed)
+    # Random triclinic cells, some atoms outside the cell, plus an isolated structure.
+    structures, numbers, positions, cells, pbc, offsets = 3, [], [], [], [], [0]
+    for s in range(structures):
+        n = int(rng.integers(1, 9))
+        cell = np.diag(rng.uniform(2.0, 5.0, 3)) + np.triu(rng.uniform(-0.8, 0.8, (3, 3)), 1)
+        frac = rng.uniform(-0.3, 1.3, (n, 3))
+        positions.append(frac @ cell)
+        numbers.append(rng.integers(1, 3, n).astype(np.int32))
+        cells.append(cell if s < 2 else np.zeros((3, 3)))
+        pbc.append([1, 1, 1] if s < 2 else [0, 0, 0])
+        offsets.append(offsets[-1] + n)
+    batch = workloads.Batch(np.concatenate(numbers), np.concatenate(positions), np.array(cells),
+                            np.array(pbc, np.int32), np.array(offsets, np.int64))
+    cutoff = float(rng.uniform(2.0, 6.0))
+    assert_graph_bit_exact(oracle.graph(batch, cutoff), ref.graph(batch, cutoff))
+
+
+def test_float32_metric_constants():
+    # The tolerances written in the tests (see tests/_util.py).
+    assert (F32_TOL, F32_FLOOR) == (1e-5, 1e-6)
+    assert (F64_TOL, F64_FLOOR) == (1e-10, 1e-4)
