@@ -12,6 +12,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <exception>
 #include <memory>
@@ -138,13 +139,13 @@ using CenterLauncher = void (*)(dim3, size_t, cudaStream_t, const SoapTables&, c
 using StructureLauncher = void (*)(dim3, size_t, cudaStream_t, const SoapTables&, const int64_t*, int64_t, int64_t,
                                    const double*, const double*, void*, int64_t);
 
-template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX>
+template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX, int MINB>
 void launch_center(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+    soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX, MINB><<<grid, kWarps * 32, smem, stream>>>(tab, p);
 }
-template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX>
+template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX, int MINB>
 const void* center_symbol() {
-    return reinterpret_cast<const void*>(&soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX>);
+    return reinterpret_cast<const void*>(&soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX, MINB>);
 }
 template <int LMAX>
 void launch_structure(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const int64_t* offsets,
@@ -158,37 +159,61 @@ const void* structure_symbol() {
 
 // Kernel variants.  Slot lengths bound 2l+1 of the channels a lane owns per
 // pass: channels are sorted by l descending, 32 per slot, and with n_max <= 8
-// the channels ranked 32s.. have l <= l_max - 4s.
+// the channels ranked 32s.. have l <= l_max - 4s.  Within a (n, l) class the
+// variants trade species register banks (MAXT, fewer passes) against
+// registers per thread (MINB resident CTAs per SM).
 struct Variant {
-    int maxt, l0, l1, l2, nmax, lmax;
+    int cls, maxt, l0, l1, l2, nmax, lmax, minb;
     CenterLauncher center;
     const void* (*center_sym)();
     StructureLauncher structure;
     const void* (*structure_sym)();
 };
 
-#define MDSOAP_VARIANT(T, A, B, C, N, L)                                                              \
-    Variant {                                                                                          \
-        T, A, B, C, N, L, &launch_center<T, A, B, C, N, L>, &center_symbol<T, A, B, C, N, L>,          \
-            &launch_structure<L>, &structure_symbol<L>                                                 \
+#define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                              \
+    Variant {                                                                                                   \
+        CLS, T, A, B, C, N, L, MB, &launch_center<T, A, B, C, N, L, MB>, &center_symbol<T, A, B, C, N, L, MB>,  \
+            &launch_structure<L>, &structure_symbol<L>                                                          \
     }
 
+// First entry of each class is the default.
+// Defaults chosen by measurement on B200 (config shapes 1-5).
 const Variant kVariants[] = {
-    MDSOAP_VARIANT(8, 7, 0, 0, 8, 3),    // n <= 8, l <= 3
-    MDSOAP_VARIANT(6, 9, 1, 0, 8, 4),    // n <= 8, l == 4
-    MDSOAP_VARIANT(4, 13, 5, 0, 8, 6),   // n <= 8, l in 5..6
-    MDSOAP_VARIANT(2, 17, 9, 1, 8, 8),   // n <= 8, l in 7..8
-    MDSOAP_VARIANT(1, 41, 0, 0, 32, 20), // any n <= 32, l <= 20
+    MDSOAP_VARIANT(0, 4, 7, 0, 0, 8, 3, 3),     // n <= 8, l <= 3
+    MDSOAP_VARIANT(0, 8, 7, 0, 0, 8, 3, 2),
+    MDSOAP_VARIANT(1, 3, 9, 1, 0, 8, 4, 3),     // n <= 8, l == 4
+    MDSOAP_VARIANT(1, 6, 9, 1, 0, 8, 4, 2),
+    MDSOAP_VARIANT(2, 4, 13, 5, 0, 8, 6, 2),    // n <= 8, l in 5..6
+    MDSOAP_VARIANT(2, 2, 13, 5, 0, 8, 6, 3),
+    MDSOAP_VARIANT(2, 1, 13, 5, 0, 8, 6, 4),
+    MDSOAP_VARIANT(3, 2, 17, 9, 1, 8, 8, 2),    // n <= 8, l in 7..8
+    MDSOAP_VARIANT(3, 1, 17, 9, 1, 8, 8, 3),
+    MDSOAP_VARIANT(4, 1, 41, 0, 0, 32, 20, 1),  // any n <= 32, l <= 20
 };
 
-const Variant& pick_variant(int n_max, int l_max) {
+int variant_class(int n_max, int l_max) {
     if (n_max <= 8) {
-        if (l_max <= 3) return kVariants[0];
-        if (l_max == 4) return kVariants[1];
-        if (l_max <= 6) return kVariants[2];
-        if (l_max <= 8) return kVariants[3];
+        if (l_max <= 3) return 0;
+        if (l_max == 4) return 1;
+        if (l_max <= 6) return 2;
+        if (l_max <= 8) return 3;
     }
-    return kVariants[4];
+    return 4;
+}
+
+// MDSOAP_MAXT (tuning knob) selects the class member with that many species
+// banks; otherwise the class default.
+const Variant& pick_variant(int n_max, int l_max) {
+    const int cls = variant_class(n_max, l_max);
+    const char* env = std::getenv("MDSOAP_MAXT");
+    const int want = env ? std::atoi(env) : 0;
+    const Variant* first = nullptr;
+    for (const Variant& v : kVariants) {
+        if (v.cls != cls) continue;
+        if (!first) first = &v;
+        if (want > 0 && v.maxt == want) return v;
+    }
+    return *first;
 }
 
 // fp64 FMA throughput probe: kProbeChains independent dependent-FMA chains per
@@ -264,6 +289,7 @@ struct mdsoap_plan {
     const Variant* variant = nullptr;
     size_t center_smem = 0;
     size_t structure_smem = 0;
+    int64_t csize = 0;
     int64_t features = 0;
     bool timing = false;
     std::mutex devices_mutex;
@@ -340,7 +366,7 @@ void mdsoap_plan::bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream
 void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, int64_t s1, int64_t a0, int64_t a1,
                             void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center) {
     const int64_t centers = a1 - a0;
-    const int64_t csize = (int64_t)n_species * n_max * tab.H;
+    const int64_t csize = tab.csize;
     SoapPointers p{};
     p.positions = b.positions;
     p.bins = st.work.bins(error);
@@ -691,9 +717,11 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         const bool single_pass = t.slot_groups == 1 && t.type_groups == 1;
         const size_t beta_bytes = (size_t)W * n * n * 8;
         t.beta_in_smem = beta_bytes <= 32768;
-        const size_t beta_smem = t.beta_in_smem ? ((beta_bytes + 15) & ~(size_t)15) : 0;
-        const size_t r_bytes = (size_t)q.n_species * n * t.H * 8;
-        const size_t pend = (size_t)kPending * 36;
+        // CTA-shared: 32-entry exp table (256 B) + optional beta copy.
+        const size_t beta_smem = 256 + (t.beta_in_smem ? ((beta_bytes + 15) & ~(size_t)15) : 0);
+        t.csize = q.n_species * n * W * (W + 1);
+        const size_t r_bytes = (size_t)t.csize * 8;
+        const size_t pend = 416 + (size_t)kPending * 36;
         auto region_a = [&](int chunk) { return pend + ((size_t)chunk * t.H + 48) * 8; };
         auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
         auto per_warp = [&](int chunk, bool r_in_smem) {
@@ -701,16 +729,18 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             if (single_pass) return align16(std::max(region_a(chunk), r_bytes));
             return align16(region_a(chunk)) + align16(r_bytes);
         };
-        // Largest chunk (<= 32) that keeps >= 2 CTAs of kWarps warps on an SM
-        // (about 113 KB each); else the smallest footprint that fits at all.
-        const size_t budget2 = 113 * 1024, budget1 = 227 * 1024;
+        // Largest chunk (<= 32) that lets the variant's MINB CTAs share an SM
+        // (228 KB per SM, 1 KB reserved per CTA); failing that, the smallest
+        // footprint that fits one CTA, with the coefficient blocks moved to
+        // global scratch if they alone are too large.
+        const size_t budget = 228 * 1024 / (size_t)v.minb - 1024, budget1 = 227 * 1024;
         int chunk = 32;
         bool r_smem = true;
-        while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, true) > budget2) chunk -= 8;
+        while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, true) > budget) chunk -= 8;
         if (beta_smem + kWarps * per_warp(chunk, true) > budget1) {
             r_smem = false;
             chunk = 32;
-            while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, false) > budget2) chunk -= 8;
+            while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, false) > budget) chunk -= 8;
         }
         t.chunk = chunk;
         t.r_global = r_smem ? 0 : 1;
@@ -718,6 +748,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         t.r_offset = (r_smem && !single_pass) ? (int32_t)align16(region_a(chunk)) : 0;
         plan->center_smem = beta_smem + kWarps * (size_t)t.warp_bytes;
         plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? r_bytes : 0;
+        plan->csize = t.csize;
         if (plan->center_smem > budget1 || plan->structure_smem > budget1)
             return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
         *plan_out = plan.release();

@@ -8,21 +8,26 @@
 //   p(t1,t2,l,n1,n2) = pi sqrt(8/(2l+1)) sum_m c[t1][n1][lm] c[t2][n2][lm]  :997-1012
 //
 // Work decomposition (one warp per centre):
-//   * candidates from the bin walk are accepted with the reference's exact
-//     geometry and appended (ballot + popc) to a per-warp queue in shared
-//     memory;
+//   * the centre's bin neighbourhood is flattened into one candidate list
+//     (32 (row, x-image) entries per round, prefix-summed across the warp), so
+//     every candidate chunk fills all 32 lanes; candidates are accepted with
+//     the reference's exact geometry and appended (ballot + popc) to a
+//     per-warp edge queue in shared memory;
 //   * per chunk of up to 32 queued edges, lane e evaluates Y_{lm} of edge e by
-//     the Cartesian recurrence and stores the row in shared memory;
+//     the Cartesian recurrence into a shared-memory row;
 //   * every lane owns up to three radial channels (l, k) (channels sorted by
-//     l descending, 32 per slot), evaluates its own exp() per edge and keeps
-//     S[t][l][k][0..2l] in registers, reading Y_{lm} rows as shared-memory
-//     broadcasts; species live in separate register banks picked by a
-//     warp-uniform branch;
-//   * the raw sums go to shared memory, beta is applied in place, and the
-//     power spectrum is written straight to the output row (lane = column r2,
-//     broadcast row r1), so no feature staging buffer is needed.
+//     l descending, 32 per slot), evaluates its own table-driven exp() per
+//     edge and keeps S[t][l][k][0..2l] in registers, reading Y rows as
+//     shared-memory broadcasts; species live in register banks picked by a
+//     warp-uniform branch (species beyond the banks take another pass);
+//   * raw sums go to a shared coefficient block (rows padded to even length
+//     so that the power spectrum reads them with 16-byte broadcasts), beta is
+//     applied in place, and the power spectrum is written straight to the
+//     output row: lane = column r2, broadcast row r1, so each warp store
+//     covers runs of consecutive features.
 #pragma once
 
+#include "expneg.cuh"
 #include "neighbors.cuh"
 
 namespace mdsoap {
@@ -48,8 +53,8 @@ struct SoapTables {
     int32_t r_offset;     // byte offset of the coefficient block inside a warp's region
     int32_t type_groups;  // passes over species groups
     int32_t slot_groups;  // passes over channel-slot groups
-    int32_t r_global;     // 1: coefficient blocks live in global scratch (too big for shared memory)
-    int32_t pad_;
+    int32_t r_global;     // 1: coefficient blocks live in global scratch
+    int32_t csize;        // coefficient block length in doubles: S n (L+1)(L+2)
     double cutoff2;
     double soap_scale;    // pi^{3/2}
     double ynorm[kTri];   // N_lm (times sqrt 2 for m > 0), index l(l+1)/2 + m
@@ -64,8 +69,8 @@ struct SoapPointers {
     BinView bins;
     const RadialItem* items;  // channels sorted by l descending
     const double* betas;      // [(l_max+1)][n_max][n_max]
-    void* out;                // average off: rows of centres; else unused
-    double* cbuf;             // average inner: per-centre coefficients (block-local rows)
+    void* out;                // average off: feature rows of centres
+    double* cbuf;             // average inner: per-centre coefficient blocks (block-local rows)
     double* pbuf;             // average outer: per-centre power spectra (block-local rows)
     double* rbuf;             // r_global: per-centre coefficient scratch (block-local rows)
     int64_t out_row_begin;    // average off: output row of centre c is c - out_row_begin
@@ -74,6 +79,10 @@ struct SoapPointers {
 };
 
 __device__ __forceinline__ int tri(int l, int m) { return l * (l + 1) / 2 + m; }
+
+// Coefficient block layout: [l][t][n][m] with each (t, n) row padded to
+// 2l+2 doubles; block l starts at S n l (l+1).
+__device__ __forceinline__ int cblock(int S, int n, int l) { return S * n * l * (l + 1); }
 
 // Real regular solid harmonics of one displacement into out[0..H), layout
 // l^2 + (l - m) = cos part, l^2 + l = m0, l^2 + (l + m) = sin part
@@ -96,8 +105,8 @@ __device__ __forceinline__ void solid_harmonics(const SoapTables& tab, double x,
             if (m == 0) {
                 out[0] = nrm * pr2;
             } else {
-                out[m * m] = nrm * pr2;              // l = m: l^2 + l - m
-                out[m * m + 2 * m] = nrm * pi2;      // l^2 + l + m
+                out[m * m] = nrm * pr2;
+                out[m * m + 2 * m] = nrm * pi2;
             }
         }
         if (m < L) {
@@ -126,89 +135,191 @@ __device__ __forceinline__ void solid_harmonics(const SoapTables& tab, double x,
     }
 }
 
-__device__ __forceinline__ int64_t feature_index(int S, int n, int L, int t1, int n1, int t2, int n2, int l) {
+// Feature offset of (t1, n1, t2, n2, l) in the compression-off layout
+// (t1 <= t2, then l, then n1, then n2 with n2 >= n1 when t1 == t2).
+__device__ __forceinline__ int64_t pair_base(int S, int n, int L, int t1, int t2) {
     const int64_t T = (int64_t)n * (n + 1) / 2;
     const int64_t nn = (int64_t)n * n;
     int64_t base = (int64_t)(L + 1) * (t1 * T + nn * ((int64_t)t1 * (S - 1) - (int64_t)t1 * (t1 - 1) / 2));
-    if (t2 > t1) {
-        base += (int64_t)(L + 1) * (T + (int64_t)(t2 - t1 - 1) * nn);
-        return base + l * nn + (int64_t)n1 * n + n2;
-    }
-    return base + l * T + (int64_t)n1 * n - (int64_t)n1 * (n1 - 1) / 2 + (n2 - n1);
+    if (t2 > t1) base += (int64_t)(L + 1) * (T + (int64_t)(t2 - t1 - 1) * nn);
+    return base;
 }
 
-// Power spectrum of one coefficient block c (layout [l][t][n][m], S n H
-// doubles in shared memory) into the feature row `out` (global memory).
-template <int LMAX, class OutT>
-__device__ __forceinline__ void power_spectrum_warp(const SoapTables& tab, const double* __restrict__ c,
-                                                    OutT* __restrict__ out, int lane) {
-    const int S = tab.n_species, n = tab.n_max, L = tab.l_max, R = tab.rows;
+// One l of the power spectrum: lane = column r2 (own row in registers), rows
+// r1 <= r2 broadcast from shared memory two doubles at a time.
+template <int LEN, class OutT>
+__device__ __forceinline__ void power_l(const double* __restrict__ cl, int R, int n, int S, int L, int l,
+                                        double pref, OutT* __restrict__ out, int lane) {
+    constexpr int PAD = LEN + 1;  // row stride, even
+    const int T = n * (n + 1) / 2;
     for (int r2base = 0; r2base < R; r2base += 32) {
         const int r2 = r2base + lane;
         const bool active = r2 < R;
         const int t2 = active ? r2 / n : 0;
         const int n2 = active ? r2 - t2 * n : 0;
+        double own[LEN];
+#pragma unroll
+        for (int m = 0; m < LEN; ++m) own[m] = active ? cl[r2 * PAD + m] : 0.0;
         const int r1_end = min(R - 1, r2base + 31);
-        for (int l = 0; l <= L; ++l) {
-            const int len = 2 * l + 1;
-            const double* cl = c + (int64_t)S * n * l * l;
-            double own[2 * LMAX + 1];
+        int t1 = 0, n1 = 0;
+        int64_t base = pair_base(S, n, L, 0, t2) + (int64_t)l * (t2 == 0 ? T : n * n);
+        for (int r1 = 0; r1 <= r1_end; ++r1) {
+            const double2* o = reinterpret_cast<const double2*>(cl + r1 * PAD);
+            double v = 0.0;
 #pragma unroll
-            for (int m = 0; m < 2 * LMAX + 1; ++m) own[m] = (m < len && active) ? cl[r2 * len + m] : 0.0;
-            const double pref = tab.power_pref[l];
-            int t1 = 0, n1 = 0;
-            for (int r1 = 0; r1 <= r1_end; ++r1) {
-                const double* o = cl + r1 * len;
-                double v = 0.0;
-#pragma unroll
-                for (int m = 0; m < 2 * LMAX + 1; ++m) {
-                    if (m < len) v = fma(o[m], own[m], v);
-                }
-                if (active && r2 >= r1) out[feature_index(S, n, L, t1, n1, t2, n2, l)] = (OutT)(pref * v);
-                if (++n1 == n) {
-                    n1 = 0;
-                    ++t1;
-                }
+            for (int m = 0; m + 1 < LEN; m += 2) {
+                const double2 q = o[m / 2];
+                v = fma(q.x, own[m], v);
+                v = fma(q.y, own[m + 1], v);
+            }
+            v = fma(cl[r1 * PAD + LEN - 1], own[LEN - 1], v);
+            if (active && r2 >= r1) {
+                const int64_t inner = t1 == t2 ? (int64_t)n1 * n - (int64_t)n1 * (n1 - 1) / 2 + (n2 - n1)
+                                               : (int64_t)n1 * n + n2;
+                out[base + inner] = (OutT)(pref * v);
+            }
+            if (++n1 == n) {
+                n1 = 0;
+                ++t1;
+                if (t1 <= t2) base = pair_base(S, n, L, t1, t2) + (int64_t)l * (t1 == t2 ? T : n * n);
             }
         }
     }
 }
 
-// In-place beta transform of the raw sums R[l][t][k][m] -> c[l][t][n][m].
+template <int l, int LMAX, class OutT>
+__device__ __forceinline__ void power_from(const SoapTables& tab, const double* __restrict__ c,
+                                           OutT* __restrict__ out, int lane) {
+    if constexpr (l <= LMAX) {
+        if (l > tab.l_max) return;
+        const int S = tab.n_species, n = tab.n_max;
+        power_l<2 * l + 1>(c + cblock(S, n, l), tab.rows, n, S, tab.l_max, l, tab.power_pref[l], out, lane);
+        power_from<l + 1, LMAX, OutT>(tab, c, out, lane);
+    }
+}
+
+template <int LMAX, class OutT>
+__device__ __forceinline__ void power_spectrum_warp(const SoapTables& tab, const double* __restrict__ c,
+                                                    OutT* __restrict__ out, int lane) {
+    power_from<0, LMAX, OutT>(tab, c, out, lane);
+}
+
+// In-place beta transform of the raw sums R[l][t][k][m] -> c[l][t][n][m]
+// (padded rows), soap.cpp:915-926.
 template <int NMAX>
 __device__ __forceinline__ void beta_transform_warp(const SoapTables& tab, const double* __restrict__ beta,
                                                     double* __restrict__ R, int lane) {
     const int S = tab.n_species, n = tab.n_max, L = tab.l_max;
     for (int l = 0; l <= L; ++l) {
-        const int len = 2 * l + 1;
+        const int len = 2 * l + 1, pad = 2 * l + 2;
         const int cols = S * len;
-        double* rl = R + (int64_t)S * n * l * l;
+        double* rl = R + cblock(S, n, l);
         const double* bl = beta + (int64_t)l * n * n;
         for (int col = lane; col < cols; col += 32) {
             const int t = col / len;
             const int m = col - t * len;
-            double* base = rl + t * n * len + m;
+            double* base = rl + t * n * pad + m;
             double r[NMAX];
 #pragma unroll
-            for (int k = 0; k < NMAX; ++k) r[k] = k < n ? base[k * len] : 0.0;
+            for (int k = 0; k < NMAX; ++k) r[k] = k < n ? base[k * pad] : 0.0;
             for (int nn = 0; nn < n; ++nn) {
                 double acc = 0.0;
 #pragma unroll
                 for (int k = 0; k < NMAX; ++k) {
                     if (k < n) acc = fma(bl[nn * n + k], r[k], acc);
                 }
-                base[nn * len] = tab.soap_scale * acc;
+                base[nn * pad] = tab.soap_scale * acc;
             }
         }
+    }
+}
+
+// Flattened candidate walk of one centre (warp-cooperative).  The bin
+// neighbourhood of the centre is a set of (row, x-image) entries, each a
+// contiguous run of sorted atoms; 32 entries per round are prefix-summed and
+// each candidate chunk then gives every lane one candidate.  visit(valid, j,
+// tx, ty, tz) is called by all lanes the same number of times.
+template <class Visit>
+__device__ __forceinline__ void for_each_candidate_flat(const StructInfo& si, const BinView& v, int64_t center,
+                                                        int lane, int* __restrict__ seg_prefix,
+                                                        int* __restrict__ seg_start, int* __restrict__ seg_t,
+                                                        Visit&& visit) {
+    const int Mx = si.M[0], My = si.M[1], Mz = si.M[2];
+    const int Kx = si.K[0], Ky = si.K[1], Kz = si.K[2];
+    const int cb = v.bin_of[center];
+    const int cx = cb % Mx, cy = (cb / Mx) % My, cz = cb / (Mx * My);
+    const int64_t bb = si.bin_base;
+    const int64_t ab = si.atom_begin;
+    const int lo = cx - Kx, hi = cx + Kx;
+    const int tx0 = si.periodic ? floor_div(lo, Mx) : 0;
+    const int nxs = si.periodic ? floor_div(hi, Mx) - tx0 + 1 : 1;
+    const int wy = 2 * Ky + 1;
+    const int entries = wy * (2 * Kz + 1) * nxs;
+    for (int round = 0; round < entries; round += 32) {
+        const int e = round + lane;
+        bool valid = e < entries;
+        int start = 0, len = 0, tpack = 0;
+        if (valid) {
+            const int row = e / nxs;
+            const int xs = e - row * nxs;
+            const int dz = row / wy - Kz;
+            const int dy = row - (row / wy) * wy - Ky;
+            const int ey = cy + dy, ez = cz + dz;
+            int ty = 0, tz = 0, tx = 0, b0, b1;
+            if (si.periodic) {
+                ty = floor_div(ey, My);
+                tz = floor_div(ez, Mz);
+                tx = tx0 + xs;
+                b0 = max(lo, tx * Mx) - tx * Mx;
+                b1 = min(hi, tx * Mx + Mx - 1) - tx * Mx;
+            } else {
+                valid = ey >= 0 && ey < My && ez >= 0 && ez < Mz;
+                b0 = max(lo, 0);
+                b1 = min(hi, Mx - 1);
+            }
+            valid = valid && b0 <= b1;
+            if (valid) {
+                const int64_t rowbase = bb + Mx * ((ey - ty * My) + My * (ez - tz * Mz));
+                start = v.bin_start[rowbase + b0];
+                len = v.bin_start[rowbase + b1 + 1] - start;
+                tpack = (tx + 512) | ((ty + 512) << 10) | ((tz + 512) << 20);
+            }
+        }
+        int incl = len;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int up = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += up;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        __syncwarp();
+        seg_prefix[lane] = incl - len;
+        seg_start[lane] = start;
+        seg_t[lane] = tpack;
+        __syncwarp();
+        for (int q0 = 0; q0 < total; q0 += 32) {
+            const int q = q0 + lane;
+            const bool cvalid = q < total;
+            int i = 0;
+#pragma unroll
+            for (int step = 16; step > 0; step >>= 1)
+                if (seg_prefix[i + step] <= q) i += step;
+            const int a = seg_start[i] + (q - seg_prefix[i]);
+            const int tp = seg_t[i];
+            const int j = cvalid ? v.sorted[ab + a] : 0;
+            visit(cvalid, j, (tp & 1023) - 512, ((tp >> 10) & 1023) - 512, ((tp >> 20) & 1023) - 512);
+        }
+        __syncwarp();
     }
 }
 
 // ---------------------------------------------------------------------------
 // Centre kernel.  Template parameters: MAXT species register banks per pass;
 // L0..L2 the padded lengths (2l+1 maxima) of the three channel slots a lane
-// owns per pass (0 = slot unused); NMAX >= n_max; LMAX >= l_max.
-template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX>
-__global__ void __launch_bounds__(kWarps * 32)
+// owns per pass (0 = slot unused); NMAX >= n_max; LMAX >= l_max; MINB the
+// minimum resident CTAs per SM the register allocation must allow.
+template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX, int MINB>
+__global__ void __launch_bounds__(kWarps * 32, MINB)
 soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
     constexpr int NS = (L0 > 0) + (L1 > 0) + (L2 > 0);
     extern __shared__ __align__(16) unsigned char smem[];
@@ -216,32 +327,36 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const int warp = threadIdx.x >> 5;
     const int S = tab.n_species, n = tab.n_max, H = tab.H;
     const int beta_count = (tab.l_max + 1) * n * n;
-    int beta_bytes = 0;
+    // CTA-shared: exp table (32 doubles), then beta (optional).
+    double* etab = reinterpret_cast<double*>(smem);
+    if (threadIdx.x < 32) etab[threadIdx.x] = kExp2Table[threadIdx.x];
+    int shared_bytes = 256;
     const double* beta = p.betas;
     if (tab.beta_in_smem) {
-        double* sbeta = reinterpret_cast<double*>(smem);
+        double* sbeta = reinterpret_cast<double*>(smem + 256);
         for (int i = threadIdx.x; i < beta_count; i += blockDim.x) sbeta[i] = p.betas[i];
         beta = sbeta;
-        beta_bytes = (beta_count * 8 + 15) & ~15;
+        shared_bytes += (beta_count * 8 + 15) & ~15;
     }
     __syncthreads();
     const int64_t center = p.center_begin + (int64_t)blockIdx.x * kWarps + warp;
     if (center >= p.center_end) return;
 
-    unsigned char* region = smem + beta_bytes + (size_t)warp * tab.warp_bytes;
-    double* pdx = reinterpret_cast<double*>(region);
+    unsigned char* region = smem + shared_bytes + (size_t)warp * tab.warp_bytes;
+    int* seg_prefix = reinterpret_cast<int*>(region);          // 33 ints (sentinel)
+    int* seg_start = seg_prefix + 40;                           // 32 ints
+    int* seg_t = seg_start + 32;                                // 32 ints
+    double* pdx = reinterpret_cast<double*>(region + 416);
     double* pdy = pdx + kPending;
     double* pdz = pdy + kPending;
     double* pr2 = pdz + kPending;
     int32_t* ptype = reinterpret_cast<int32_t*>(pr2 + kPending);
-    double* ybuf = reinterpret_cast<double*>(region + kPending * 36);
+    double* ybuf = reinterpret_cast<double*>(region + 416 + kPending * 36);
     const int64_t local = center - p.center_begin;
-    double* R = tab.r_global ? p.rbuf + local * ((int64_t)S * n * H)
-                             : reinterpret_cast<double*>(region + tab.r_offset);
+    double* R = tab.r_global ? p.rbuf + local * tab.csize : reinterpret_cast<double*>(region + tab.r_offset);
 
     const BinView& bv = p.bins;
-    const StructInfo* si_ptr = bv.info + bv.struct_of[center];
-    const StructInfo si = *si_ptr;
+    const StructInfo si = bv.info[bv.struct_of[center]];
     const int wi[3] = {bv.wrap[3 * center], bv.wrap[3 * center + 1], bv.wrap[3 * center + 2]};
     const int chunk = tab.chunk;
 
@@ -250,7 +365,7 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         const int te = min(S, tb + MAXT);
         for (int sg = 0; sg < tab.slot_groups; ++sg) {
             double pref[3], expo[3];
-            int yoff[3], il[3], ik[3];
+            int il[3], ik[3];
             bool ivalid[3];
 #pragma unroll
             for (int s = 0; s < 3; ++s) {
@@ -258,11 +373,13 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 ivalid[s] = s < NS && idx < tab.items;
                 const RadialItem it = ivalid[s] ? p.items[idx] : RadialItem{0.0, 0.0, 0, 0};
                 pref[s] = it.prefactor;
-                expo[s] = it.exponent;
+                expo[s] = -it.exponent;
                 il[s] = it.l;
                 ik[s] = it.k;
-                yoff[s] = it.l * it.l;
             }
+            const double* ybase0 = ybuf + il[0] * il[0];
+            const double* ybase1 = ybuf + il[1] * il[1];
+            const double* ybase2 = ybuf + il[2] * il[2];
             double a0[MAXT][L0 > 0 ? L0 : 1];
             double a1[MAXT][L1 > 0 ? L1 : 1];
             double a2[MAXT][L2 > 0 ? L2 : 1];
@@ -276,34 +393,52 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 for (int m = 0; m < (L2 > 0 ? L2 : 1); ++m) a2[t][m] = 0.0;
             }
 
+            auto accumulate = [&](int t, double g0, double g1, double g2, int eo) {
+#pragma unroll
+                for (int tt = 0; tt < MAXT; ++tt) {
+                    if (tt == t) {
+#pragma unroll
+                        for (int m = 0; m < L0; ++m) a0[tt][m] = fma(g0, ybase0[eo + m], a0[tt][m]);
+#pragma unroll
+                        for (int m = 0; m < L1; ++m) a1[tt][m] = fma(g1, ybase1[eo + m], a1[tt][m]);
+#pragma unroll
+                        for (int m = 0; m < L2; ++m) a2[tt][m] = fma(g2, ybase2[eo + m], a2[tt][m]);
+                    }
+                }
+            };
             auto process = [&](int count) {
                 if (lane < count) solid_harmonics(tab, pdx[lane], pdy[lane], pdz[lane], pr2[lane], ybuf + lane * H);
                 __syncwarp();
-                for (int e = 0; e < count; ++e) {
-                    const double r2 = pr2[e];
-                    const int t = ptype[e];
-                    const double w = tab.species_weight[tb + t];
-                    const double g0 = L0 > 0 ? w * pref[0] * exp(-expo[0] * r2) : 0.0;
-                    const double g1 = L1 > 0 ? w * pref[1] * exp(-expo[1] * r2) : 0.0;
-                    const double g2 = L2 > 0 ? w * pref[2] * exp(-expo[2] * r2) : 0.0;
-                    const double* yr = ybuf + e * H;
-#pragma unroll
-                    for (int tt = 0; tt < MAXT; ++tt) {
-                        if (tt == t) {
-#pragma unroll
-                            for (int m = 0; m < L0; ++m) a0[tt][m] = fma(g0, yr[yoff[0] + m], a0[tt][m]);
-#pragma unroll
-                            for (int m = 0; m < L1; ++m) a1[tt][m] = fma(g1, yr[yoff[1] + m], a1[tt][m]);
-#pragma unroll
-                            for (int m = 0; m < L2; ++m) a2[tt][m] = fma(g2, yr[yoff[2] + m], a2[tt][m]);
-                        }
-                    }
+                // Two edges per iteration: four independent exp() chains in flight.
+                int e = 0;
+                for (; e + 1 < count; e += 2) {
+                    const double ra = pr2[e], rb = pr2[e + 1];
+                    const int ta = ptype[e], tb2 = ptype[e + 1];
+                    const double wa = tab.species_weight[tb + ta], wb = tab.species_weight[tb + tb2];
+                    const double ga0 = L0 > 0 ? wa * pref[0] * exp_nonpositive(expo[0] * ra, etab) : 0.0;
+                    const double gb0 = L0 > 0 ? wb * pref[0] * exp_nonpositive(expo[0] * rb, etab) : 0.0;
+                    const double ga1 = L1 > 0 ? wa * pref[1] * exp_nonpositive(expo[1] * ra, etab) : 0.0;
+                    const double gb1 = L1 > 0 ? wb * pref[1] * exp_nonpositive(expo[1] * rb, etab) : 0.0;
+                    const double ga2 = L2 > 0 ? wa * pref[2] * exp_nonpositive(expo[2] * ra, etab) : 0.0;
+                    const double gb2 = L2 > 0 ? wb * pref[2] * exp_nonpositive(expo[2] * rb, etab) : 0.0;
+                    accumulate(ta, ga0, ga1, ga2, e * H);
+                    accumulate(tb2, gb0, gb1, gb2, (e + 1) * H);
+                }
+                if (e < count) {
+                    const double ra = pr2[e];
+                    const int ta = ptype[e];
+                    const double wa = tab.species_weight[tb + ta];
+                    const double ga0 = L0 > 0 ? wa * pref[0] * exp_nonpositive(expo[0] * ra, etab) : 0.0;
+                    const double ga1 = L1 > 0 ? wa * pref[1] * exp_nonpositive(expo[1] * ra, etab) : 0.0;
+                    const double ga2 = L2 > 0 ? wa * pref[2] * exp_nonpositive(expo[2] * ra, etab) : 0.0;
+                    accumulate(ta, ga0, ga1, ga2, e * H);
                 }
                 __syncwarp();
             };
 
             int pcount = 0;
-            for_each_candidate(si, bv, center, lane, [&](bool valid, int j, int tx, int ty, int tz) {
+            for_each_candidate_flat(si, bv, center, lane, seg_prefix, seg_start, seg_t,
+                                    [&](bool valid, int j, int tx, int ty, int tz) {
                 int nimg[3];
                 double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0;
                 int t = -1;
@@ -324,7 +459,9 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     ptype[q] = t - tb;
                 }
                 pcount += __popc(mask);
-                if (pcount >= chunk) {
+                // Drain whole chunks; the queue holds < chunk entries between
+                // candidate batches, so it never exceeds chunk + 31 <= 63 < kPending.
+                while (pcount >= chunk) {
                     __syncwarp();
                     process(chunk);
                     const int rem = pcount - chunk;
@@ -352,28 +489,28 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             __syncwarp();
             if (pcount > 0) process(pcount);
 
-            // Flush the raw sums: R[l][t][k][m] at S n l^2 + (t n + k)(2l+1) + m.
+            // Flush the raw sums: R[l][t][k][m], rows padded to 2l+2.
 #pragma unroll
             for (int tt = 0; tt < MAXT; ++tt) {
                 const int t = tb + tt;
                 if (t < te) {
                     if (L0 > 0 && ivalid[0]) {
                         const int len = 2 * il[0] + 1;
-                        double* dst = R + (int64_t)S * n * il[0] * il[0] + (t * n + ik[0]) * len;
+                        double* dst = R + cblock(S, n, il[0]) + (t * n + ik[0]) * (len + 1);
 #pragma unroll
                         for (int m = 0; m < L0; ++m)
                             if (m < len) dst[m] = a0[tt][m];
                     }
                     if (L1 > 0 && ivalid[1]) {
                         const int len = 2 * il[1] + 1;
-                        double* dst = R + (int64_t)S * n * il[1] * il[1] + (t * n + ik[1]) * len;
+                        double* dst = R + cblock(S, n, il[1]) + (t * n + ik[1]) * (len + 1);
 #pragma unroll
                         for (int m = 0; m < L1; ++m)
                             if (m < len) dst[m] = a1[tt][m];
                     }
                     if (L2 > 0 && ivalid[2]) {
                         const int len = 2 * il[2] + 1;
-                        double* dst = R + (int64_t)S * n * il[2] * il[2] + (t * n + ik[2]) * len;
+                        double* dst = R + cblock(S, n, il[2]) + (t * n + ik[2]) * (len + 1);
 #pragma unroll
                         for (int m = 0; m < L2; ++m)
                             if (m < len) dst[m] = a2[tt][m];
@@ -393,9 +530,8 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         else
             power_spectrum_warp<LMAX>(tab, R, static_cast<float*>(p.out) + row * tab.features, lane);
     } else if (tab.average == 1) {
-        const int64_t csize = (int64_t)S * n * H;
-        double* dst = p.cbuf + local * csize;
-        for (int64_t i = lane; i < csize; i += 32) dst[i] = R[i];
+        double* dst = p.cbuf + local * tab.csize;
+        for (int i = lane; i < tab.csize; i += 32) dst[i] = R[i];
     } else {
         power_spectrum_warp<LMAX>(tab, R, p.pbuf + local * tab.features, lane);
     }
@@ -420,9 +556,9 @@ soap_structure_kernel(const __grid_constant__ SoapTables tab, const int64_t* __r
     const double scale = count > 0 ? 1.0 / (double)count : 0.0;
     const int64_t F = tab.features;
     if (tab.average == 1) {
-        const int64_t csize = (int64_t)tab.n_species * tab.n_max * tab.H;
+        const int csize = tab.csize;
         double* c = reinterpret_cast<double*>(smem);
-        for (int64_t i = threadIdx.x; i < csize; i += blockDim.x) {
+        for (int i = threadIdx.x; i < csize; i += blockDim.x) {
             double sum = 0.0;
             for (int64_t a = 0; a < count; ++a) sum += cbuf[(a0 + a) * csize + i];
             c[i] = sum * scale;
