@@ -9,9 +9,11 @@ path in its place.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmdsoap.so"
+# MDSOAP_LIBRARY may point at another build of the same ABI (e.g. a debug build).
+LIB_PATH = Path(os.environ.get("MDSOAP_LIBRARY") or Path(__file__).resolve().parent / "lib" / "libmdsoap.so")
 
 OK = 0
 INVALID_ARGUMENT = 1

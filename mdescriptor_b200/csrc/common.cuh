@@ -12,6 +12,7 @@ constexpr int kMaxL = 20;
 constexpr int kMaxN = 32;
 constexpr int kWarps = 4;             // warps per CTA of the centre kernel
 constexpr int kPending = 64;          // accepted-edge queue per warp (>= 2 * 32)
+constexpr int kRegionHeader = 544;    // per-warp candidate tables + chunk permutation (bytes)
 constexpr int kTri = (kMaxL + 1) * (kMaxL + 2) / 2;
 
 // Bits of the per-device error word that kernels raise instead of trapping.

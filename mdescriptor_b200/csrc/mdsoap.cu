@@ -5,7 +5,7 @@
 // there, so building a plan touches no GPU (the reference's construction-time
 // contract, tests/test_cuda_backend.py:266-279).
 #include "../../include/mdsoap.h"
-#include "soap.cuh"
+#include "soap_pair.cuh"
 
 #include <cuda_runtime.h>
 
@@ -147,6 +147,15 @@ template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX, int MINB>
 const void* center_symbol() {
     return reinterpret_cast<const void*>(&soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX, MINB>);
 }
+// Two-warp variant: one CTA of 64 threads per centre (grid = centres).
+template <int MAXT, int LA, int LB1, int LB2, int NMAX, int LMAX, int MINB>
+void launch_pair(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_pair_kernel<MAXT, LA, LB1, LB2, NMAX, LMAX, MINB><<<grid, 64, smem, stream>>>(tab, p);
+}
+template <int MAXT, int LA, int LB1, int LB2, int NMAX, int LMAX, int MINB>
+const void* pair_symbol() {
+    return reinterpret_cast<const void*>(&soap_pair_kernel<MAXT, LA, LB1, LB2, NMAX, LMAX, MINB>);
+}
 template <int LMAX>
 void launch_structure(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const int64_t* offsets,
                       int64_t s0, int64_t s1, const double* cbuf, const double* pbuf, void* out, int64_t row0) {
@@ -164,30 +173,36 @@ const void* structure_symbol() {
 // registers per thread (MINB resident CTAs per SM).
 struct Variant {
     int cls, maxt, l0, l1, l2, nmax, lmax, minb;
+    bool pair;  // two warps per centre (soap_pair_kernel), channel slots A | B1 B2
     CenterLauncher center;
     const void* (*center_sym)();
     StructureLauncher structure;
     const void* (*structure_sym)();
 };
 
-#define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                              \
-    Variant {                                                                                                   \
-        CLS, T, A, B, C, N, L, MB, &launch_center<T, A, B, C, N, L, MB>, &center_symbol<T, A, B, C, N, L, MB>,  \
-            &launch_structure<L>, &structure_symbol<L>                                                          \
+#define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
+    Variant {                                                                                             \
+        CLS, T, A, B, C, N, L, MB, false, &launch_center<T, A, B, C, N, L, MB>,                             \
+            &center_symbol<T, A, B, C, N, L, MB>, &launch_structure<L>, &structure_symbol<L>              \
+    }
+#define MDSOAP_PAIR_VARIANT(CLS, T, A, B, C, N, L, MB)                                                   \
+    Variant {                                                                                             \
+        CLS, T, A, B, C, N, L, MB, true, &launch_pair<T, A, B, C, N, L, MB>, &pair_symbol<T, A, B, C, N, L, MB>, \
+            &launch_structure<L>, &structure_symbol<L>                                                    \
     }
 
 // First entry of each class is the default.
 // Defaults chosen by measurement on B200 (config shapes 1-5).
 const Variant kVariants[] = {
-    MDSOAP_VARIANT(0, 4, 7, 0, 0, 8, 3, 3),     // n <= 8, l <= 3
+    MDSOAP_VARIANT(0, 4, 7, 0, 0, 8, 3, 3),         // n <= 8, l <= 3
     MDSOAP_VARIANT(0, 8, 7, 0, 0, 8, 3, 2),
-    MDSOAP_VARIANT(1, 3, 9, 1, 0, 8, 4, 3),     // n <= 8, l == 4
+    MDSOAP_VARIANT(1, 3, 9, 1, 0, 8, 4, 3),         // n <= 8, l == 4
     MDSOAP_VARIANT(1, 6, 9, 1, 0, 8, 4, 2),
-    MDSOAP_VARIANT(2, 4, 13, 5, 0, 8, 6, 2),    // n <= 8, l in 5..6
-    MDSOAP_VARIANT(2, 2, 13, 5, 0, 8, 6, 3),
-    MDSOAP_VARIANT(2, 1, 13, 5, 0, 8, 6, 4),
-    MDSOAP_VARIANT(3, 2, 17, 9, 1, 8, 8, 2),    // n <= 8, l in 7..8
-    MDSOAP_VARIANT(3, 1, 17, 9, 1, 8, 8, 3),
+    MDSOAP_VARIANT(2, 4, 13, 5, 0, 8, 6, 2),        // n <= 8, l in 5..6
+    MDSOAP_PAIR_VARIANT(2, 4, 13, 9, 0, 8, 6, 6),
+    MDSOAP_PAIR_VARIANT(2, 3, 13, 9, 0, 8, 6, 6),
+    MDSOAP_VARIANT(3, 2, 17, 9, 1, 8, 8, 2),        // n <= 8, l in 7..8
+    MDSOAP_PAIR_VARIANT(3, 2, 17, 13, 5, 8, 8, 6),
     MDSOAP_VARIANT(4, 1, 41, 0, 0, 32, 20, 1),  // any n <= 32, l <= 20
 };
 
@@ -201,19 +216,46 @@ int variant_class(int n_max, int l_max) {
     return 4;
 }
 
-// MDSOAP_MAXT (tuning knob) selects the class member with that many species
-// banks; otherwise the class default.
-const Variant& pick_variant(int n_max, int l_max) {
+// MDSOAP_VARIANT=<k> (tuning knob) selects the k-th member of the class;
+// otherwise the class default, its first member (the fastest measured on
+// B200 for the config shapes; the two-warp pair kernels are alternatives).
+const Variant& pick_variant(int n_max, int l_max, int n_species) {
     const int cls = variant_class(n_max, l_max);
-    const char* env = std::getenv("MDSOAP_MAXT");
-    const int want = env ? std::atoi(env) : 0;
+    const char* env = std::getenv("MDSOAP_VARIANT");
+    int want = env ? std::atoi(env) : -1;
     const Variant* first = nullptr;
+    int k = 0;
     for (const Variant& v : kVariants) {
         if (v.cls != cls) continue;
         if (!first) first = &v;
-        if (want > 0 && v.maxt == want) return v;
+        if (k++ == want) return v;
     }
     return *first;
+}
+
+// Channel order for the kernels: the one-warp kernel takes channels sorted
+// by l descending, 32 per slot; the pair kernel takes three padded slots of
+// 32 (padding has l = -1): A = {L, L-1, 1, 0} (warp A), B1 = {L-2 .. L-5}
+// and B2 = the rest (warp B), which bounds each slot's 2l+1 by the variant's
+// slot lengths and balances the two warps.
+std::vector<RadialItem> order_items(const std::vector<RadialItem>& by_l, int l_max, int n_max, bool pair) {
+    if (!pair) return by_l;
+    std::vector<RadialItem> out(96, RadialItem{0.0, 0.0, -1, 0});
+    auto put = [&](int slot, const std::vector<int>& ls) {
+        int pos = 32 * slot;
+        for (int l : ls)
+            for (const RadialItem& it : by_l)
+                if (it.l == l) out[pos++] = it;
+    };
+    const int L = l_max;
+    std::vector<int> a{L, L - 1, 1, 0}, b1, b2;
+    for (int l = L - 2; l >= 2 && l >= L - 5; --l) b1.push_back(l);
+    for (int l = L - 6; l >= 2; --l) b2.push_back(l);
+    put(0, a);
+    put(1, b1);
+    put(2, b2);
+    (void)n_max;
+    return out;
 }
 
 // fp64 FMA throughput probe: kProbeChains independent dependent-FMA chains per
@@ -388,7 +430,7 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         p.rbuf = st.work.rbuf.as<double>();
     }
     if (centers > 0) {
-        const int64_t grid = (centers + kWarps - 1) / kWarps;
+        const int64_t grid = variant->pair ? centers : (centers + kWarps - 1) / kWarps;
         variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
         check(cudaGetLastError(), "centre kernel launch");
     }
@@ -708,11 +750,13 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             }
         }
         for (int i = 0; i < q.n_species; ++i) t.species_weight[i] = plan->weights[i];
-        const Variant& v = pick_variant(n, L);
+        const Variant& v = pick_variant(n, L, q.n_species);
         plan->variant = &v;
+        plan->items = order_items(plan->items, L, n, v.pair);
+        if (v.pair) t.items = (int32_t)plan->items.size();
         const int ns = (v.l0 > 0) + (v.l1 > 0) + (v.l2 > 0);
         const int slots = (t.items + 31) / 32;
-        t.slot_groups = (slots + ns - 1) / ns;
+        t.slot_groups = v.pair ? 1 : (slots + ns - 1) / ns;
         t.type_groups = (q.n_species + v.maxt - 1) / v.maxt;
         const bool single_pass = t.slot_groups == 1 && t.type_groups == 1;
         const size_t beta_bytes = (size_t)W * n * n * 8;
@@ -720,9 +764,11 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         // CTA-shared: 32-entry exp table (256 B) + optional beta copy.
         const size_t beta_smem = 256 + (t.beta_in_smem ? ((beta_bytes + 15) & ~(size_t)15) : 0);
         t.csize = q.n_species * n * W * (W + 1);
+        t.hp = W * (W + 1);
         const size_t r_bytes = (size_t)t.csize * 8;
-        const size_t pend = 416 + (size_t)kPending * 36;
-        auto region_a = [&](int chunk) { return pend + ((size_t)chunk * t.H + 48) * 8; };
+        const size_t pend = v.pair ? (size_t)kPairHeader + (size_t)kPairPending * 36
+                                   : kRegionHeader + (size_t)kPending * 36;
+        auto region_a = [&](int chunk) { return pend + ((size_t)chunk * t.hp + 48) * 8; };
         auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
         auto per_warp = [&](int chunk, bool r_in_smem) {
             if (!r_in_smem) return align16(region_a(chunk));
@@ -742,11 +788,27 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             chunk = 32;
             while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, false) > budget) chunk -= 8;
         }
+        if (v.pair) {
+            // One region per CTA (one centre), no beta copy; offsets relative
+            // to the queue (after the exp table and the header).
+            t.beta_in_smem = 0;
+            auto cta = [&](int c, bool r_in) { return 256 + per_warp(c, r_in); };
+            chunk = 32;
+            r_smem = true;
+            while (chunk > 8 && cta(chunk, true) > budget) chunk -= 8;
+            if (cta(chunk, true) > budget1) r_smem = false;
+            t.chunk = chunk;
+            t.r_global = r_smem ? 0 : 1;
+            t.warp_bytes = (int32_t)per_warp(chunk, r_smem);
+            t.r_offset = (r_smem && !single_pass) ? (int32_t)(align16(region_a(chunk)) - kPairHeader) : 0;
+            plan->center_smem = cta(chunk, r_smem);
+        } else {
         t.chunk = chunk;
         t.r_global = r_smem ? 0 : 1;
         t.warp_bytes = (int32_t)per_warp(chunk, r_smem);
         t.r_offset = (r_smem && !single_pass) ? (int32_t)align16(region_a(chunk)) : 0;
         plan->center_smem = beta_smem + kWarps * (size_t)t.warp_bytes;
+        }
         plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? r_bytes : 0;
         plan->csize = t.csize;
         if (plan->center_smem > budget1 || plan->structure_smem > budget1)

@@ -27,6 +27,8 @@
 //     covers runs of consecutive features.
 #pragma once
 
+#include <type_traits>
+
 #include "expneg.cuh"
 #include "neighbors.cuh"
 
@@ -55,6 +57,8 @@ struct SoapTables {
     int32_t slot_groups;  // passes over channel-slot groups
     int32_t r_global;     // 1: coefficient blocks live in global scratch
     int32_t csize;        // coefficient block length in doubles: S n (L+1)(L+2)
+    int32_t hp;           // padded harmonic row length: (L+1)(L+2)
+    int32_t pad2_;
     double cutoff2;
     double soap_scale;    // pi^{3/2}
     double ynorm[kTri];   // N_lm (times sqrt 2 for m > 0), index l(l+1)/2 + m
@@ -80,13 +84,24 @@ struct SoapPointers {
 
 __device__ __forceinline__ int tri(int l, int m) { return l * (l + 1) / 2 + m; }
 
+// Compile-time loop: f(std::integral_constant<int, I>) for I in [I0, N).
+template <int I0, int N, class F>
+__device__ __forceinline__ void static_for(F&& f) {
+    if constexpr (I0 < N) {
+        f(std::integral_constant<int, I0>{});
+        static_for<I0 + 1, N>(f);
+    }
+}
+
 // Coefficient block layout: [l][t][n][m] with each (t, n) row padded to
 // 2l+2 doubles; block l starts at S n l (l+1).
 __device__ __forceinline__ int cblock(int S, int n, int l) { return S * n * l * (l + 1); }
 
-// Real regular solid harmonics of one displacement into out[0..H), layout
-// l^2 + (l - m) = cos part, l^2 + l = m0, l^2 + (l + m) = sin part
-// (soap.cpp:101-216 generic Cartesian recurrence, all l).
+// Real regular solid harmonics of one displacement into a padded row: the
+// block of degree l starts at l (l + 1) (even, so 16-byte aligned) and holds
+// j = l - m (cos part), j = l (m = 0), j = l + m (sin part) at offset j, the
+// reference's within-l order (soap.cpp:101-216 generic Cartesian recurrence,
+// all l); offset 2l+1 is padding.
 __device__ __forceinline__ void solid_harmonics(const SoapTables& tab, double x, double y, double z, double r2,
                                                 double* __restrict__ out) {
     const int L = tab.l_max;
@@ -105,8 +120,8 @@ __device__ __forceinline__ void solid_harmonics(const SoapTables& tab, double x,
             if (m == 0) {
                 out[0] = nrm * pr2;
             } else {
-                out[m * m] = nrm * pr2;
-                out[m * m + 2 * m] = nrm * pi2;
+                out[m * (m + 1)] = nrm * pr2;
+                out[m * (m + 1) + 2 * m] = nrm * pi2;
             }
         }
         if (m < L) {
@@ -115,8 +130,8 @@ __device__ __forceinline__ void solid_harmonics(const SoapTables& tab, double x,
             {
                 const int l = m + 1;
                 const double nrm = tab.ynorm[tri(l, m)];
-                out[l * l + l - m] = nrm * pr1;
-                if (m > 0) out[l * l + l + m] = nrm * pi1;
+                out[l * (l + 1) + l - m] = nrm * pr1;
+                if (m > 0) out[l * (l + 1) + l + m] = nrm * pi1;
             }
             for (int l = m + 2; l <= L; ++l) {
                 const double a = tab.yra[tri(l, m)] * z;
@@ -128,11 +143,69 @@ __device__ __forceinline__ void solid_harmonics(const SoapTables& tab, double x,
                 pr1 = nr;
                 pi1 = ni;
                 const double nrm = tab.ynorm[tri(l, m)];
-                out[l * l + l - m] = nrm * nr;
-                if (m > 0) out[l * l + l + m] = nrm * ni;
+                out[l * (l + 1) + l - m] = nrm * nr;
+                if (m > 0) out[l * (l + 1) + l + m] = nrm * ni;
             }
         }
     }
+}
+
+// Same recurrence with a compile-time l_max: every index and coefficient
+// offset is a constant, so the constant-bank coefficients feed the FP64
+// instructions directly.
+template <int L>
+__device__ __forceinline__ void solid_harmonics_fixed(const SoapTables& tab, double x, double y, double z, double r2,
+                                                      double* __restrict__ out) {
+    double dr = 1.0, di = 0.0;
+#pragma unroll
+    for (int m = 0; m <= L; ++m) {
+        if (m > 0) {
+            const double f = -(2.0 * m - 1.0);
+            const double nr = f * (x * dr - y * di);
+            const double ni = f * (x * di + y * dr);
+            dr = nr;
+            di = ni;
+        }
+        double pr2 = dr, pi2 = di;
+        if (m == 0) {
+            out[0] = tab.ynorm[0] * pr2;
+        } else {
+            out[m * (m + 1)] = tab.ynorm[m * (m + 1) / 2 + m] * pr2;
+            out[m * (m + 1) + 2 * m] = tab.ynorm[m * (m + 1) / 2 + m] * pi2;
+        }
+        if (m < L) {
+            const double c = (2.0 * m + 1.0) * z;
+            double pr1 = c * dr, pi1 = c * di;
+            {
+                const int l = m + 1;
+                out[l * (l + 1) + l - m] = tab.ynorm[l * (l + 1) / 2 + m] * pr1;
+                if (m > 0) out[l * (l + 1) + l + m] = tab.ynorm[l * (l + 1) / 2 + m] * pi1;
+            }
+#pragma unroll
+            for (int l = m + 2; l <= L; ++l) {
+                const int i = l * (l + 1) / 2 + m;
+                const double a = tab.yra[i] * z;
+                const double b = tab.yrb[i] * r2;
+                const double nr = fma(a, pr1, -b * pr2);
+                const double ni = fma(a, pi1, -b * pi2);
+                pr2 = pr1;
+                pi2 = pi1;
+                pr1 = nr;
+                pi1 = ni;
+                out[l * (l + 1) + l - m] = tab.ynorm[i] * nr;
+                if (m > 0) out[l * (l + 1) + l + m] = tab.ynorm[i] * ni;
+            }
+        }
+    }
+}
+
+template <int LMAX>
+__device__ __forceinline__ void harmonics_any(const SoapTables& tab, double x, double y, double z, double r2,
+                                              double* __restrict__ out) {
+    if (tab.l_max == LMAX)
+        solid_harmonics_fixed<LMAX>(tab, x, y, z, r2, out);
+    else
+        solid_harmonics(tab, x, y, z, r2, out);
 }
 
 // Feature offset of (t1, n1, t2, n2, l) in the compression-off layout
@@ -145,90 +218,146 @@ __device__ __forceinline__ int64_t pair_base(int S, int n, int L, int t1, int t2
     return base;
 }
 
-// One l of the power spectrum: lane = column r2 (own row in registers), rows
-// r1 <= r2 broadcast from shared memory two doubles at a time.
-template <int LEN, class OutT>
-__device__ __forceinline__ void power_l(const double* __restrict__ cl, int R, int n, int S, int L, int l,
-                                        double pref, OutT* __restrict__ out, int lane) {
-    constexpr int PAD = LEN + 1;  // row stride, even
-    const int T = n * (n + 1) / 2;
+// Power spectrum for l in [LA, LB]: lane = column r2, whose rows of every l
+// in the group sit in registers; the loop over rows r1 <= r2 reads each row
+// r1 once per l as 16-byte shared-memory broadcasts, and one feature index
+// per (r1, r2) serves all l of the group.
+template <int LA, int LB, class OutT>
+__device__ __forceinline__ void power_group(const SoapTables& tab, const double* __restrict__ c,
+                                            OutT* __restrict__ out, int lane, int r1_first, int r1_step) {
+    constexpr int NOWN = (LB + 1) * (LB + 1) - LA * LA;
+    constexpr int NL = LB - LA + 1;
+    const int S = tab.n_species, n = tab.n_max, L = tab.l_max, R = tab.rows;
+    if (LA > L) return;
+    const int64_t T = (int64_t)n * (n + 1) / 2, nn = (int64_t)n * n;
+    const int sn = S * n;
     for (int r2base = 0; r2base < R; r2base += 32) {
         const int r2 = r2base + lane;
         const bool active = r2 < R;
         const int t2 = active ? r2 / n : 0;
         const int n2 = active ? r2 - t2 * n : 0;
-        double own[LEN];
+        double own[NOWN];
 #pragma unroll
-        for (int m = 0; m < LEN; ++m) own[m] = active ? cl[r2 * PAD + m] : 0.0;
+        for (int l = LA; l <= LB; ++l) {
+            const double* cl = c + sn * l * (l + 1) + r2 * (2 * l + 2);
+#pragma unroll
+            for (int m = 0; m < 2 * l + 1; ++m) own[l * l - LA * LA + m] = (active && l <= L) ? cl[m] : 0.0;
+        }
         const int r1_end = min(R - 1, r2base + 31);
-        int t1 = 0, n1 = 0;
-        int64_t base = pair_base(S, n, L, 0, t2) + (int64_t)l * (t2 == 0 ? T : n * n);
-        for (int r1 = 0; r1 <= r1_end; ++r1) {
-            const double2* o = reinterpret_cast<const double2*>(cl + r1 * PAD);
-            double v = 0.0;
+        int t1 = r1_first / n, n1 = r1_first - (r1_first / n) * n;
+        int64_t base = pair_base(S, n, L, t1, t2);
+        int64_t bs = t1 == t2 ? T : nn;
+        for (int r1 = r1_first; r1 <= r1_end; r1 += r1_step) {
+            double v[NL];
 #pragma unroll
-            for (int m = 0; m + 1 < LEN; m += 2) {
-                const double2 q = o[m / 2];
-                v = fma(q.x, own[m], v);
-                v = fma(q.y, own[m + 1], v);
+            for (int l = LA; l <= LB; ++l) {
+                double acc = 0.0;
+                if (l <= L) {
+                    const double2* o = reinterpret_cast<const double2*>(c + sn * l * (l + 1) + r1 * (2 * l + 2));
+#pragma unroll
+                    for (int m = 0; m < 2 * l + 1; m += 2) {
+                        const double2 q = o[m / 2];
+                        acc = fma(q.x, own[l * l - LA * LA + m], acc);
+                        if (m + 1 < 2 * l + 1) acc = fma(q.y, own[l * l - LA * LA + m + 1], acc);
+                    }
+                }
+                v[l - LA] = acc;
             }
-            v = fma(cl[r1 * PAD + LEN - 1], own[LEN - 1], v);
             if (active && r2 >= r1) {
                 const int64_t inner = t1 == t2 ? (int64_t)n1 * n - (int64_t)n1 * (n1 - 1) / 2 + (n2 - n1)
                                                : (int64_t)n1 * n + n2;
-                out[base + inner] = (OutT)(pref * v);
+                OutT* dst = out + base + inner;
+#pragma unroll
+                for (int l = LA; l <= LB; ++l)
+                    if (l <= L) dst[l * bs] = (OutT)(tab.power_pref[l] * v[l - LA]);
             }
-            if (++n1 == n) {
-                n1 = 0;
-                ++t1;
-                if (t1 <= t2) base = pair_base(S, n, L, t1, t2) + (int64_t)l * (t1 == t2 ? T : n * n);
+            n1 += r1_step;
+            if (n1 >= n) {
+                while (n1 >= n) {
+                    n1 -= n;
+                    ++t1;
+                }
+                if (t1 <= t2) {
+                    base = pair_base(S, n, L, t1, t2);
+                    bs = t1 == t2 ? T : nn;
+                }
             }
         }
     }
 }
 
-template <int l, int LMAX, class OutT>
-__device__ __forceinline__ void power_from(const SoapTables& tab, const double* __restrict__ c,
-                                           OutT* __restrict__ out, int lane) {
-    if constexpr (l <= LMAX) {
-        if (l > tab.l_max) return;
-        const int S = tab.n_species, n = tab.n_max;
-        power_l<2 * l + 1>(c + cblock(S, n, l), tab.rows, n, S, tab.l_max, l, tab.power_pref[l], out, lane);
-        power_from<l + 1, LMAX, OutT>(tab, c, out, lane);
+// l groups sized so that a lane's register rows stay near 50 doubles.
+// Rows r1 = r1_first, r1_first + r1_step, ... (several warps split a centre).
+template <int LMAX, class OutT>
+__device__ __forceinline__ void power_spectrum_warp(const SoapTables& tab, const double* __restrict__ c,
+                                                    OutT* __restrict__ out, int lane, int r1_first = 0,
+                                                    int r1_step = 1) {
+    if constexpr (LMAX <= 6) {
+        power_group<0, LMAX, OutT>(tab, c, out, lane, r1_first, r1_step);
+    } else if constexpr (LMAX <= 8) {
+        power_group<0, 5, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<6, LMAX, OutT>(tab, c, out, lane, r1_first, r1_step);
+    } else {
+        power_group<0, 6, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<7, 9, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<10, 11, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<12, 13, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<14, 15, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<16, 17, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<18, 19, OutT>(tab, c, out, lane, r1_first, r1_step);
+        power_group<20, 20, OutT>(tab, c, out, lane, r1_first, r1_step);
     }
 }
 
-template <int LMAX, class OutT>
-__device__ __forceinline__ void power_spectrum_warp(const SoapTables& tab, const double* __restrict__ c,
-                                                    OutT* __restrict__ out, int lane) {
-    power_from<0, LMAX, OutT>(tab, c, out, lane);
-}
-
 // In-place beta transform of the raw sums R[l][t][k][m] -> c[l][t][n][m]
-// (padded rows), soap.cpp:915-926.
+// (padded rows), soap.cpp:915-926.  For n_max <= 8 the n x n block beta_l
+// sits in registers while the warp sweeps the (t, m) columns of that l.
 template <int NMAX>
 __device__ __forceinline__ void beta_transform_warp(const SoapTables& tab, const double* __restrict__ beta,
-                                                    double* __restrict__ R, int lane) {
+                                                    double* __restrict__ R, int lane, int nthreads = 32) {
     const int S = tab.n_species, n = tab.n_max, L = tab.l_max;
     for (int l = 0; l <= L; ++l) {
         const int len = 2 * l + 1, pad = 2 * l + 2;
         const int cols = S * len;
         double* rl = R + cblock(S, n, l);
         const double* bl = beta + (int64_t)l * n * n;
-        for (int col = lane; col < cols; col += 32) {
-            const int t = col / len;
-            const int m = col - t * len;
-            double* base = rl + t * n * pad + m;
-            double r[NMAX];
+        if constexpr (NMAX <= 8) {
+            double b[NMAX][NMAX];
 #pragma unroll
-            for (int k = 0; k < NMAX; ++k) r[k] = k < n ? base[k * pad] : 0.0;
-            for (int nn = 0; nn < n; ++nn) {
-                double acc = 0.0;
+            for (int i = 0; i < NMAX; ++i)
 #pragma unroll
-                for (int k = 0; k < NMAX; ++k) {
-                    if (k < n) acc = fma(bl[nn * n + k], r[k], acc);
+                for (int k = 0; k < NMAX; ++k) b[i][k] = (i < n && k < n) ? tab.soap_scale * bl[i * n + k] : 0.0;
+            for (int col = lane; col < cols; col += nthreads) {
+                const int t = col / len;
+                const int m = col - t * len;
+                double* base = rl + t * n * pad + m;
+                double r[NMAX];
+#pragma unroll
+                for (int k = 0; k < NMAX; ++k) r[k] = k < n ? base[k * pad] : 0.0;
+#pragma unroll
+                for (int i = 0; i < NMAX; ++i) {
+                    double acc = 0.0;
+#pragma unroll
+                    for (int k = 0; k < NMAX; ++k) acc = fma(b[i][k], r[k], acc);
+                    if (i < n) base[i * pad] = acc;
                 }
-                base[nn * pad] = tab.soap_scale * acc;
+            }
+        } else {
+            for (int col = lane; col < cols; col += nthreads) {
+                const int t = col / len;
+                const int m = col - t * len;
+                double* base = rl + t * n * pad + m;
+                double r[NMAX];
+#pragma unroll
+                for (int k = 0; k < NMAX; ++k) r[k] = k < n ? base[k * pad] : 0.0;
+                for (int nn = 0; nn < n; ++nn) {
+                    double acc = 0.0;
+#pragma unroll
+                    for (int k = 0; k < NMAX; ++k) {
+                        if (k < n) acc = fma(bl[nn * n + k], r[k], acc);
+                    }
+                    base[nn * pad] = tab.soap_scale * acc;
+                }
             }
         }
     }
@@ -325,7 +454,7 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int S = tab.n_species, n = tab.n_max, H = tab.H;
+    const int S = tab.n_species, n = tab.n_max, H = tab.hp;
     const int beta_count = (tab.l_max + 1) * n * n;
     // CTA-shared: exp table (32 doubles), then beta (optional).
     double* etab = reinterpret_cast<double*>(smem);
@@ -343,15 +472,16 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     if (center >= p.center_end) return;
 
     unsigned char* region = smem + shared_bytes + (size_t)warp * tab.warp_bytes;
-    int* seg_prefix = reinterpret_cast<int*>(region);          // 33 ints (sentinel)
+    int* seg_prefix = reinterpret_cast<int*>(region);          // 40 ints
     int* seg_start = seg_prefix + 40;                           // 32 ints
     int* seg_t = seg_start + 32;                                // 32 ints
-    double* pdx = reinterpret_cast<double*>(region + 416);
+    int* perm = seg_t + 32;                                     // 32 ints: chunk order by species
+    double* pdx = reinterpret_cast<double*>(region + kRegionHeader);
     double* pdy = pdx + kPending;
     double* pdz = pdy + kPending;
     double* pr2 = pdz + kPending;
     int32_t* ptype = reinterpret_cast<int32_t*>(pr2 + kPending);
-    double* ybuf = reinterpret_cast<double*>(region + 416 + kPending * 36);
+    double* ybuf = reinterpret_cast<double*>(region + kRegionHeader + kPending * 36);
     const int64_t local = center - p.center_begin;
     double* R = tab.r_global ? p.rbuf + local * tab.csize : reinterpret_cast<double*>(region + tab.r_offset);
 
@@ -377,9 +507,9 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 il[s] = it.l;
                 ik[s] = it.k;
             }
-            const double* ybase0 = ybuf + il[0] * il[0];
-            const double* ybase1 = ybuf + il[1] * il[1];
-            const double* ybase2 = ybuf + il[2] * il[2];
+            const double* ybase0 = ybuf + il[0] * (il[0] + 1);
+            const double* ybase1 = ybuf + il[1] * (il[1] + 1);
+            const double* ybase2 = ybuf + il[2] * (il[2] + 1);
             double a0[MAXT][L0 > 0 ? L0 : 1];
             double a1[MAXT][L1 > 0 ? L1 : 1];
             double a2[MAXT][L2 > 0 ? L2 : 1];
@@ -393,46 +523,75 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 for (int m = 0; m < (L2 > 0 ? L2 : 1); ++m) a2[t][m] = 0.0;
             }
 
-            auto accumulate = [&](int t, double g0, double g1, double g2, int eo) {
+            // One edge into species bank TT: 16-byte broadcast reads of the
+            // harmonic row (padding only feeds accumulators that are never stored).
+            auto accumulate = [&](auto bank, double g0, double g1, double g2, int eo) {
+                constexpr int TT = decltype(bank)::value;
 #pragma unroll
-                for (int tt = 0; tt < MAXT; ++tt) {
-                    if (tt == t) {
+                for (int m = 0; m < L0; m += 2) {
+                    const double2 y = *reinterpret_cast<const double2*>(ybase0 + eo + m);
+                    a0[TT][m] = fma(g0, y.x, a0[TT][m]);
+                    if (m + 1 < L0) a0[TT][m + 1] = fma(g0, y.y, a0[TT][m + 1]);
+                }
 #pragma unroll
-                        for (int m = 0; m < L0; ++m) a0[tt][m] = fma(g0, ybase0[eo + m], a0[tt][m]);
+                for (int m = 0; m < L1; m += 2) {
+                    const double2 y = *reinterpret_cast<const double2*>(ybase1 + eo + m);
+                    a1[TT][m] = fma(g1, y.x, a1[TT][m]);
+                    if (m + 1 < L1) a1[TT][m + 1] = fma(g1, y.y, a1[TT][m + 1]);
+                }
 #pragma unroll
-                        for (int m = 0; m < L1; ++m) a1[tt][m] = fma(g1, ybase1[eo + m], a1[tt][m]);
-#pragma unroll
-                        for (int m = 0; m < L2; ++m) a2[tt][m] = fma(g2, ybase2[eo + m], a2[tt][m]);
-                    }
+                for (int m = 0; m < L2; m += 2) {
+                    const double2 y = *reinterpret_cast<const double2*>(ybase2 + eo + m);
+                    a2[TT][m] = fma(g2, y.x, a2[TT][m]);
+                    if (m + 1 < L2) a2[TT][m + 1] = fma(g2, y.y, a2[TT][m + 1]);
                 }
             };
+            auto radial = [&](int e, double w, double& g0, double& g1, double& g2) {
+                const double r2e = pr2[e];
+                g0 = L0 > 0 ? w * pref[0] * exp_nonpositive(expo[0] * r2e, etab) : 0.0;
+                g1 = L1 > 0 ? w * pref[1] * exp_nonpositive(expo[1] * r2e, etab) : 0.0;
+                g2 = L2 > 0 ? w * pref[2] * exp_nonpositive(expo[2] * r2e, etab) : 0.0;
+            };
             auto process = [&](int count) {
-                if (lane < count) solid_harmonics(tab, pdx[lane], pdy[lane], pdz[lane], pr2[lane], ybuf + lane * H);
+                if (lane < count)
+                    harmonics_any<LMAX>(tab, pdx[lane], pdy[lane], pdz[lane], pr2[lane], ybuf + lane * H);
+                // Stable counting sort of the chunk by species bank: each bank
+                // then runs over a contiguous range with a static register bank.
+                const int mine = lane < count ? ptype[lane] : MAXT;
+                const unsigned lt = (1u << lane) - 1u;
+                int run_start[MAXT + 1];
+                run_start[0] = 0;
+                int rank = 0;
+#pragma unroll
+                for (int tt = 0; tt < MAXT; ++tt) {
+                    const unsigned m = __ballot_sync(0xffffffffu, mine == tt);
+                    if (mine == tt) rank = run_start[tt] + __popc(m & lt);
+                    run_start[tt + 1] = run_start[tt] + __popc(m);
+                }
+                if (lane < count) perm[rank] = lane;
                 __syncwarp();
-                // Two edges per iteration: four independent exp() chains in flight.
-                int e = 0;
-                for (; e + 1 < count; e += 2) {
-                    const double ra = pr2[e], rb = pr2[e + 1];
-                    const int ta = ptype[e], tb2 = ptype[e + 1];
-                    const double wa = tab.species_weight[tb + ta], wb = tab.species_weight[tb + tb2];
-                    const double ga0 = L0 > 0 ? wa * pref[0] * exp_nonpositive(expo[0] * ra, etab) : 0.0;
-                    const double gb0 = L0 > 0 ? wb * pref[0] * exp_nonpositive(expo[0] * rb, etab) : 0.0;
-                    const double ga1 = L1 > 0 ? wa * pref[1] * exp_nonpositive(expo[1] * ra, etab) : 0.0;
-                    const double gb1 = L1 > 0 ? wb * pref[1] * exp_nonpositive(expo[1] * rb, etab) : 0.0;
-                    const double ga2 = L2 > 0 ? wa * pref[2] * exp_nonpositive(expo[2] * ra, etab) : 0.0;
-                    const double gb2 = L2 > 0 ? wb * pref[2] * exp_nonpositive(expo[2] * rb, etab) : 0.0;
-                    accumulate(ta, ga0, ga1, ga2, e * H);
-                    accumulate(tb2, gb0, gb1, gb2, (e + 1) * H);
-                }
-                if (e < count) {
-                    const double ra = pr2[e];
-                    const int ta = ptype[e];
-                    const double wa = tab.species_weight[tb + ta];
-                    const double ga0 = L0 > 0 ? wa * pref[0] * exp_nonpositive(expo[0] * ra, etab) : 0.0;
-                    const double ga1 = L1 > 0 ? wa * pref[1] * exp_nonpositive(expo[1] * ra, etab) : 0.0;
-                    const double ga2 = L2 > 0 ? wa * pref[2] * exp_nonpositive(expo[2] * ra, etab) : 0.0;
-                    accumulate(ta, ga0, ga1, ga2, e * H);
-                }
+                static_for<0, MAXT>([&](auto bank) {
+                    constexpr int TT = decltype(bank)::value;
+                    const int end = run_start[TT + 1];
+                    if (run_start[TT] == end) return;
+                    const double w = tab.species_weight[tb + TT];
+                    int i = run_start[TT];
+                    // Two edges per step: more independent exp() chains in flight.
+                    for (; i + 1 < end; i += 2) {
+                        const int ea = perm[i], eb = perm[i + 1];
+                        double ga0, ga1, ga2, gb0, gb1, gb2;
+                        radial(ea, w, ga0, ga1, ga2);
+                        radial(eb, w, gb0, gb1, gb2);
+                        accumulate(bank, ga0, ga1, ga2, ea * H);
+                        accumulate(bank, gb0, gb1, gb2, eb * H);
+                    }
+                    if (i < end) {
+                        const int ea = perm[i];
+                        double ga0, ga1, ga2;
+                        radial(ea, w, ga0, ga1, ga2);
+                        accumulate(bank, ga0, ga1, ga2, ea * H);
+                    }
+                });
                 __syncwarp();
             };
 

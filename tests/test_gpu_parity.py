@@ -295,3 +295,15 @@ def test_multi_device_sharding_matches_single(cuda_device):
     single = soap_for(meta, "off").compute(batch, devices=[0])
     multi = soap_for(meta, "off").compute(batch, devices=list(range(device_count())))
     np.testing.assert_array_equal(single, multi)
+
+
+@pytest.mark.parametrize("config,variant", [(2, 1), (2, 2), (3, 1)])
+def test_alternative_kernel_variants_match(cuda_device, monkeypatch, config, variant):
+    """The two-warp pair kernels (selected with MDSOAP_VARIANT) give the same features."""
+    name = f"cfg{config}"
+    meta = CFG_META[name]
+    batch = batch_from(CFG, f"{name}/input")
+    default = soap_for(meta, "off", "float64").compute(batch, devices=[cuda_device])
+    monkeypatch.setenv("MDSOAP_VARIANT", str(variant))
+    alt = soap_for(meta, "off", "float64").compute(batch, devices=[cuda_device])
+    assert max_rel_err(alt, default, 1e-3) <= 1e-12
