@@ -139,6 +139,42 @@ int mdsoap_compute_device(mdsoap_plan* plan, const mdsoap_batch* batch, void* ou
  * `device` since the last check (and clear it). */
 int mdsoap_plan_check(mdsoap_plan* plan, int32_t device, void* stream);
 
+/* Size of the fixed device scratch area used by mdsoap_compute_device_noalloc:
+ * 32 MiB, held by every GPU that loads this library until the process exits. */
+#define MDSOAP_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+
+/* Device-resident compute that allocates no memory (this entry point has no
+ * counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory while they run: a process
+ * whose framework allocator has already reserved the GPU's memory (a cudaMalloc
+ * would fail or fragment that pool), or a latency-critical loop that must not
+ * take the device-wide synchronisation cudaMalloc/cudaFree imply.  Such a
+ * caller passes device inputs and a device output exactly as for
+ * mdsoap_compute_device; every working buffer (neighbour bins, copies of the
+ * plan's radial tables, the error word, per-centre coefficient blocks for the
+ * averages) lives in one file-scope __device__ array of
+ * MDSOAP_NOALLOC_SCRATCH_BYTES, and the call makes no cudaMalloc, cudaFree or
+ * other allocating call.
+ *
+ * Limits and rules:
+ *  - A batch whose working set does not fit the scratch array is rejected with
+ *    MDSOAP_CAPACITY_OVERFLOW before any device work (roughly 44 bytes per atom
+ *    plus 300 per structure for average "off"; the averages add one
+ *    coefficient block or feature row per atom).
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress, with `device` made current) and raises the
+ *    kernels' shared-memory limit; make that first call before any stream
+ *    capture.
+ *  - All calls in the process share the one array and it keeps the last
+ *    call's contents; everything that must start at zero is cleared by each
+ *    call.  Calls whose GPU work overlaps (different streams or threads)
+ *    race on the array: serialise them.
+ *  - The call waits for its work on `stream` and returns device-detected input
+ *    errors (unknown species, mixed pbc, singular cell) as its status. */
+int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, void* out, int32_t device,
+                                  void* stream);
+
 /* Per-kernel CUDA-event timing of mdsoap_compute_device calls (measurement
  * support; no counterpart in the reference).  While enabled, each device call
  * records events around its binning, centre and structure kernels on the

@@ -23,6 +23,8 @@ CANCELLED = 4
 CAPACITY_OVERFLOW = 5
 INTERNAL = 6
 
+NOALLOC_SCRATCH_BYTES = 32 << 20  # MDSOAP_NOALLOC_SCRATCH_BYTES
+
 FLOAT32 = 0
 FLOAT64 = 1
 AVERAGE = {"off": 0, "inner": 1, "outer": 2}
@@ -82,6 +84,8 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_compute_device.restype = ctypes.c_int
     lib.mdsoap_plan_check.argtypes = [_P, ctypes.c_int32, _P]
     lib.mdsoap_plan_check.restype = ctypes.c_int
+    lib.mdsoap_compute_device_noalloc.argtypes = [_P, ctypes.POINTER(BatchView), _P, ctypes.c_int32, _P]
+    lib.mdsoap_compute_device_noalloc.restype = ctypes.c_int
     lib.mdsoap_plan_set_timing.argtypes = [_P, ctypes.c_int32]
     lib.mdsoap_plan_set_timing.restype = ctypes.c_int
     lib.mdsoap_plan_last_timing.argtypes = [_P, ctypes.c_int32, _P, _P, _P]
@@ -113,6 +117,7 @@ EXPORTED = (
     "mdsoap_compute",
     "mdsoap_compute_device",
     "mdsoap_plan_check",
+    "mdsoap_compute_device_noalloc",
     "mdsoap_plan_set_timing",
     "mdsoap_plan_last_timing",
     "mdsoap_probe_fp64_fma",

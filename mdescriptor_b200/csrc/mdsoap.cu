@@ -950,6 +950,151 @@ int mdsoap_plan_check(mdsoap_plan* plan, int32_t device, void* stream) {
     }
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free device entry point.  The scratch array below is the only
+// device memory it uses; its host-side name is only a stand-in, so the device
+// address is looked up once per device with cudaGetSymbolAddress.
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[MDSOAP_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_noalloc_mutex;
+unsigned char* g_noalloc_base[64] = {};  // device address of the array, per device ordinal
+
+unsigned char* noalloc_base(int device) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (device < 0 || device >= 64) raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device index out of range");
+    if (g_noalloc_base[device]) return g_noalloc_base[device];
+    void* ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    check(err, "cudaGetSymbolAddress(no-allocation scratch)");
+    g_noalloc_base[device] = static_cast<unsigned char*>(ptr);
+    return g_noalloc_base[device];
+}
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+extern "C" {
+
+int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, void* out, int32_t device,
+                                  void* stream) {
+    if (!plan || !batch) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    if (batch->structures < 0 || batch->atoms < 0) return fail(MDSOAP_INVALID_ARGUMENT, "invalid structure batch");
+    const int64_t S = batch->structures, N = batch->atoms;
+    // Scratch layout (each piece 256-byte aligned).
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = off;
+        off = align256(off + std::max<size_t>(bytes, 1));
+        return at;
+    };
+    const size_t o_items = take(sizeof(RadialItem) * plan->items.size());
+    const size_t o_betas = take(8 * plan->betas.size());
+    const size_t o_species = take(4 * plan->species.size());
+    const size_t o_error = take(sizeof(unsigned));
+    const size_t o_info = take(sizeof(StructInfo) * (size_t)std::max<int64_t>(S, 1));
+    const size_t o_struct = take(4 * (size_t)N);
+    const size_t o_type = take(4 * (size_t)N);
+    const size_t o_bin = take(4 * (size_t)N);
+    const size_t o_wrap = take(12 * (size_t)N);
+    const size_t o_sorted = take(4 * (size_t)N);
+    const size_t bins = (size_t)(2 * N + 8 * S + 8);
+    const size_t o_bstart = take(4 * bins);
+    const size_t o_bcursor = take(4 * bins);
+    size_t o_cbuf = 0, o_pbuf = 0, o_rbuf = 0;
+    if (plan->average == MDSOAP_AVERAGE_INNER) o_cbuf = take(8 * (size_t)N * (size_t)plan->csize);
+    if (plan->average == MDSOAP_AVERAGE_OUTER) o_pbuf = take(8 * (size_t)N * (size_t)plan->features);
+    if (plan->tab.r_global) o_rbuf = take(8 * (size_t)N * (size_t)plan->csize);
+    if (off > MDSOAP_NOALLOC_SCRATCH_BYTES)
+        return fail(MDSOAP_CAPACITY_OVERFLOW,
+                    "batch needs " + std::to_string(off) + " bytes of scratch; the no-allocation entry point holds " +
+                        std::to_string((size_t)MDSOAP_NOALLOC_SCRATCH_BYTES) + " bytes (split the batch)");
+    if (N > 2147483647LL) return fail(MDSOAP_INVALID_ARGUMENT, "neighbor atom index exceeds int32 range");
+    try {
+        int count = 0;
+        if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+            cudaGetLastError();
+            raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device unavailable");
+        }
+        check(cudaSetDevice(device), "cudaSetDevice");
+        unsigned char* base = noalloc_base(device);
+        int optin = 0;
+        check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device), "smem attribute");
+        if (plan->center_smem > (size_t)optin || plan->structure_smem > (size_t)optin)
+            raise(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
+        check(cudaFuncSetAttribute(plan->variant->center_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+              "center kernel smem");
+        check(cudaFuncSetAttribute(plan->variant->structure_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+              "structure kernel smem");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        // Plan tables (the array keeps the previous call's contents: refresh them).
+        check(cudaMemcpyAsync(base + o_items, plan->items.data(), sizeof(RadialItem) * plan->items.size(),
+                              cudaMemcpyHostToDevice, st),
+              "upload radial items");
+        check(cudaMemcpyAsync(base + o_betas, plan->betas.data(), 8 * plan->betas.size(), cudaMemcpyHostToDevice, st),
+              "upload betas");
+        check(cudaMemcpyAsync(base + o_species, plan->species.data(), 4 * plan->species.size(),
+                              cudaMemcpyHostToDevice, st),
+              "upload species");
+        unsigned* error = reinterpret_cast<unsigned*>(base + o_error);
+        check(cudaMemsetAsync(error, 0, sizeof(unsigned), st), "clear error word");
+        BinView v;
+        v.info = reinterpret_cast<StructInfo*>(base + o_info);
+        v.struct_of = reinterpret_cast<int32_t*>(base + o_struct);
+        v.type = reinterpret_cast<int32_t*>(base + o_type);
+        v.bin_of = reinterpret_cast<int32_t*>(base + o_bin);
+        v.wrap = reinterpret_cast<int32_t*>(base + o_wrap);
+        v.sorted = reinterpret_cast<int32_t*>(base + o_sorted);
+        v.bin_start = reinterpret_cast<int32_t*>(base + o_bstart);
+        v.bin_cursor = reinterpret_cast<int32_t*>(base + o_bcursor);
+        v.error = error;
+        DeviceBatch db{batch->numbers, batch->positions, batch->cells, batch->pbc, batch->offsets, S, N};
+        if (S > 0) {
+            bin_structures_kernel<<<(unsigned)S, 256, 0, st>>>(db, v, plan->cutoff,
+                                                               reinterpret_cast<int32_t*>(base + o_species),
+                                                               plan->n_species);
+            check(cudaGetLastError(), "bin kernel launch");
+        }
+        SoapPointers p{};
+        p.positions = db.positions;
+        p.bins = v;
+        p.items = reinterpret_cast<RadialItem*>(base + o_items);
+        p.betas = reinterpret_cast<double*>(base + o_betas);
+        p.out = out;
+        p.cbuf = o_cbuf ? reinterpret_cast<double*>(base + o_cbuf) : nullptr;
+        p.pbuf = o_pbuf ? reinterpret_cast<double*>(base + o_pbuf) : nullptr;
+        p.rbuf = o_rbuf ? reinterpret_cast<double*>(base + o_rbuf) : nullptr;
+        p.out_row_begin = 0;
+        p.center_begin = 0;
+        p.center_end = N;
+        if (N > 0) {
+            const int64_t grid = plan->variant->pair ? N : (N + kWarps - 1) / kWarps;
+            plan->variant->center(dim3((unsigned)grid), plan->center_smem, st, plan->tab, p);
+            check(cudaGetLastError(), "centre kernel launch");
+        }
+        if (plan->average != MDSOAP_AVERAGE_OFF && S > 0) {
+            plan->variant->structure(dim3((unsigned)S), plan->structure_smem, st, plan->tab, db.offsets, 0, S, p.cbuf,
+                                     p.pbuf, out, 0);
+            check(cudaGetLastError(), "structure kernel launch");
+        }
+        unsigned bits = 0;
+        check(cudaMemcpyAsync(&bits, error, sizeof(unsigned), cudaMemcpyDeviceToHost, st), "read error word");
+        check(cudaStreamSynchronize(st), "stream sync");
+        if (bits)
+            return fail(bits & (kErrUnknownSpecies | kErrMixedPbc | kErrSingularCell) ? MDSOAP_INVALID_ARGUMENT
+                                                                                      : MDSOAP_INTERNAL,
+                        device_error_text(bits));
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    }
+}
+
 int mdsoap_plan_set_timing(mdsoap_plan* plan, int32_t enable) {
     if (!plan) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
     plan->timing = enable != 0;
