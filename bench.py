@@ -47,8 +47,8 @@ L2_FLUSH_BYTES = 256 << 20
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=5)
-    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--config", type=int, default=2)
     p.add_argument("--structures", type=int, default=None, help="structures per rank (default: the config's)")
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
@@ -64,11 +64,70 @@ def dist_env():
     return rank, world, local
 
 
-def config_record(args, batch, cfg, world):
+def rank_seed(config: int, rank: int) -> int:
+    """Each rank owns its own seeded batch (weak scaling, no exchange)."""
+    from mdescriptor_b200 import workloads
+
+    return workloads.SEED_BASE + config + 1000 * rank
+
+
+class Ranks:
+    """One process per GPU, launched by torchrun (RANK/WORLD_SIZE/LOCAL_RANK).
+
+    The only collectives are a barrier around the timed regions and the
+    max / sum reductions of the per-rank timings and unit counts -- the SOAP
+    path itself shards by structure with no exchange.  ``backend`` is "nccl"
+    on GPUs and "gloo" for the CPU tests of this logic.
+    """
+
+    def __init__(self, backend: str = "nccl", device=None, timeout_s: float = 120.0):
+        self.rank, self.world, self.local = dist_env()
+        self.device = device
+        self.group = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            kwargs = {"device_id": device} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
+            self.group = dist
+
+    def barrier(self):
+        if self.group is not None:
+            self.group.barrier()
+
+    def _reduce(self, x: float, op) -> float:
+        if self.group is None:
+            return float(x)
+        import torch
+
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        self.group.all_reduce(t, op=op)
+        return float(t.item())
+
+    def max(self, x: float) -> float:
+        return self._reduce(x, None if self.group is None else self.group.ReduceOp.MAX)
+
+    def sum(self, x: float) -> float:
+        return self._reduce(x, None if self.group is None else self.group.ReduceOp.SUM)
+
+    def close(self):
+        if self.group is not None:
+            self.group.destroy_process_group()
+            self.group = None
+
+
+def job_throughput(units_all_ranks: float, steps: int, max_ms: float) -> float:
+    """Whole-job units/s: every rank's units over the slowest rank's time."""
+    return units_all_ranks * steps / (max_ms * 1e-3)
+
+
+def config_record(args, cfg, structures, atoms, world, parallelism=None):
     return {
         "workload": f"{cfg.name} (BASELINE config {args.config})",
-        "structures_per_rank": batch.structures,
-        "atoms_per_rank": batch.atoms,
+        "structures_per_rank": structures,
+        "atoms_per_rank": atoms,
         "species": list(cfg.species),
         "r_cut": cfg.r_cut,
         "n_max": cfg.n_max,
@@ -76,7 +135,7 @@ def config_record(args, batch, cfg, world):
         "sigma": cfg.sigma,
         "average": cfg.average,
         "output_dtype": cfg.dtype,
-        "parallelism": f"structure-sharded x{world} (no collective)",
+        "parallelism": parallelism or f"structure-sharded x{world} (no collective)",
         "l2": "flushed between steps (256 MiB device write, outside the timed events)",
     }
 
@@ -90,7 +149,12 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons every 200 ms, timestamped on arrival.
+
+    Started before the warm-up (nvidia-smi needs a moment to print its first
+    sample); only samples that arrive inside a window marked with
+    ``begin()``/``end()`` -- the timed regions -- enter the summary.
+    """
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -100,10 +164,12 @@ class ClockSampler:
     def __init__(self, device: int):
         self.device = device
         self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, str]] = []
+        self.windows: list[list[float]] = []
         self.thread = None
+        self.first = threading.Event()
 
-    def start(self):
+    def start(self, wait_s: float = 5.0):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -113,10 +179,19 @@ class ClockSampler:
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        self.first.wait(wait_s)
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.samples.append((time.monotonic(), line.strip()))
+            self.first.set()
+
+    def begin(self):
+        self.windows.append([time.monotonic(), float("inf")])
+
+    def end(self):
+        if self.windows:
+            self.windows[-1][1] = time.monotonic()
 
     def stop(self):
         if self.proc is None:
@@ -128,23 +203,34 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, sm_max, reasons = [], [], set()
-        for line in self.lines:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                sm_max.append(float(parts[1]))
-            except ValueError:
-                continue
-            for name, flag in zip(self.NAMES, parts[3:7]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(sm_max), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return summarize_clocks(self.samples, self.windows, self.NAMES)
+
+
+def summarize_clocks(samples, windows, names=ClockSampler.NAMES):
+    """Median SM clock, max clock and active reasons over samples inside the windows."""
+    sm, sm_max, power, reasons = [], [], [], set()
+    for t, line in samples:
+        if not any(a <= t <= b for a, b in windows):
+            continue
+        parts = [x.strip() for x in line.split(",")]
+        if len(parts) < 7:
+            continue
+        try:
+            sm.append(float(parts[0]))
+            sm_max.append(float(parts[1]))
+        except ValueError:
+            continue
+        try:
+            power.append(float(parts[2]))
+        except ValueError:
+            pass
+        for name, flag in zip(names, parts[3:7]):
+            if flag.lower() == "active":
+                reasons.add(name)
+    if not sm:
+        return None
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(sm_max), "reasons": sorted(reasons),
+            "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
 def algorithmic_flops_per_atom(cfg, edges_per_atom):
@@ -225,16 +311,18 @@ def run_reference(args):
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = batch.atoms * args.steps / total
+    # The GPU arm's config (same workload and shapes); the CPU arm times a
+    # bounded sample of it each step, described in cpu_baseline.sample.
+    full = workloads.make(args.config, args.structures, seed=rank_seed(args.config, 0))
+    ours_config = config_record(args, cfg, full.structures, full.atoms, args.gpus)
     sample = (f"{batch.structures} structures x {batch.atoms // max(batch.structures, 1)} atoms of config "
               f"{args.config} per step")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic (seeded, config shapes)",
-        "config": {"workload": f"{cfg.name} (BASELINE config {args.config})", "species": list(cfg.species),
-                   "r_cut": cfg.r_cut, "n_max": cfg.n_max, "l_max": cfg.l_max, "average": cfg.average,
-                   "parallelism": f"OpenMP over structures, {threads} host threads"},
+        "data": "synthetic (seeded generators with the config's shapes; no public dataset)",
+        "config": ours_config,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -246,44 +334,31 @@ def main():
     if args.impl == "reference":
         run_reference(args)
         return
-    rank, world, local = dist_env()
     import torch
 
+    _, _, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    group = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-        group = dist
-
-    def barrier():
-        if group is not None:
-            group.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if group is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        group.all_reduce(t, op=group.ReduceOp.MAX)
-        return float(t.item())
+    ranks = Ranks("nccl", dev)
+    rank, world = ranks.rank, ranks.world
 
     from mdescriptor_b200 import workloads
     from mdescriptor_b200.basis import basis_gto
     from mdescriptor_b200.soap import Soap, device_view, neighbor_graph, probe_fp64_fma
 
     cfg = workloads.CONFIGS[args.config]
-    seed = workloads.SEED_BASE + args.config + 1000 * rank
-    batch = workloads.make(args.config, args.structures, seed=seed)
+    batch = workloads.make(args.config, args.structures, seed=rank_seed(args.config, rank))
     alphas, betas = basis_gto(cfg.r_cut, cfg.n_max, cfg.l_max)
     soap = Soap(cfg.species, r_cut=cfg.r_cut, n_max=cfg.n_max, l_max=cfg.l_max, sigma=cfg.sigma,
                 average=cfg.average, dtype=cfg.dtype, alphas=alphas, betas=betas)
     rows = soap.rows(batch)
     out_dtype = torch.float32 if cfg.dtype == "float32" else torch.float64
     elem = 4 if cfg.dtype == "float32" else 8
+    atoms_all = ranks.sum(batch.atoms)
+    rows_all = ranks.sum(rows)
+
+    sampler = ClockSampler(local)
+    sampler.start()
 
     # ---- device-resident value
     names = ("numbers", "positions", "cells", "pbc", "offsets")
@@ -294,14 +369,15 @@ def main():
     stream = torch.cuda.current_stream(dev)
     soap.set_timing(True)
     for _ in range(args.warmup):
+        flush.fill_(1)
         soap.compute_device(view, out.data_ptr(), local, stream.cuda_stream)
     soap.check(local, stream.cuda_stream)
-    sampler = ClockSampler(local)
-    sampler.start()
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     center_ms, bin_ms = [], []
-    barrier()
+    ranks.barrier()
     torch.cuda.synchronize(dev)
+    launches0 = soap.launch_count()
+    sampler.begin()
     for start, stop in events:
         flush.fill_(1)
         start.record(stream)
@@ -311,14 +387,13 @@ def main():
         bin_ms.append(b)
         center_ms.append(c)
     torch.cuda.synchronize(dev)
-    barrier()
-    clocks = sampler.stop()
+    sampler.end()
+    ranks.barrier()
     soap.check(local, stream.cuda_stream)
-    total_ms = sum(s.elapsed_time(e) for s, e in events)
-    total_ms = max_over_ranks(total_ms)
-    atoms_all = batch.atoms * world
-    value = atoms_all * args.steps / (total_ms * 1e-3)
-    gpu_launches = 2 * args.steps + (args.steps if cfg.average != "off" else 0)
+    total_ms = ranks.max(sum(s.elapsed_time(e) for s, e in events))
+    value = job_throughput(atoms_all, args.steps, total_ms)
+    gpu_launches = soap.launch_count() - launches0
+    launches_per_step = gpu_launches / args.steps
 
     # ---- end to end through the public host API (pinned host buffers)
     e2e = None
@@ -331,19 +406,27 @@ def main():
             pinned[k] = t.numpy()
         pbatch = workloads.Batch(*(pinned[k] for k in names))
         host_out = torch.empty((rows, soap.feature_count), dtype=out_dtype, pin_memory=True).numpy()
-        soap.compute(pbatch, devices=[local], out=host_out)
-        barrier()
+        for _ in range(max(1, args.warmup)):
+            soap.compute(pbatch, devices=[local], out=host_out)
+        ranks.barrier()
         torch.cuda.synchronize(dev)
+        launches1 = soap.launch_count()
+        sampler.begin()
         t0 = time.perf_counter()
         for _ in range(args.steps):
             soap.compute(pbatch, devices=[local], out=host_out)
         torch.cuda.synchronize(dev)
-        barrier()
-        e2e_s = max_over_ranks(time.perf_counter() - t0)
-        h2d = int(sum(pinned[k].nbytes for k in names))
-        e2e = {"value": atoms_all * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-               "d2h_bytes_per_step": rows * soap.feature_count * elem * world,
-               "path": "Soap.compute (C ABI mdsoap_compute): pinned host in/out, H2D + kernels + D2H per step"}
+        e2e_s = time.perf_counter() - t0
+        sampler.end()
+        ranks.barrier()
+        e2e_s = ranks.max(e2e_s)
+        h2d = ranks.sum(sum(pinned[k].nbytes for k in names))
+        e2e = {"value": job_throughput(atoms_all, args.steps, e2e_s * 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(rows_all * soap.feature_count * elem),
+               "path": "Soap.compute (C ABI mdsoap_compute): pinned host in/out, H2D + kernels + D2H per step; "
+                       "host clock around synchronous calls, synchronize + barrier on both sides, max over ranks"}
+        e2e["gpu_launches"] = soap.launch_count() - launches1
+    clocks = sampler.stop()
 
     if rank == 0:
         # measured neighbour count (edges per atom incl. self) on a sample
@@ -357,7 +440,8 @@ def main():
         traffic = None
         tf = ROOT / "profiles" / f"traffic_config{args.config}.json"
         if tf.is_file():
-            traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+            per_atom = json.loads(tf.read_text()).get("dram_bytes_per_atom")
+            traffic = None if per_atom is None else per_atom * batch.atoms
         fp64_peak = probe_fp64_fma(local)
         flops = algorithmic_flops_per_atom(cfg, edges) * batch.atoms
         achieved_tf = flops / center_avg_s / 1e12
@@ -366,9 +450,10 @@ def main():
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (seeded generators with the config's shapes; no public dataset)",
-            "config": config_record(args, batch, cfg, world),
+            "config": config_record(args, cfg, batch.structures, batch.atoms, world),
             "e2e": e2e,
             "gpu_launches": gpu_launches,
+            "gpu_launches_per_step": launches_per_step,
             "kernel_ms": {"bin": statistics.mean(bin_ms), "center": statistics.mean(center_ms)},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved_gbs / hbm_peak, "traffic": traffic,
@@ -384,8 +469,7 @@ def main():
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, args)
         print(json.dumps(line), flush=True)
-    if group is not None:
-        group.destroy_process_group()
+    ranks.close()
 
 
 if __name__ == "__main__":

@@ -184,6 +184,11 @@ int mdsoap_plan_set_timing(mdsoap_plan* plan, int32_t enable);
 int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, double* center_ms,
                             double* structure_ms);
 
+/* Number of kernels the plan has launched so far, over all devices and entry
+ * points (measurement support; no counterpart in the reference).  A
+ * benchmark reads it before and after its timed region to count its launches. */
+int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count);
+
 /* Measured fp64 FMA throughput of `device` in TFLOP/s (2 flops per FMA) from a
  * register-resident FMA chain kernel over every SM (measurement support; no
  * counterpart in the reference).  Used as the roofline denominator of the

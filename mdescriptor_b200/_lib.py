@@ -90,6 +90,8 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_plan_set_timing.restype = ctypes.c_int
     lib.mdsoap_plan_last_timing.argtypes = [_P, ctypes.c_int32, _P, _P, _P]
     lib.mdsoap_plan_last_timing.restype = ctypes.c_int
+    lib.mdsoap_plan_launch_count.argtypes = [_P, _P]
+    lib.mdsoap_plan_launch_count.restype = ctypes.c_int
     lib.mdsoap_probe_fp64_fma.argtypes = [ctypes.c_int32, _P]
     lib.mdsoap_probe_fp64_fma.restype = ctypes.c_int
     lib.mdsoap_graph_build.argtypes = [ctypes.POINTER(BatchView), ctypes.c_double, ctypes.c_int32, ctypes.POINTER(_P)]
@@ -120,6 +122,7 @@ EXPORTED = (
     "mdsoap_compute_device_noalloc",
     "mdsoap_plan_set_timing",
     "mdsoap_plan_last_timing",
+    "mdsoap_plan_launch_count",
     "mdsoap_probe_fp64_fma",
     "mdsoap_graph_build",
     "mdsoap_graph_pairs",

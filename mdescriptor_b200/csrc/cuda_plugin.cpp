@@ -25,6 +25,16 @@ namespace py = pybind11;
 
 namespace {
 
+// Element symbols by atomic number (1..118), for species-keyed option maps.
+constexpr const char* kElementSymbols[118] = {
+    "H",  "He", "Li", "Be", "B",  "C",  "N",  "O",  "F",  "Ne", "Na", "Mg", "Al", "Si", "P",  "S",  "Cl", "Ar",
+    "K",  "Ca", "Sc", "Ti", "V",  "Cr", "Mn", "Fe", "Co", "Ni", "Cu", "Zn", "Ga", "Ge", "As", "Se", "Br", "Kr",
+    "Rb", "Sr", "Y",  "Zr", "Nb", "Mo", "Tc", "Ru", "Rh", "Pd", "Ag", "Cd", "In", "Sn", "Sb", "Te", "I",  "Xe",
+    "Cs", "Ba", "La", "Ce", "Pr", "Nd", "Pm", "Sm", "Eu", "Gd", "Tb", "Dy", "Ho", "Er", "Tm", "Yb", "Lu", "Hf",
+    "Ta", "W",  "Re", "Os", "Ir", "Pt", "Au", "Hg", "Tl", "Pb", "Bi", "Po", "At", "Rn", "Fr", "Ra", "Ac", "Th",
+    "Pa", "U",  "Np", "Pu", "Am", "Cm", "Bk", "Cf", "Es", "Fm", "Md", "No", "Lr", "Rf", "Db", "Sg", "Bh", "Hs",
+    "Mt", "Ds", "Rg", "Cn", "Nh", "Fl", "Mc", "Lv", "Ts", "Og"};
+
 struct CudaCancelledError : std::runtime_error {
     using std::runtime_error::runtime_error;
 };
@@ -137,14 +147,24 @@ public:
         const py::dict weighting = child_dict(options_, "weighting");
         if (option(weighting, "function", std::string()) != "" || weighting.contains("w0"))
             throw std::invalid_argument("unsupported CUDA SOAP weighting");
+        // A species' weight is looked up as an int key, then its decimal
+        // string (the adapter's options have been through JSON), then its
+        // element symbol; species without an entry weigh 1.0
+        // (cpp/cuda/src/extended_descriptors_common.cuh:257-294).
         weights_.assign(species_.size(), 1.0);
         if (compression.contains("species_weighting") && !compression["species_weighting"].is_none()) {
             const py::dict map = py::cast<py::dict>(compression["species_weighting"]);
             for (size_t i = 0; i < species_.size(); ++i) {
-                const py::int_ key(species_[i]);
-                if (!map.contains(key))
-                    throw std::invalid_argument("species_weighting must contain exactly the configured species");
-                weights_[i] = py::cast<double>(map[key]);
+                const py::int_ number(species_[i]);
+                const py::str text(std::to_string(species_[i]));
+                if (map.contains(number)) {
+                    weights_[i] = py::cast<double>(map[number]);
+                } else if (map.contains(text)) {
+                    weights_[i] = py::cast<double>(map[text]);
+                } else if (species_[i] >= 1 && species_[i] <= 118) {
+                    const py::str symbol(kElementSymbols[species_[i] - 1]);
+                    if (map.contains(symbol)) weights_[i] = py::cast<double>(map[symbol]);
+                }
             }
         }
         const py::dict output = child_dict(options_, "output");

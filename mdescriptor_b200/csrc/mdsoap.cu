@@ -334,6 +334,7 @@ struct mdsoap_plan {
     int64_t csize = 0;
     int64_t features = 0;
     bool timing = false;
+    std::atomic<int64_t> launches{0};  // kernels this plan has launched, all devices
     std::mutex devices_mutex;
     std::vector<std::unique_ptr<DeviceState>> devices;
 
@@ -401,6 +402,7 @@ void mdsoap_plan::bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream
     bin_structures_kernel<<<(unsigned)b.structures, 256, 0, stream>>>(b, st.work.bins(error), cutoff,
                                                                        st.species.as<int32_t>(), n_species);
     check(cudaGetLastError(), "bin kernel launch");
+    launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 // Centres [a0, a1) = atoms of structures [s0, s1); rows go to `out` starting
@@ -433,12 +435,14 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         const int64_t grid = variant->pair ? centers : (centers + kWarps - 1) / kWarps;
         variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
         check(cudaGetLastError(), "centre kernel launch");
+        launches.fetch_add(1, std::memory_order_relaxed);
     }
     if (after_center) check(cudaEventRecord(after_center, stream), "timing event");
     if (average != MDSOAP_AVERAGE_OFF && s1 > s0) {
         variant->structure(dim3((unsigned)(s1 - s0)), structure_smem, stream, tab, b.offsets, s0, s1, p.cbuf, p.pbuf,
                            out, s0);
         check(cudaGetLastError(), "structure kernel launch");
+        launches.fetch_add(1, std::memory_order_relaxed);
     }
 }
 
@@ -1059,6 +1063,7 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
                                                                reinterpret_cast<int32_t*>(base + o_species),
                                                                plan->n_species);
             check(cudaGetLastError(), "bin kernel launch");
+            plan->launches.fetch_add(1, std::memory_order_relaxed);
         }
         SoapPointers p{};
         p.positions = db.positions;
@@ -1076,11 +1081,13 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
             const int64_t grid = plan->variant->pair ? N : (N + kWarps - 1) / kWarps;
             plan->variant->center(dim3((unsigned)grid), plan->center_smem, st, plan->tab, p);
             check(cudaGetLastError(), "centre kernel launch");
+            plan->launches.fetch_add(1, std::memory_order_relaxed);
         }
         if (plan->average != MDSOAP_AVERAGE_OFF && S > 0) {
             plan->variant->structure(dim3((unsigned)S), plan->structure_smem, st, plan->tab, db.offsets, 0, S, p.cbuf,
                                      p.pbuf, out, 0);
             check(cudaGetLastError(), "structure kernel launch");
+            plan->launches.fetch_add(1, std::memory_order_relaxed);
         }
         unsigned bits = 0;
         check(cudaMemcpyAsync(&bits, error, sizeof(unsigned), cudaMemcpyDeviceToHost, st), "read error word");
@@ -1120,6 +1127,12 @@ int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, d
     } catch (const Failure& f) {
         return fail(f.status, f.message);
     }
+}
+
+int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count) {
+    if (!plan || !count) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    *count = plan->launches.load(std::memory_order_relaxed);
+    return MDSOAP_OK;
 }
 
 int mdsoap_probe_fp64_fma(int32_t device, double* tflops) {

@@ -129,6 +129,12 @@ class Soap:
     def set_timing(self, enable: bool) -> None:
         raise_for(lib.mdsoap_plan_set_timing(self._plan, 1 if enable else 0))
 
+    def launch_count(self) -> int:
+        """Kernels this plan has launched so far (all devices, all entry points)."""
+        value = ctypes.c_int64()
+        raise_for(lib.mdsoap_plan_launch_count(self._plan, ctypes.byref(value)))
+        return int(value.value)
+
     def last_timing(self, device: int = 0) -> tuple[float, float, float]:
         """(bin_ms, center_ms, structure_ms) of the last timed ``compute_device`` call."""
         values = (ctypes.c_double * 3)()

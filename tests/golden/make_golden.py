@@ -11,6 +11,12 @@ Outputs
   external_{input,expected_output}.npz: DScribe 2.1.2 static golden) and the
   NeighborList golden (tests/golden/neighborlist), copied verbatim as data
   with their manifests' parameters and tolerances.
+* ``adapter_options.json``: the exact options MDescriptor's unchanged adapter
+  hands to ``mdescriptor._cuda.create_backend`` (captured by replacing
+  ``mdescriptor._runtime.create_cuda_backend`` with a recorder) for two SOAP
+  configurations, so the GPU plugin test can replay them where MDescriptor is
+  not installed; ``adapter_expected.npz`` holds the batch they run on and the
+  reference's CPU result (values, row_offsets) for each.
 * ``config_goldens.npz`` + ``config_goldens.json``: for seeded slices of the
   five benchmark configs, the reference's features computed through its
   unchanged public API (``mdescriptor.descriptors.SOAP(..., device="cpu")``),
@@ -69,6 +75,77 @@ def import_reference(root: Path):
     return SOAP, StructureBatch, OutputOptions, ExecutionOptions, _basis_gto
 
 
+def _jsonable(value):
+    if isinstance(value, np.ndarray):
+        return {"__ndarray__": value.tolist(), "dtype": str(value.dtype), "shape": list(value.shape)}
+    if isinstance(value, dict):
+        return {str(k): _jsonable(v) for k, v in value.items()}
+    if isinstance(value, (list, tuple)):
+        return [_jsonable(v) for v in value]
+    return value
+
+
+def adapter_batch():
+    """Two periodic config-1 boxes and the first box again as an isolated cluster."""
+    base = workloads.config1(structures=2)
+    first = base.slice(0, 1)
+    return workloads.Batch(
+        np.concatenate([base.numbers, first.numbers]),
+        np.concatenate([base.positions, first.positions]),
+        np.concatenate([base.cells, first.cells]),
+        np.concatenate([base.pbc, np.zeros_like(first.pbc)]),
+        np.concatenate([base.offsets, base.offsets[-1] + first.offsets[1:]]),
+    )
+
+
+ADAPTER_KWARGS = [
+    dict(species=[1, 8], r_cut=4.5, n_max=4, l_max=3, average="off"),
+    dict(species=[8, 1], r_cut=4.0, n_max=3, l_max=4, sigma=0.8, average="inner",
+         compression={"mode": "off", "species_weighting": {1: 0.5, 8: 2.0}}),
+]
+
+
+def capture_adapter_options(SOAP, StructureBatch, OutputOptions, ExecutionOptions):
+    """Options the adapter passes to the CUDA plugin factory for ADAPTER_KWARGS,
+    plus the reference's CPU features for the same options on adapter_batch()."""
+    import mdescriptor._runtime as runtime
+
+    captured = []
+
+    class Recorder:
+        feature_count = None
+
+        def __init__(self, name, options):
+            captured.append({"name": name, "options": options})
+
+        def compute(self, batch, control=None):
+            raise ImportError("recorder")
+
+    batch = adapter_batch()
+    sb = StructureBatch(batch.numbers, batch.positions, batch.cells, batch.pbc, batch.offsets,
+                        tuple(f"s{i}" for i in range(batch.structures)))
+    original = runtime.create_cuda_backend
+    runtime.create_cuda_backend = lambda name, options: Recorder(name, options)
+    cases = []
+    try:
+        for kw in ADAPTER_KWARGS:
+            soap = SOAP(**kw, output=OutputOptions(dtype="float32"), execution=ExecutionOptions(device="cuda"))
+            try:
+                soap.compute(sb)
+            except Exception:  # the recorder stops the computation
+                pass
+            cases.append({"kwargs": _jsonable(kw), "name": captured[-1]["name"],
+                          "options": _jsonable(captured[-1]["options"])})
+    finally:
+        runtime.create_cuda_backend = original
+    arrays = {f"input/{k}": getattr(batch, k) for k in ("numbers", "positions", "cells", "pbc", "offsets")}
+    for index, kw in enumerate(ADAPTER_KWARGS):
+        result = SOAP(**kw, output=OutputOptions(dtype="float32"), execution=ExecutionOptions(device="cpu")).compute(sb)
+        arrays[f"case{index}/values"] = np.asarray(result.values)
+        arrays[f"case{index}/row_offsets"] = np.asarray(result.row_offsets)
+    return cases, arrays
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference-root", default="/root/reference")
@@ -78,6 +155,10 @@ def main() -> None:
     from oracle import RefLib
 
     ref = RefLib()
+
+    cases, adapter_arrays = capture_adapter_options(SOAP, StructureBatch, OutputOptions, ExecutionOptions)
+    (HERE / "adapter_options.json").write_text(json.dumps(cases, indent=1) + "\n")
+    np.savez_compressed(HERE / "adapter_expected.npz", **adapter_arrays)
 
     # 1. Reference goldens, copied as data.
     arrays, meta = {}, {}

@@ -1,0 +1,95 @@
+"""bench.py's multi-rank logic on CPU: world_size-2 ``gloo`` ranks.
+
+The SOAP path shards by structure with no data exchange, so the only
+collectives are the barrier and the max / sum reductions around the timed
+regions; these tests run exactly those helpers on two processes, plus the
+reference arm's "rank 0 alone works" rule.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, queue):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    ranks = bench.Ranks("gloo", None, timeout_s=30)
+    try:
+        ranks.barrier()
+        local_ms = 10.0 * (rank + 1)        # rank 1 is the slow one
+        local_atoms = 100 + 28 * rank       # ragged shards
+        total_ms = ranks.max(local_ms)
+        atoms_all = ranks.sum(local_atoms)
+        value = bench.job_throughput(atoms_all, 4, total_ms)
+        queue.put((rank, ranks.world, total_ms, atoms_all, value, bench.rank_seed(2, rank)))
+    finally:
+        ranks.close()
+
+
+def test_two_gloo_ranks_take_max_time_and_sum_units():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(queue.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    (r0, w0, t0, a0, v0, s0), (r1, w1, t1, a1, v1, s1) = results
+    assert (r0, r1, w0, w1) == (0, 1, 2, 2)
+    assert t0 == t1 == 20.0                       # max over ranks
+    assert a0 == a1 == 228                        # units of all ranks
+    assert v0 == v1 == pytest.approx(228 * 4 / 0.020)
+    assert s0 != s1                               # each rank owns its own batch
+
+
+def test_single_process_ranks_are_identity():
+    for key in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+        os.environ.pop(key, None)
+    ranks = bench.Ranks("gloo")
+    assert (ranks.rank, ranks.world, ranks.group) == (0, 1, None)
+    assert ranks.max(3.5) == 3.5 and ranks.sum(7) == 7.0
+    ranks.barrier()
+    ranks.close()
+
+
+def test_reference_arm_runs_on_rank_zero_only():
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2"],
+                         env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == ""
+
+
+def test_clock_summary_keeps_only_samples_inside_timed_windows():
+    samples = [(0.5, "600, 1965, 100.0, Not Active, Not Active, Not Active, Not Active"),
+               (1.5, "1900, 1965, 900.0, Not Active, Not Active, Not Active, Active"),
+               (1.7, "1800, 1965, 950.0, Not Active, Not Active, Not Active, Not Active"),
+               (3.0, "500, 1965, 90.0, Active, Not Active, Not Active, Not Active")]
+    summary = bench.summarize_clocks(samples, [[1.0, 2.0]])
+    assert summary["samples"] == 2
+    assert summary["sm_mhz"] == 1850.0 and summary["sm_max_mhz"] == 1965.0
+    assert summary["reasons"] == ["sw_power_cap"]
+    assert bench.summarize_clocks(samples, [[10.0, 11.0]]) is None
