@@ -142,7 +142,8 @@ def capture_adapter_options(SOAP, StructureBatch, OutputOptions, ExecutionOption
     for index, kw in enumerate(ADAPTER_KWARGS):
         result = SOAP(**kw, output=OutputOptions(dtype="float32"), execution=ExecutionOptions(device="cpu")).compute(sb)
         arrays[f"case{index}/values"] = np.asarray(result.values)
-        arrays[f"case{index}/row_offsets"] = np.asarray(result.row_offsets)
+        if result.row_offsets is not None:  # structure-level results have none
+            arrays[f"case{index}/row_offsets"] = np.asarray(result.row_offsets)
     return cases, arrays
 
 

@@ -200,3 +200,11 @@ def test_reference_public_api_reaches_the_plugin(monkeypatch):
         soap.compute(sb)
     assert info.value.code == "device_unavailable"
     assert Path(sys.modules["mdescriptor._cuda"].__file__).parent.resolve() == PLUGIN_DIR.resolve()
+
+
+def test_golden_archives_load_without_pickle():
+    golden = Path(__file__).resolve().parent / "golden"
+    for path in sorted(golden.glob("*.npz")):
+        with np.load(path) as archive:
+            for key in archive.files:
+                assert archive[key].dtype != object, (path.name, key)
