@@ -440,8 +440,10 @@ def main():
         traffic = None
         tf = ROOT / "profiles" / f"traffic_config{args.config}.json"
         if tf.is_file():
-            per_atom = json.loads(tf.read_text()).get("dram_bytes_per_atom")
-            traffic = None if per_atom is None else per_atom * batch.atoms
+            # one-pass ncu capture of the full-size launch (dram read + write);
+            # other sizes scale it by atoms (the rows are the traffic)
+            record = json.loads(tf.read_text())
+            traffic = record["dram_bytes_per_launch"] * batch.atoms / record["atoms"]
         fp64_peak = probe_fp64_fma(local)
         flops = algorithmic_flops_per_atom(cfg, edges) * batch.atoms
         achieved_tf = flops / center_avg_s / 1e12
