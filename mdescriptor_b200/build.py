@@ -52,8 +52,7 @@ def _stale(target: Path, sources: list[Path]) -> bool:
 
 
 def build_library(force: bool = False, verbose: bool = False) -> Path:
-    sources = [CSRC / "mdsoap.cu", CSRC / "soap.cuh", CSRC / "neighbors.cuh", CSRC / "common.cuh",
-               INCLUDE / "mdsoap.h"]
+    sources = [CSRC / "mdsoap.cu", *sorted(CSRC.glob("*.cuh")), INCLUDE / "mdsoap.h"]
     if force or _stale(LIB, sources):
         LIB.parent.mkdir(parents=True, exist_ok=True)
         extra = ["-Xptxas", "-v"] if verbose else []

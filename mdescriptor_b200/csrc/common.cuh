@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 namespace mdsoap {
 
@@ -65,6 +66,31 @@ __host__ __device__ inline int64_t bin_capacity(int64_t atoms) { return 2 * atom
 __device__ __forceinline__ int floor_div(int a, int b) {
     const int q = a / b;
     return (a % b != 0 && ((a < 0) != (b < 0))) ? q - 1 : q;
+}
+
+__device__ __forceinline__ int tri(int l, int m) { return l * (l + 1) / 2 + m; }
+
+// Compile-time loop: f(std::integral_constant<int, I>) for I in [I0, N).
+template <int I0, int N, class F>
+__device__ __forceinline__ void static_for(F&& f) {
+    if constexpr (I0 < N) {
+        f(std::integral_constant<int, I0>{});
+        static_for<I0 + 1, N>(f);
+    }
+}
+
+// Coefficient block layout: [l][t][n][m] with each (t, n) row padded to
+// 2l+2 doubles; block l starts at S n l (l+1).
+__device__ __forceinline__ int cblock(int S, int n, int l) { return S * n * l * (l + 1); }
+
+// Feature offset of (t1, n1, t2, n2, l) in the compression-off layout
+// (t1 <= t2, then l, then n1, then n2 with n2 >= n1 when t1 == t2).
+__device__ __forceinline__ int64_t pair_base(int S, int n, int L, int t1, int t2) {
+    const int64_t T = (int64_t)n * (n + 1) / 2;
+    const int64_t nn = (int64_t)n * n;
+    int64_t base = (int64_t)(L + 1) * (t1 * T + nn * ((int64_t)t1 * (S - 1) - (int64_t)t1 * (t1 - 1) / 2));
+    if (t2 > t1) base += (int64_t)(L + 1) * (T + (int64_t)(t2 - t1 - 1) * nn);
+    return base;
 }
 
 }  // namespace mdsoap

@@ -1,0 +1,201 @@
+// fp64 tensor-core (DMMA) building blocks shared by the centre kernels:
+// coefficient-block layout, mma.sync wrappers, the in-place beta transform and
+// the power spectrum (cpp/src/standalone/soap.cpp:915-926, :997-1012).
+//
+// Coefficient block of one centre: rows r = t n_max + n (species t, radial
+// n), fp64; degree l occupies columns [col_off(l), col_off(l) + kpad(l)),
+// 2l+1 values in the reference's within-l order, zero padded to a multiple of
+// 4 (one mma K step).  The row stride is = 4 (mod 16) doubles, so the
+// fragment reads below -- 4 rows x 4 columns per half warp -- hit 16
+// distinct 8-byte bank pairs.
+#pragma once
+
+#include "common.cuh"
+
+namespace mdsoap {
+
+namespace mma {
+
+
+__host__ __device__ constexpr int kpad(int l) { return (2 * l + 1 + 3) & ~3; }     // columns of degree l
+__host__ __device__ constexpr int blocks8(int l) { return (2 * l + 1 + 7) / 8; }    // 8-row blocks of degree l
+__host__ __device__ constexpr int col_off(int l) {                                  // first column of degree l
+    int o = 0;
+    for (int i = 0; i < l; ++i) o += kpad(i);
+    return o;
+}
+__host__ __device__ constexpr int acc_off(int l) {                                  // first accumulator of degree l
+    int o = 0;
+    for (int i = 0; i < l; ++i) o += 2 * blocks8(i);
+    return o;
+}
+__host__ __device__ constexpr int stride4(int x) { return x + ((4 - x % 16) + 16) % 16; }  // next >= x, = 4 mod 16
+
+// Coefficient-block row stride (doubles) for l_max = L.
+__host__ __device__ constexpr int row_stride(int L) { return stride4(col_off(L + 1)); }
+// Harmonic row stride: block l at l*l, fragment reads reach l*l + 8*blocks8(l) - 1.
+__host__ __device__ constexpr int y_stride(int L) {
+    int need = (L + 1) * (L + 1);
+    for (int l = 0; l <= L; ++l) need = need > l * l + 8 * blocks8(l) ? need : l * l + 8 * blocks8(l);
+    return stride4(need);
+}
+
+__device__ __forceinline__ void dmma8(double& c0, double& c1, double a0, double b0) {
+    asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+        : "+d"(c0), "+d"(c1)
+        : "d"(a0), "d"(b0));
+}
+__device__ __forceinline__ void dmma16(double& c0, double& c1, double& c2, double& c3, double a0, double a1,
+                                       double b0) {
+    asm("mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+        : "+d"(c0), "+d"(c1), "+d"(c2), "+d"(c3)
+        : "d"(a0), "d"(a1), "d"(b0));
+}
+
+// In-place beta transform of every species' block (soap.cpp:915-926).
+template <int LMAX>
+__device__ __forceinline__ void beta_mma(const double* __restrict__ bt, double* __restrict__ reg, int rs, int L,
+                                         int S, int n, int g, int q) {
+    static_for<0, LMAX + 1>([&](auto lc) {
+        constexpr int l = decltype(lc)::value;
+        if (l <= L) {
+            const double a0 = bt[(l * 8 + g) * 8 + q];
+            const double a1 = bt[(l * 8 + g) * 8 + 4 + q];
+            for (int s = 0; s < S; ++s) {
+                double* blk = reg + s * n * rs + col_off(l);
+#pragma unroll
+                for (int mb = 0; mb < (kpad(l) + 7) / 8; ++mb) {
+                    const int m = 8 * mb + g;
+                    const bool mok = m < kpad(l);
+                    const double b0 = (mok && q < n) ? blk[q * rs + m] : 0.0;
+                    const double b1 = (mok && q + 4 < n) ? blk[(q + 4) * rs + m] : 0.0;
+                    double c0 = 0.0, c1 = 0.0;
+                    dmma8(c0, c1, a0, b0);
+                    dmma8(c0, c1, a1, b1);
+                    __syncwarp();
+                    const int mo = 8 * mb + 2 * q;
+                    if (g < n) {
+                        if (mo < kpad(l)) blk[g * rs + mo] = c0;
+                        if (mo + 1 < kpad(l)) blk[g * rs + mo + 1] = c1;
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+    });
+}
+
+// Output placement of the power spectrum (compression off: t1 <= t2, then
+// l, then n1, then n2 with n2 >= n1 when t1 == t2), soap.cpp:997-1012.
+struct FeatureMap {
+    int S, n, L, R;
+    unsigned n_magic;  // floor(2^32 / n) + 1 (0 for n = 1): r / n == umulhi(r, n_magic) for r < 2^16, n <= 32
+    __device__ __forceinline__ int div_n(int r) const {
+        return n_magic ? (int)__umulhi((unsigned)r, n_magic) : r;
+    }
+    // Offset of (r1, r2, l = 0) and the l stride, r1 <= r2.
+    __device__ __forceinline__ int64_t base(int r1, int r2, int& bs) const {
+        const int t1 = div_n(r1), n1 = r1 - t1 * n;
+        const int t2 = div_n(r2), n2 = r2 - t2 * n;
+        bs = t1 == t2 ? n * (n + 1) / 2 : n * n;
+        return pair_base(S, n, L, t1, t2) +
+               (t1 == t2 ? (int64_t)n1 * n - (int64_t)n1 * (n1 - 1) / 2 + (n2 - n1) : (int64_t)n1 * n + n2);
+    }
+};
+
+__device__ __forceinline__ void store_pair(float* p, double a, double b) {
+    *reinterpret_cast<float2*>(p) = make_float2((float)a, (float)b);
+}
+__device__ __forceinline__ void store_pair(double* p, double a, double b) {
+    *reinterpret_cast<double2*>(p) = make_double2(a, b);
+}
+
+// Power spectrum of one centre from its coefficient block: P_l = C_l C_l^T
+// over the rows, in 16 x 8 tiles on or above the diagonal.  Lane (g, q) holds
+// rows r1 = 16i + g (+8) and columns r2 = 8j + 2q (+1); with n_max even the
+// two columns are consecutive features of one pair block, written as one
+// 8-byte (float) or 16-byte (double) store when aligned.  `out` is the
+// centre's feature row; `pref` the factors pi sqrt(8 / (2l + 1)).
+template <int LMAX, class OutT>
+__device__ __forceinline__ void power_mma(const FeatureMap& fm, const double* __restrict__ pref,
+                                          const double* __restrict__ reg, int rs, OutT* __restrict__ out, int g,
+                                          int q) {
+    const int L = fm.L, R = fm.R;
+    const int RB = (R + 15) / 16, CB = (R + 7) / 8;
+    const bool even = (fm.n & 1) == 0;
+    const bool row_aligned = (reinterpret_cast<uintptr_t>(out) % (2 * sizeof(OutT))) == 0;
+    for (int i = 0; i < RB; ++i) {
+        for (int j = 2 * i; j < CB; ++j) {
+            const int r2a = 8 * j + 2 * q, r2b = r2a + 1;
+            const int rb = 8 * j + g;
+            const double* rc = reg + rb * rs + q;
+            const bool okc = rb < R;
+            int64_t f[2][2];
+            int s[2][2];
+            bool v[2][2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r1 = 16 * i + g + 8 * h;
+                v[h][0] = r1 <= r2a && r2a < R;
+                v[h][1] = r1 <= r2b && r2b < R;
+                f[h][0] = f[h][1] = 0;
+                s[h][0] = s[h][1] = 0;
+                if (even) {
+                    // r2a even, so r2a and r2b share species; when both are
+                    // stored the second feature follows the first.
+                    if (v[h][0]) {
+                        f[h][0] = fm.base(r1, r2a, s[h][0]);
+                        f[h][1] = f[h][0] + 1;
+                        s[h][1] = s[h][0];
+                    } else if (v[h][1]) {
+                        f[h][1] = fm.base(r1, r2b, s[h][1]);
+                    }
+                } else {
+                    if (v[h][0]) f[h][0] = fm.base(r1, r2a, s[h][0]);
+                    if (v[h][1]) f[h][1] = fm.base(r1, r2b, s[h][1]);
+                }
+            }
+            const int r1a = 16 * i + g, r1b = r1a + 8;
+            const double* ra = reg + r1a * rs + q;
+            const double* rbp = reg + r1b * rs + q;
+            const bool oka = r1a < R, okb = r1b < R;
+            double c[LMAX + 1][4];
+            static_for<0, LMAX + 1>([&](auto lc) {
+                constexpr int l = decltype(lc)::value;
+                c[l][0] = c[l][1] = c[l][2] = c[l][3] = 0.0;
+                if (l <= L) {
+#pragma unroll
+                    for (int kb = 0; kb < kpad(l); kb += 4) {
+                        const int o = col_off(l) + kb;
+                        const double a0 = oka ? ra[o] : 0.0;
+                        const double a1 = okb ? rbp[o] : 0.0;
+                        const double b0 = okc ? rc[o] : 0.0;
+                        dmma16(c[l][0], c[l][1], c[l][2], c[l][3], a0, a1, b0);
+                    }
+                }
+            });
+#pragma unroll
+            for (int l = 0; l <= LMAX; ++l) {
+                if (l <= L) {
+                    const double p = pref[l];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const double x = p * c[l][2 * h], y = p * c[l][2 * h + 1];
+                        const int64_t fa = f[h][0] + (int64_t)l * s[h][0];
+                        const int64_t fb = f[h][1] + (int64_t)l * s[h][1];
+                        if (even && row_aligned && v[h][0] && (fa & 1) == 0) {
+                            store_pair(out + fa, x, y);
+                        } else {
+                            if (v[h][0]) out[fa] = (OutT)x;
+                            if (v[h][1]) out[fb] = (OutT)y;
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
+}  // namespace mma
+
+}  // namespace mdsoap

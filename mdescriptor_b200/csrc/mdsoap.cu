@@ -5,6 +5,7 @@
 // there, so building a plan touches no GPU (the reference's construction-time
 // contract, tests/test_cuda_backend.py:266-279).
 #include "../../include/mdsoap.h"
+#include "soap_mma.cuh"
 #include "soap_pair.cuh"
 
 #include <cuda_runtime.h>
@@ -156,6 +157,15 @@ template <int MAXT, int LA, int LB1, int LB2, int NMAX, int LMAX, int MINB>
 const void* pair_symbol() {
     return reinterpret_cast<const void*>(&soap_pair_kernel<MAXT, LA, LB1, LB2, NMAX, LMAX, MINB>);
 }
+// fp64 tensor-core kernel: one warp per centre, n_max <= 8.
+template <int LMAX, int MINB>
+void launch_mma(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_mma_kernel<LMAX, MINB><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <int LMAX, int MINB>
+const void* mma_symbol() {
+    return reinterpret_cast<const void*>(&soap_mma_kernel<LMAX, MINB>);
+}
 template <int LMAX>
 void launch_structure(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const int64_t* offsets,
                       int64_t s0, int64_t s1, const double* cbuf, const double* pbuf, void* out, int64_t row0) {
@@ -174,6 +184,7 @@ const void* structure_symbol() {
 struct Variant {
     int cls, maxt, l0, l1, l2, nmax, lmax, minb;
     bool pair;  // two warps per centre (soap_pair_kernel), channel slots A | B1 B2
+    bool mma;   // fp64 tensor-core kernel (soap_mma_kernel)
     CenterLauncher center;
     const void* (*center_sym)();
     StructureLauncher structure;
@@ -182,27 +193,40 @@ struct Variant {
 
 #define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
     Variant {                                                                                             \
-        CLS, T, A, B, C, N, L, MB, false, &launch_center<T, A, B, C, N, L, MB>,                             \
+        CLS, T, A, B, C, N, L, MB, false, false, &launch_center<T, A, B, C, N, L, MB>,                      \
             &center_symbol<T, A, B, C, N, L, MB>, &launch_structure<L>, &structure_symbol<L>              \
     }
 #define MDSOAP_PAIR_VARIANT(CLS, T, A, B, C, N, L, MB)                                                   \
     Variant {                                                                                             \
-        CLS, T, A, B, C, N, L, MB, true, &launch_pair<T, A, B, C, N, L, MB>, &pair_symbol<T, A, B, C, N, L, MB>, \
+        CLS, T, A, B, C, N, L, MB, true, false, &launch_pair<T, A, B, C, N, L, MB>,                         \
+            &pair_symbol<T, A, B, C, N, L, MB>,                                                           \
             &launch_structure<L>, &structure_symbol<L>                                                    \
     }
 
-// First entry of each class is the default.
-// Defaults chosen by measurement on B200 (config shapes 1-5).
+#define MDSOAP_MMA_VARIANT(CLS, L, MB)                                                                  \
+    Variant {                                                                                             \
+        CLS, 0, 0, 0, 0, 8, L, MB, false, true, &launch_mma<L, MB>, &mma_symbol<L, MB>, &launch_structure<L>, \
+            &structure_symbol<L>                                                                          \
+    }
+
+// First entry of each class is the default.  Defaults chosen by measurement
+// on B200 (config shapes 1-5): the one-warp scalar-expansion kernel with the
+// tensor-core tail; the two-warp pair kernels and the all-tensor-core kernel
+// (soap_mma_kernel) are alternatives (MDSOAP_VARIANT=k).
 const Variant kVariants[] = {
     MDSOAP_VARIANT(0, 4, 7, 0, 0, 8, 3, 3),         // n <= 8, l <= 3
     MDSOAP_VARIANT(0, 8, 7, 0, 0, 8, 3, 2),
+    MDSOAP_MMA_VARIANT(0, 3, 2),
     MDSOAP_VARIANT(1, 3, 9, 1, 0, 8, 4, 3),         // n <= 8, l == 4
     MDSOAP_VARIANT(1, 6, 9, 1, 0, 8, 4, 2),
+    MDSOAP_MMA_VARIANT(1, 4, 2),
     MDSOAP_VARIANT(2, 4, 13, 5, 0, 8, 6, 2),        // n <= 8, l in 5..6
     MDSOAP_PAIR_VARIANT(2, 4, 13, 9, 0, 8, 6, 6),
     MDSOAP_PAIR_VARIANT(2, 3, 13, 9, 0, 8, 6, 6),
+    MDSOAP_MMA_VARIANT(2, 6, 2),
     MDSOAP_VARIANT(3, 2, 17, 9, 1, 8, 8, 2),        // n <= 8, l in 7..8
     MDSOAP_PAIR_VARIANT(3, 2, 17, 13, 5, 8, 8, 6),
+    MDSOAP_MMA_VARIANT(3, 8, 2),
     MDSOAP_VARIANT(4, 1, 41, 0, 0, 32, 20, 1),  // any n <= 32, l <= 20
 };
 
@@ -214,6 +238,13 @@ int variant_class(int n_max, int l_max) {
         if (l_max <= 8) return 3;
     }
     return 4;
+}
+
+// First scalar (non tensor-core) member of a class.
+const Variant& scalar_variant(int cls) {
+    for (const Variant& v : kVariants)
+        if (v.cls == cls && !v.mma) return v;
+    return kVariants[sizeof(kVariants) / sizeof(kVariants[0]) - 1];
 }
 
 // MDSOAP_VARIANT=<k> (tuning knob) selects the k-th member of the class;
@@ -428,7 +459,7 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         p.pbuf = st.work.pbuf.as<double>();
     }
     if (tab.r_global) {
-        st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * csize, "coefficient scratch");
+        st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * tab.rsize, "coefficient scratch");
         p.rbuf = st.work.rbuf.as<double>();
     }
     if (centers > 0) {
@@ -754,23 +785,37 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             }
         }
         for (int i = 0; i < q.n_species; ++i) t.species_weight[i] = plan->weights[i];
-        const Variant& v = pick_variant(n, L, q.n_species);
+        // The tensor-core kernel keeps a centre's whole coefficient block in
+        // shared memory; when that does not fit, the class's scalar kernel runs.
+        const Variant* picked = &pick_variant(n, L, q.n_species);
+        const mma::Layout lay = mma::layout(L, q.n_species * n);
+        const size_t mma_smem = (size_t)lay.shared + kWarps * (size_t)lay.warp_bytes;
+        if (picked->mma && mma_smem > 227 * 1024) picked = &scalar_variant(picked->cls);
+        const Variant& v = *picked;
+        // Tables of the scalar kernels (the tensor-core kernel shares csize/hp).
+        const Variant& sv = v.mma ? scalar_variant(v.cls) : v;
         plan->variant = &v;
-        plan->items = order_items(plan->items, L, n, v.pair);
-        if (v.pair) t.items = (int32_t)plan->items.size();
-        const int ns = (v.l0 > 0) + (v.l1 > 0) + (v.l2 > 0);
+        plan->items = order_items(plan->items, L, n, sv.pair);
+        if (sv.pair) t.items = (int32_t)plan->items.size();
+        const int ns = (sv.l0 > 0) + (sv.l1 > 0) + (sv.l2 > 0);
         const int slots = (t.items + 31) / 32;
-        t.slot_groups = v.pair ? 1 : (slots + ns - 1) / ns;
-        t.type_groups = (q.n_species + v.maxt - 1) / v.maxt;
+        t.slot_groups = sv.pair ? 1 : (slots + ns - 1) / ns;
+        t.type_groups = (q.n_species + sv.maxt - 1) / sv.maxt;
         const bool single_pass = t.slot_groups == 1 && t.type_groups == 1;
-        const size_t beta_bytes = (size_t)W * n * n * 8;
-        t.beta_in_smem = beta_bytes <= 32768;
+        // One-warp scalar kernels with n_max <= 8 finish on the tensor cores:
+        // row-strided coefficient block, padded 8 x 8 beta table in shared memory.
+        const bool mma_tail = !sv.pair && sv.nmax <= 8;
+        const size_t beta_bytes = mma_tail ? (size_t)W * 64 * 8 : (size_t)W * n * n * 8;
+        t.beta_in_smem = mma_tail || beta_bytes <= 32768;
         // CTA-shared: 32-entry exp table (256 B) + optional beta copy.
         const size_t beta_smem = 256 + (t.beta_in_smem ? ((beta_bytes + 15) & ~(size_t)15) : 0);
         t.csize = q.n_species * n * W * (W + 1);
         t.hp = W * (W + 1);
-        const size_t r_bytes = (size_t)t.csize * 8;
-        const size_t pend = v.pair ? (size_t)kPairHeader + (size_t)kPairPending * 36
+        t.rs = (mma_tail || v.mma) ? mma::row_stride(L) : 0;
+        t.rsize = mma_tail ? q.n_species * n * t.rs : t.csize;
+        t.n_magic = n == 1 ? 0u : (uint32_t)((1ull << 32) / (uint64_t)n + 1ull);
+        const size_t r_bytes = (size_t)t.rsize * 8;
+        const size_t pend = sv.pair ? (size_t)kPairHeader + (size_t)kPairPending * 36
                                    : kRegionHeader + (size_t)kPending * 36;
         auto region_a = [&](int chunk) { return pend + ((size_t)chunk * t.hp + 48) * 8; };
         auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
@@ -783,7 +828,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         // (228 KB per SM, 1 KB reserved per CTA); failing that, the smallest
         // footprint that fits one CTA, with the coefficient blocks moved to
         // global scratch if they alone are too large.
-        const size_t budget = 228 * 1024 / (size_t)v.minb - 1024, budget1 = 227 * 1024;
+        const size_t budget = 228 * 1024 / (size_t)sv.minb - 1024, budget1 = 227 * 1024;
         int chunk = 32;
         bool r_smem = true;
         while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, true) > budget) chunk -= 8;
@@ -792,7 +837,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             chunk = 32;
             while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, false) > budget) chunk -= 8;
         }
-        if (v.pair) {
+        if (sv.pair) {
             // One region per CTA (one centre), no beta copy; offsets relative
             // to the queue (after the exp table and the header).
             t.beta_in_smem = 0;
@@ -813,7 +858,12 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         t.r_offset = (r_smem && !single_pass) ? (int32_t)align16(region_a(chunk)) : 0;
         plan->center_smem = beta_smem + kWarps * (size_t)t.warp_bytes;
         }
-        plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? r_bytes : 0;
+        if (v.mma) {
+            t.r_global = 0;
+            t.warp_bytes = lay.warp_bytes;
+            plan->center_smem = mma_smem;
+        }
+        plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? (size_t)t.csize * 8 : 0;
         plan->csize = t.csize;
         if (plan->center_smem > budget1 || plan->structure_smem > budget1)
             return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
@@ -1013,7 +1063,7 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
     size_t o_cbuf = 0, o_pbuf = 0, o_rbuf = 0;
     if (plan->average == MDSOAP_AVERAGE_INNER) o_cbuf = take(8 * (size_t)N * (size_t)plan->csize);
     if (plan->average == MDSOAP_AVERAGE_OUTER) o_pbuf = take(8 * (size_t)N * (size_t)plan->features);
-    if (plan->tab.r_global) o_rbuf = take(8 * (size_t)N * (size_t)plan->csize);
+    if (plan->tab.r_global) o_rbuf = take(8 * (size_t)N * (size_t)plan->tab.rsize);
     if (off > MDSOAP_NOALLOC_SCRATCH_BYTES)
         return fail(MDSOAP_CAPACITY_OVERFLOW,
                     "batch needs " + std::to_string(off) + " bytes of scratch; the no-allocation entry point holds " +

@@ -27,8 +27,7 @@
 //     covers runs of consecutive features.
 #pragma once
 
-#include <type_traits>
-
+#include "dmma.cuh"
 #include "expneg.cuh"
 #include "neighbors.cuh"
 
@@ -58,7 +57,9 @@ struct SoapTables {
     int32_t r_global;     // 1: coefficient blocks live in global scratch
     int32_t csize;        // coefficient block length in doubles: S n (L+1)(L+2)
     int32_t hp;           // padded harmonic row length: (L+1)(L+2)
-    int32_t pad2_;
+    int32_t rs;           // tensor-core tail: coefficient-block row stride (0: scalar tail)
+    int32_t rsize;        // doubles of one centre's coefficient block
+    uint32_t n_magic;     // floor(2^32 / n_max) + 1
     double cutoff2;
     double soap_scale;    // pi^{3/2}
     double ynorm[kTri];   // N_lm (times sqrt 2 for m > 0), index l(l+1)/2 + m
@@ -81,21 +82,6 @@ struct SoapPointers {
     int64_t center_begin;
     int64_t center_end;
 };
-
-__device__ __forceinline__ int tri(int l, int m) { return l * (l + 1) / 2 + m; }
-
-// Compile-time loop: f(std::integral_constant<int, I>) for I in [I0, N).
-template <int I0, int N, class F>
-__device__ __forceinline__ void static_for(F&& f) {
-    if constexpr (I0 < N) {
-        f(std::integral_constant<int, I0>{});
-        static_for<I0 + 1, N>(f);
-    }
-}
-
-// Coefficient block layout: [l][t][n][m] with each (t, n) row padded to
-// 2l+2 doubles; block l starts at S n l (l+1).
-__device__ __forceinline__ int cblock(int S, int n, int l) { return S * n * l * (l + 1); }
 
 // Real regular solid harmonics of one displacement into a padded row: the
 // block of degree l starts at l (l + 1) (even, so 16-byte aligned) and holds
@@ -206,16 +192,6 @@ __device__ __forceinline__ void harmonics_any(const SoapTables& tab, double x, d
         solid_harmonics_fixed<LMAX>(tab, x, y, z, r2, out);
     else
         solid_harmonics(tab, x, y, z, r2, out);
-}
-
-// Feature offset of (t1, n1, t2, n2, l) in the compression-off layout
-// (t1 <= t2, then l, then n1, then n2 with n2 >= n1 when t1 == t2).
-__device__ __forceinline__ int64_t pair_base(int S, int n, int L, int t1, int t2) {
-    const int64_t T = (int64_t)n * (n + 1) / 2;
-    const int64_t nn = (int64_t)n * n;
-    int64_t base = (int64_t)(L + 1) * (t1 * T + nn * ((int64_t)t1 * (S - 1) - (int64_t)t1 * (t1 - 1) / 2));
-    if (t2 > t1) base += (int64_t)(L + 1) * (T + (int64_t)(t2 - t1 - 1) * nn);
-    return base;
 }
 
 // Power spectrum for l in [LA, LB]: lane = column r2, whose rows of every l
@@ -451,6 +427,9 @@ template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX, int MINB>
 __global__ void __launch_bounds__(kWarps * 32, MINB)
 soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
     constexpr int NS = (L0 > 0) + (L1 > 0) + (L2 > 0);
+    // n_max <= 8: the beta transform and power spectrum run on the fp64 tensor
+    // cores (dmma.cuh) from a row-strided coefficient block; otherwise scalar.
+    constexpr bool kMmaTail = NMAX <= 8;
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -461,7 +440,16 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     if (threadIdx.x < 32) etab[threadIdx.x] = kExp2Table[threadIdx.x];
     int shared_bytes = 256;
     const double* beta = p.betas;
-    if (tab.beta_in_smem) {
+    if constexpr (kMmaTail) {
+        // [l][n][k] scaled by pi^{3/2}, zero padded to 8 x 8.
+        double* bt = reinterpret_cast<double*>(smem + 256);
+        for (int i = threadIdx.x; i < (tab.l_max + 1) * 64; i += blockDim.x) {
+            const int l = i / 64, nn = (i / 8) % 8, k = i % 8;
+            bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
+        }
+        beta = bt;
+        shared_bytes += (tab.l_max + 1) * 64 * 8;
+    } else if (tab.beta_in_smem) {
         double* sbeta = reinterpret_cast<double*>(smem + 256);
         for (int i = threadIdx.x; i < beta_count; i += blockDim.x) sbeta[i] = p.betas[i];
         beta = sbeta;
@@ -483,7 +471,7 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     int32_t* ptype = reinterpret_cast<int32_t*>(pr2 + kPending);
     double* ybuf = reinterpret_cast<double*>(region + kRegionHeader + kPending * 36);
     const int64_t local = center - p.center_begin;
-    double* R = tab.r_global ? p.rbuf + local * tab.csize : reinterpret_cast<double*>(region + tab.r_offset);
+    double* R = tab.r_global ? p.rbuf + local * tab.rsize : reinterpret_cast<double*>(region + tab.r_offset);
 
     const BinView& bv = p.bins;
     const StructInfo si = bv.info[bv.struct_of[center]];
@@ -648,38 +636,71 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             __syncwarp();
             if (pcount > 0) process(pcount);
 
-            // Flush the raw sums: R[l][t][k][m], rows padded to 2l+2.
+            // Flush the raw sums.  Tensor-core tail: row (t, k), columns
+            // col_off(l) .. + kpad(l), padding written as 0; scalar tail:
+            // R[l][t][k][m], rows padded to 2l+2.
+            auto flush_slot = [&](auto len_c, auto& a, int sl, int tt) {
+                constexpr int LS = decltype(len_c)::value;
+                const int t = tb + tt;
+                const int len = 2 * il[sl] + 1;
+                if constexpr (kMmaTail) {
+                    double* dst = R + (t * n + ik[sl]) * tab.rs + mma::col_off(il[sl]);
+                    const int kp = mma::kpad(il[sl]);
+#pragma unroll
+                    for (int m = 0; m < LS; ++m)
+                        if (m < kp) dst[m] = m < len ? a[tt][m] : 0.0;
+#pragma unroll
+                    for (int m = LS; m < ((LS + 3) & ~3); ++m)
+                        if (m < kp) dst[m] = 0.0;
+                } else {
+                    double* dst = R + cblock(S, n, il[sl]) + (t * n + ik[sl]) * (len + 1);
+#pragma unroll
+                    for (int m = 0; m < LS; ++m)
+                        if (m < len) dst[m] = a[tt][m];
+                }
+            };
 #pragma unroll
             for (int tt = 0; tt < MAXT; ++tt) {
-                const int t = tb + tt;
-                if (t < te) {
-                    if (L0 > 0 && ivalid[0]) {
-                        const int len = 2 * il[0] + 1;
-                        double* dst = R + cblock(S, n, il[0]) + (t * n + ik[0]) * (len + 1);
-#pragma unroll
-                        for (int m = 0; m < L0; ++m)
-                            if (m < len) dst[m] = a0[tt][m];
-                    }
-                    if (L1 > 0 && ivalid[1]) {
-                        const int len = 2 * il[1] + 1;
-                        double* dst = R + cblock(S, n, il[1]) + (t * n + ik[1]) * (len + 1);
-#pragma unroll
-                        for (int m = 0; m < L1; ++m)
-                            if (m < len) dst[m] = a1[tt][m];
-                    }
-                    if (L2 > 0 && ivalid[2]) {
-                        const int len = 2 * il[2] + 1;
-                        double* dst = R + cblock(S, n, il[2]) + (t * n + ik[2]) * (len + 1);
-#pragma unroll
-                        for (int m = 0; m < L2; ++m)
-                            if (m < len) dst[m] = a2[tt][m];
-                    }
+                if (tb + tt < te) {
+                    if (L0 > 0 && ivalid[0]) flush_slot(std::integral_constant<int, L0>{}, a0, 0, tt);
+                    if (L1 > 0 && ivalid[1]) flush_slot(std::integral_constant<int, L1>{}, a1, 1, tt);
+                    if (L2 > 0 && ivalid[2]) flush_slot(std::integral_constant<int, L2>{}, a2, 2, tt);
                 }
             }
             __syncwarp();
         }
     }
 
+    if constexpr (kMmaTail) {
+        const int g = lane >> 2, q = lane & 3, L = tab.l_max, R_rows = tab.rows;
+        mma::beta_mma<LMAX>(beta, R, tab.rs, L, S, n, g, q);
+        __syncwarp();
+        const mma::FeatureMap fm{S, n, L, R_rows, tab.n_magic};
+        if (tab.average == 0) {
+            const int64_t row = center - p.out_row_begin;
+            if (tab.out_f64)
+                mma::power_mma<LMAX>(fm, tab.power_pref, R, tab.rs, static_cast<double*>(p.out) + row * tab.features,
+                                     g, q);
+            else
+                mma::power_mma<LMAX>(fm, tab.power_pref, R, tab.rs, static_cast<float*>(p.out) + row * tab.features,
+                                     g, q);
+        } else if (tab.average == 1) {
+            // The structure kernel's layout: [l][r][m], rows padded to 2l+2.
+            double* dst = p.cbuf + local * tab.csize;
+            for (int l = 0; l <= L; ++l) {
+                const int pad = 2 * l + 2;
+                double* dl = dst + cblock(S, n, l);
+                const double* src = R + mma::col_off(l);
+                for (int i = lane; i < R_rows * pad; i += 32) {
+                    const int r = i / pad, m = i - r * pad;
+                    dl[i] = m < 2 * l + 1 ? src[r * tab.rs + m] : 0.0;
+                }
+            }
+        } else {
+            mma::power_mma<LMAX>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, g, q);
+        }
+        return;
+    } else {
     beta_transform_warp<NMAX>(tab, beta, R, lane);
     __syncwarp();
     if (tab.average == 0) {
@@ -693,6 +714,7 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         for (int i = lane; i < tab.csize; i += 32) dst[i] = R[i];
     } else {
         power_spectrum_warp<LMAX>(tab, R, p.pbuf + local * tab.features, lane);
+    }
     }
 }
 
