@@ -189,6 +189,13 @@ int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, d
  * benchmark reads it before and after its timed region to count its launches. */
 int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count);
 
+/* The engine's exp() for non-positive arguments (Tang's table-driven
+ * method, used for every radial factor exp(-a r^2)) and CUDA's exp(), both
+ * evaluated on `device` for `count` host arguments; results are written to
+ * the host arrays `ours` and `cuda_exp` (test support; no counterpart in the
+ * reference, whose CPU path calls std::exp, soap.cpp:895-896). */
+int mdsoap_probe_exp(int32_t device, const double* x, int64_t count, double* ours, double* cuda_exp);
+
 /* Measured fp64 FMA throughput of `device` in TFLOP/s (2 flops per FMA) from a
  * register-resident FMA chain kernel over every SM (measurement support; no
  * counterpart in the reference).  Used as the roofline denominator of the

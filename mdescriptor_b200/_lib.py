@@ -92,6 +92,8 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_plan_last_timing.restype = ctypes.c_int
     lib.mdsoap_plan_launch_count.argtypes = [_P, _P]
     lib.mdsoap_plan_launch_count.restype = ctypes.c_int
+    lib.mdsoap_probe_exp.argtypes = [ctypes.c_int32, _P, ctypes.c_int64, _P, _P]
+    lib.mdsoap_probe_exp.restype = ctypes.c_int
     lib.mdsoap_probe_fp64_fma.argtypes = [ctypes.c_int32, _P]
     lib.mdsoap_probe_fp64_fma.restype = ctypes.c_int
     lib.mdsoap_graph_build.argtypes = [ctypes.POINTER(BatchView), ctypes.c_double, ctypes.c_int32, ctypes.POINTER(_P)]
@@ -123,6 +125,7 @@ EXPORTED = (
     "mdsoap_plan_set_timing",
     "mdsoap_plan_last_timing",
     "mdsoap_plan_launch_count",
+    "mdsoap_probe_exp",
     "mdsoap_probe_fp64_fma",
     "mdsoap_graph_build",
     "mdsoap_graph_pairs",

@@ -307,6 +307,18 @@ __global__ void fma_probe_kernel(double* sink, int iters) {
     sink[blockIdx.x * blockDim.x + threadIdx.x] = s;
 }
 
+// The engine's exp() (expneg.cuh) beside CUDA's exp() on the same arguments.
+__global__ void exp_probe_kernel(const double* __restrict__ x, int64_t count, double* __restrict__ ours,
+                                 double* __restrict__ cuda_exp) {
+    __shared__ double table[32];
+    if (threadIdx.x < 32) table[threadIdx.x] = kExp2Table[threadIdx.x];
+    __syncthreads();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        ours[i] = exp_nonpositive(x[i], table);
+        cuda_exp[i] = exp(x[i]);
+    }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -1183,6 +1195,30 @@ int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count) {
     if (!plan || !count) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
     *count = plan->launches.load(std::memory_order_relaxed);
     return MDSOAP_OK;
+}
+
+int mdsoap_probe_exp(int32_t device, const double* x, int64_t count, double* ours, double* cuda_exp) {
+    if (count < 0 || (count > 0 && (!x || !ours || !cuda_exp))) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        int devices = 0;
+        if (cudaGetDeviceCount(&devices) != cudaSuccess || device < 0 || device >= devices)
+            raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device unavailable");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        if (count == 0) return MDSOAP_OK;
+        DeviceBytes dx, d1, d2;
+        const size_t bytes = 8 * (size_t)count;
+        dx.reserve(bytes, "probe input");
+        d1.reserve(bytes, "probe output");
+        d2.reserve(bytes, "probe output");
+        check(cudaMemcpy(dx.ptr, x, bytes, cudaMemcpyHostToDevice), "probe upload");
+        exp_probe_kernel<<<256, 256>>>(dx.as<double>(), count, d1.as<double>(), d2.as<double>());
+        check(cudaGetLastError(), "probe launch");
+        check(cudaMemcpy(ours, d1.ptr, bytes, cudaMemcpyDeviceToHost), "probe download");
+        check(cudaMemcpy(cuda_exp, d2.ptr, bytes, cudaMemcpyDeviceToHost), "probe download");
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    }
 }
 
 int mdsoap_probe_fp64_fma(int32_t device, double* tflops) {

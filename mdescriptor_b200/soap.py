@@ -187,6 +187,15 @@ def probe_fp64_fma(device: int = 0) -> float:
     return float(value.value)
 
 
+def probe_exp(x, device: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """The engine's exp() and CUDA's exp() of the same arguments on one device."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    ours = np.empty_like(x)
+    cuda = np.empty_like(x)
+    raise_for(lib.mdsoap_probe_exp(int(device), x.ctypes.data, x.size, ours.ctypes.data, cuda.ctypes.data))
+    return ours, cuda
+
+
 def device_count() -> int:
     return int(lib.mdsoap_device_count())
 
