@@ -10,8 +10,8 @@
 // Taylor series through r^6/720 (truncation < 4e-18 for |r| <= 0.0109), and
 // 2^(j/32) from a 32-entry table of correctly rounded doubles.  2^m is built
 // from its exponent bits, so no conversion instruction is needed.  Arguments
-// below -708 return 0 (the result would be subnormal; SOAP radial factors
-// there are below 1e-307 and vanish against every other term).
+// below -708 return 0 (the true value is under exp(-708) = 3.31e-308; SOAP
+// radial factors there vanish against every other term).
 #pragma once
 
 #include <cuda_runtime.h>
