@@ -42,6 +42,7 @@ struct StructInfo {
     int32_t atom_count;
     int32_t pad_;
     int64_t bin_base;    // first bin_start entry of this structure
+    double pre_cut2;     // prefilter radius^2: cutoff plus a margin far above fp64 rounding of any displacement
 };
 
 struct BinView {
@@ -54,6 +55,8 @@ struct BinView {
     int32_t* bin_start;      // [2*atoms + 8*structures] bin offsets (+1 sentinel per structure)
     int32_t* bin_cursor;     // same size, scatter cursors
     unsigned* error;         // device error word
+    double4* spos;           // [atoms] in `sorted` order: wrapped position (x, y, z) and species index (w);
+                             // may be null (then not written)
 };
 
 // Capacity of the bin table of a structure with `atoms` atoms: its bin count

@@ -53,4 +53,42 @@ __device__ __forceinline__ double exp_nonpositive(double x, const double* __rest
     return x < -708.0 ? 0.0 : mant * scale;
 }
 
+// pref * exp(x) for x in [-708, 0] when the product is a normal double (the
+// plan checks pref exp(x) >= 1e-300 over its whole argument range before it
+// picks a kernel that calls this).  Same method as exp_nonpositive, with the
+// prefactor folded into the table factor and 2^m applied by adding m to the
+// exponent field (exact for normal results), so no clamp and no scaling
+// multiply are needed:
+//   PRECISE  two-step reduction and the series through r^6/720 (as above);
+//   !PRECISE one-step reduction (the dropped k ln2/32 tail is below
+//            |k| 7.3e-19 <= 2.4e-14 absolute in r) and the series through
+//            r^5/120 (truncation < 2.2e-15): relative error a few 1e-14, for
+//            float32 output rows.
+template <bool PRECISE>
+__device__ __forceinline__ double scaled_exp(double x, double pref, const double* __restrict__ table) {
+    constexpr double kInvLn2Over32 = 46.16624130844683;
+    constexpr double kShift = 6755399441055744.0;
+    constexpr double kLn2Over32Hi = 0.02166084939249829;
+    constexpr double kLn2Over32Lo = 7.247021293269686e-19;
+    const double t = fma(x, kInvLn2Over32, kShift);
+    const int k = __double2loint(t);
+    const double kd = t - kShift;
+    double r = fma(kd, -kLn2Over32Hi, x);
+    double p;
+    if constexpr (PRECISE) {
+        r = fma(kd, -kLn2Over32Lo, r);
+        p = fma(r, 1.0 / 720.0, 1.0 / 120.0);
+        p = fma(r, p, 1.0 / 24.0);
+    } else {
+        p = fma(r, 1.0 / 120.0, 1.0 / 24.0);
+    }
+    p = fma(r, p, 1.0 / 6.0);
+    p = fma(r, p, 0.5);
+    p = fma(r, p, 1.0);
+    p = r * p;
+    const double tj = pref * table[k & 31];
+    const double v = fma(tj, p, tj);
+    return __hiloint2double(__double2hiint(v) + (k >> 5) * (1 << 20), __double2loint(v));
+}
+
 }  // namespace mdsoap

@@ -7,6 +7,7 @@
 #include "../../include/mdsoap.h"
 #include "soap_mma.cuh"
 #include "soap_pair.cuh"
+#include "soap_paired.cuh"
 
 #include <cuda_runtime.h>
 
@@ -102,11 +103,11 @@ struct PinnedBytes {
 // Device workspace for one batch (or one shard of one).
 struct Workspace {
     DeviceBytes numbers, positions, cells, pbc, offsets;
-    DeviceBytes info, struct_of, type, bin_of, wrap, sorted, bin_start, bin_cursor;
+    DeviceBytes info, struct_of, type, bin_of, wrap, sorted, bin_start, bin_cursor, spos;
     DeviceBytes cbuf, pbuf, rbuf;
     void release() {
         for (DeviceBytes* b : {&numbers, &positions, &cells, &pbc, &offsets, &info, &struct_of, &type, &bin_of,
-                               &wrap, &sorted, &bin_start, &bin_cursor, &cbuf, &pbuf, &rbuf})
+                               &wrap, &sorted, &bin_start, &bin_cursor, &spos, &cbuf, &pbuf, &rbuf})
             b->release();
     }
     BinView bins(unsigned* error) {
@@ -120,6 +121,7 @@ struct Workspace {
         v.bin_start = bin_start.as<int32_t>();
         v.bin_cursor = bin_cursor.as<int32_t>();
         v.error = error;
+        v.spos = spos.as<double4>();
         return v;
     }
     void reserve_bins(int64_t atoms, int64_t structures) {
@@ -130,6 +132,7 @@ struct Workspace {
         bin_of.reserve(4 * a, "bin bin_of");
         wrap.reserve(12 * a, "bin wrap");
         sorted.reserve(4 * a, "bin sorted");
+        spos.reserve(32 * a, "bin sorted positions");
         const size_t bins = (size_t)(2 * atoms + 8 * structures + 8);
         bin_start.reserve(4 * bins, "bin starts");
         bin_cursor.reserve(4 * bins, "bin cursors");
@@ -166,6 +169,15 @@ template <int LMAX, int MINB>
 const void* mma_symbol() {
     return reinterpret_cast<const void*>(&soap_mma_kernel<LMAX, MINB>);
 }
+// Paired-channel kernel: one warp per centre, l_max == L exactly.
+template <int T, int L, bool PRECISE, int MINB>
+void launch_paired(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_paired_kernel<T, L, PRECISE, MINB><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <int T, int L, bool PRECISE, int MINB>
+const void* paired_symbol() {
+    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB>);
+}
 template <int LMAX>
 void launch_structure(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const int64_t* offsets,
                       int64_t s0, int64_t s1, const double* cbuf, const double* pbuf, void* out, int64_t row0) {
@@ -189,6 +201,8 @@ struct Variant {
     const void* (*center_sym)();
     StructureLauncher structure;
     const void* (*structure_sym)();
+    bool paired = false;   // paired-channel kernel (soap_paired_kernel), l_max == lmax exactly
+    bool precise = false;  // paired: full-accuracy radial factors (float64 rows)
 };
 
 #define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
@@ -230,6 +244,29 @@ const Variant kVariants[] = {
     MDSOAP_VARIANT(4, 1, 41, 0, 0, 32, 20, 1),  // any n <= 32, l <= 20
 };
 
+#define MDSOAP_PAIRED_VARIANT(T, L, PREC, MB)                                                              \
+    Variant {                                                                                              \
+        -1, T, 0, 0, 0, 8, L, MB, false, false, &launch_paired<T, L, PREC, MB>,                             \
+            &paired_symbol<T, L, PREC, MB>, &launch_structure<L>, &structure_symbol<L>, true, PREC          \
+    }
+
+// Paired-channel kernels: the default wherever they apply (n_max <= 8,
+// n_max (1 + (l_max + 1) / 2) <= 32 lanes, an instantiated l_max, and radial
+// factors that stay normal doubles; see paired_applies).
+const Variant kPairedVariants[] = {
+    MDSOAP_PAIRED_VARIANT(4, 3, false, 2), MDSOAP_PAIRED_VARIANT(4, 3, true, 2),
+    MDSOAP_PAIRED_VARIANT(4, 4, false, 2), MDSOAP_PAIRED_VARIANT(4, 4, true, 2),
+    MDSOAP_PAIRED_VARIANT(4, 5, false, 2), MDSOAP_PAIRED_VARIANT(4, 5, true, 2),
+    MDSOAP_PAIRED_VARIANT(4, 6, false, 2), MDSOAP_PAIRED_VARIANT(4, 6, true, 2),
+};
+
+const Variant* paired_variant(int n_max, int l_max, bool precise) {
+    if (n_max > 8 || n_max * (1 + (l_max + 1) / 2) > 32) return nullptr;
+    for (const Variant& v : kPairedVariants)
+        if (v.lmax == l_max && v.precise == precise) return &v;
+    return nullptr;
+}
+
 int variant_class(int n_max, int l_max) {
     if (n_max <= 8) {
         if (l_max <= 3) return 0;
@@ -247,13 +284,10 @@ const Variant& scalar_variant(int cls) {
     return kVariants[sizeof(kVariants) / sizeof(kVariants[0]) - 1];
 }
 
-// MDSOAP_VARIANT=<k> (tuning knob) selects the k-th member of the class;
-// otherwise the class default, its first member (the fastest measured on
-// B200 for the config shapes; the two-warp pair kernels are alternatives).
-const Variant& pick_variant(int n_max, int l_max, int n_species) {
+// The want-th member of the class of (n_max, l_max), or its first member
+// when `want` is out of range.
+const Variant& pick_variant(int n_max, int l_max, int want) {
     const int cls = variant_class(n_max, l_max);
-    const char* env = std::getenv("MDSOAP_VARIANT");
-    int want = env ? std::atoi(env) : -1;
     const Variant* first = nullptr;
     int k = 0;
     for (const Variant& v : kVariants) {
@@ -797,9 +831,77 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             }
         }
         for (int i = 0; i < q.n_species; ++i) t.species_weight[i] = plan->weights[i];
+        // Kernel choice.  The paired-channel kernel is the default where it
+        // applies: its scaled_exp needs every radial factor P exp(-E r^2),
+        // r <= cutoff, to be a normal double with E r^2 <= 708.  MDSOAP_VARIANT=k
+        // (tuning knob) picks the k-th of [paired kernel if it applies, the
+        // class's kernels...] instead; an index past the list gives the default.
+        bool radial_normal = true;
+        for (const RadialItem& it : plan->items) {
+            const double span = it.exponent * t.cutoff2;
+            if (!(it.prefactor > 0.0) || !std::isfinite(it.prefactor) || !(it.exponent >= 0.0) || !(span <= 700.0) ||
+                std::log(it.prefactor) - span < -690.0)
+                radial_normal = false;
+        }
+        const Variant* paired = radial_normal ? paired_variant(n, L, q.output_dtype == MDSOAP_FLOAT64) : nullptr;
+        const char* env = std::getenv("MDSOAP_VARIANT");
+        const int want = env ? std::atoi(env) : -1;
+        const Variant* picked = nullptr;
+        if (paired && want <= 0) picked = paired;
+        else picked = &pick_variant(n, L, paired ? want - 1 : want);
+        if (paired && picked != paired && want > 0 && want - 1 >= 0) {
+            // An index past the class list falls back to the default (the paired kernel).
+            int members = 0;
+            for (const Variant& cv : kVariants) members += cv.cls == variant_class(n, L);
+            if (want - 1 >= members) picked = paired;
+        }
+        if (picked->paired) {
+            const Variant& v = *picked;
+            plan->variant = &v;
+            t.type_groups = (q.n_species + v.maxt - 1) / v.maxt;
+            t.slot_groups = 1;
+            t.beta_in_smem = 1;
+            t.csize = q.n_species * n * W * (W + 1);
+            t.hp = W * (W + 1);
+            t.rs = mma::row_stride(L);
+            t.rsize = q.n_species * n * t.rs;
+            t.n_magic = n == 1 ? 0u : (uint32_t)((1ull << 32) / (uint64_t)n + 1ull);
+            const bool single_pass = t.type_groups == 1;
+            const size_t shared = 256 + (size_t)W * 64 * 8;
+            // paired::Layout<L>::ROW: G views of 2L+2 doubles, padded to = 2 (mod 4).
+            const size_t views = (size_t)(1 + (L + 1) / 2) * (size_t)(2 * L + 2);
+            const size_t row = views + (2 - views % 4 + 4) % 4;
+            const size_t r_bytes = (size_t)t.rsize * 8;
+            auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
+            auto walk = [&](int c) { return (size_t)paired::kHeaderBytes + (size_t)c * row * 8; };
+            auto per_warp = [&](int c, bool r_in) {
+                if (!r_in) return align16(walk(c));
+                if (single_pass) return align16(std::max(walk(c), r_bytes));
+                return align16(walk(c)) + align16(r_bytes);
+            };
+            const size_t budget = 228 * 1024 / (size_t)v.minb - 1024, budget1 = 227 * 1024;
+            int chunk = 32;
+            bool r_smem = true;
+            while (chunk > 8 && shared + kWarps * per_warp(chunk, true) > budget) chunk -= 8;
+            if (shared + kWarps * per_warp(chunk, true) > budget1) {
+                r_smem = false;
+                chunk = 32;
+                while (chunk > 8 && shared + kWarps * per_warp(chunk, false) > budget) chunk -= 8;
+            }
+            t.chunk = chunk;
+            t.r_global = r_smem ? 0 : 1;
+            t.warp_bytes = (int32_t)per_warp(chunk, r_smem);
+            t.r_offset = (r_smem && !single_pass) ? (int32_t)align16(walk(chunk)) : 0;
+            plan->center_smem = shared + kWarps * (size_t)t.warp_bytes;
+            plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? (size_t)t.csize * 8 : 0;
+            plan->csize = t.csize;
+            if (plan->center_smem > budget1 || plan->structure_smem > budget1)
+                return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
+            *plan_out = plan.release();
+            return MDSOAP_OK;
+        }
         // The tensor-core kernel keeps a centre's whole coefficient block in
         // shared memory; when that does not fit, the class's scalar kernel runs.
-        const Variant* picked = &pick_variant(n, L, q.n_species);
         const mma::Layout lay = mma::layout(L, q.n_species * n);
         const size_t mma_smem = (size_t)lay.shared + kWarps * (size_t)lay.warp_bytes;
         if (picked->mma && mma_smem > 227 * 1024) picked = &scalar_variant(picked->cls);
@@ -1069,6 +1171,7 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
     const size_t o_bin = take(4 * (size_t)N);
     const size_t o_wrap = take(12 * (size_t)N);
     const size_t o_sorted = take(4 * (size_t)N);
+    const size_t o_spos = take(32 * (size_t)N);
     const size_t bins = (size_t)(2 * N + 8 * S + 8);
     const size_t o_bstart = take(4 * bins);
     const size_t o_bcursor = take(4 * bins);
@@ -1119,6 +1222,7 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
         v.bin_start = reinterpret_cast<int32_t*>(base + o_bstart);
         v.bin_cursor = reinterpret_cast<int32_t*>(base + o_bcursor);
         v.error = error;
+        v.spos = reinterpret_cast<double4*>(base + o_spos);
         DeviceBatch db{batch->numbers, batch->positions, batch->cells, batch->pbc, batch->offsets, S, N};
         if (S > 0) {
             bin_structures_kernel<<<(unsigned)S, 256, 0, st>>>(db, v, plan->cutoff,

@@ -60,6 +60,22 @@ __device__ inline void cap_bins(int* M, int64_t cap) {
     }
 }
 
+// Position of an atom in the frame its bin lives in: periodic structures
+// subtract the lattice translation wrap . A (the atom's image in the home
+// cell); isolated ones keep the raw position.  Used only for the candidate
+// prefilter, never for an accepted displacement.
+__device__ __forceinline__ void wrapped_position(const StructInfo& si, const double* __restrict__ x,
+                                                 const int32_t* __restrict__ wrap, double* w) {
+    if (si.periodic) {
+        const double f0 = (double)wrap[0], f1 = (double)wrap[1], f2 = (double)wrap[2];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) w[c] = x[c] - fma(f2, si.cell[6 + c], fma(f1, si.cell[3 + c], f0 * si.cell[c]));
+    } else {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) w[c] = x[c];
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 1: per structure (one CTA each): geometry plan, species lookup, and a
 // deterministic counting sort of its atoms into bins.
@@ -70,7 +86,7 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
     const int64_t count = b.offsets[s + 1] - begin;
     const int tid = threadIdx.x;
     __shared__ StructInfo si;
-    __shared__ double red[6][32];
+    __shared__ double red[7][32];
     __shared__ int32_t flags;
     __shared__ int32_t scan_carry;
     __shared__ int32_t warp_sums[32];
@@ -86,6 +102,14 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
     if (periodic < 0) {
         if (tid == 0) atomicOr(v.error, kErrMixedPbc);
         return;
+    }
+    // Largest |coordinate| (bounds the prefilter margin).
+    {
+        double amax = 0.0;
+        for (int64_t a = tid; a < 3 * count; a += blockDim.x) amax = fmax(amax, fabs(b.positions[3 * begin + a]));
+        for (int o = 16; o > 0; o >>= 1) amax = fmax(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if ((tid & 31) == 0) red[6][tid >> 5] = amax;
+        __syncthreads();
     }
     // Bounding box of an isolated structure.
     double lo[3] = {INFINITY, INFINITY, INFINITY}, hi[3] = {-INFINITY, -INFINITY, -INFINITY};
@@ -170,6 +194,20 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
                               : 0;
             }
         }
+        // Prefilter radius: every quantity in either displacement formula is
+        // below Z in magnitude, so both carry rounding errors of a few 1e-16 Z;
+        // a margin of 1e-11 (Z + cutoff) keeps every pair the exact test accepts.
+        double amax = 0.0;
+        for (int w = 0; w < (int)((blockDim.x + 31) / 32); ++w) amax = fmax(amax, red[6][w]);
+        double cellsum = 0.0;
+        int bmax = 0;
+        if (periodic) {
+            for (int k = 0; k < 9; ++k) cellsum += fabs(si.cell[k]);
+            bmax = max(si.bounds[0], max(si.bounds[1], si.bounds[2]));
+        }
+        const double Z = 2.0 * amax + (bmax + 4.0) * cellsum;
+        const double pre = cutoff + 1e-11 * (Z + cutoff);
+        si.pre_cut2 = pre * pre * (1.0 + 1e-14);
         v.info[s] = si;
     }
     __syncthreads();
@@ -269,6 +307,15 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
             }
             list[q + 1] = key;
         }
+    }
+    if (v.spos == nullptr) return;
+    __syncthreads();
+    // Wrapped positions and species in bin order (the centre kernels' prefilter reads them coalesced).
+    for (int64_t p = tid; p < count; p += blockDim.x) {
+        const int64_t atom = begin + v.sorted[begin + p];
+        double w[3];
+        wrapped_position(si, b.positions + 3 * atom, v.wrap + 3 * atom, w);
+        v.spos[begin + p] = make_double4(w[0], w[1], w[2], (double)v.type[atom]);
     }
 }
 

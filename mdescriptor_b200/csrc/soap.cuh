@@ -60,6 +60,10 @@ struct SoapTables {
     int32_t rs;           // tensor-core tail: coefficient-block row stride (0: scalar tail)
     int32_t rsize;        // doubles of one centre's coefficient block
     uint32_t n_magic;     // floor(2^32 / n_max) + 1
+    int32_t weighted;     // 1: per-edge weights (a weighting function and/or w0); paired kernel only
+    int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)
+    int32_t has_w0;       // the exact self pair takes weight w0
+    double w_r0, w_c, w_d, w_m, w_0;
     double cutoff2;
     double soap_scale;    // pi^{3/2}
     double ynorm[kTri];   // N_lm (times sqrt 2 for m > 0), index l(l+1)/2 + m
@@ -82,6 +86,27 @@ struct SoapPointers {
     int64_t center_begin;
     int64_t center_end;
 };
+
+// Radial weight of one edge (soap_weight, cpp/src/standalone/soap.cpp:389-420,
+// without its species factor, which the kernels apply per species): the
+// weighting function of the distance, replaced by w0 for the exact self pair.
+__device__ __forceinline__ double soap_edge_weight(const SoapTables& tab, double d2, bool exact_self) {
+    double value = 1.0;
+    if (tab.weight_fn != 0) {
+        const double distance = sqrt(d2);
+        const double ratio = distance / tab.w_r0;
+        if (tab.weight_fn == 1) {
+            value = distance > tab.w_r0 ? 0.0
+                                        : tab.w_c * pow(1.0 + 2.0 * ratio * ratio * ratio - 3.0 * ratio * ratio, tab.w_m);
+        } else if (tab.weight_fn == 2) {
+            value = tab.w_c / (tab.w_d + pow(ratio, tab.w_m));
+        } else {
+            value = tab.w_c / (tab.w_d + exp(-ratio));
+        }
+    }
+    if (exact_self && tab.has_w0) value = tab.w_0;
+    return value;
+}
 
 // Real regular solid harmonics of one displacement into a padded row: the
 // block of degree l starts at l (l + 1) (even, so 16-byte aligned) and holds

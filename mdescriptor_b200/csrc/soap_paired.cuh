@@ -1,0 +1,517 @@
+// SOAP centre kernel with paired radial channels (sm_100a, IEEE fp64).
+//
+// Same arithmetic as soap_center_kernel (soap.cuh, reference
+// cpp/src/standalone/soap.cpp:598-1017); three things differ:
+//
+//   * Channel pairs.  With l_max = L compile-time, the (L+1) degrees of one
+//     radial index k are grouped as {L}, {L-1, 0}, {L-2, 1}, ...: every group
+//     holds at most 2L+1 harmonic components, and lane (g, k) owns group g of
+//     radial index k for every species.  A lane therefore keeps 2L+1
+//     accumulators per species (13 for L = 6, against 13 + 5 when channels
+//     are dealt out by degree) and evaluates two radial factors per edge.
+//     The harmonic row of an edge is stored group by group ("views"), so a
+//     lane reads its components as one contiguous run; the component m of a
+//     lane belongs to the first channel below the split 2 l_A + 1 and to the
+//     second above it, and since every split is odd, each pair of components
+//     (2p+1, 2p+2) above the smallest split picks its radial factor with one
+//     select per edge.
+//   * Prefiltered walk.  The binning kernel stores every atom's wrapped
+//     position and species in bin order (BinView::spos).  A candidate is
+//     first tested on those (one coalesced 32-byte load, six fp64 operations,
+//     against the structure's pre_cut2 = (cutoff + margin)^2, the margin four
+//     orders above any rounding difference); survivors are compacted and
+//     tested exactly by accept_candidate (the reference's own arithmetic) 32
+//     at a time, so the pair set and the displacement bits stay those of the
+//     reference graph.
+//   * Radial factors by scaled_exp (prefactor folded, 2^m through the
+//     exponent field); species weights multiply the raw sums once, at the
+//     flush, instead of every edge.
+//
+// The coefficient block layout, the beta transform and the power spectrum on
+// the fp64 tensor cores are dmma.cuh's, as in soap_center_kernel.
+#pragma once
+
+#include "soap.cuh"
+
+namespace mdsoap {
+
+namespace paired {
+
+template <int L>
+struct Layout {
+    static constexpr int G = 1 + (L + 1) / 2;  // channel groups per radial index
+    static constexpr int W = 2 * L + 1;        // accumulators per species per lane
+    static constexpr int VS = W + 1;           // view stride (even: 16-byte loads)
+    // Harmonic row of one edge (doubles): G views, padded to = 2 (mod 4) so
+    // that the lane-per-edge row writes spread over 8 bank pairs.
+    static constexpr int ROW = G * VS + ((2 - (G * VS) % 4) + 4) % 4;
+    __host__ __device__ static constexpr int la(int g) { return g == 0 ? L : L - g; }
+    __host__ __device__ static constexpr int lb(int g) { return (g == 0 || g - 1 >= L - g) ? -1 : g - 1; }
+    static constexpr int LAMIN = la(G - 1);    // smallest first-channel degree
+    static constexpr int NSEL = L - LAMIN;     // radial-factor selects per edge
+    // Offset of harmonic component j of degree l in the row.
+    __host__ __device__ static constexpr int pos(int l, int j) {
+        for (int g = 0; g < G; ++g) {
+            if (la(g) == l) return g * VS + j;
+            if (lb(g) == l) return g * VS + 2 * la(g) + 1 + j;
+        }
+        return 0;
+    }
+};
+
+// Per-warp shared-memory region (bytes); the harmonic rows follow.
+constexpr int kSegBytes = 544;                     // seg_prefix[40] seg_start[32] seg_t[32] perm[32]
+constexpr int kSegOffBytes = 3 * 32 * 8;           // per-segment offset vectors
+constexpr int kPreQueue = 64;                      // prefilter survivors awaiting the exact test
+constexpr int kPreBytes = 3 * kPreQueue * 4;
+constexpr int kEdgeBytes = kPending * (5 * 8 + 4); // dx dy dz r2 weight + species
+constexpr int kHeaderBytes = kSegBytes + kSegOffBytes + kPreBytes + kEdgeBytes;
+static_assert(kHeaderBytes % 16 == 0, "harmonic rows must start 16-byte aligned");
+
+// Real regular solid harmonics of one displacement into the paired row
+// (soap.cpp:101-216, generic Cartesian recurrence; within a degree, j = l - m
+// is the cos part, j = l (m = 0), j = l + m the sin part).
+// Every loop index is a compile-time constant, so each row offset is one.
+template <int L>
+__device__ __forceinline__ void harmonics_row(const SoapTables& tab, double x, double y, double z, double r2,
+                                              double* __restrict__ out) {
+    using P = Layout<L>;
+    double dr = 1.0, di = 0.0;
+    static_for<0, L + 1>([&](auto mc) {
+        constexpr int m = decltype(mc)::value;
+        if constexpr (m > 0) {
+            const double f = -(2.0 * m - 1.0);
+            const double nr = f * (x * dr - y * di);
+            const double ni = f * (x * di + y * dr);
+            dr = nr;
+            di = ni;
+        }
+        double pr2 = dr, pi2 = di;
+        constexpr int id = m * (m + 1) / 2 + m;
+        if constexpr (m == 0) {
+            out[P::pos(0, 0)] = tab.ynorm[0] * pr2;
+        } else {
+            constexpr int o1 = P::pos(m, 0), o2 = P::pos(m, 2 * m);
+            out[o1] = tab.ynorm[id] * pr2;
+            out[o2] = tab.ynorm[id] * pi2;
+        }
+        if constexpr (m < L) {
+            const double c = (2.0 * m + 1.0) * z;
+            double pr1 = c * dr, pi1 = c * di;
+            {
+                constexpr int l = m + 1;
+                constexpr int i = l * (l + 1) / 2 + m;
+                constexpr int o1 = P::pos(l, l - m), o2 = P::pos(l, l + m);
+                out[o1] = tab.ynorm[i] * pr1;
+                if constexpr (m > 0) out[o2] = tab.ynorm[i] * pi1;
+            }
+            static_for<m + 2, L + 1>([&](auto lc) {
+                constexpr int l = decltype(lc)::value;
+                constexpr int i = l * (l + 1) / 2 + m;
+                constexpr int o1 = P::pos(l, l - m), o2 = P::pos(l, l + m);
+                const double a = tab.yra[i] * z;
+                const double b = tab.yrb[i] * r2;
+                const double nr = fma(a, pr1, -b * pr2);
+                const double ni = fma(a, pi1, -b * pi2);
+                pr2 = pr1;
+                pi2 = pi1;
+                pr1 = nr;
+                pi1 = ni;
+                out[o1] = tab.ynorm[i] * nr;
+                if constexpr (m > 0) out[o2] = tab.ynorm[i] * ni;
+            });
+        }
+    });
+}
+
+}  // namespace paired
+
+// One warp per centre.  MAXT species register banks per pass over the
+// neighbourhood; L = l_max exactly; PRECISE selects the radial-factor
+// accuracy (float64 rows need the full one); MINB resident CTAs per SM.
+template <int MAXT, int L, bool PRECISE, int MINB>
+__global__ void __launch_bounds__(kWarps * 32, MINB)
+soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
+    using P = paired::Layout<L>;
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int S = tab.n_species, n = tab.n_max;
+    // CTA-shared: exp table (32 doubles), then beta as [l][n][k] scaled by
+    // pi^{3/2} and zero padded to 8 x 8.
+    double* etab = reinterpret_cast<double*>(smem);
+    if (threadIdx.x < 32) etab[threadIdx.x] = kExp2Table[threadIdx.x];
+    double* bt = reinterpret_cast<double*>(smem + 256);
+    for (int i = threadIdx.x; i < (L + 1) * 64; i += blockDim.x) {
+        const int l = i / 64, nn = (i / 8) % 8, k = i % 8;
+        bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
+    }
+    constexpr int kShared = 256 + (L + 1) * 64 * 8;
+    __syncthreads();
+    const int64_t center = p.center_begin + (int64_t)blockIdx.x * kWarps + warp;
+    if (center >= p.center_end) return;
+
+    unsigned char* region = smem + kShared + (size_t)warp * tab.warp_bytes;
+    int* seg_prefix = reinterpret_cast<int*>(region);  // 40
+    int* seg_start = seg_prefix + 40;                   // 32
+    int* seg_t = seg_start + 32;                        // 32
+    int* perm = seg_t + 32;                             // 32
+    double* seg_off = reinterpret_cast<double*>(region + paired::kSegBytes);  // [3][32]
+    int* qa = reinterpret_cast<int*>(region + paired::kSegBytes + paired::kSegOffBytes);
+    int* qt = qa + paired::kPreQueue;
+    int* qs = qt + paired::kPreQueue;
+    double* pdx = reinterpret_cast<double*>(region + paired::kSegBytes + paired::kSegOffBytes + paired::kPreBytes);
+    double* pdy = pdx + kPending;
+    double* pdz = pdy + kPending;
+    double* pr2 = pdz + kPending;
+    double* pw = pr2 + kPending;
+    int32_t* ptype = reinterpret_cast<int32_t*>(pw + kPending);
+    double* ybuf = reinterpret_cast<double*>(region + paired::kHeaderBytes);
+    const int64_t local = center - p.center_begin;
+    double* R = tab.r_global ? p.rbuf + local * tab.rsize : reinterpret_cast<double*>(region + tab.r_offset);
+
+    const BinView& bv = p.bins;
+    const StructInfo& si = bv.info[bv.struct_of[center]];
+    const int wi[3] = {bv.wrap[3 * center], bv.wrap[3 * center + 1], bv.wrap[3 * center + 2]};
+    double wpos[3];
+    wrapped_position(si, p.positions + 3 * center, bv.wrap + 3 * center, wpos);
+    const int chunk = tab.chunk;
+
+    // This lane's channel pair: group g of radial index k.
+    const int g = lane / n, k = lane - (lane / n) * n;
+    const bool lane_on = g < P::G;
+    const int lA = lane_on ? (g == 0 ? L : L - g) : 0;
+    const int lB = (lane_on && g > 0 && g - 1 < L - g) ? g - 1 : -1;
+    const int split = 2 * lA + 1;
+    double prefA = 0.0, nEA = 0.0, prefB = 0.0, nEB = 0.0;
+    if (lane_on) {
+        const RadialItem a = p.items[(L - lA) * n + k];  // items are sorted by l descending
+        prefA = a.prefactor;
+        nEA = -a.exponent;
+        if (lB >= 0) {
+            const RadialItem b = p.items[(L - lB) * n + k];
+            prefB = b.prefactor;
+            nEB = -b.exponent;
+        }
+    }
+    bool first_above[P::NSEL > 0 ? P::NSEL : 1];
+#pragma unroll
+    for (int q = 0; q < P::NSEL; ++q) first_above[q] = lA > P::LAMIN + q;
+    const int view = lane_on ? g * P::VS : 0;
+
+    // Candidate walk geometry.
+    const int Mx = si.M[0], My = si.M[1], Mz = si.M[2];
+    const int Kx = si.K[0], Ky = si.K[1], Kz = si.K[2];
+    const int periodic = si.periodic;
+    const int cb = bv.bin_of[center];
+    const int cx = cb % Mx, cy = (cb / Mx) % My, cz = cb / (Mx * My);
+    const int64_t bb = si.bin_base;
+    const int64_t ab = si.atom_begin;
+    const int xlo = cx - Kx, xhi = cx + Kx;
+    const int tx0 = periodic ? floor_div(xlo, Mx) : 0;
+    const int nxs = periodic ? floor_div(xhi, Mx) - tx0 + 1 : 1;
+    const int wy = 2 * Ky + 1;
+    const int entries = wy * (2 * Kz + 1) * nxs;
+    const double pre2 = si.pre_cut2;
+
+    for (int tb = 0; tb < S; tb += MAXT) {
+        const int te = min(S, tb + MAXT);
+        double acc[MAXT][P::W];
+#pragma unroll
+        for (int t = 0; t < MAXT; ++t)
+#pragma unroll
+            for (int m = 0; m < P::W; ++m) acc[t][m] = 0.0;
+
+        // One edge into bank TT.
+        auto accumulate = [&](auto bank, double gA, double gB, int e) {
+            constexpr int TT = decltype(bank)::value;
+            double gs[P::NSEL > 0 ? P::NSEL : 1];
+#pragma unroll
+            for (int q = 0; q < P::NSEL; ++q) gs[q] = first_above[q] ? gA : gB;
+            const double2* yv = reinterpret_cast<const double2*>(ybuf + e * P::ROW + view);
+#pragma unroll
+            for (int mm = 0; mm < (P::W + 1) / 2; ++mm) {
+                const double2 y = yv[mm];
+                const int m0 = 2 * mm, m1 = 2 * mm + 1;
+                const double g0 = m0 < 2 * P::LAMIN + 1 ? gA : gs[(m0 - 1) / 2 - P::LAMIN];
+                acc[TT][m0] = fma(g0, y.x, acc[TT][m0]);
+                if (m1 < P::W) {
+                    const double g1 = m1 < 2 * P::LAMIN + 1 ? gA : gs[(m1 - 1) / 2 - P::LAMIN];
+                    acc[TT][m1] = fma(g1, y.y, acc[TT][m1]);
+                }
+            }
+        };
+        auto process = [&](int count) {
+            if (lane < count) paired::harmonics_row<L>(tab, pdx[lane], pdy[lane], pdz[lane], pr2[lane],
+                                                       ybuf + lane * P::ROW);
+            // Stable counting sort of the chunk by species bank.
+            const int mine = lane < count ? ptype[lane] : MAXT;
+            const unsigned lt = (1u << lane) - 1u;
+            int run_start[MAXT + 1];
+            run_start[0] = 0;
+            int rank = 0;
+#pragma unroll
+            for (int tt = 0; tt < MAXT; ++tt) {
+                const unsigned msk = __ballot_sync(0xffffffffu, mine == tt);
+                if (mine == tt) rank = run_start[tt] + __popc(msk & lt);
+                run_start[tt + 1] = run_start[tt] + __popc(msk);
+            }
+            if (lane < count) perm[rank] = lane;
+            __syncwarp();
+            const bool weighted = tab.weighted != 0;
+            static_for<0, MAXT>([&](auto bank) {
+                constexpr int TT = decltype(bank)::value;
+                const int end = run_start[TT + 1];
+                int i = run_start[TT];
+                for (; i + 1 < end; i += 2) {
+                    const int ea = perm[i], eb = perm[i + 1];
+                    const double ua = pr2[ea], ub = pr2[eb];
+                    double gAa = scaled_exp<PRECISE>(nEA * ua, prefA, etab);
+                    double gBa = scaled_exp<PRECISE>(nEB * ua, prefB, etab);
+                    double gAb = scaled_exp<PRECISE>(nEA * ub, prefA, etab);
+                    double gBb = scaled_exp<PRECISE>(nEB * ub, prefB, etab);
+                    if (weighted) {
+                        const double wa = pw[ea], wb = pw[eb];
+                        gAa *= wa;
+                        gBa *= wa;
+                        gAb *= wb;
+                        gBb *= wb;
+                    }
+                    accumulate(bank, gAa, gBa, ea);
+                    accumulate(bank, gAb, gBb, eb);
+                }
+                if (i < end) {
+                    const int ea = perm[i];
+                    const double ua = pr2[ea];
+                    double gAa = scaled_exp<PRECISE>(nEA * ua, prefA, etab);
+                    double gBa = scaled_exp<PRECISE>(nEB * ua, prefB, etab);
+                    if (weighted) {
+                        const double wa = pw[ea];
+                        gAa *= wa;
+                        gBa *= wa;
+                    }
+                    accumulate(bank, gAa, gBa, ea);
+                }
+            });
+            __syncwarp();
+        };
+
+        int qn = 0;      // prefilter survivors queued (warp-uniform)
+        int pcount = 0;  // accepted edges queued (warp-uniform)
+        // Exact test of queued survivors [0, count): the reference's geometry.
+        auto exact_stage = [&](int count) {
+            bool ok = false;
+            double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0, w = 1.0;
+            int t = 0;
+            if (lane < count) {
+                const int a = qa[lane], tp = qt[lane];
+                t = qs[lane];
+                const int j = bv.sorted[ab + a];
+                int nimg[3];
+                ok = accept_candidate(si, bv, p.positions, center, wi, j, (tp & 1023) - 512,
+                                      ((tp >> 10) & 1023) - 512, ((tp >> 20) & 1023) - 512, tab.cutoff2, nimg, dx,
+                                      dy, dz, d2);
+                if (ok && tab.weighted)
+                    w = soap_edge_weight(tab, d2, ab + j == center && nimg[0] == 0 && nimg[1] == 0 && nimg[2] == 0);
+            }
+            const unsigned mask = __ballot_sync(0xffffffffu, ok);
+            if (ok) {
+                const int q = pcount + __popc(mask & ((1u << lane) - 1u));
+                pdx[q] = dx;
+                pdy[q] = dy;
+                pdz[q] = dz;
+                pr2[q] = d2;
+                pw[q] = w;
+                ptype[q] = t - tb;
+            }
+            pcount += __popc(mask);
+            // The edge queue holds < chunk entries before this stage adds at
+            // most 32, so it never exceeds chunk + 31 <= 63 < kPending.
+            while (pcount >= chunk) {
+                __syncwarp();
+                process(chunk);
+                const int rem = pcount - chunk;
+                double sx = 0.0, sy = 0.0, sz = 0.0, sr = 0.0, sw = 0.0;
+                int st = 0;
+                if (lane < rem) {
+                    sx = pdx[chunk + lane];
+                    sy = pdy[chunk + lane];
+                    sz = pdz[chunk + lane];
+                    sr = pr2[chunk + lane];
+                    sw = pw[chunk + lane];
+                    st = ptype[chunk + lane];
+                }
+                __syncwarp();
+                if (lane < rem) {
+                    pdx[lane] = sx;
+                    pdy[lane] = sy;
+                    pdz[lane] = sz;
+                    pr2[lane] = sr;
+                    pw[lane] = sw;
+                    ptype[lane] = st;
+                }
+                __syncwarp();
+                pcount = rem;
+            }
+        };
+
+        for (int round = 0; round < entries; round += 32) {
+            // Segment of this lane: one (y, z) bin row at one x image.
+            const int e = round + lane;
+            bool valid = e < entries;
+            int start = 0, len = 0, tpack = 0;
+            double ox = 0.0, oy = 0.0, oz = 0.0;
+            if (valid) {
+                const int row = e / nxs;
+                const int xs = e - row * nxs;
+                const int dz = row / wy - Kz;
+                const int dy = row - (row / wy) * wy - Ky;
+                const int ey = cy + dy, ez = cz + dz;
+                int ty = 0, tz = 0, tx = 0, b0, b1;
+                if (periodic) {
+                    ty = floor_div(ey, My);
+                    tz = floor_div(ez, Mz);
+                    tx = tx0 + xs;
+                    b0 = max(xlo, tx * Mx) - tx * Mx;
+                    b1 = min(xhi, tx * Mx + Mx - 1) - tx * Mx;
+                } else {
+                    valid = ey >= 0 && ey < My && ez >= 0 && ez < Mz;
+                    b0 = max(xlo, 0);
+                    b1 = min(xhi, Mx - 1);
+                }
+                valid = valid && b0 <= b1;
+                if (valid) {
+                    const int64_t rowbase = bb + Mx * ((ey - ty * My) + My * (ez - tz * Mz));
+                    start = bv.bin_start[rowbase + b0];
+                    len = bv.bin_start[rowbase + b1 + 1] - start;
+                    tpack = (tx + 512) | ((ty + 512) << 10) | ((tz + 512) << 20);
+                    // Approximate displacement = wrapped neighbour + t.A - wrapped centre.
+                    const double fx = (double)tx, fy = (double)ty, fz = (double)tz;
+                    ox = fma(fz, si.cell[6], fma(fy, si.cell[3], fx * si.cell[0])) - wpos[0];
+                    oy = fma(fz, si.cell[7], fma(fy, si.cell[4], fx * si.cell[1])) - wpos[1];
+                    oz = fma(fz, si.cell[8], fma(fy, si.cell[5], fx * si.cell[2])) - wpos[2];
+                }
+            }
+            int incl = len;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int up = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += up;
+            }
+            const int total = __shfl_sync(0xffffffffu, incl, 31);
+            __syncwarp();
+            seg_prefix[lane] = incl - len;
+            seg_start[lane] = start;
+            seg_t[lane] = tpack;
+            seg_off[lane] = ox;
+            seg_off[32 + lane] = oy;
+            seg_off[64 + lane] = oz;
+            __syncwarp();
+            for (int q0 = 0; q0 < total; q0 += 32) {
+                const int q = q0 + lane;
+                bool pass = false;
+                int a = 0, ty = 0, i = 0;
+                if (q < total) {
+#pragma unroll
+                    for (int step = 16; step > 0; step >>= 1)
+                        if (seg_prefix[i + step] <= q) i += step;
+                    a = seg_start[i] + (q - seg_prefix[i]);
+                    const double4 sp = bv.spos[ab + a];
+                    ty = (int)sp.w;
+                    const double dx = sp.x + seg_off[i], dy = sp.y + seg_off[32 + i], dz = sp.z + seg_off[64 + i];
+                    pass = ty >= tb && ty < te && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
+                }
+                const unsigned mask = __ballot_sync(0xffffffffu, pass);
+                if (pass) {
+                    const int slot = qn + __popc(mask & ((1u << lane) - 1u));
+                    qa[slot] = a;
+                    qt[slot] = seg_t[i];
+                    qs[slot] = ty;
+                }
+                qn += __popc(mask);
+                // The survivor queue holds < 32 entries before a candidate
+                // batch adds at most 32: at most 63 < kPreQueue.
+                if (qn >= 32) {
+                    __syncwarp();
+                    exact_stage(32);
+                    const int rem = qn - 32;
+                    int sa = 0, st = 0, ss = 0;
+                    if (lane < rem) {
+                        sa = qa[32 + lane];
+                        st = qt[32 + lane];
+                        ss = qs[32 + lane];
+                    }
+                    __syncwarp();
+                    if (lane < rem) {
+                        qa[lane] = sa;
+                        qt[lane] = st;
+                        qs[lane] = ss;
+                    }
+                    qn = rem;
+                }
+                __syncwarp();
+            }
+        }
+        __syncwarp();
+        if (qn > 0) exact_stage(qn);
+        __syncwarp();
+        if (pcount > 0) process(pcount);
+
+        // Flush the raw sums times the species weight: row (t, k), degree l
+        // at columns col_off(l) .. + kpad(l), padding written as 0.
+        if (lane_on) {
+            const int colA = mma::col_off(lA);
+            const int colB = lB >= 0 ? mma::col_off(lB) - split : 0;
+            const int padA = mma::kpad(lA), padB = lB >= 0 ? mma::kpad(lB) : 0;
+#pragma unroll
+            for (int tt = 0; tt < MAXT; ++tt) {
+                const int t = tb + tt;
+                if (t < te) {
+                    const double w = tab.species_weight[t];
+                    double* row = R + (t * n + k) * tab.rs;
+#pragma unroll
+                    for (int m = 0; m < P::W; ++m) {
+                        if (m < split)
+                            row[colA + m] = w * acc[tt][m];
+                        else if (lB >= 0)
+                            row[colB + m] = w * acc[tt][m];
+                    }
+                    for (int m = split; m < padA; ++m) row[colA + m] = 0.0;
+                    if (lB >= 0)
+                        for (int m = 2 * lB + 1; m < padB; ++m) row[colB + split + m] = 0.0;
+                }
+            }
+        }
+        __syncwarp();
+    }
+
+    const int gq = lane >> 2, qq = lane & 3, R_rows = tab.rows;
+    mma::beta_mma<L>(bt, R, tab.rs, L, S, n, gq, qq);
+    __syncwarp();
+    const mma::FeatureMap fm{S, n, L, R_rows, tab.n_magic};
+    if (tab.average == 0) {
+        const int64_t row = center - p.out_row_begin;
+        if (tab.out_f64)
+            mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, static_cast<double*>(p.out) + row * tab.features, gq,
+                              qq);
+        else
+            mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, static_cast<float*>(p.out) + row * tab.features, gq,
+                              qq);
+    } else if (tab.average == 1) {
+        // The structure kernel's layout: [l][r][m], rows padded to 2l+2.
+        double* dst = p.cbuf + local * tab.csize;
+        for (int l = 0; l <= L; ++l) {
+            const int pad = 2 * l + 2;
+            double* dl = dst + cblock(S, n, l);
+            const double* src = R + mma::col_off(l);
+            for (int i = lane; i < R_rows * pad; i += 32) {
+                const int r = i / pad, m = i - r * pad;
+                dl[i] = m < 2 * l + 1 ? src[r * tab.rs + m] : 0.0;
+            }
+        }
+    } else {
+        mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, gq, qq);
+    }
+}
+
+}  // namespace mdsoap

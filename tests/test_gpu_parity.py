@@ -14,7 +14,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from _util import (AGREE_FLOOR, AGREE_TOL, F32_FLOOR, F64_FLOOR, F64_TOL, assert_features_close,
+from _util import (AGREE_FLOOR, AGREE_TOL, F32_FLOOR, F32_TOL, F64_FLOOR, F64_TOL, assert_features_close,
                    assert_graph_bit_exact, max_rel_err)
 from mdescriptor_b200 import workloads
 from mdescriptor_b200.basis import basis_gto, graph_cutoff
@@ -246,14 +246,20 @@ def test_invalid_inputs_raise(cuda_device):
 
 
 def test_deterministic_and_dtype_consistent(cuda_device):
+    """Repeated runs give the same bits; float32 rows agree with the float64
+    rows within the float32 bound (float32 plans evaluate the radial factors
+    to a few 1e-14 instead of full fp64 accuracy, so a row can differ from the
+    rounded float64 row in its last bit)."""
     meta = CFG_META["cfg2"]
     batch = batch_from(CFG, "cfg2/input")
     soap64 = soap_for(meta, "off", "float64")
     a = soap64.compute(batch, devices=[cuda_device])
     b = soap64.compute(batch, devices=[cuda_device])
     np.testing.assert_array_equal(a, b)
-    f32 = soap_for(meta, "off", "float32").compute(batch, devices=[cuda_device])
-    np.testing.assert_array_equal(f32, a.astype(np.float32))
+    soap32 = soap_for(meta, "off", "float32")
+    f32 = soap32.compute(batch, devices=[cuda_device])
+    np.testing.assert_array_equal(f32, soap32.compute(batch, devices=[cuda_device]))
+    assert max_rel_err(f32, a, F32_FLOOR) <= F32_TOL
 
 
 def test_blocked_pipeline_matches_single_block(cuda_device, monkeypatch):
