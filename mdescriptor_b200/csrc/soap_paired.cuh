@@ -296,50 +296,38 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             __syncwarp();
         };
 
+        // The walk runs as one flat loop in which each stage has a single
+        // call site (the hot code is then inlined once, which keeps it in the
+        // instruction cache).  Every step takes the first applicable action:
+        //   1. a full chunk of accepted edges (or the last edges) -> process;
+        //   2. 32 prefilter survivors (or the last ones) -> exact test;
+        //   3. candidates left in this round -> prefilter 32 of them;
+        //   4. segments left -> set up the next round of 32 segments;
+        //   5. otherwise done.
+        // Stage 1 runs whenever pcount >= chunk, so stage 2 starts with
+        // pcount < chunk and the edge queue never exceeds chunk + 31 <= 63 <
+        // kPending; likewise stage 2 runs whenever qn >= 32, so stage 3 leaves
+        // at most 63 < kPreQueue survivors queued.
         int qn = 0;      // prefilter survivors queued (warp-uniform)
         int pcount = 0;  // accepted edges queued (warp-uniform)
-        // Exact test of queued survivors [0, count): the reference's geometry.
-        auto exact_stage = [&](int count) {
-            bool ok = false;
-            double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0, w = 1.0;
-            int t = 0;
-            if (lane < count) {
-                const int a = qa[lane], tp = qt[lane];
-                t = qs[lane];
-                const int j = bv.sorted[ab + a];
-                int nimg[3];
-                ok = accept_candidate(si, bv, p.positions, center, wi, j, (tp & 1023) - 512,
-                                      ((tp >> 10) & 1023) - 512, ((tp >> 20) & 1023) - 512, tab.cutoff2, nimg, dx,
-                                      dy, dz, d2);
-                if (ok && tab.weighted)
-                    w = soap_edge_weight(tab, d2, ab + j == center && nimg[0] == 0 && nimg[1] == 0 && nimg[2] == 0);
-            }
-            const unsigned mask = __ballot_sync(0xffffffffu, ok);
-            if (ok) {
-                const int q = pcount + __popc(mask & ((1u << lane) - 1u));
-                pdx[q] = dx;
-                pdy[q] = dy;
-                pdz[q] = dz;
-                pr2[q] = d2;
-                pw[q] = w;
-                ptype[q] = t - tb;
-            }
-            pcount += __popc(mask);
-            // The edge queue holds < chunk entries before this stage adds at
-            // most 32, so it never exceeds chunk + 31 <= 63 < kPending.
-            while (pcount >= chunk) {
+        int round = 0;   // next segment index
+        int q0 = 0, total = 0;
+        while (true) {
+            const bool walk_done = q0 >= total && round >= entries;
+            if (pcount >= chunk || (walk_done && qn == 0 && pcount > 0)) {
+                const int count = min(pcount, chunk);
                 __syncwarp();
-                process(chunk);
-                const int rem = pcount - chunk;
+                process(count);
+                const int rem = pcount - count;
                 double sx = 0.0, sy = 0.0, sz = 0.0, sr = 0.0, sw = 0.0;
                 int st = 0;
                 if (lane < rem) {
-                    sx = pdx[chunk + lane];
-                    sy = pdy[chunk + lane];
-                    sz = pdz[chunk + lane];
-                    sr = pr2[chunk + lane];
-                    sw = pw[chunk + lane];
-                    st = ptype[chunk + lane];
+                    sx = pdx[count + lane];
+                    sy = pdy[count + lane];
+                    sz = pdz[count + lane];
+                    sr = pr2[count + lane];
+                    sw = pw[count + lane];
+                    st = ptype[count + lane];
                 }
                 __syncwarp();
                 if (lane < rem) {
@@ -352,62 +340,53 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 }
                 __syncwarp();
                 pcount = rem;
-            }
-        };
-
-        for (int round = 0; round < entries; round += 32) {
-            // Segment of this lane: one (y, z) bin row at one x image.
-            const int e = round + lane;
-            bool valid = e < entries;
-            int start = 0, len = 0, tpack = 0;
-            double ox = 0.0, oy = 0.0, oz = 0.0;
-            if (valid) {
-                const int row = e / nxs;
-                const int xs = e - row * nxs;
-                const int dz = row / wy - Kz;
-                const int dy = row - (row / wy) * wy - Ky;
-                const int ey = cy + dy, ez = cz + dz;
-                int ty = 0, tz = 0, tx = 0, b0, b1;
-                if (periodic) {
-                    ty = floor_div(ey, My);
-                    tz = floor_div(ez, Mz);
-                    tx = tx0 + xs;
-                    b0 = max(xlo, tx * Mx) - tx * Mx;
-                    b1 = min(xhi, tx * Mx + Mx - 1) - tx * Mx;
-                } else {
-                    valid = ey >= 0 && ey < My && ez >= 0 && ez < Mz;
-                    b0 = max(xlo, 0);
-                    b1 = min(xhi, Mx - 1);
+            } else if (qn >= 32 || (walk_done && qn > 0)) {
+                // Exact test of queued survivors [0, count): the reference's geometry.
+                const int count = min(qn, 32);
+                __syncwarp();
+                bool ok = false;
+                double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0, w = 1.0;
+                int t = 0;
+                if (lane < count) {
+                    const int a = qa[lane], tp = qt[lane];
+                    t = qs[lane];
+                    const int j = bv.sorted[ab + a];
+                    int nimg[3];
+                    ok = accept_candidate(si, bv, p.positions, center, wi, j, (tp & 1023) - 512,
+                                          ((tp >> 10) & 1023) - 512, ((tp >> 20) & 1023) - 512, tab.cutoff2, nimg,
+                                          dx, dy, dz, d2);
+                    if (ok && tab.weighted)
+                        w = soap_edge_weight(tab, d2,
+                                             ab + j == center && nimg[0] == 0 && nimg[1] == 0 && nimg[2] == 0);
                 }
-                valid = valid && b0 <= b1;
-                if (valid) {
-                    const int64_t rowbase = bb + Mx * ((ey - ty * My) + My * (ez - tz * Mz));
-                    start = bv.bin_start[rowbase + b0];
-                    len = bv.bin_start[rowbase + b1 + 1] - start;
-                    tpack = (tx + 512) | ((ty + 512) << 10) | ((tz + 512) << 20);
-                    // Approximate displacement = wrapped neighbour + t.A - wrapped centre.
-                    const double fx = (double)tx, fy = (double)ty, fz = (double)tz;
-                    ox = fma(fz, si.cell[6], fma(fy, si.cell[3], fx * si.cell[0])) - wpos[0];
-                    oy = fma(fz, si.cell[7], fma(fy, si.cell[4], fx * si.cell[1])) - wpos[1];
-                    oz = fma(fz, si.cell[8], fma(fy, si.cell[5], fx * si.cell[2])) - wpos[2];
+                const unsigned mask = __ballot_sync(0xffffffffu, ok);
+                if (ok) {
+                    const int q = pcount + __popc(mask & ((1u << lane) - 1u));
+                    pdx[q] = dx;
+                    pdy[q] = dy;
+                    pdz[q] = dz;
+                    pr2[q] = d2;
+                    pw[q] = w;
+                    ptype[q] = t - tb;
                 }
-            }
-            int incl = len;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int up = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += up;
-            }
-            const int total = __shfl_sync(0xffffffffu, incl, 31);
-            __syncwarp();
-            seg_prefix[lane] = incl - len;
-            seg_start[lane] = start;
-            seg_t[lane] = tpack;
-            seg_off[lane] = ox;
-            seg_off[32 + lane] = oy;
-            seg_off[64 + lane] = oz;
-            __syncwarp();
-            for (int q0 = 0; q0 < total; q0 += 32) {
+                pcount += __popc(mask);
+                const int rem = qn - count;
+                int sa = 0, st = 0, ss = 0;
+                if (lane < rem) {
+                    sa = qa[count + lane];
+                    st = qt[count + lane];
+                    ss = qs[count + lane];
+                }
+                __syncwarp();
+                if (lane < rem) {
+                    qa[lane] = sa;
+                    qt[lane] = st;
+                    qs[lane] = ss;
+                }
+                __syncwarp();
+                qn = rem;
+            } else if (q0 < total) {
+                // Prefilter candidates q0 .. q0 + 31 of this round.
                 const int q = q0 + lane;
                 bool pass = false;
                 int a = 0, ty = 0, i = 0;
@@ -429,33 +408,66 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     qs[slot] = ty;
                 }
                 qn += __popc(mask);
-                // The survivor queue holds < 32 entries before a candidate
-                // batch adds at most 32: at most 63 < kPreQueue.
-                if (qn >= 32) {
-                    __syncwarp();
-                    exact_stage(32);
-                    const int rem = qn - 32;
-                    int sa = 0, st = 0, ss = 0;
-                    if (lane < rem) {
-                        sa = qa[32 + lane];
-                        st = qt[32 + lane];
-                        ss = qs[32 + lane];
-                    }
-                    __syncwarp();
-                    if (lane < rem) {
-                        qa[lane] = sa;
-                        qt[lane] = st;
-                        qs[lane] = ss;
-                    }
-                    qn = rem;
-                }
+                q0 += 32;
                 __syncwarp();
+            } else if (round < entries) {
+                // Segments round .. round + 31: one (y, z) bin row at one x image each.
+                const int e = round + lane;
+                bool valid = e < entries;
+                int start = 0, len = 0, tpack = 0;
+                double ox = 0.0, oy = 0.0, oz = 0.0;
+                if (valid) {
+                    const int row = e / nxs;
+                    const int xs = e - row * nxs;
+                    const int dz = row / wy - Kz;
+                    const int dy = row - (row / wy) * wy - Ky;
+                    const int ey = cy + dy, ez = cz + dz;
+                    int ty = 0, tz = 0, tx = 0, b0, b1;
+                    if (periodic) {
+                        ty = floor_div(ey, My);
+                        tz = floor_div(ez, Mz);
+                        tx = tx0 + xs;
+                        b0 = max(xlo, tx * Mx) - tx * Mx;
+                        b1 = min(xhi, tx * Mx + Mx - 1) - tx * Mx;
+                    } else {
+                        valid = ey >= 0 && ey < My && ez >= 0 && ez < Mz;
+                        b0 = max(xlo, 0);
+                        b1 = min(xhi, Mx - 1);
+                    }
+                    valid = valid && b0 <= b1;
+                    if (valid) {
+                        const int64_t rowbase = bb + Mx * ((ey - ty * My) + My * (ez - tz * Mz));
+                        start = bv.bin_start[rowbase + b0];
+                        len = bv.bin_start[rowbase + b1 + 1] - start;
+                        tpack = (tx + 512) | ((ty + 512) << 10) | ((tz + 512) << 20);
+                        // Approximate displacement = wrapped neighbour + t.A - wrapped centre.
+                        const double fx = (double)tx, fy = (double)ty, fz = (double)tz;
+                        ox = fma(fz, si.cell[6], fma(fy, si.cell[3], fx * si.cell[0])) - wpos[0];
+                        oy = fma(fz, si.cell[7], fma(fy, si.cell[4], fx * si.cell[1])) - wpos[1];
+                        oz = fma(fz, si.cell[8], fma(fy, si.cell[5], fx * si.cell[2])) - wpos[2];
+                    }
+                }
+                int incl = len;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int up = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += up;
+                }
+                total = __shfl_sync(0xffffffffu, incl, 31);
+                q0 = 0;
+                round += 32;
+                __syncwarp();
+                seg_prefix[lane] = incl - len;
+                seg_start[lane] = start;
+                seg_t[lane] = tpack;
+                seg_off[lane] = ox;
+                seg_off[32 + lane] = oy;
+                seg_off[64 + lane] = oz;
+                __syncwarp();
+            } else {
+                break;
             }
         }
-        __syncwarp();
-        if (qn > 0) exact_stage(qn);
-        __syncwarp();
-        if (pcount > 0) process(pcount);
 
         // Flush the raw sums times the species weight: row (t, k), degree l
         // at columns col_off(l) .. + kpad(l), padding written as 0.
