@@ -196,6 +196,117 @@ __device__ __forceinline__ void power_mma(const FeatureMap& fm, const double* __
     }
 }
 
+// ---------------------------------------------------------------------------
+// n_max == 8 tail: one species is exactly one 8-row block of the coefficient
+// block, so every product tile is one species pair.
+
+// In-place beta transform, two species per batch: all loads of a batch, then
+// its tensor-core products, then its stores (soap.cpp:915-926).
+template <int L>
+__device__ __forceinline__ void beta_n8(const double* __restrict__ bt, double* __restrict__ reg, int rs, int S, int g,
+                                        int q) {
+    static_for<0, L + 1>([&](auto lc) {
+        constexpr int l = decltype(lc)::value;
+        constexpr int KP = kpad(l), MB = (KP + 7) / 8, C0 = col_off(l);
+        const double a0 = bt[(l * 8 + g) * 8 + q];
+        const double a1 = bt[(l * 8 + g) * 8 + 4 + q];
+        for (int s = 0; s < S; s += 2) {
+            double b[2][MB][2], c[2][MB][2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const double* blk = reg + (s + u) * 8 * rs + C0;
+#pragma unroll
+                for (int mb = 0; mb < MB; ++mb) {
+                    const int m = 8 * mb + g;
+                    const bool ok = s + u < S && m < KP;
+                    b[u][mb][0] = ok ? blk[q * rs + m] : 0.0;
+                    b[u][mb][1] = ok ? blk[(q + 4) * rs + m] : 0.0;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+                for (int mb = 0; mb < MB; ++mb) {
+                    c[u][mb][0] = c[u][mb][1] = 0.0;
+                    dmma8(c[u][mb][0], c[u][mb][1], a0, b[u][mb][0]);
+                    dmma8(c[u][mb][0], c[u][mb][1], a1, b[u][mb][1]);
+                }
+            __syncwarp();
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                double* blk = reg + (s + u) * 8 * rs + C0;
+#pragma unroll
+                for (int mb = 0; mb < MB; ++mb) {
+                    const int mo = 8 * mb + 2 * q;
+                    if (s + u < S) {
+                        if (mo < KP) blk[g * rs + mo] = c[u][mb][0];
+                        if (mo + 1 < KP) blk[g * rs + mo + 1] = c[u][mb][1];
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    });
+}
+
+// Power spectrum with n_max == 8 (compression off, soap.cpp:997-1012): for
+// each species pair t1 <= t2 in feature order and each l, the 8 x 8 product
+// C_{t1,l} C_{t2,l}^T on the tensor cores.  Lane (g, q) holds rows n1 = g,
+// columns n2 = 2q, 2q+1: in an off-diagonal block those are features
+// base + 8 g + 2q (+1), so a warp stores 64 consecutive features per l; in a
+// diagonal block (n2 >= n1 kept) the offset is g*8 - g(g-1)/2 + (n2 - g).
+// Feature offsets fit in 32 bits (F < 2^31 for any plan).
+template <int L, class OutT>
+__device__ __forceinline__ void power_n8(const double* __restrict__ pref, const double* __restrict__ reg, int rs,
+                                         int S, OutT* __restrict__ out, int g, int q) {
+    const int od = 8 * g + 2 * q;
+    const int n2a = 2 * q, n2b = 2 * q + 1;
+    const bool va = n2a >= g, vb = n2b >= g;
+    const int dd = 8 * g - g * (g - 1) / 2 - g;  // diagonal offset of (g, n2) is dd + n2
+    const bool row_aligned = (reinterpret_cast<uintptr_t>(out) % (2 * sizeof(OutT))) == 0;
+    int base = 0;
+    for (int t1 = 0; t1 < S; ++t1) {
+        const double* A = reg + (t1 * 8 + g) * rs + q;
+        for (int t2 = t1; t2 < S; ++t2) {
+            const double* B = reg + (t2 * 8 + g) * rs + q;
+            double c[L + 1][2];
+            static_for<0, L + 1>([&](auto lc) {
+                constexpr int l = decltype(lc)::value;
+                c[l][0] = c[l][1] = 0.0;
+#pragma unroll
+                for (int kb = 0; kb < kpad(l); kb += 4) dmma8(c[l][0], c[l][1], A[col_off(l) + kb], B[col_off(l) + kb]);
+            });
+            if (t1 != t2) {
+#pragma unroll
+                for (int l = 0; l <= L; ++l) {
+                    OutT* dst = out + base + 64 * l + od;
+                    const double x = pref[l] * c[l][0], y = pref[l] * c[l][1];
+                    if (row_aligned) {
+                        store_pair(dst, x, y);
+                    } else {
+                        dst[0] = (OutT)x;
+                        dst[1] = (OutT)y;
+                    }
+                }
+                base += 64 * (L + 1);
+            } else {
+#pragma unroll
+                for (int l = 0; l <= L; ++l) {
+                    OutT* dst = out + base + 36 * l + dd;
+                    const double x = pref[l] * c[l][0], y = pref[l] * c[l][1];
+                    if (va && row_aligned && ((base + 36 * l + dd + n2a) & 1) == 0) {
+                        store_pair(dst + n2a, x, y);
+                    } else {
+                        if (va) dst[n2a] = (OutT)x;
+                        if (vb) dst[n2b] = (OutT)y;
+                    }
+                }
+                base += 36 * (L + 1);
+            }
+        }
+    }
+}
+
 }  // namespace mma
 
 }  // namespace mdsoap

@@ -498,17 +498,28 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     }
 
     const int gq = lane >> 2, qq = lane & 3, R_rows = tab.rows;
-    mma::beta_mma<L>(bt, R, tab.rs, L, S, n, gq, qq);
+    const bool n8 = n == 8;
+    if (n8)
+        mma::beta_n8<L>(bt, R, tab.rs, S, gq, qq);
+    else
+        mma::beta_mma<L>(bt, R, tab.rs, L, S, n, gq, qq);
     __syncwarp();
     const mma::FeatureMap fm{S, n, L, R_rows, tab.n_magic};
     if (tab.average == 0) {
         const int64_t row = center - p.out_row_begin;
-        if (tab.out_f64)
-            mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, static_cast<double*>(p.out) + row * tab.features, gq,
-                              qq);
-        else
-            mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, static_cast<float*>(p.out) + row * tab.features, gq,
-                              qq);
+        if (tab.out_f64) {
+            double* dst = static_cast<double*>(p.out) + row * tab.features;
+            if (n8)
+                mma::power_n8<L>(tab.power_pref, R, tab.rs, S, dst, gq, qq);
+            else
+                mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, dst, gq, qq);
+        } else {
+            float* dst = static_cast<float*>(p.out) + row * tab.features;
+            if (n8)
+                mma::power_n8<L>(tab.power_pref, R, tab.rs, S, dst, gq, qq);
+            else
+                mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, dst, gq, qq);
+        }
     } else if (tab.average == 1) {
         // The structure kernel's layout: [l][r][m], rows padded to 2l+2.
         double* dst = p.cbuf + local * tab.csize;
@@ -522,7 +533,10 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             }
         }
     } else {
-        mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, gq, qq);
+        if (n8)
+            mma::power_n8<L>(tab.power_pref, R, tab.rs, S, p.pbuf + local * tab.features, gq, qq);
+        else
+            mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, gq, qq);
     }
 }
 
