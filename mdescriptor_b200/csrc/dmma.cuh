@@ -307,6 +307,108 @@ __device__ __forceinline__ void power_n8(const double* __restrict__ pref, const 
     }
 }
 
+// Beta transform and power spectrum with the coefficients held in registers
+// (n_max == 8, at most MAXS species, compression off; soap.cpp:915-926 and
+// :997-1012).  Per degree l:
+//   1. C_t = beta_l R_t for every species t on the tensor cores: A = beta_l
+//      (n x k, pi^{3/2} folded in), B = the raw sums of the coefficient block
+//      (k x m, 8 columns per tile).  The accumulator tile (lane (g, q) holds
+//      C[g][8mb + 2q] and C[g][8mb + 2q + 1]) is moved into the operand layout
+//      of the power products (lane (g, q) holds C[g][4kb + q]) by shuffles,
+//      and columns m >= 2l + 1 -- the block's padding, never cleared -- are
+//      set to 0 there, so the padding may hold anything.
+//   2. P = pi sqrt(8 / (2l + 1)) C_t1 C_t2^T for every pair t1 <= t2, each
+//      lane storing its two features (see power_n8 for the offsets).
+// The coefficients of one degree are loaded once and shared by all pairs,
+// and every pair's product chain is independent of the others.
+template <int L, int MAXS, class OutT>
+__device__ __forceinline__ void tail_regs_n8(const double* __restrict__ bt, const double* __restrict__ reg, int rs,
+                                             int S, const double* __restrict__ pref, OutT* __restrict__ out, int lane) {
+    const int g = lane >> 2, q = lane & 3;
+    const int od = 8 * g + 2 * q;
+    const int n2a = 2 * q, n2b = 2 * q + 1;
+    const bool va = n2a >= g, vb = n2b >= g;
+    const int dd = 8 * g - g * (g - 1) / 2 - g;  // diagonal block: offset of (g, n2) is dd + n2
+    const bool row_aligned = (reinterpret_cast<uintptr_t>(out) % (2 * sizeof(OutT))) == 0;
+    const int src_lo = (lane & ~3) | (q >> 1), src_hi = src_lo + 2;
+    const bool odd = (q & 1) != 0;
+    constexpr int NKMAX = kpad(L) / 4;          // k steps of the largest degree
+    constexpr int MBMAX = (kpad(L) + 7) / 8;    // 8-column tiles of the largest degree
+    int pb[MAXS][MAXS];
+#pragma unroll
+    for (int t1 = 0; t1 < MAXS; ++t1)
+#pragma unroll
+        for (int t2 = t1; t2 < MAXS; ++t2) pb[t1][t2] = (int)pair_base(S, 8, L, t1, t2);
+    // A runtime loop over l (one copy of the code); trip counts inside are
+    // warp-uniform, the register arrays sized for the largest degree.
+#pragma unroll 1
+    for (int l = 0; l <= L; ++l) {
+        const int KP = (2 * l + 1 + 3) & ~3, NK = KP / 4, MB = (KP + 7) / 8;
+        int C0 = 0;
+        for (int i = 0; i < l; ++i) C0 += (2 * i + 1 + 3) & ~3;
+        const double a0 = bt[(l * 8 + g) * 8 + q];
+        const double a1 = bt[(l * 8 + g) * 8 + 4 + q];
+        double f[MAXS][NKMAX];
+#pragma unroll
+        for (int t = 0; t < MAXS; ++t) {
+#pragma unroll
+            for (int kb = 0; kb < NKMAX; ++kb) f[t][kb] = 0.0;
+            if (t < S) {
+                const double* blk = reg + t * 8 * rs + C0;
+#pragma unroll
+                for (int mb = 0; mb < MBMAX; ++mb) {
+                    if (mb < MB) {
+                        const int m = 8 * mb + g;
+                        const double b0 = blk[q * rs + m], b1 = blk[(q + 4) * rs + m];
+                        double c0 = 0.0, c1 = 0.0;
+                        dmma8(c0, c1, a0, b0);
+                        dmma8(c0, c1, a1, b1);
+                        const double x0 = __shfl_sync(0xffffffffu, c0, src_lo);
+                        const double x1 = __shfl_sync(0xffffffffu, c1, src_lo);
+                        const double y0 = __shfl_sync(0xffffffffu, c0, src_hi);
+                        const double y1 = __shfl_sync(0xffffffffu, c1, src_hi);
+                        if (2 * mb < NKMAX) f[t][2 * mb] = (8 * mb + q < 2 * l + 1) ? (odd ? x1 : x0) : 0.0;
+                        if (2 * mb + 1 < NKMAX)
+                            f[t][2 * mb + 1] = (8 * mb + 4 + q < 2 * l + 1) ? (odd ? y1 : y0) : 0.0;
+                    }
+                }
+            }
+        }
+        const double pl = pref[l];
+#pragma unroll
+        for (int t1 = 0; t1 < MAXS; ++t1) {
+#pragma unroll
+            for (int t2 = t1; t2 < MAXS; ++t2) {
+                if (t2 < S) {
+                    double c0 = 0.0, c1 = 0.0;
+#pragma unroll
+                    for (int kb = 0; kb < NKMAX; ++kb)
+                        if (kb < NK) dmma8(c0, c1, f[t1][kb], f[t2][kb]);
+                    const double x = pl * c0, y = pl * c1;
+                    if (t1 != t2) {
+                        OutT* dst = out + pb[t1][t2] + 64 * l + od;
+                        if (row_aligned) {
+                            store_pair(dst, x, y);
+                        } else {
+                            dst[0] = (OutT)x;
+                            dst[1] = (OutT)y;
+                        }
+                    } else {
+                        const int o = pb[t1][t2] + 36 * l + dd;
+                        OutT* dst = out + o;
+                        if (va && row_aligned && ((o + n2a) & 1) == 0) {
+                            store_pair(dst + n2a, x, y);
+                        } else {
+                            if (va) dst[n2a] = (OutT)x;
+                            if (vb) dst[n2b] = (OutT)y;
+                        }
+                    }
+                }
+            }
+        }
+    }
+}
+
 }  // namespace mma
 
 }  // namespace mdsoap

@@ -470,7 +470,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         }
 
         // Flush the raw sums times the species weight: row (t, k), degree l
-        // at columns col_off(l) .. + kpad(l), padding written as 0.
+        // at columns col_off(l) .. + kpad(l), padding written as 0 where the
+        // tail reads it.
         if (lane_on) {
             const int colA = mma::col_off(lA);
             const int colB = lB >= 0 ? mma::col_off(lB) - split : 0;
@@ -488,9 +489,12 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                         else if (lB >= 0)
                             row[colB + m] = w * acc[tt][m];
                     }
-                    for (int m = split; m < padA; ++m) row[colA + m] = 0.0;
-                    if (lB >= 0)
-                        for (int m = 2 * lB + 1; m < padB; ++m) row[colB + split + m] = 0.0;
+                    // n_max == 8 tails never read the padding (tail_regs_n8 masks it).
+                    if (n != 8) {
+                        for (int m = split; m < padA; ++m) row[colA + m] = 0.0;
+                        if (lB >= 0)
+                            for (int m = 2 * lB + 1; m < padB; ++m) row[colB + split + m] = 0.0;
+                    }
                 }
             }
         }
@@ -499,6 +503,21 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
 
     const int gq = lane >> 2, qq = lane & 3, R_rows = tab.rows;
     const bool n8 = n == 8;
+    if (n8 && tab.average != 1 && S <= MAXT) {
+        // Coefficients stay in registers from the beta transform to the power spectrum.
+        if (tab.average == 0) {
+            const int64_t row = center - p.out_row_begin;
+            if (tab.out_f64)
+                mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.power_pref,
+                                           static_cast<double*>(p.out) + row * tab.features, lane);
+            else
+                mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.power_pref,
+                                           static_cast<float*>(p.out) + row * tab.features, lane);
+        } else {
+            mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.power_pref, p.pbuf + local * tab.features, lane);
+        }
+        return;
+    }
     if (n8)
         mma::beta_n8<L>(bt, R, tab.rs, S, gq, qq);
     else
