@@ -259,28 +259,13 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             if (lane < count) perm[rank] = lane;
             __syncwarp();
             const bool weighted = tab.weighted != 0;
+            // One edge per step: two independent exp chains per lane are
+            // enough to cover their latency, and the shorter loop body (one
+            // copy per species bank) stays in the instruction cache.
             static_for<0, MAXT>([&](auto bank) {
                 constexpr int TT = decltype(bank)::value;
                 const int end = run_start[TT + 1];
-                int i = run_start[TT];
-                for (; i + 1 < end; i += 2) {
-                    const int ea = perm[i], eb = perm[i + 1];
-                    const double ua = pr2[ea], ub = pr2[eb];
-                    double gAa = scaled_exp<PRECISE>(nEA * ua, prefA, etab);
-                    double gBa = scaled_exp<PRECISE>(nEB * ua, prefB, etab);
-                    double gAb = scaled_exp<PRECISE>(nEA * ub, prefA, etab);
-                    double gBb = scaled_exp<PRECISE>(nEB * ub, prefB, etab);
-                    if (weighted) {
-                        const double wa = pw[ea], wb = pw[eb];
-                        gAa *= wa;
-                        gBa *= wa;
-                        gAb *= wb;
-                        gBb *= wb;
-                    }
-                    accumulate(bank, gAa, gBa, ea);
-                    accumulate(bank, gAb, gBb, eb);
-                }
-                if (i < end) {
+                for (int i = run_start[TT]; i < end; ++i) {
                     const int ea = perm[i];
                     const double ua = pr2[ea];
                     double gAa = scaled_exp<PRECISE>(nEA * ua, prefA, etab);
