@@ -438,12 +438,15 @@ def main():
         hbm_peak, hbm_src = measured_peaks()
         achieved_gbs = bytes_per_launch / center_avg_s / 1e9
         traffic = None
+        kernel = soap.kernel()
         tf = ROOT / "profiles" / f"traffic_config{args.config}.json"
         if tf.is_file():
-            # one-pass ncu capture of the full-size launch (dram read + write);
-            # other sizes scale it by atoms (the rows are the traffic)
+            # one-pass ncu capture of the full-size launch (dram read + write)
+            # of the same kernel; other sizes scale it by atoms (the rows are
+            # the traffic)
             record = json.loads(tf.read_text())
-            traffic = record["dram_bytes_per_launch"] * batch.atoms / record["atoms"]
+            if record.get("kernel") == kernel:
+                traffic = record["dram_bytes_per_launch"] * batch.atoms / record["atoms"]
         fp64_peak = probe_fp64_fma(local)
         flops = algorithmic_flops_per_atom(cfg, edges) * batch.atoms
         achieved_tf = flops / center_avg_s / 1e12
@@ -459,10 +462,10 @@ def main():
             "kernel_ms": {"bin": statistics.mean(bin_ms), "center": statistics.mean(center_ms)},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved_gbs / hbm_peak, "traffic": traffic,
-                         "kernel": "soap_center_kernel", "peak_source": hbm_src,
+                         "kernel": kernel, "peak_source": hbm_src,
                          "algorithmic_bytes_per_atom": bytes_per_launch / batch.atoms},
             "roofline_fp64": {"bound": "fp64", "achieved": achieved_tf, "peak": fp64_peak, "unit": "TFLOP/s",
-                              "frac": achieved_tf / fp64_peak, "kernel": "soap_center_kernel",
+                              "frac": achieved_tf / fp64_peak, "kernel": kernel,
                               "peak_source": "measured in-run (mdsoap_probe_fp64_fma, FMA chains on every SM)",
                               "flops_per_atom": flops / batch.atoms, "edges_per_atom": edges,
                               "exp_per_atom": edges * (cfg.l_max + 1) * cfg.n_max},

@@ -159,7 +159,7 @@ int mdsoap_plan_check(mdsoap_plan* plan, int32_t device, void* stream);
  *
  * Limits and rules:
  *  - A batch whose working set does not fit the scratch array is rejected with
- *    MDSOAP_CAPACITY_OVERFLOW before any device work (roughly 44 bytes per atom
+ *    MDSOAP_CAPACITY_OVERFLOW before any device work (roughly 76 bytes per atom
  *    plus 300 per structure for average "off"; the averages add one
  *    coefficient block or feature row per atom).
  *  - The first call on a device looks up the array's device address
@@ -188,6 +188,11 @@ int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, d
  * points (measurement support; no counterpart in the reference).  A
  * benchmark reads it before and after its timed region to count its launches. */
 int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count);
+
+/* Name and template arguments of the centre kernel the plan launches, e.g.
+ * "soap_paired_kernel<4, 6, false, 2>" (measurement support, for matching
+ * profiler records; no counterpart in the reference).  Never NULL. */
+const char* mdsoap_plan_kernel(const mdsoap_plan* plan);
 
 /* The engine's exp() for non-positive arguments (Tang's table-driven
  * method, used for every radial factor exp(-a r^2)) and CUDA's exp(), both

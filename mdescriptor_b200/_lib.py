@@ -78,6 +78,8 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_plan_feature_count.restype = ctypes.c_int64
     lib.mdsoap_plan_rows.argtypes = [_P, ctypes.POINTER(BatchView)]
     lib.mdsoap_plan_rows.restype = ctypes.c_int64
+    lib.mdsoap_plan_kernel.argtypes = [_P]
+    lib.mdsoap_plan_kernel.restype = ctypes.c_char_p
     lib.mdsoap_compute.argtypes = [_P, ctypes.POINTER(BatchView), _P, _P, ctypes.c_int32, _P, _P]
     lib.mdsoap_compute.restype = ctypes.c_int
     lib.mdsoap_compute_device.argtypes = [_P, ctypes.POINTER(BatchView), _P, ctypes.c_int32, _P]
@@ -118,6 +120,7 @@ EXPORTED = (
     "mdsoap_plan_destroy",
     "mdsoap_plan_feature_count",
     "mdsoap_plan_rows",
+    "mdsoap_plan_kernel",
     "mdsoap_compute",
     "mdsoap_compute_device",
     "mdsoap_plan_check",

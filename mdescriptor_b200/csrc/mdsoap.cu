@@ -203,24 +203,27 @@ struct Variant {
     const void* (*structure_sym)();
     bool paired = false;   // paired-channel kernel (soap_paired_kernel), l_max == lmax exactly
     bool precise = false;  // paired: full-accuracy radial factors (float64 rows)
+    const char* name = "";  // kernel and template arguments, for measurement records
 };
 
 #define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
     Variant {                                                                                             \
         CLS, T, A, B, C, N, L, MB, false, false, &launch_center<T, A, B, C, N, L, MB>,                      \
-            &center_symbol<T, A, B, C, N, L, MB>, &launch_structure<L>, &structure_symbol<L>              \
+            &center_symbol<T, A, B, C, N, L, MB>, &launch_structure<L>, &structure_symbol<L>, false, false, \
+            "soap_center_kernel<" #T ", " #A ", " #B ", " #C ", " #N ", " #L ", " #MB ">"                   \
     }
 #define MDSOAP_PAIR_VARIANT(CLS, T, A, B, C, N, L, MB)                                                   \
     Variant {                                                                                             \
         CLS, T, A, B, C, N, L, MB, true, false, &launch_pair<T, A, B, C, N, L, MB>,                         \
             &pair_symbol<T, A, B, C, N, L, MB>,                                                           \
-            &launch_structure<L>, &structure_symbol<L>                                                    \
+            &launch_structure<L>, &structure_symbol<L>, false, false,                                     \
+            "soap_pair_kernel<" #T ", " #A ", " #B ", " #C ", " #N ", " #L ", " #MB ">"                     \
     }
 
 #define MDSOAP_MMA_VARIANT(CLS, L, MB)                                                                  \
     Variant {                                                                                             \
         CLS, 0, 0, 0, 0, 8, L, MB, false, true, &launch_mma<L, MB>, &mma_symbol<L, MB>, &launch_structure<L>, \
-            &structure_symbol<L>                                                                          \
+            &structure_symbol<L>, false, false, "soap_mma_kernel<" #L ", " #MB ">"                          \
     }
 
 // First entry of each class is the default.  Defaults chosen by measurement
@@ -247,7 +250,8 @@ const Variant kVariants[] = {
 #define MDSOAP_PAIRED_VARIANT(T, L, PREC, MB)                                                              \
     Variant {                                                                                              \
         -1, T, 0, 0, 0, 8, L, MB, false, false, &launch_paired<T, L, PREC, MB>,                             \
-            &paired_symbol<T, L, PREC, MB>, &launch_structure<L>, &structure_symbol<L>, true, PREC          \
+            &paired_symbol<T, L, PREC, MB>, &launch_structure<L>, &structure_symbol<L>, true, PREC,         \
+            "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">"                                        \
     }
 
 // Paired-channel kernels: the default wherever they apply (n_max <= 8,
@@ -1293,6 +1297,10 @@ int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, d
     } catch (const Failure& f) {
         return fail(f.status, f.message);
     }
+}
+
+const char* mdsoap_plan_kernel(const mdsoap_plan* plan) {
+    return plan && plan->variant ? plan->variant->name : "";
 }
 
 int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count) {

@@ -129,6 +129,10 @@ class Soap:
     def set_timing(self, enable: bool) -> None:
         raise_for(lib.mdsoap_plan_set_timing(self._plan, 1 if enable else 0))
 
+    def kernel(self) -> str:
+        """Name and template arguments of the centre kernel this plan launches."""
+        return lib.mdsoap_plan_kernel(self._plan).decode()
+
     def launch_count(self) -> int:
         """Kernels this plan has launched so far (all devices, all entry points)."""
         value = ctypes.c_int64()
