@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define MDSOAP_ABI_VERSION 1
+#define MDSOAP_ABI_VERSION 2
 
 /* Status codes.  They mirror the reference plugin's error classes
  * (cpp/cuda/include/mdescriptor/cuda/error.hpp:15-28 and
@@ -42,9 +42,26 @@ typedef enum { MDSOAP_FLOAT32 = 0, MDSOAP_FLOAT64 = 1 } mdsoap_dtype;
 
 typedef enum { MDSOAP_AVERAGE_OFF = 0, MDSOAP_AVERAGE_INNER = 1, MDSOAP_AVERAGE_OUTER = 2 } mdsoap_average;
 
-/* Descriptor parameters; the fields of the reference's SoapOptions that the
- * GTO / compression-off path reads (cpp/include/mdescriptor/descriptor.hpp:17-43,
- * filled by SoapKernel._ensure_native, _kernels/core.py:207-258). */
+/* Power-spectrum layouts (SoapOptions::compression; soap.cpp:373-387, 933-1012). */
+typedef enum {
+    MDSOAP_COMPRESSION_OFF = 0,       /* all species pairs t1 <= t2, (S n)(S n + 1)/2 (L + 1) features */
+    MDSOAP_COMPRESSION_MU2 = 1,       /* one pooled density, n (n + 1)/2 (L + 1) features */
+    MDSOAP_COMPRESSION_MU1NU1 = 2,    /* species x pooled density, S n^2 (L + 1) features */
+    MDSOAP_COMPRESSION_CROSSOVER = 3  /* same-species pairs only, S n (n + 1)/2 (L + 1) features */
+} mdsoap_compression;
+
+/* Radial weighting functions of the neighbour density (soap_weight,
+ * soap.cpp:389-420). */
+typedef enum {
+    MDSOAP_WEIGHTING_NONE = 0,
+    MDSOAP_WEIGHTING_POLY = 1,  /* c (1 + 2 x^3 - 3 x^2)^m for r <= r0, else 0; x = r / r0 */
+    MDSOAP_WEIGHTING_POW = 2,   /* c / (d + x^m) */
+    MDSOAP_WEIGHTING_EXP = 3    /* c / (d + exp(-x)) */
+} mdsoap_weighting;
+
+/* Descriptor parameters; the fields of the reference's SoapOptions for the
+ * GTO basis (cpp/include/mdescriptor/descriptor.hpp:17-43, filled by
+ * SoapKernel._ensure_native, _kernels/core.py:207-269). */
 typedef struct {
     int32_t n_species;
     const int32_t* species;        /* atomic numbers in declared order (feature order follows it) */
@@ -57,6 +74,14 @@ typedef struct {
     const double* betas;           /* (l_max+1)*n_max*n_max, index (l*n_max + n)*n_max + k */
     int32_t average;               /* mdsoap_average */
     int32_t output_dtype;          /* mdsoap_dtype */
+    int32_t compression;           /* mdsoap_compression */
+    int32_t weighting_function;    /* mdsoap_weighting */
+    int32_t weighting_has_w0;      /* non-zero: the exact self pair weighs weighting_w0 */
+    double weighting_r0;           /* > 0 when a function is set */
+    double weighting_c;            /* >= 0 */
+    double weighting_d;            /* >= 0 */
+    double weighting_m;            /* >= 0 */
+    double weighting_w0;           /* >= 0 */
 } mdsoap_params;
 
 /* A flat batch with StructureBatch's layout (src/mdescriptor/core/input.py:20-131):

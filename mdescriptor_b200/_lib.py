@@ -15,6 +15,8 @@ from pathlib import Path
 # MDSOAP_LIBRARY may point at another build of the same ABI (e.g. a debug build).
 LIB_PATH = Path(os.environ.get("MDSOAP_LIBRARY") or Path(__file__).resolve().parent / "lib" / "libmdsoap.so")
 
+ABI_VERSION = 2  # MDSOAP_ABI_VERSION: layout of Params below
+
 OK = 0
 INVALID_ARGUMENT = 1
 DEVICE_UNAVAILABLE = 2
@@ -28,6 +30,8 @@ NOALLOC_SCRATCH_BYTES = 32 << 20  # MDSOAP_NOALLOC_SCRATCH_BYTES
 FLOAT32 = 0
 FLOAT64 = 1
 AVERAGE = {"off": 0, "inner": 1, "outer": 2}
+COMPRESSION = {"off": 0, "mu2": 1, "mu1nu1": 2, "crossover": 3}
+WEIGHTING = {None: 0, "poly": 1, "pow": 2, "exp": 3}
 
 _P = ctypes.c_void_p
 CancelFn = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
@@ -46,6 +50,14 @@ class Params(ctypes.Structure):
         ("betas", _P),
         ("average", ctypes.c_int32),
         ("output_dtype", ctypes.c_int32),
+        ("compression", ctypes.c_int32),
+        ("weighting_function", ctypes.c_int32),
+        ("weighting_has_w0", ctypes.c_int32),
+        ("weighting_r0", ctypes.c_double),
+        ("weighting_c", ctypes.c_double),
+        ("weighting_d", ctypes.c_double),
+        ("weighting_m", ctypes.c_double),
+        ("weighting_w0", ctypes.c_double),
     ]
 
 
@@ -67,6 +79,10 @@ def _load() -> ctypes.CDLL:
             f"mdsoap CUDA library not built ({LIB_PATH}); run `python -m mdescriptor_b200.build`"
         )
     lib = ctypes.CDLL(str(LIB_PATH))
+    lib.mdsoap_abi_version.restype = ctypes.c_int32
+    if lib.mdsoap_abi_version() != ABI_VERSION:
+        raise ImportError(f"{LIB_PATH} has C ABI {lib.mdsoap_abi_version()}, this binding needs {ABI_VERSION}; "
+                          "rebuild with `python -m mdescriptor_b200.build`")
     lib.mdsoap_last_error.restype = ctypes.c_char_p
     lib.mdsoap_abi_version.restype = ctypes.c_int32
     lib.mdsoap_device_count.restype = ctypes.c_int32

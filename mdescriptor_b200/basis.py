@@ -34,26 +34,50 @@ def basis_gto(r_cut: float, n_max: int, l_max: int) -> tuple[np.ndarray, np.ndar
     return alphas, betas
 
 
-def feature_count(n_species: int, n_max: int, l_max: int) -> int:
-    """Features for compression "off": (S n)(S n + 1)/2 (L + 1) (_kernels/core.py:272-284)."""
+def feature_count(n_species: int, n_max: int, l_max: int, compression: str = "off") -> int:
+    """Features per row by compression mode (_kernels/core.py:272-284; soap.cpp:373-387)."""
+    if compression == "mu2":
+        return n_max * (n_max + 1) // 2 * (l_max + 1)
+    if compression == "mu1nu1":
+        return n_species * n_max * n_max * (l_max + 1)
+    if compression == "crossover":
+        return n_species * n_max * (n_max + 1) // 2 * (l_max + 1)
     width = n_species * n_max
     return width * (width + 1) // 2 * (l_max + 1)
 
 
-def labels(species, n_max: int, l_max: int) -> tuple[str, ...]:
-    """Feature labels in output order (_kernels/core.py:306-329, compression off).
+def labels(species, n_max: int, l_max: int, compression: str = "off") -> tuple[str, ...]:
+    """Feature labels in output order (_kernels/core.py:306-329).
 
     Species pairs follow the declared (not sorted) species order, z1 <= z2 by
-    position; then l, then n1, then n2 (n2 >= n1 within a species).
+    position; then l, then n1, then n2 (n2 >= n1 within a species).  mu2 has
+    one pooled density; mu1nu1 pairs each species with it (all n2); crossover
+    keeps same-species pairs only.
     """
     species = list(species)
     out = []
-    for i, first in enumerate(species):
-        for second in species[i:]:
+    if compression == "mu2":
+        for degree in range(l_max + 1):
+            for n1 in range(n_max):
+                for n2 in range(n1, n_max):
+                    out.append(f"soap:compression=mu2,l={degree},n1={n1},n2={n2}")
+        return tuple(out)
+    if compression == "mu1nu1":
+        for first in species:
             for degree in range(l_max + 1):
                 for n1 in range(n_max):
-                    for n2 in range(n1 if first == second else 0, n_max):
-                        out.append(f"soap:z1={first},z2={second},l={degree},n1={n1},n2={n2}")
+                    for n2 in range(n_max):
+                        out.append(f"soap:compression=mu1nu1,z1={first},l={degree},n1={n1},n2={n2}")
+        return tuple(out)
+    if compression == "crossover":
+        pairs = [(first, first) for first in species]
+    else:
+        pairs = [(first, second) for i, first in enumerate(species) for second in species[i:]]
+    for first, second in pairs:
+        for degree in range(l_max + 1):
+            for n1 in range(n_max):
+                for n2 in range(n1 if first == second else 0, n_max):
+                    out.append(f"soap:z1={first},z2={second},l={degree},n1={n1},n2={n2}")
     return tuple(out)
 
 

@@ -137,16 +137,33 @@ public:
             throw std::invalid_argument("invalid CUDA SOAP parameters");
         if (option(options_, "rbf", std::string("gto")) != "gto")
             throw std::invalid_argument("unsupported CUDA SOAP radial basis");
+        // extended_descriptors_soap.cuh:819-828, 878-884: compression mode and
+        // weighting function names.
         const py::dict compression = child_dict(options_, "compression");
-        if (option(compression, "mode", std::string("off")) != "off")
-            throw std::invalid_argument("unsupported CUDA SOAP compression");
+        const std::string mode = option(compression, "mode", std::string("off"));
+        compression_ = mode == "off" ? MDSOAP_COMPRESSION_OFF
+                       : mode == "mu2" ? MDSOAP_COMPRESSION_MU2
+                       : mode == "mu1nu1" ? MDSOAP_COMPRESSION_MU1NU1
+                       : mode == "crossover" ? MDSOAP_COMPRESSION_CROSSOVER : -1;
+        if (compression_ < 0) throw std::invalid_argument("unsupported CUDA SOAP compression");
         const std::string average = option(options_, "average", std::string("inner"));
         if (average != "off" && average != "inner" && average != "outer")
             throw std::invalid_argument("unsupported CUDA SOAP average mode");
         average_ = average == "off" ? MDSOAP_AVERAGE_OFF : average == "inner" ? MDSOAP_AVERAGE_INNER : MDSOAP_AVERAGE_OUTER;
         const py::dict weighting = child_dict(options_, "weighting");
-        if (option(weighting, "function", std::string()) != "" || weighting.contains("w0"))
-            throw std::invalid_argument("unsupported CUDA SOAP weighting");
+        const std::string function = option(weighting, "function", std::string());
+        weighting_function_ = function == "" ? MDSOAP_WEIGHTING_NONE
+                              : function == "poly" ? MDSOAP_WEIGHTING_POLY
+                              : function == "pow" ? MDSOAP_WEIGHTING_POW
+                              : function == "exp" ? MDSOAP_WEIGHTING_EXP : -1;
+        if (weighting_function_ < 0) throw std::invalid_argument("unsupported CUDA SOAP weighting");
+        // Defaults of SoapKernel._ensure_native (_kernels/core.py:247-254).
+        weighting_has_w0_ = weighting.contains("w0");
+        weighting_r0_ = option(weighting, "r0", 1.0);
+        weighting_c_ = option(weighting, "c", 1.0);
+        weighting_d_ = option(weighting, "d", 0.0);
+        weighting_m_ = option(weighting, "m", 1.0);
+        weighting_w0_ = option(weighting, "w0", 1.0);
         // A species' weight is looked up as an int key, then its decimal
         // string (the adapter's options have been through JSON), then its
         // element symbol; species without an entry weigh 1.0
@@ -190,6 +207,14 @@ public:
         params.betas = betas_.data();
         params.average = average_;
         params.output_dtype = f64_ ? MDSOAP_FLOAT64 : MDSOAP_FLOAT32;
+        params.compression = compression_;
+        params.weighting_function = weighting_function_;
+        params.weighting_has_w0 = weighting_has_w0_ ? 1 : 0;
+        params.weighting_r0 = weighting_r0_;
+        params.weighting_c = weighting_c_;
+        params.weighting_d = weighting_d_;
+        params.weighting_m = weighting_m_;
+        params.weighting_w0 = weighting_w0_;
         mdsoap_plan* plan = nullptr;
         const int status = mdsoap_plan_create(&params, &plan);
         if (status != MDSOAP_OK) throw_status(status);
@@ -314,6 +339,9 @@ private:
     std::vector<double> weights_, alphas_, betas_;
     int n_max_ = 8, l_max_ = 6, average_ = MDSOAP_AVERAGE_INNER;
     double r_cut_ = 6.0, sigma_ = 1.0;
+    int compression_ = MDSOAP_COMPRESSION_OFF, weighting_function_ = MDSOAP_WEIGHTING_NONE;
+    bool weighting_has_w0_ = false;
+    double weighting_r0_ = 1.0, weighting_c_ = 1.0, weighting_d_ = 0.0, weighting_m_ = 1.0, weighting_w0_ = 1.0;
     bool f64_ = true;
     int64_t features_ = 0;
     py::list labels_;

@@ -318,12 +318,17 @@ __device__ __forceinline__ void power_n8(const double* __restrict__ pref, const 
 //      and columns m >= 2l + 1 -- the block's padding, never cleared -- are
 //      set to 0 there, so the padding may hold anything.
 //   2. P = pi sqrt(8 / (2l + 1)) C_t1 C_t2^T for every pair t1 <= t2, each
-//      lane storing its two features (see power_n8 for the offsets).
+//      lane storing its two features (see power_n8 for the offsets); with
+//      compression crossover only t1 == t2 (species t's block at
+//      t (L+1) n(n+1)/2), with mu1nu1 C_t (sum_t' C_t')^T in full n x n
+//      blocks (species t's block at t (L+1) n^2).  mu2 arrives as one pooled
+//      species in the compression-off layout.
 // The coefficients of one degree are loaded once and shared by all pairs,
 // and every pair's product chain is independent of the others.
 template <int L, int MAXS, class OutT>
 __device__ __forceinline__ void tail_regs_n8(const double* __restrict__ bt, const double* __restrict__ reg, int rs,
-                                             int S, const double* __restrict__ pref, OutT* __restrict__ out, int lane) {
+                                             int S, int compression, const double* __restrict__ pref,
+                                             OutT* __restrict__ out, int lane) {
     const int g = lane >> 2, q = lane & 3;
     const int od = 8 * g + 2 * q;
     const int n2a = 2 * q, n2b = 2 * q + 1;
@@ -375,11 +380,37 @@ __device__ __forceinline__ void tail_regs_n8(const double* __restrict__ bt, cons
             }
         }
         const double pl = pref[l];
+        if (compression == 2) {
+            double fs[NKMAX];
+#pragma unroll
+            for (int kb = 0; kb < NKMAX; ++kb) {
+                fs[kb] = 0.0;
+#pragma unroll
+                for (int t = 0; t < MAXS; ++t) fs[kb] += f[t][kb];
+            }
+#pragma unroll
+            for (int t = 0; t < MAXS; ++t) {
+                if (t < S) {
+                    double c0 = 0.0, c1 = 0.0;
+#pragma unroll
+                    for (int kb = 0; kb < NKMAX; ++kb)
+                        if (kb < NK) dmma8(c0, c1, f[t][kb], fs[kb]);
+                    OutT* dst = out + t * 64 * (L + 1) + 64 * l + od;
+                    if (row_aligned) {
+                        store_pair(dst, pl * c0, pl * c1);
+                    } else {
+                        dst[0] = (OutT)(pl * c0);
+                        dst[1] = (OutT)(pl * c1);
+                    }
+                }
+            }
+            continue;
+        }
 #pragma unroll
         for (int t1 = 0; t1 < MAXS; ++t1) {
 #pragma unroll
             for (int t2 = t1; t2 < MAXS; ++t2) {
-                if (t2 < S) {
+                if (t2 < S && (compression != 3 || t1 == t2)) {
                     double c0 = 0.0, c1 = 0.0;
 #pragma unroll
                     for (int kb = 0; kb < NKMAX; ++kb)
@@ -394,7 +425,7 @@ __device__ __forceinline__ void tail_regs_n8(const double* __restrict__ bt, cons
                             dst[1] = (OutT)y;
                         }
                     } else {
-                        const int o = pb[t1][t2] + 36 * l + dd;
+                        const int o = (compression == 3 ? t1 * 36 * (L + 1) : pb[t1][t2]) + 36 * l + dd;
                         OutT* dst = out + o;
                         if (va && row_aligned && ((o + n2a) & 1) == 0) {
                             store_pair(dst + n2a, x, y);

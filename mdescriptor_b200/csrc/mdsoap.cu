@@ -258,6 +258,9 @@ const Variant kVariants[] = {
 // n_max (1 + (l_max + 1) / 2) <= 32 lanes, an instantiated l_max, and radial
 // factors that stay normal doubles; see paired_applies).
 const Variant kPairedVariants[] = {
+    MDSOAP_PAIRED_VARIANT(4, 0, false, 2), MDSOAP_PAIRED_VARIANT(4, 0, true, 2),
+    MDSOAP_PAIRED_VARIANT(4, 1, false, 2), MDSOAP_PAIRED_VARIANT(4, 1, true, 2),
+    MDSOAP_PAIRED_VARIANT(4, 2, false, 2), MDSOAP_PAIRED_VARIANT(4, 2, true, 2),
     MDSOAP_PAIRED_VARIANT(4, 3, false, 2), MDSOAP_PAIRED_VARIANT(4, 3, true, 2),
     MDSOAP_PAIRED_VARIANT(4, 4, false, 2), MDSOAP_PAIRED_VARIANT(4, 4, true, 2),
     MDSOAP_PAIRED_VARIANT(4, 5, false, 2), MDSOAP_PAIRED_VARIANT(4, 5, true, 2),
@@ -403,7 +406,7 @@ struct DeviceState {
 };
 
 struct mdsoap_plan {
-    int n_species = 0, n_max = 0, l_max = 0, average = 0, out_dtype = 0;
+    int n_species = 0, n_max = 0, l_max = 0, average = 0, out_dtype = 0, compression = 0;
     double r_cut = 0, sigma = 0, cutoff = 0;
     std::vector<int32_t> species;
     std::vector<double> weights, alphas, betas;
@@ -756,6 +759,18 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
     if (q.average < 0 || q.average > 2) return fail(MDSOAP_INVALID_ARGUMENT, "unsupported CUDA SOAP average mode");
     if (q.output_dtype != MDSOAP_FLOAT32 && q.output_dtype != MDSOAP_FLOAT64)
         return fail(MDSOAP_INVALID_ARGUMENT, "output dtype must be float32 or float64");
+    if (q.compression < MDSOAP_COMPRESSION_OFF || q.compression > MDSOAP_COMPRESSION_CROSSOVER)
+        return fail(MDSOAP_INVALID_ARGUMENT, "unsupported CUDA SOAP compression");
+    // soap.cpp:1198-1210 weighting checks.
+    if (q.weighting_function < MDSOAP_WEIGHTING_NONE || q.weighting_function > MDSOAP_WEIGHTING_EXP)
+        return fail(MDSOAP_INVALID_ARGUMENT, "unsupported CUDA SOAP weighting");
+    if (q.weighting_function != MDSOAP_WEIGHTING_NONE &&
+        (!std::isfinite(q.weighting_r0) || q.weighting_r0 <= 0.0 || !std::isfinite(q.weighting_c) ||
+         q.weighting_c < 0.0 || !std::isfinite(q.weighting_d) || q.weighting_d < 0.0 ||
+         !std::isfinite(q.weighting_m) || q.weighting_m < 0.0))
+        return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP weighting parameters");
+    if (q.weighting_has_w0 && (!std::isfinite(q.weighting_w0) || q.weighting_w0 < 0.0))
+        return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP w0 weighting");
     if (!q.alphas || !q.betas) return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP radial basis size");
     for (int i = 0; i < q.n_species; ++i) {
         if (q.species[i] <= 0) return fail(MDSOAP_INVALID_ARGUMENT, "species must be positive atomic numbers");
@@ -813,10 +828,30 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         t.l_max = L;
         t.H = W * W;
         t.items = W * n;
-        t.rows = q.n_species * n;
+        // mu2 pools every species into one density (soap.cpp:613-615).
+        const int coef_species = q.compression == MDSOAP_COMPRESSION_MU2 ? 1 : q.n_species;
+        t.rows = coef_species * n;
+        t.coef_species = coef_species;
+        t.compression = q.compression;
+        plan->compression = q.compression;
         const int64_t width = (int64_t)q.n_species * n;
-        plan->features = width * (width + 1) / 2 * W;
+        switch (q.compression) {  // soap_features, soap.cpp:373-387
+            case MDSOAP_COMPRESSION_MU2: plan->features = (int64_t)n * (n + 1) / 2 * W; break;
+            case MDSOAP_COMPRESSION_MU1NU1: plan->features = (int64_t)q.n_species * n * n * W; break;
+            case MDSOAP_COMPRESSION_CROSSOVER: plan->features = (int64_t)q.n_species * n * (n + 1) / 2 * W; break;
+            default: plan->features = width * (width + 1) / 2 * W;
+        }
         t.features = plan->features;
+        t.weight_fn = q.weighting_function;
+        t.has_w0 = q.weighting_has_w0 ? 1 : 0;
+        t.w_r0 = q.weighting_r0;
+        t.w_c = q.weighting_c;
+        t.w_d = q.weighting_d;
+        t.w_m = q.weighting_m;
+        t.w_0 = q.weighting_w0;
+        // Per-edge weights: a weighting function or w0, and mu2 (the species
+        // weight then multiplies each edge of the pooled density).
+        t.weighted = (t.weight_fn != 0 || t.has_w0 || q.compression == MDSOAP_COMPRESSION_MU2) ? 1 : 0;
         t.average = q.average;
         t.out_f64 = q.output_dtype == MDSOAP_FLOAT64;
         t.cutoff2 = plan->cutoff * plan->cutoff;
@@ -853,6 +888,8 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         const Variant* picked = nullptr;
         if (paired && want <= 0) picked = paired;
         else picked = &pick_variant(n, L, paired ? want - 1 : want);
+        const bool needs_paired = t.weighted || q.compression != MDSOAP_COMPRESSION_OFF;
+        if (needs_paired && paired) picked = paired;
         if (paired && picked != paired && want > 0 && want - 1 >= 0) {
             // An index past the class list falls back to the default (the paired kernel).
             int members = 0;
@@ -862,13 +899,13 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         if (picked->paired) {
             const Variant& v = *picked;
             plan->variant = &v;
-            t.type_groups = (q.n_species + v.maxt - 1) / v.maxt;
+            t.type_groups = (coef_species + v.maxt - 1) / v.maxt;
             t.slot_groups = 1;
             t.beta_in_smem = 1;
-            t.csize = q.n_species * n * W * (W + 1);
+            t.csize = coef_species * n * W * (W + 1);
             t.hp = W * (W + 1);
             t.rs = mma::row_stride(L);
-            t.rsize = q.n_species * n * t.rs;
+            t.rsize = coef_species * n * t.rs;
             t.n_magic = n == 1 ? 0u : (uint32_t)((1ull << 32) / (uint64_t)n + 1ull);
             const bool single_pass = t.type_groups == 1;
             const size_t shared = 256 + (size_t)W * 64 * 8;
@@ -904,6 +941,10 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             *plan_out = plan.release();
             return MDSOAP_OK;
         }
+        if (needs_paired)
+            return fail(MDSOAP_INVALID_ARGUMENT,
+                        "SOAP weighting and compression run on the paired-channel kernel, which needs n_max <= 8, "
+                        "n_max (1 + (l_max + 1) / 2) <= 32 and l_max <= 6");
         // The tensor-core kernel keeps a centre's whole coefficient block in
         // shared memory; when that does not fit, the class's scalar kernel runs.
         const mma::Layout lay = mma::layout(L, q.n_species * n);

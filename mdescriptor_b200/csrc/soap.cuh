@@ -60,7 +60,9 @@ struct SoapTables {
     int32_t rs;           // tensor-core tail: coefficient-block row stride (0: scalar tail)
     int32_t rsize;        // doubles of one centre's coefficient block
     uint32_t n_magic;     // floor(2^32 / n_max) + 1
-    int32_t weighted;     // 1: per-edge weights (a weighting function and/or w0); paired kernel only
+    int32_t compression;  // 0 off, 1 mu2, 2 mu1nu1, 3 crossover (paired kernel only when not 0)
+    int32_t coef_species; // species of the coefficient block: n_species, or 1 for mu2
+    int32_t weighted;     // 1: per-edge weights (weighting function, w0, or mu2 pooling); paired kernel only
     int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)
     int32_t has_w0;       // the exact self pair takes weight w0
     double w_r0, w_c, w_d, w_m, w_0;
@@ -228,7 +230,7 @@ __device__ __forceinline__ void power_group(const SoapTables& tab, const double*
                                             OutT* __restrict__ out, int lane, int r1_first, int r1_step) {
     constexpr int NOWN = (LB + 1) * (LB + 1) - LA * LA;
     constexpr int NL = LB - LA + 1;
-    const int S = tab.n_species, n = tab.n_max, L = tab.l_max, R = tab.rows;
+    const int S = tab.coef_species, n = tab.n_max, L = tab.l_max, R = tab.rows;
     if (LA > L) return;
     const int64_t T = (int64_t)n * (n + 1) / 2, nn = (int64_t)n * n;
     const int sn = S * n;
@@ -284,6 +286,55 @@ __device__ __forceinline__ void power_group(const SoapTables& tab, const double*
                 }
             }
         }
+    }
+}
+
+// Power spectrum in any compression layout (soap.cpp:933-1012), one feature
+// per lane and a warp-uniform walk over the layout; coef(t, k, l, m) reads
+// coefficient (species t, radial k, degree l, component m) -- the species sum
+// of mu1nu1 is formed on the fly.  Used where the tensor-core tails do not
+// cover a layout.
+template <class Coef, class OutT>
+__device__ __forceinline__ void power_generic(const Coef& coef, const double* __restrict__ pref, int S, int n, int L,
+                                              int compression, OutT* __restrict__ out, int lane) {
+    int64_t f = 0;
+    auto dot = [&](int t1, int n1, int t2, int n2, int l) {
+        double acc = 0.0;
+        for (int m = 0; m < 2 * l + 1; ++m) {
+            double b;
+            if (t2 < 0) {  // species sum (mu1nu1)
+                b = 0.0;
+                for (int t = 0; t < S; ++t) b += coef(t, n2, l, m);
+            } else {
+                b = coef(t2, n2, l, m);
+            }
+            acc = fma(coef(t1, n1, l, m), b, acc);
+        }
+        return pref[l] * acc;
+    };
+    if (compression == 2) {  // mu1nu1: species -> l -> n1 -> n2 (all)
+        for (int t = 0; t < S; ++t)
+            for (int l = 0; l <= L; ++l)
+                for (int n1 = 0; n1 < n; ++n1) {
+                    for (int n2 = lane; n2 < n; n2 += 32) out[f + n2] = (OutT)dot(t, n1, -1, n2, l);
+                    f += n;
+                }
+    } else if (compression == 3) {  // crossover: species -> l -> n1 -> n2 >= n1
+        for (int t = 0; t < S; ++t)
+            for (int l = 0; l <= L; ++l)
+                for (int n1 = 0; n1 < n; ++n1) {
+                    for (int n2 = n1 + lane; n2 < n; n2 += 32) out[f + n2 - n1] = (OutT)dot(t, n1, t, n2, l);
+                    f += n - n1;
+                }
+    } else {  // off (and mu2, one pooled species): t1 <= t2 -> l -> n1 -> n2 (>= n1 when t1 == t2)
+        for (int t1 = 0; t1 < S; ++t1)
+            for (int t2 = t1; t2 < S; ++t2)
+                for (int l = 0; l <= L; ++l)
+                    for (int n1 = 0; n1 < n; ++n1) {
+                        const int lo = t1 == t2 ? n1 : 0;
+                        for (int n2 = lo + lane; n2 < n; n2 += 32) out[f + n2 - lo] = (OutT)dot(t1, n1, t2, n2, l);
+                        f += n - lo;
+                    }
     }
 }
 
@@ -771,10 +822,21 @@ soap_structure_kernel(const __grid_constant__ SoapTables tab, const int64_t* __r
         }
         __syncthreads();
         if (threadIdx.x < 32) {
-            if (tab.out_f64)
+            if (tab.compression == 2 || tab.compression == 3) {
+                // c layout: [l][t n + k][m], rows padded to 2l + 2.
+                const int S = tab.coef_species, n = tab.n_max;
+                auto coef = [&](int t, int k, int l, int m) { return c[cblock(S, n, l) + (t * n + k) * (2 * l + 2) + m]; };
+                if (tab.out_f64)
+                    power_generic(coef, tab.power_pref, S, n, tab.l_max, tab.compression,
+                                  static_cast<double*>(out) + (s - out_row_begin) * F, (int)threadIdx.x);
+                else
+                    power_generic(coef, tab.power_pref, S, n, tab.l_max, tab.compression,
+                                  static_cast<float*>(out) + (s - out_row_begin) * F, (int)threadIdx.x);
+            } else if (tab.out_f64) {
                 power_spectrum_warp<LMAX>(tab, c, static_cast<double*>(out) + (s - out_row_begin) * F, threadIdx.x);
-            else
+            } else {
                 power_spectrum_warp<LMAX>(tab, c, static_cast<float*>(out) + (s - out_row_begin) * F, threadIdx.x);
+            }
         }
     } else {
         for (int64_t i = threadIdx.x; i < F; i += blockDim.x) {

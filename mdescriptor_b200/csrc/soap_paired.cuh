@@ -136,7 +136,9 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int S = tab.n_species, n = tab.n_max;
+    // S: species of the coefficient block (1 when mu2 pools them all).
+    const int S = tab.coef_species, n = tab.n_max;
+    const bool pooled = tab.compression == 1;
     // CTA-shared: exp table (32 doubles), then beta as [l][n][k] scaled by
     // pi^{3/2} and zero padded to 8 x 8.
     double* etab = reinterpret_cast<double*>(smem);
@@ -176,6 +178,9 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     double wpos[3];
     wrapped_position(si, p.positions + 3 * center, bv.wrap + 3 * center, wpos);
     const int chunk = tab.chunk;
+    // Beta transform and power spectrum in registers (n_max == 8, the whole
+    // coefficient block in one pass of banks, per-centre rows).
+    const bool regs_tail = n == 8 && S <= MAXT && tab.average != 1;
 
     // This lane's channel pair: group g of radial index k.
     const int g = lane / n, k = lane - (lane / n) * n;
@@ -340,9 +345,12 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     ok = accept_candidate(si, bv, p.positions, center, wi, j, (tp & 1023) - 512,
                                           ((tp >> 10) & 1023) - 512, ((tp >> 20) & 1023) - 512, tab.cutoff2, nimg,
                                           dx, dy, dz, d2);
-                    if (ok && tab.weighted)
+                    if (ok && tab.weighted) {
                         w = soap_edge_weight(tab, d2,
                                              ab + j == center && nimg[0] == 0 && nimg[1] == 0 && nimg[2] == 0);
+                        // The pooled density carries each neighbour's species weight.
+                        if (pooled) w *= tab.species_weight[t];
+                    }
                 }
                 const unsigned mask = __ballot_sync(0xffffffffu, ok);
                 if (ok) {
@@ -352,7 +360,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     pdz[q] = dz;
                     pr2[q] = d2;
                     pw[q] = w;
-                    ptype[q] = t - tb;
+                    ptype[q] = pooled ? 0 : t - tb;
                 }
                 pcount += __popc(mask);
                 const int rem = qn - count;
@@ -383,7 +391,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     const double4 sp = bv.spos[ab + a];
                     ty = (int)sp.w;
                     const double dx = sp.x + seg_off[i], dy = sp.y + seg_off[32 + i], dz = sp.z + seg_off[64 + i];
-                    pass = ty >= tb && ty < te && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
+                    pass = (pooled || (ty >= tb && ty < te)) && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
                 }
                 const unsigned mask = __ballot_sync(0xffffffffu, pass);
                 if (pass) {
@@ -465,7 +473,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             for (int tt = 0; tt < MAXT; ++tt) {
                 const int t = tb + tt;
                 if (t < te) {
-                    const double w = tab.species_weight[t];
+                    const double w = pooled ? 1.0 : tab.species_weight[t];
                     double* row = R + (t * n + k) * tab.rs;
 #pragma unroll
                     for (int m = 0; m < P::W; ++m) {
@@ -474,8 +482,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                         else if (lB >= 0)
                             row[colB + m] = w * acc[tt][m];
                     }
-                    // n_max == 8 tails never read the padding (tail_regs_n8 masks it).
-                    if (n != 8) {
+                    // The register tail never reads the padding (tail_regs_n8 masks it).
+                    if (!regs_tail) {
                         for (int m = split; m < padA; ++m) row[colA + m] = 0.0;
                         if (lB >= 0)
                             for (int m = 2 * lB + 1; m < padB; ++m) row[colB + split + m] = 0.0;
@@ -488,18 +496,19 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
 
     const int gq = lane >> 2, qq = lane & 3, R_rows = tab.rows;
     const bool n8 = n == 8;
-    if (n8 && tab.average != 1 && S <= MAXT) {
+    if (regs_tail) {
         // Coefficients stay in registers from the beta transform to the power spectrum.
         if (tab.average == 0) {
             const int64_t row = center - p.out_row_begin;
             if (tab.out_f64)
-                mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.power_pref,
+                mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
                                            static_cast<double*>(p.out) + row * tab.features, lane);
             else
-                mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.power_pref,
+                mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
                                            static_cast<float*>(p.out) + row * tab.features, lane);
         } else {
-            mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.power_pref, p.pbuf + local * tab.features, lane);
+            mma::tail_regs_n8<L, MAXT>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
+                                       p.pbuf + local * tab.features, lane);
         }
         return;
     }
@@ -509,6 +518,22 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         mma::beta_mma<L>(bt, R, tab.rs, L, S, n, gq, qq);
     __syncwarp();
     const mma::FeatureMap fm{S, n, L, R_rows, tab.n_magic};
+    if (tab.average != 1 && (tab.compression == 2 || tab.compression == 3)) {
+        const int rs = tab.rs;
+        auto coef = [&](int t, int k, int l, int m) { return R[(t * n + k) * rs + mma::col_off(l) + m]; };
+        if (tab.average == 0) {
+            const int64_t row = center - p.out_row_begin;
+            if (tab.out_f64)
+                power_generic(coef, tab.power_pref, S, n, L, tab.compression,
+                              static_cast<double*>(p.out) + row * tab.features, lane);
+            else
+                power_generic(coef, tab.power_pref, S, n, L, tab.compression,
+                              static_cast<float*>(p.out) + row * tab.features, lane);
+        } else {
+            power_generic(coef, tab.power_pref, S, n, L, tab.compression, p.pbuf + local * tab.features, lane);
+        }
+        return;
+    }
     if (tab.average == 0) {
         const int64_t row = center - p.out_row_begin;
         if (tab.out_f64) {

@@ -52,7 +52,8 @@ class Soap:
     def __init__(self, species: Sequence[int], r_cut: float = 6.0, n_max: int = 8, l_max: int = 6,
                  sigma: float = 1.0, average: str = "inner", dtype: str = "float64",
                  species_weights: dict | Sequence[float] | None = None,
-                 alphas: np.ndarray | None = None, betas: np.ndarray | None = None) -> None:
+                 alphas: np.ndarray | None = None, betas: np.ndarray | None = None,
+                 compression: str = "off", weighting: dict | None = None) -> None:
         self.species = tuple(int(z) for z in species)
         self.r_cut = float(r_cut)
         self.n_max = int(n_max)
@@ -77,24 +78,35 @@ class Soap:
             self._weights = np.asarray([float(species_weights[z]) for z in self.species], np.float64)
         else:
             self._weights = np.ascontiguousarray(species_weights, dtype=np.float64)
+        if compression not in _lib.COMPRESSION:
+            raise ValueError("invalid SOAP compression mode")
+        self.compression = compression
+        self.weighting = dict(weighting or {})
+        function = self.weighting.get("function")
+        if function not in _lib.WEIGHTING:
+            raise ValueError("SOAP weighting function must be 'poly', 'pow', or 'exp'")
         params = Params(
             len(self.species), self._species.ctypes.data,
             None if self._weights is None else self._weights.ctypes.data,
             self.r_cut, self.sigma, self.n_max, self.l_max, self._alphas.ctypes.data,
             self._betas.ctypes.data, _lib.AVERAGE[average],
-            _lib.FLOAT64 if self.dtype == np.float64 else _lib.FLOAT32)
+            _lib.FLOAT64 if self.dtype == np.float64 else _lib.FLOAT32,
+            _lib.COMPRESSION[compression], _lib.WEIGHTING[function], 1 if "w0" in self.weighting else 0,
+            float(self.weighting.get("r0", 1.0)), float(self.weighting.get("c", 1.0)),
+            float(self.weighting.get("d", 0.0)), float(self.weighting.get("m", 1.0)),
+            float(self.weighting.get("w0", 1.0)))
         handle = ctypes.c_void_p()
         raise_for(lib.mdsoap_plan_create(ctypes.byref(params), ctypes.byref(handle)))
         self._plan = handle
         self.feature_count = int(lib.mdsoap_plan_feature_count(self._plan))
-        assert self.feature_count == feature_count(len(self.species), self.n_max, self.l_max)
+        assert self.feature_count == feature_count(len(self.species), self.n_max, self.l_max, compression)
 
     @property
     def cutoff(self) -> float:
         return graph_cutoff(self.r_cut, self.sigma)
 
     def labels(self) -> tuple[str, ...]:
-        return labels(self.species, self.n_max, self.l_max)
+        return labels(self.species, self.n_max, self.l_max, self.compression)
 
     def rows(self, batch) -> int:
         return int(batch.offsets.shape[0]) - 1 if self.average != "off" else int(batch.offsets[-1])
@@ -214,4 +226,5 @@ def options_from_payload(options: dict[str, Any]) -> dict[str, Any]:
                 l_max=options.get("l_max", 6), sigma=options.get("sigma", 1.0),
                 average=options.get("average", "inner"), dtype=output.get("dtype", "float64"),
                 species_weights=compression.get("species_weighting"),
+                compression=compression.get("mode", "off"), weighting=options.get("weighting"),
                 alphas=payload["alphas"], betas=payload["betas"])

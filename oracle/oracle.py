@@ -42,9 +42,30 @@ def _batch_arrays(batch):
     return numbers, positions, cells, pbc, offsets
 
 
-def feature_count(n_species: int, n_max: int, l_max: int) -> int:
+_COMPRESSION = {"off": 0, "mu2": 1, "mu1nu1": 2, "crossover": 3}
+_WEIGHTING = {None: 0, "poly": 1, "pow": 2, "exp": 3}
+
+
+def feature_count(n_species: int, n_max: int, l_max: int, compression: str = "off") -> int:
+    if compression == "mu2":
+        return n_max * (n_max + 1) // 2 * (l_max + 1)
+    if compression == "mu1nu1":
+        return n_species * n_max * n_max * (l_max + 1)
+    if compression == "crossover":
+        return n_species * n_max * (n_max + 1) // 2 * (l_max + 1)
     width = n_species * n_max
     return width * (width + 1) // 2 * (l_max + 1)
+
+
+def _weighting_args(weighting):
+    """(function, has_w0, r0, c, d, m, w0) with SoapKernel._ensure_native's
+    defaults (_kernels/core.py:247-254)."""
+    w = dict(weighting or {})
+    return (_WEIGHTING[w.get("function")], 1 if "w0" in w else 0, float(w.get("r0", 1.0)),
+            float(w.get("c", 1.0)), float(w.get("d", 0.0)), float(w.get("m", 1.0)), float(w.get("w0", 1.0)))
+
+
+_EX_TAIL = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int] + [ctypes.c_double] * 5 + [ctypes.c_int, _P]
 
 
 class _Checker:
@@ -108,6 +129,11 @@ class OracleLib(_Checker):
                                 ctypes.c_int, ctypes.c_int, ctypes.c_double, _P, _P, ctypes.c_int,
                                 ctypes.c_int, _P])
 
+        self._soap_ex = self.lib.oracle_soap_compute_ex
+        self._soap_ex.restype = ctypes.c_int
+        self._soap_ex.argtypes = ([_P] * 5 + [ctypes.c_int64, _P, ctypes.c_int, _P, ctypes.c_double,
+                                   ctypes.c_int, ctypes.c_int, ctypes.c_double, _P, _P] + _EX_TAIL)
+
         self._rows = self.lib.oracle_soap_rows
         self._rows.restype = ctypes.c_int
         self._rows.argtypes = ([_P] * 5 + [ctypes.c_int64, _P, ctypes.c_int, _P, ctypes.c_double,
@@ -134,19 +160,19 @@ class OracleLib(_Checker):
         return out
 
     def soap(self, batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average="off",
-             species_weights=None, num_threads=0):
+             species_weights=None, num_threads=0, compression="off", weighting=None):
         arrays = _batch_arrays(batch)
         structures = len(arrays[4]) - 1
         species = np.ascontiguousarray(species, dtype=np.int32)
         rows = structures if average != "off" else int(arrays[4][-1])
-        out = np.zeros((rows, feature_count(len(species), n_max, l_max)), np.float64)
+        out = np.zeros((rows, feature_count(len(species), n_max, l_max, compression)), np.float64)
         weights = None if species_weights is None else np.ascontiguousarray(species_weights, np.float64)
         alphas = np.ascontiguousarray(alphas, np.float64)
         betas = np.ascontiguousarray(betas, np.float64)
-        status = self._soap(*map(_ptr, arrays), structures, _ptr(species), len(species),
-                            None if weights is None else _ptr(weights), float(r_cut), int(n_max),
-                            int(l_max), float(sigma), _ptr(alphas), _ptr(betas), _AVERAGE[average],
-                            int(num_threads), _ptr(out))
+        status = self._soap_ex(*map(_ptr, arrays), structures, _ptr(species), len(species),
+                               None if weights is None else _ptr(weights), float(r_cut), int(n_max),
+                               int(l_max), float(sigma), _ptr(alphas), _ptr(betas), _AVERAGE[average],
+                               _COMPRESSION[compression], *_weighting_args(weighting), int(num_threads), _ptr(out))
         if status:
             raise ValueError(self.error())
         return out
@@ -168,6 +194,29 @@ class RefLib(_Checker):
 
     def _graph_handle(self, arrays, structures, cutoff):
         return self._build(*map(_ptr, arrays), structures, cutoff, 1)
+
+    def soap_ex(self, batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average="off",
+                species_weights=None, num_threads=0, compression="off", weighting=None):
+        """compute_soap with species weights, compression and weighting (ref_soap_compute_ex)."""
+        fn = self.lib.ref_soap_compute_ex
+        fn.restype = ctypes.c_int
+        fn.argtypes = ([_P] * 5 + [ctypes.c_int64, _P, ctypes.c_int, _P, ctypes.c_double, ctypes.c_int,
+                                   ctypes.c_int, ctypes.c_double, _P, _P] + _EX_TAIL)
+        arrays = _batch_arrays(batch)
+        structures = len(arrays[4]) - 1
+        species = np.ascontiguousarray(species, dtype=np.int32)
+        rows = structures if average != "off" else int(arrays[4][-1])
+        out = np.zeros((rows, feature_count(len(species), n_max, l_max, compression)), np.float64)
+        weights = None if species_weights is None else np.ascontiguousarray(species_weights, np.float64)
+        alphas = np.ascontiguousarray(alphas, np.float64)
+        betas = np.ascontiguousarray(betas, np.float64)
+        status = fn(*map(_ptr, arrays), structures, _ptr(species), len(species),
+                    None if weights is None else _ptr(weights), float(r_cut), int(n_max), int(l_max), float(sigma),
+                    _ptr(alphas), _ptr(betas), _AVERAGE[average], _COMPRESSION[compression],
+                    *_weighting_args(weighting), int(num_threads), _ptr(out))
+        if status:
+            raise ValueError(self.error())
+        return out
 
     def soap(self, batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average="off",
              species_weights=None, num_threads=0):

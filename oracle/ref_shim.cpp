@@ -74,6 +74,52 @@ int ref_soap_compute(
     }
 }
 
+// compute_soap with every SoapOptions field this engine covers: species
+// weights (NULL: 1.0 each), compression 0..3, weighting function 0..3 with
+// its parameters, w0.
+int ref_soap_compute_ex(
+    const int32_t* numbers, const double* positions, const double* cells,
+    const int32_t* pbc, const int64_t* offsets, int64_t structures,
+    const int32_t* species, int n_species, const double* species_weights, double r_cut, int n_max,
+    int l_max, double sigma, const double* alphas, const double* betas, int average, int compression,
+    int weighting_function, int weighting_has_w0, double weighting_r0, double weighting_c,
+    double weighting_d, double weighting_m, double weighting_w0, int num_threads, double* out) {
+    try {
+        mdescriptor::SoapOptions options;
+        options.species.assign(species, species + n_species);
+        options.r_cut = r_cut;
+        options.n_max = n_max;
+        options.l_max = l_max;
+        options.sigma = sigma;
+        options.radial_basis = 0;
+        const size_t count = static_cast<size_t>((l_max + 1) * n_max);
+        options.alphas.assign(alphas, alphas + count);
+        options.betas.assign(betas, betas + count * n_max);
+        if (species_weights)
+            options.species_weights.assign(species_weights, species_weights + n_species);
+        else
+            options.species_weights.assign(static_cast<size_t>(n_species), 1.0);
+        options.compression = compression;
+        options.weighting_has_function = weighting_function != 0;
+        options.weighting_function = weighting_function;
+        options.weighting_has_w0 = weighting_has_w0 != 0;
+        options.weighting_r0 = weighting_r0;
+        options.weighting_c = weighting_c;
+        options.weighting_d = weighting_d;
+        options.weighting_m = weighting_m;
+        options.weighting_w0 = weighting_w0;
+        options.inner_average = average == 1;
+        options.outer_average = average == 2;
+        options.num_threads = num_threads;
+        mdescriptor::compute_soap(
+            make_view(numbers, positions, cells, pbc, offsets, structures), options, out, nullptr);
+        return 0;
+    } catch (const std::exception& error) {
+        g_error = error.what();
+        return 1;
+    }
+}
+
 void* ref_graph_build(
     const int32_t* numbers, const double* positions, const double* cells,
     const int32_t* pbc, const int64_t* offsets, int64_t structures, double cutoff,

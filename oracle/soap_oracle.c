@@ -348,6 +348,10 @@ void oracle_graph_free(void* handle) {
 
 typedef struct {
     int n_species, n_max, l_max, width, harmonics;
+    int compression;            /* 0 off, 1 mu2, 2 mu1nu1, 3 crossover */
+    int weighting_function;     /* 0 none, 1 poly, 2 pow, 3 exp */
+    int weighting_has_w0;
+    double weighting_r0, weighting_c, weighting_d, weighting_m, weighting_w0;
     const int32_t* species;
     const double* species_weights;
     const double* betas;
@@ -399,6 +403,27 @@ static void solid_harmonics(const soap_plan* plan, double x, double y, double z,
     }
 }
 
+/* soap_weight (soap.cpp:389-420): weighting function of the distance, w0 for
+ * the exact self pair, times the species weight. */
+static double soap_weight(const soap_plan* plan, double distance, int exact_self, int type) {
+    double value = 1.0;
+    if (plan->weighting_function != 0) {
+        const double ratio = distance / plan->weighting_r0;
+        if (plan->weighting_function == 1) {
+            value = distance > plan->weighting_r0
+                        ? 0.0
+                        : plan->weighting_c * pow(1.0 + 2.0 * ratio * ratio * ratio - 3.0 * ratio * ratio,
+                                                  plan->weighting_m);
+        } else if (plan->weighting_function == 2) {
+            value = plan->weighting_c / (plan->weighting_d + pow(ratio, plan->weighting_m));
+        } else {
+            value = plan->weighting_c / (plan->weighting_d + exp(-ratio));
+        }
+    }
+    if (exact_self && plan->weighting_has_w0) value = plan->weighting_w0;
+    return value * plan->species_weights[type];
+}
+
 static int species_type(const soap_plan* plan, int32_t z) {
     for (int t = 0; t < plan->n_species; ++t)
         if (plan->species[t] == z) return t;
@@ -413,7 +438,9 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
     const int S = plan->n_species, n = plan->n_max, L = plan->l_max, H = plan->harmonics;
     const int w = plan->width;
     const int64_t count = pair_end - pair_begin;
-    memset(coefficients, 0, sizeof(double) * (size_t)S * n * H);
+    const int pooled = plan->compression == 1;  /* mu2: one density over all species */
+    const int CT = pooled ? 1 : S;
+    memset(coefficients, 0, sizeof(double) * (size_t)CT * n * H);
     /* scratch layout */
     int64_t* order = (int64_t*)scratch;
     double* harm = scratch + count;                 /* [count][H] */
@@ -424,13 +451,19 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
     int64_t type_offsets[65];
     int64_t cursor[64];
     for (int t = 0; t <= S; ++t) type_offsets[t] = 0;
-    for (int64_t i = 0; i < count; ++i)
-        ++type_offsets[atom_types[pairs->atoms[pair_begin + i] - structure_begin_index] + 1];
-    for (int t = 0; t < S; ++t) type_offsets[t + 1] += type_offsets[t];
-    for (int t = 0; t < S; ++t) cursor[t] = type_offsets[t];
-    for (int64_t i = 0; i < count; ++i) {
-        const int t = atom_types[pairs->atoms[pair_begin + i] - structure_begin_index];
-        order[cursor[t]++] = pair_begin + i;
+    if (pooled) {
+        /* graph order, one type range (soap.cpp:716-737) */
+        type_offsets[1] = count;
+        for (int64_t i = 0; i < count; ++i) order[i] = pair_begin + i;
+    } else {
+        for (int64_t i = 0; i < count; ++i)
+            ++type_offsets[atom_types[pairs->atoms[pair_begin + i] - structure_begin_index] + 1];
+        for (int t = 0; t < S; ++t) type_offsets[t + 1] += type_offsets[t];
+        for (int t = 0; t < S; ++t) cursor[t] = type_offsets[t];
+        for (int64_t i = 0; i < count; ++i) {
+            const int t = atom_types[pairs->atoms[pair_begin + i] - structure_begin_index];
+            order[cursor[t]++] = pair_begin + i;
+        }
     }
     for (int64_t j = 0; j < count; ++j) {
         const int64_t p = order[j];
@@ -438,10 +471,15 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
         solid_harmonics(plan, d[0], d[1], d[2], d[0] * d[0] + d[1] * d[1] + d[2] * d[2], real, imag,
                         harm + j * H);
     }
-    for (int t = 0; t < S; ++t)
-        for (int64_t j = type_offsets[t]; j < type_offsets[t + 1]; ++j) weight[j] = plan->species_weights[t];
-    (void)local;
-    for (int t = 0; t < S; ++t) {
+    for (int64_t j = 0; j < count; ++j) {
+        /* NeighborView::exact_self (neighbor.cpp:683-689): the centre itself, image 0 */
+        const int64_t p = order[j];
+        const int32_t* sh = pairs->shifts + 3 * p;
+        const int self = pairs->atoms[p] - structure_begin_index == local && sh[0] == 0 && sh[1] == 0 && sh[2] == 0;
+        const int type = atom_types[pairs->atoms[p] - structure_begin_index];
+        weight[j] = soap_weight(plan, sqrt(pairs->distance2[p]), self, type);
+    }
+    for (int t = 0; t < CT; ++t) {
         for (int l = 0; l <= L; ++l) {
             const int off = l * l, mc = 2 * l + 1;
             for (int k = 0; k < n; ++k) {
@@ -462,10 +500,49 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
     }
 }
 
-/* power spectrum, compression off (soap.cpp:997-1012) */
+/* power spectrum in every compression layout (soap.cpp:933-1017) */
 static void power_spectrum(const soap_plan* plan, const double* c, double* out) {
     const int S = plan->n_species, n = plan->n_max, L = plan->l_max, H = plan->harmonics;
     int64_t f = 0;
+    if (plan->compression == 1) { /* mu2: one pooled density, l -> n1 -> n2 >= n1 */
+        for (int l = 0; l <= L; ++l)
+            for (int n1 = 0; n1 < n; ++n1)
+                for (int n2 = n1; n2 < n; ++n2) {
+                    double sum = 0.0;
+                    for (int m = 0; m < 2 * l + 1; ++m) sum += c[n1 * H + l * l + m] * c[n2 * H + l * l + m];
+                    out[f++] = plan->power_prefactors[l] * sum;
+                }
+        return;
+    }
+    if (plan->compression == 2) { /* mu1nu1: species x species-summed density, all n2 */
+        double* summed = calloc((size_t)n * H, sizeof(double));
+        for (int t = 0; t < S; ++t)
+            for (int k = 0; k < n; ++k)
+                for (int i = 0; i < H; ++i) summed[k * H + i] += c[(t * n + k) * H + i];
+        for (int t = 0; t < S; ++t)
+            for (int l = 0; l <= L; ++l)
+                for (int n1 = 0; n1 < n; ++n1)
+                    for (int n2 = 0; n2 < n; ++n2) {
+                        double sum = 0.0;
+                        for (int m = 0; m < 2 * l + 1; ++m)
+                            sum += c[(t * n + n1) * H + l * l + m] * summed[n2 * H + l * l + m];
+                        out[f++] = plan->power_prefactors[l] * sum;
+                    }
+        free(summed);
+        return;
+    }
+    if (plan->compression == 3) { /* crossover: same-species pairs, l -> n1 -> n2 >= n1 */
+        for (int t = 0; t < S; ++t)
+            for (int l = 0; l <= L; ++l)
+                for (int n1 = 0; n1 < n; ++n1)
+                    for (int n2 = n1; n2 < n; ++n2) {
+                        double sum = 0.0;
+                        for (int m = 0; m < 2 * l + 1; ++m)
+                            sum += c[(t * n + n1) * H + l * l + m] * c[(t * n + n2) * H + l * l + m];
+                        out[f++] = plan->power_prefactors[l] * sum;
+                    }
+        return;
+    }
     for (int t1 = 0; t1 < S; ++t1)
         for (int t2 = t1; t2 < S; ++t2)
             for (int l = 0; l <= L; ++l) {
@@ -481,9 +558,16 @@ static void power_spectrum(const soap_plan* plan, const double* c, double* out) 
             }
 }
 
+int64_t oracle_soap_feature_count_ex(int n_species, int n_max, int l_max, int compression) {
+    const int64_t W = l_max + 1, n = n_max, S = n_species;
+    if (compression == 1) return n * (n + 1) / 2 * W;
+    if (compression == 2) return S * n * n * W;
+    if (compression == 3) return S * n * (n + 1) / 2 * W;
+    return (S * n) * (S * n + 1) / 2 * W;
+}
+
 int64_t oracle_soap_feature_count(int n_species, int n_max, int l_max) {
-    const int64_t width = (int64_t)n_species * n_max;
-    return width * (width + 1) / 2 * (l_max + 1);
+    return oracle_soap_feature_count_ex(n_species, n_max, l_max, 0);
 }
 
 /*
@@ -491,16 +575,27 @@ int64_t oracle_soap_feature_count(int n_species, int n_max, int l_max) {
  * average: 0 off (rows = atoms), 1 inner, 2 outer (rows = structures).
  * species_weights may be NULL (all 1.0).  out is fp64 (rows, F).
  */
-int oracle_soap_compute(const int32_t* numbers, const double* positions, const double* cells,
-                        const int32_t* pbc, const int64_t* offsets, int64_t structures,
-                        const int32_t* species, int n_species, const double* species_weights,
-                        double r_cut, int n_max, int l_max, double sigma, const double* alphas,
-                        const double* betas, int average, int num_threads, double* out) {
+int oracle_soap_compute_ex(const int32_t* numbers, const double* positions, const double* cells,
+                           const int32_t* pbc, const int64_t* offsets, int64_t structures,
+                           const int32_t* species, int n_species, const double* species_weights,
+                           double r_cut, int n_max, int l_max, double sigma, const double* alphas,
+                           const double* betas, int average, int compression, int weighting_function,
+                           int weighting_has_w0, double weighting_r0, double weighting_c, double weighting_d,
+                           double weighting_m, double weighting_w0, int num_threads, double* out) {
     if (validate_batch(numbers, positions, cells, pbc, offsets, structures)) return 1;
     if (!isfinite(r_cut) || !isfinite(sigma) || r_cut <= 0.0 || sigma <= 0.0 || n_max < 1 || l_max < 0
-        || l_max > 20 || n_species < 1 || n_species > 64 || average < 0 || average > 2)
+        || l_max > 20 || n_species < 1 || n_species > 64 || average < 0 || average > 2 || compression < 0
+        || compression > 3 || weighting_function < 0 || weighting_function > 3)
         return fail("invalid SOAP parameters");
     soap_plan plan;
+    plan.compression = compression;
+    plan.weighting_function = weighting_function;
+    plan.weighting_has_w0 = weighting_has_w0;
+    plan.weighting_r0 = weighting_r0;
+    plan.weighting_c = weighting_c;
+    plan.weighting_d = weighting_d;
+    plan.weighting_m = weighting_m;
+    plan.weighting_w0 = weighting_w0;
     plan.n_species = n_species;
     plan.n_max = n_max;
     plan.l_max = l_max;
@@ -536,8 +631,8 @@ int oracle_soap_compute(const int32_t* numbers, const double* positions, const d
         }
     }
     const double cutoff = r_cut + sigma * sqrt(-2.0 * log(1e-3));
-    const int64_t F = oracle_soap_feature_count(n_species, n_max, l_max);
-    const int64_t csize = (int64_t)n_species * n_max * plan.harmonics;
+    const int64_t F = oracle_soap_feature_count_ex(n_species, n_max, l_max, compression);
+    const int64_t csize = (int64_t)(compression == 1 ? 1 : n_species) * n_max * plan.harmonics;
     int status = 0;
 #ifdef _OPENMP
     const int threads = num_threads > 0 ? num_threads : omp_get_max_threads();
@@ -601,6 +696,17 @@ int oracle_soap_compute(const int32_t* numbers, const double* positions, const d
     return status;
 }
 
+/* compute_soap with compression off and no weighting function. */
+int oracle_soap_compute(const int32_t* numbers, const double* positions, const double* cells,
+                        const int32_t* pbc, const int64_t* offsets, int64_t structures,
+                        const int32_t* species, int n_species, const double* species_weights,
+                        double r_cut, int n_max, int l_max, double sigma, const double* alphas,
+                        const double* betas, int average, int num_threads, double* out) {
+    return oracle_soap_compute_ex(numbers, positions, cells, pbc, offsets, structures, species, n_species,
+                                  species_weights, r_cut, n_max, l_max, sigma, alphas, betas, average, 0, 0, 0, 1.0,
+                                  1.0, 0.0, 1.0, 1.0, num_threads, out);
+}
+
 /*
  * Rows of the average-"off" feature matrix for selected atoms only (global
  * indices `rows`, any order): the same per-centre arithmetic as
@@ -617,6 +723,11 @@ int oracle_soap_rows(const int32_t* numbers, const double* positions, const doub
         || l_max > 20 || n_species < 1 || n_species > 64)
         return fail("invalid SOAP parameters");
     soap_plan plan;
+    plan.compression = 0;
+    plan.weighting_function = 0;
+    plan.weighting_has_w0 = 0;
+    plan.weighting_r0 = plan.weighting_c = plan.weighting_m = plan.weighting_w0 = 1.0;
+    plan.weighting_d = 0.0;
     plan.n_species = n_species;
     plan.n_max = n_max;
     plan.l_max = l_max;

@@ -102,6 +102,11 @@ ADAPTER_KWARGS = [
     dict(species=[1, 8], r_cut=4.5, n_max=4, l_max=3, average="off"),
     dict(species=[8, 1], r_cut=4.0, n_max=3, l_max=4, sigma=0.8, average="inner",
          compression={"mode": "off", "species_weighting": {1: 0.5, 8: 2.0}}),
+    dict(species=[1, 8], r_cut=4.5, n_max=8, l_max=6, average="off",
+         compression={"mode": "mu1nu1", "species_weighting": {1: 0.8, 8: 1.25}},
+         weighting={"function": "poly", "r0": 6.0, "c": 1.0, "m": 2.0}),
+    dict(species=[8, 1], r_cut=4.0, n_max=4, l_max=3, average="outer", compression={"mode": "mu2"},
+         weighting={"function": "exp", "r0": 1.5, "c": 2.0, "d": 0.5, "w0": 0.25}),
 ]
 
 

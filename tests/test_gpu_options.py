@@ -1,0 +1,104 @@
+"""GPU parity of compression layouts and radial weighting (paired-channel
+kernel) against the CPU checker, which tests/test_oracle_options.py pins to
+the reference's own compute_soap."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _util import AGREE_FLOOR, AGREE_TOL, assert_features_close, max_rel_err
+from mdescriptor_b200 import workloads
+from mdescriptor_b200.basis import basis_gto
+from mdescriptor_b200.soap import Soap
+from test_oracle_options import WEIGHTINGS, mixed_batch
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = {
+    # species, r_cut, n_max, l_max, sigma
+    "n8l6": ((1, 6, 7, 8), 4.0, 8, 6, 1.0),   # register tail (n_max = 8)
+    "n4l3": ((1, 6, 8), 3.6, 4, 3, 0.8),      # tensor-core / generic tails
+    "n6l4": ((1, 6, 8), 3.8, 6, 4, 1.0),
+}
+
+
+def cluster_batch(seed: int, structures: int = 6) -> workloads.Batch:
+    rng = np.random.default_rng(seed)
+    numbers, positions, offsets = [], [], [0]
+    for _ in range(structures):
+        n = int(rng.integers(3, 30))
+        positions.append(rng.uniform(-3.0, 3.0, (n, 3)))
+        numbers.append(rng.choice([1, 6, 7, 8], n).astype(np.int32))
+        offsets.append(offsets[-1] + n)
+    return workloads.Batch(np.concatenate(numbers), np.concatenate(positions), np.zeros((structures, 3, 3)),
+                           np.zeros((structures, 3), np.int32), np.array(offsets, np.int64))
+
+
+def assert_close(got, want, dtype):
+    """float32 rows: the float32 bound; float64 rows: the agreement bound of two
+    fp64 implementations that sum in different orders (the l = 6 cancellations
+    of the harmonic recurrences differ by up to ~5e-10 at floor 1e-4)."""
+    if dtype == "float32":
+        assert_features_close(got, want, dtype)
+    else:
+        err = max_rel_err(got, want, AGREE_FLOOR)
+        assert err <= AGREE_TOL, f"float64 max rel err {err:.3e} > {AGREE_TOL}"
+
+
+def run_both(oracle, shape, batch, average, dtype, compression, weighting, species_weights=None):
+    species, r_cut, n_max, l_max, sigma = SHAPES[shape]
+    alphas, betas = basis_gto(r_cut, n_max, l_max)
+    soap = Soap(species, r_cut=r_cut, n_max=n_max, l_max=l_max, sigma=sigma, average=average, dtype=dtype,
+                species_weights=species_weights, alphas=alphas, betas=betas, compression=compression,
+                weighting=weighting)
+    got = soap.compute(batch, devices=[0])
+    want = oracle.soap(batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average=average,
+                       species_weights=species_weights, compression=compression, weighting=weighting)
+    return soap, got, want
+
+
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+@pytest.mark.parametrize("compression", ["off", "mu2", "mu1nu1", "crossover"])
+@pytest.mark.parametrize("average", ["off", "inner", "outer"])
+def test_compression_layouts(oracle, cuda_device, shape, compression, average):
+    batch = cluster_batch(11) if shape == "n8l6" else mixed_batch(3)
+    species = SHAPES[shape][0]
+    weights = list(np.linspace(0.6, 1.8, len(species)))
+    for dtype in ("float64", "float32"):
+        soap, got, want = run_both(oracle, shape, batch, average, dtype, compression, None, weights)
+        assert "soap_paired_kernel" in soap.kernel()
+        assert_close(got, want, dtype)
+
+
+@pytest.mark.parametrize("weighting", sorted(WEIGHTINGS))
+@pytest.mark.parametrize("shape", ["n8l6", "n4l3"])
+def test_weighting_functions(oracle, cuda_device, weighting, shape):
+    batch = cluster_batch(5) if shape == "n8l6" else mixed_batch(9)
+    for compression, average in (("off", "off"), ("mu2", "inner"), ("crossover", "outer")):
+        _, got, want = run_both(oracle, shape, batch, average, "float64", compression, WEIGHTINGS[weighting])
+        assert_close(got, want, "float64")
+
+
+def test_config2_rows_with_weighting(oracle, cuda_device):
+    """A full config-2 structure slice (the benchmark shape) under poly weighting and mu1nu1."""
+    cfg = workloads.CONFIGS[2]
+    batch = workloads.config2(structures=3)
+    alphas, betas = basis_gto(cfg.r_cut, cfg.n_max, cfg.l_max)
+    weighting = {"function": "poly", "r0": 7.0, "c": 1.0, "m": 2.0, "w0": 0.5}
+    for compression in ("off", "mu1nu1"):
+        soap = Soap(cfg.species, r_cut=cfg.r_cut, n_max=cfg.n_max, l_max=cfg.l_max, average="off",
+                    dtype="float32", alphas=alphas, betas=betas, compression=compression, weighting=weighting)
+        got = soap.compute(batch, devices=[0])
+        want = oracle.soap(batch, cfg.species, cfg.r_cut, cfg.n_max, cfg.l_max, cfg.sigma, alphas, betas,
+                           compression=compression, weighting=weighting)
+        assert_features_close(got, want, "float32")
+
+
+def test_weighting_needs_paired_kernel_shape():
+    """Shapes outside the paired kernel (here l_max = 8) reject weighting and
+    compression with a clear error instead of computing something else."""
+    alphas, betas = basis_gto(5.0, 8, 8)
+    with pytest.raises(ValueError, match="paired-channel kernel"):
+        Soap((13, 29), r_cut=5.0, n_max=8, l_max=8, average="off", dtype="float64", alphas=alphas, betas=betas,
+             compression="mu2")

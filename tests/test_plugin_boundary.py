@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
     lib = ctypes.CDLL(str(_lib.LIB_PATH))
     for name in declared:
         assert hasattr(lib, name), name
-    assert _lib.lib.mdsoap_abi_version() == 1
+    assert _lib.lib.mdsoap_abi_version() == 2
 
 
 def test_plugin_module_attributes():
@@ -78,8 +78,8 @@ def test_unsupported_descriptors_and_options_raise_mapped_errors():
         plugin.create_backend("ACSF", {"species": [1, 8]})
     for key, value, match in [
         ("rbf", "polynomial", "radial basis"),
-        ("compression", {"mode": "mu2"}, "compression"),
-        ("weighting", {"function": "poly", "r0": 3.0, "c": 1.0, "m": 2.0}, "weighting"),
+        ("compression", {"mode": "mu3"}, "compression"),
+        ("weighting", {"function": "gauss", "r0": 3.0, "c": 1.0}, "weighting"),
         ("average", "median", "average"),
         ("_cuda_feature_count", 7, "feature count"),
         ("n_max", 40, "invalid CUDA SOAP parameters"),
@@ -115,7 +115,8 @@ def test_labels_follow_declared_species_order():
     from mdescriptor_b200.basis import labels
 
     for _, options, _ in adapter_cases():
-        assert tuple(options["_cuda_labels"]) == labels(options["species"], options["n_max"], options["l_max"])
+        mode = (options.get("compression") or {}).get("mode", "off")
+        assert tuple(options["_cuda_labels"]) == labels(options["species"], options["n_max"], options["l_max"], mode)
 
 
 def _reference_api():
