@@ -100,6 +100,7 @@ typedef struct {
 
 typedef struct mdsoap_plan mdsoap_plan;
 typedef struct mdsoap_graph mdsoap_graph;
+typedef struct mdsoap_pairs mdsoap_pairs;
 
 /* Cooperative cancellation probe; non-zero means "stop".  Polled between
  * blocks of work, never inside a kernel. */
@@ -251,6 +252,28 @@ int mdsoap_graph_copy(const mdsoap_graph* graph, int64_t* offsets, int32_t* atom
                       double* displacements, double* distance2);
 
 void mdsoap_graph_destroy(mdsoap_graph* graph);
+
+/* The NeighborList descriptor of a host batch, computed on `device`: every
+ * pair within `cutoff` (inclusive), without the exact self pair unless
+ * `self_pairs`, and only one orientation of each pair unless `full_list`
+ * (keep_half_neighbor: the larger atom index, ties broken by the first
+ * non-zero image shift being positive).  Rows come in the reference's order
+ * (centre by centre, then the reference cell-list order within a centre).
+ * A centre may hold at most 2048 listed pairs (MDSOAP_CAPACITY_OVERFLOW beyond).
+ * Replaces: compute_neighbor_list (cpp/src/standalone/neighbor_list.cpp:15-75)
+ * and the reference plugin's NeighborList branch (cpp/cuda/src/backend.cu:358-471). */
+int mdsoap_neighbor_list(const mdsoap_batch* batch, double cutoff, int32_t full_list, int32_t self_pairs,
+                         int32_t device, mdsoap_pairs** pairs);
+
+int64_t mdsoap_pairs_count(const mdsoap_pairs* pairs);
+
+/* Copy the table out: records float64[pairs*5] = (centre, atom, shift a, shift
+ * b, shift c) with batch-global atom indices, values float64[pairs*4] = (dx,
+ * dy, dz, distance), row_offsets int64[structures+1] = first row of each
+ * structure.  Any pointer may be NULL to skip that array. */
+int mdsoap_pairs_copy(const mdsoap_pairs* pairs, double* records, double* values, int64_t* row_offsets);
+
+void mdsoap_pairs_destroy(mdsoap_pairs* pairs);
 
 #ifdef __cplusplus
 }

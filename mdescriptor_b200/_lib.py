@@ -94,6 +94,15 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_plan_feature_count.restype = ctypes.c_int64
     lib.mdsoap_plan_rows.argtypes = [_P, ctypes.POINTER(BatchView)]
     lib.mdsoap_plan_rows.restype = ctypes.c_int64
+    lib.mdsoap_neighbor_list.argtypes = [ctypes.POINTER(BatchView), ctypes.c_double, ctypes.c_int32, ctypes.c_int32,
+                                         ctypes.c_int32, ctypes.POINTER(_P)]
+    lib.mdsoap_neighbor_list.restype = ctypes.c_int
+    lib.mdsoap_pairs_count.argtypes = [_P]
+    lib.mdsoap_pairs_count.restype = ctypes.c_int64
+    lib.mdsoap_pairs_copy.argtypes = [_P, _P, _P, _P]
+    lib.mdsoap_pairs_copy.restype = ctypes.c_int
+    lib.mdsoap_pairs_destroy.argtypes = [_P]
+    lib.mdsoap_pairs_destroy.restype = None
     lib.mdsoap_plan_kernel.argtypes = [_P]
     lib.mdsoap_plan_kernel.restype = ctypes.c_char_p
     lib.mdsoap_compute.argtypes = [_P, ctypes.POINTER(BatchView), _P, _P, ctypes.c_int32, _P, _P]
@@ -150,6 +159,10 @@ EXPORTED = (
     "mdsoap_graph_pairs",
     "mdsoap_graph_copy",
     "mdsoap_graph_destroy",
+    "mdsoap_neighbor_list",
+    "mdsoap_pairs_count",
+    "mdsoap_pairs_copy",
+    "mdsoap_pairs_destroy",
 )
 
 

@@ -23,6 +23,7 @@ enum DeviceError : unsigned {
     kErrMixedPbc = 4u,         // pbc neither all 0 nor all 1
     kErrSingularCell = 8u,     // |det(cell)| < 1e-14 for a periodic structure
     kErrPairCapacity = 16u,    // neighbour CSR fill overran its counted capacity
+    kErrExtendedRange = 32u,   // image-expanded structure beyond int32 atom indices
 };
 
 // Per-structure geometry and binning plan, written by bin_structures_kernel.

@@ -125,8 +125,22 @@ int cancel_probe(void* context) {
 class Backend {
 public:
     Backend(std::string name, py::dict options) : name_(std::move(name)), options_(std::move(options)) {
+        if (name_ == "NeighborList") {
+            // cpp/cuda/src/backend.cu:358-362 option names and defaults.
+            list_ = true;
+            list_cutoff_ = option(options_, "cutoff", 6.0);
+            list_full_ = option(options_, "full_neighbor_list", true);
+            list_self_ = option(options_, "self_pairs", false);
+            if (!(list_cutoff_ > 0.0) || !std::isfinite(list_cutoff_))
+                throw std::invalid_argument("neighbor cutoff must be finite and positive");
+            features_ = 4;
+            for (const char* label : {"dx", "dy", "dz", "distance"}) labels_.append(label);
+            devices_ = device_list();
+            return;
+        }
         if (name_ != "SOAP")
-            throw CudaUnavailable("this CUDA plugin implements SOAP only; '" + name_ + "' has no CUDA backend here");
+            throw CudaUnavailable("this CUDA plugin implements SOAP and NeighborList only; '" + name_ +
+                                  "' has no CUDA backend here");
         species_ = option(options_, "species", std::vector<int32_t>{});
         if (species_.empty()) throw std::invalid_argument("SOAP species must not be empty");
         n_max_ = option(options_, "n_max", 8);
@@ -242,7 +256,7 @@ public:
             py::gil_scoped_release release;
             guard.lock();
         }
-        if (closed_ || plan_ == nullptr) throw std::runtime_error("CUDA backend is closed");
+        if (closed_ || (plan_ == nullptr && !list_)) throw std::runtime_error("CUDA backend is closed");
         auto numbers = py::array_t<int32_t, py::array::c_style | py::array::forcecast>::ensure(batch.attr("numbers"));
         auto positions = py::array_t<double, py::array::c_style | py::array::forcecast>::ensure(batch.attr("positions"));
         auto cells = py::array_t<double, py::array::c_style | py::array::forcecast>::ensure(batch.attr("cells"));
@@ -261,6 +275,7 @@ public:
                 throw CudaCancelledError("descriptor computation was cancelled");
         }
         mdsoap_batch view{numbers.data(), positions.data(), cells.data(), pbc.data(), offsets.data(), structures, atoms};
+        if (list_) return compute_list(view, structures, control);
         const int64_t rows = average_ == MDSOAP_AVERAGE_OFF ? atoms : structures;
         py::array values = f64_ ? py::array(py::array_t<double>({(py::ssize_t)rows, (py::ssize_t)features_}))
                                 : py::array(py::array_t<float>({(py::ssize_t)rows, (py::ssize_t)features_}));
@@ -285,6 +300,39 @@ public:
             std::copy(offsets.data(), offsets.data() + structures + 1, row_offsets.mutable_data());
             result["row_offsets"] = row_offsets;
         }
+        result["labels"] = labels_;
+        result["metadata"] = metadata();
+        return std::move(result);
+    }
+
+    // NeighborList: pair records and features (cpp/cuda/src/backend.cu:418-470).
+    py::object compute_list(const mdsoap_batch& view, int64_t structures, py::object control) {
+        mdsoap_pairs* pairs = nullptr;
+        int status;
+        {
+            py::gil_scoped_release release;
+            status = mdsoap_neighbor_list(&view, list_cutoff_, list_full_ ? 1 : 0, list_self_ ? 1 : 0,
+                                          devices_.empty() ? 0 : devices_[0], &pairs);
+        }
+        if (status != MDSOAP_OK) throw_status(status);
+        const int64_t rows = mdsoap_pairs_count(pairs);
+        py::array_t<double> values({(py::ssize_t)rows, (py::ssize_t)4});
+        py::array_t<double> records({(py::ssize_t)rows, (py::ssize_t)5});
+        py::array_t<int64_t> row_offsets(structures + 1);
+        mdsoap_pairs_copy(pairs, records.mutable_data(), values.mutable_data(), row_offsets.mutable_data());
+        mdsoap_pairs_destroy(pairs);
+        if (!control.is_none()) {
+            if (py::cast<bool>(control.attr("cancelled")()))
+                throw CudaCancelledError("descriptor computation was cancelled");
+            if (py::hasattr(control, "mark_completed"))
+                for (int64_t s = 0; s < structures; ++s) control.attr("mark_completed")();
+        }
+        py::dict result;
+        result["values"] = values;
+        result["_mdescriptor_owned_values"] = true;
+        result["level"] = "pair";
+        result["row_offsets"] = row_offsets;
+        result["pair_records"] = records;
         result["labels"] = labels_;
         result["metadata"] = metadata();
         return std::move(result);
@@ -316,6 +364,7 @@ public:
         }
         if (!closed_) {
             closed_ = true;
+            list_ = false;
             if (plan_) mdsoap_plan_destroy(plan_);
             plan_ = nullptr;
         }
@@ -343,6 +392,8 @@ private:
     bool weighting_has_w0_ = false;
     double weighting_r0_ = 1.0, weighting_c_ = 1.0, weighting_d_ = 0.0, weighting_m_ = 1.0, weighting_w0_ = 1.0;
     bool f64_ = true;
+    bool list_ = false, list_full_ = true, list_self_ = false;  // NeighborList backend
+    double list_cutoff_ = 6.0;
     int64_t features_ = 0;
     py::list labels_;
     std::vector<int32_t> devices_;

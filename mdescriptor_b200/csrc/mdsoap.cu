@@ -8,6 +8,7 @@
 #include "soap_mma.cuh"
 #include "soap_pair.cuh"
 #include "soap_paired.cuh"
+#include "neighbor_list.cuh"
 
 #include <cuda_runtime.h>
 
@@ -56,7 +57,8 @@ std::string device_error_text(unsigned bits) {
     if (bits & kErrMixedPbc) return "mixed periodicity is not supported; use all-zero or all-one pbc";
     if (bits & kErrSingularCell) return "cells must be nonsingular";
     if (bits & kErrWrapRange) return "periodic image range exceeds integer range";
-    if (bits & kErrPairCapacity) return "neighbour graph fill exceeded its counted capacity";
+    if (bits & kErrPairCapacity) return "neighbour list: a centre has more pairs than the GPU list holds (2048)";
+    if (bits & kErrExtendedRange) return "neighbor extended atom index exceeds int32 range";
     return "device error";
 }
 
@@ -724,6 +726,12 @@ struct mdsoap_graph {
     std::vector<int64_t> offsets;
     std::vector<int32_t> atom_ids, shifts;
     std::vector<double> displacements, distance2;
+};
+
+struct mdsoap_pairs {
+    std::vector<double> records;      // [pairs][5]
+    std::vector<double> values;       // [pairs][4]
+    std::vector<int64_t> row_offsets; // [structures + 1]
 };
 
 // ---------------------------------------------------------------------------
@@ -1515,6 +1523,130 @@ int mdsoap_graph_build(const mdsoap_batch* batch, double cutoff, int32_t device,
         return fail(MDSOAP_INTERNAL, e.what());
     }
 }
+
+int mdsoap_neighbor_list(const mdsoap_batch* batch, double cutoff, int32_t full_list, int32_t self_pairs,
+                         int32_t device, mdsoap_pairs** pairs_out) {
+    if (!batch || !pairs_out) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    *pairs_out = nullptr;
+    if (!std::isfinite(cutoff) || cutoff <= 0.0)
+        return fail(MDSOAP_INVALID_ARGUMENT, "neighbor cutoff must be finite and positive");
+    try {
+        validate_host_batch(nullptr, *batch);
+        int count = 0;
+        const cudaError_t probe_err = cudaGetDeviceCount(&count);
+        if (probe_err != cudaSuccess || count == 0)
+            raise(MDSOAP_DEVICE_UNAVAILABLE, std::string("no CUDA device available: ") + cudaGetErrorString(probe_err));
+        if (device < 0 || device >= count) raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device index out of range");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        auto out = std::make_unique<mdsoap_pairs>();
+        const int64_t atoms = batch->atoms, S = batch->structures;
+        out->row_offsets.assign(S + 1, 0);
+        if (atoms == 0 || S == 0) {
+            *pairs_out = out.release();
+            return MDSOAP_OK;
+        }
+        cudaStream_t stream = nullptr;
+        check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+        struct StreamGuard {
+            cudaStream_t s;
+            ~StreamGuard() { cudaStreamDestroy(s); }
+        } guard{stream};
+        Workspace w;
+        struct WorkGuard {
+            Workspace& w;
+            ~WorkGuard() { w.release(); }
+        } wguard{w};
+        DeviceBytes error, counts, offsets_d, grids, records_d, values_d;
+        struct BytesGuard {
+            std::vector<DeviceBytes*> list;
+            ~BytesGuard() {
+                for (auto* b : list) b->release();
+            }
+        } bguard{{&error, &counts, &offsets_d, &grids, &records_d, &values_d}};
+        w.numbers.reserve(4 * atoms, "numbers");
+        w.positions.reserve(24 * atoms, "positions");
+        w.cells.reserve(72 * S, "cells");
+        w.pbc.reserve(12 * S, "pbc");
+        w.offsets.reserve(8 * (S + 1), "offsets");
+        check(cudaMemcpyAsync(w.numbers.ptr, batch->numbers, 4 * atoms, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.positions.ptr, batch->positions, 24 * atoms, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.cells.ptr, batch->cells, 72 * S, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.pbc.ptr, batch->pbc, 12 * S, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.offsets.ptr, batch->offsets, 8 * (S + 1), cudaMemcpyHostToDevice, stream), "H2D");
+        error.reserve(64, "error");
+        check(cudaMemsetAsync(error.ptr, 0, 64, stream), "memset");
+        w.reserve_bins(atoms, S);
+        DeviceBatch db{w.numbers.as<int32_t>(), w.positions.as<double>(), w.cells.as<double>(), w.pbc.as<int32_t>(),
+                       w.offsets.as<int64_t>(), S, atoms};
+        BinView bins = w.bins(error.as<unsigned>());
+        bin_structures_kernel<<<(unsigned)S, 256, 0, stream>>>(db, bins, cutoff, nullptr, 0);
+        check(cudaGetLastError(), "bin kernel");
+        grids.reserve(sizeof(CanonGrid) * S, "neighbour list grids");
+        canon_grid_kernel<<<(unsigned)S, 256, 0, stream>>>(db, bins, cutoff, grids.as<CanonGrid>());
+        check(cudaGetLastError(), "grid kernel");
+        counts.reserve(8 * atoms, "counts");
+        const double cutoff2 = cutoff * cutoff;
+        const unsigned grid = (unsigned)((atoms + kWarps - 1) / kWarps);
+        list_count_kernel<<<grid, kWarps * 32, 0, stream>>>(db.positions, bins, atoms, cutoff2, full_list != 0,
+                                                              self_pairs != 0, counts.as<int64_t>());
+        check(cudaGetLastError(), "count kernel");
+        std::vector<int64_t> host_counts(atoms);
+        check(cudaMemcpyAsync(host_counts.data(), counts.ptr, 8 * atoms, cudaMemcpyDeviceToHost, stream), "D2H counts");
+        check(cudaStreamSynchronize(stream), "sync");
+        unsigned bits = 0;
+        check(cudaMemcpy(&bits, error.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "error word");
+        bits &= ~kErrUnknownSpecies;
+        if (bits) raise(bits & (kErrMixedPbc | kErrSingularCell) ? MDSOAP_INVALID_ARGUMENT : MDSOAP_INTERNAL,
+                        device_error_text(bits));
+        std::vector<int64_t> centre_rows(atoms + 1, 0);
+        for (int64_t a = 0; a < atoms; ++a) centre_rows[a + 1] = centre_rows[a] + host_counts[a];
+        for (int64_t s = 0; s <= S; ++s) out->row_offsets[s] = centre_rows[batch->offsets[s]];
+        const int64_t pairs = centre_rows[atoms];
+        out->records.resize(5 * pairs);
+        out->values.resize(4 * pairs);
+        if (pairs > 0) {
+            offsets_d.reserve(8 * (atoms + 1), "row offsets");
+            records_d.reserve(40 * pairs, "pair records");
+            values_d.reserve(32 * pairs, "pair values");
+            check(cudaMemcpyAsync(offsets_d.ptr, centre_rows.data(), 8 * (atoms + 1), cudaMemcpyHostToDevice, stream),
+                  "H2D");
+            const size_t smem = (size_t)kWarps * kListCapacity * sizeof(unsigned long long);
+            check(cudaFuncSetAttribute(list_fill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                  "list kernel smem");
+            list_fill_kernel<<<grid, kWarps * 32, smem, stream>>>(db.positions, bins, grids.as<CanonGrid>(), atoms,
+                                                                   cutoff2, full_list != 0, self_pairs != 0,
+                                                                   offsets_d.as<int64_t>(), records_d.as<double>(),
+                                                                   values_d.as<double>());
+            check(cudaGetLastError(), "list kernel");
+            check(cudaMemcpyAsync(out->records.data(), records_d.ptr, 40 * pairs, cudaMemcpyDeviceToHost, stream),
+                  "D2H");
+            check(cudaMemcpyAsync(out->values.data(), values_d.ptr, 32 * pairs, cudaMemcpyDeviceToHost, stream), "D2H");
+        }
+        check(cudaStreamSynchronize(stream), "sync");
+        check(cudaMemcpy(&bits, error.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "error word");
+        bits &= ~kErrUnknownSpecies;
+        if (bits) raise(bits & kErrPairCapacity ? MDSOAP_CAPACITY_OVERFLOW : MDSOAP_INTERNAL, device_error_text(bits));
+        *pairs_out = out.release();
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
+
+int64_t mdsoap_pairs_count(const mdsoap_pairs* pairs) { return pairs ? (int64_t)pairs->values.size() / 4 : 0; }
+
+int mdsoap_pairs_copy(const mdsoap_pairs* pairs, double* records, double* values, int64_t* row_offsets) {
+    if (!pairs) return fail(MDSOAP_INVALID_ARGUMENT, "null pair table");
+    if (records && !pairs->records.empty())
+        std::memcpy(records, pairs->records.data(), 8 * pairs->records.size());
+    if (values && !pairs->values.empty()) std::memcpy(values, pairs->values.data(), 8 * pairs->values.size());
+    if (row_offsets) std::memcpy(row_offsets, pairs->row_offsets.data(), 8 * pairs->row_offsets.size());
+    return MDSOAP_OK;
+}
+
+void mdsoap_pairs_destroy(mdsoap_pairs* pairs) { delete pairs; }
 
 int64_t mdsoap_graph_pairs(const mdsoap_graph* graph) { return graph ? (int64_t)graph->atom_ids.size() : 0; }
 

@@ -196,6 +196,28 @@ def neighbor_graph(batch, cutoff: float, device: int = 0):
     return offsets, atoms, shifts, displacements, distance2
 
 
+def neighbor_list(batch, cutoff: float, full_neighbor_list: bool = True, self_pairs: bool = False,
+                  device: int = 0):
+    """The NeighborList descriptor on the GPU (C ABI ``mdsoap_neighbor_list``):
+    (records (P, 5), values (P, 4), row_offsets (S+1,)) like the reference's
+    compute_neighbor_list split into pair records and features
+    (cpp/src/standalone/neighbor_list.cpp:15-75, _kernels/local.py:73-112)."""
+    arrays = _contiguous(batch)
+    view = host_view(arrays)
+    handle = ctypes.c_void_p()
+    raise_for(lib.mdsoap_neighbor_list(ctypes.byref(view), float(cutoff), 1 if full_neighbor_list else 0,
+                                       1 if self_pairs else 0, int(device), ctypes.byref(handle)))
+    try:
+        pairs = int(lib.mdsoap_pairs_count(handle))
+        records = np.zeros((pairs, 5), np.float64)
+        values = np.zeros((pairs, 4), np.float64)
+        row_offsets = np.zeros(int(arrays[4].shape[0]), np.int64)
+        raise_for(lib.mdsoap_pairs_copy(handle, records.ctypes.data, values.ctypes.data, row_offsets.ctypes.data))
+    finally:
+        lib.mdsoap_pairs_destroy(handle)
+    return records, values, row_offsets
+
+
 def probe_fp64_fma(device: int = 0) -> float:
     """Measured fp64 FMA throughput of one device, TFLOP/s."""
     value = ctypes.c_double()

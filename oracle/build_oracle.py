@@ -8,6 +8,7 @@ Two things are built here, neither of which is part of the product:
 * ``oracle/_ref/`` -- the reference's own CPU path compiled from its sources
   where they lie (never copied into this repository):
   - ``libref_soap.so``: ``cpp/src/standalone/soap.cpp``,
+    ``cpp/src/standalone/neighbor_list.cpp``,
     ``cpp/src/common/neighbor.cpp``, ``cpp/src/common/control.cpp`` plus the
     C entry layer ``oracle/ref_shim.cpp``.  This is the "reference" CPU
     baseline timed by ``bench.py --impl reference`` and the pin for the C
@@ -67,6 +68,7 @@ _NATIVE_SOURCES = [
 ]
 _SOAP_SOURCES = [
     "cpp/src/standalone/soap.cpp",
+    "cpp/src/standalone/neighbor_list.cpp",
     "cpp/src/common/neighbor.cpp",
     "cpp/src/common/control.cpp",
 ]
@@ -109,10 +111,10 @@ def _includes(root: Path) -> list[str]:
 
 def build_ref_soap(root: Path, force: bool = False) -> Path:
     target = REF_OUT / "libref_soap.so"
-    sources = [root / s for s in _SOAP_SOURCES] + [ORACLE_DIR / "ref_shim.cpp"]
+    sources = [root / s for s in _SOAP_SOURCES] + [ORACLE_DIR / "ref_shim.cpp", Path(__file__).resolve()]
     if force or _stale(target, sources):
         REF_OUT.mkdir(parents=True, exist_ok=True)
-        _run(["g++", *_REF_FLAGS, "-shared", *_includes(root), *map(str, sources),
+        _run(["g++", *_REF_FLAGS, "-shared", *_includes(root), *map(str, sources[:-1]),
               "-o", str(target)])
     return target
 

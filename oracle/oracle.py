@@ -237,6 +237,58 @@ class RefLib(_Checker):
         return out
 
 
+def neighbor_list(checker, batch, cutoff: float, full_neighbor_list: bool = True, self_pairs: bool = False):
+    """compute_neighbor_list (cpp/src/standalone/neighbor_list.cpp:15-75) over a
+    checker's graph (which keeps the reference CPU pair order): drop the exact
+    self pair unless self_pairs, keep one orientation unless full
+    (keep_half_neighbor, cpp/include/mdescriptor/detail/neighbor_filter.hpp:16-36);
+    returns (records (P, 5), values (P, 4), row_offsets (S+1,))."""
+    offsets, atoms, shifts, disp, d2 = checker.graph(batch, cutoff)
+    n_atoms = len(offsets) - 1
+    centre = np.repeat(np.arange(n_atoms, dtype=np.int64), np.diff(offsets))
+    atom = atoms.astype(np.int64)
+    zero = (shifts == 0).all(axis=1)
+    keep = np.ones(len(atom), bool)
+    if not self_pairs:
+        keep &= ~((atom == centre) & zero)
+    if not full_neighbor_list:
+        first = np.where(shifts[:, 0] != 0, shifts[:, 0], np.where(shifts[:, 1] != 0, shifts[:, 1], shifts[:, 2]))
+        keep &= np.where(atom != centre, atom > centre, np.where(zero, True, first > 0))
+    records = np.column_stack([centre, atom, shifts]).astype(np.float64)[keep]
+    values = np.column_stack([disp, np.sqrt(np.maximum(0.0, d2))])[keep]
+    kept_before = np.concatenate([[0], np.cumsum(keep)])
+    pair_offsets_per_atom = kept_before[offsets]
+    structure_offsets = np.asarray(batch.offsets, np.int64)
+    return records, values, pair_offsets_per_atom[structure_offsets]
+
+
+def reference_neighbor_list(batch, cutoff: float, full_neighbor_list: bool = True, self_pairs: bool = False):
+    """The reference's own compute_neighbor_list (oracle/_ref), split like neighbor_list()."""
+    lib = ctypes.CDLL(str(ORACLE_DIR / "_ref" / "libref_soap.so"))
+    lib.ref_neighbor_list.restype = _P
+    lib.ref_neighbor_list.argtypes = [_P] * 5 + [ctypes.c_int64, ctypes.c_double, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_int]
+    lib.ref_neighbor_list_rows.restype = ctypes.c_int64
+    lib.ref_neighbor_list_rows.argtypes = [_P]
+    lib.ref_neighbor_list_copy.argtypes = [_P, _P, _P]
+    lib.ref_neighbor_list_free.argtypes = [_P]
+    lib.ref_last_error.restype = ctypes.c_char_p
+    arrays = _batch_arrays(batch)
+    structures = len(arrays[4]) - 1
+    handle = lib.ref_neighbor_list(*map(_ptr, arrays), structures, float(cutoff), int(full_neighbor_list),
+                                   int(self_pairs), 1)
+    if not handle:
+        raise ValueError(lib.ref_last_error().decode())
+    try:
+        rows = int(lib.ref_neighbor_list_rows(handle))
+        table = np.zeros((rows, 9), np.float64)
+        offsets = np.zeros(structures + 1, np.int64)
+        lib.ref_neighbor_list_copy(handle, _ptr(table), _ptr(offsets))
+    finally:
+        lib.ref_neighbor_list_free(handle)
+    return table[:, :5], table[:, 5:], offsets
+
+
 def reference_available() -> bool:
     return (ORACLE_DIR / "_ref" / "libref_soap.so").is_file()
 

@@ -7,7 +7,9 @@
 // Wrapped reference entry points:
 //   mdescriptor::compute_soap            cpp/src/standalone/soap.cpp:1149
 //   mdescriptor::build_neighbor_graph    cpp/src/common/neighbor.cpp:703
+//   mdescriptor::compute_neighbor_list   cpp/src/standalone/neighbor_list.cpp:15
 #include "mdescriptor/descriptor.hpp"
+#include "mdescriptor/local_descriptors.hpp"
 #include "mdescriptor/neighbor.hpp"
 
 #include <cstdint>
@@ -119,6 +121,39 @@ int ref_soap_compute_ex(
         return 1;
     }
 }
+
+struct PairHandle {
+    mdescriptor::DescriptorPairTable table;
+};
+
+// NeighborList: the reference's pair table (9 columns per row, offsets per structure).
+void* ref_neighbor_list(
+    const int32_t* numbers, const double* positions, const double* cells,
+    const int32_t* pbc, const int64_t* offsets, int64_t structures, double cutoff,
+    int full_neighbor_list, int self_pairs, int num_threads) {
+    try {
+        auto* handle = new PairHandle;
+        handle->table = mdescriptor::compute_neighbor_list(
+            make_view(numbers, positions, cells, pbc, offsets, structures), cutoff,
+            full_neighbor_list != 0, self_pairs != 0, num_threads, nullptr);
+        return handle;
+    } catch (const std::exception& error) {
+        g_error = error.what();
+        return nullptr;
+    }
+}
+
+int64_t ref_neighbor_list_rows(void* handle) {
+    return static_cast<int64_t>(static_cast<PairHandle*>(handle)->table.values.size() / 9);
+}
+
+void ref_neighbor_list_copy(void* handle, double* values, int64_t* offsets) {
+    const auto& table = static_cast<PairHandle*>(handle)->table;
+    std::memcpy(values, table.values.data(), table.values.size() * sizeof(double));
+    std::memcpy(offsets, table.offsets.data(), table.offsets.size() * sizeof(int64_t));
+}
+
+void ref_neighbor_list_free(void* handle) { delete static_cast<PairHandle*>(handle); }
 
 void* ref_graph_build(
     const int32_t* numbers, const double* positions, const double* cells,

@@ -74,7 +74,7 @@ def test_backend_construction_touches_no_gpu_and_compute_fails_loudly():
 def test_unsupported_descriptors_and_options_raise_mapped_errors():
     plugin = load_plugin()
     name, options, _ = adapter_cases()[0]
-    with pytest.raises(ImportError, match="SOAP only"):
+    with pytest.raises(ImportError, match="SOAP and NeighborList only"):
         plugin.create_backend("ACSF", {"species": [1, 8]})
     for key, value, match in [
         ("rbf", "polynomial", "radial basis"),
