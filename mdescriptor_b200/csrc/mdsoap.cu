@@ -171,6 +171,15 @@ template <int LMAX, int MINB>
 const void* mma_symbol() {
     return reinterpret_cast<const void*>(&soap_mma_kernel<LMAX, MINB>);
 }
+// Split tail of the paired kernel: one warp per centre.
+template <int L, int T>
+void launch_tail(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_tail_kernel<L, T><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <int L, int T>
+const void* tail_symbol() {
+    return reinterpret_cast<const void*>(&soap_tail_kernel<L, T>);
+}
 // Paired-channel kernel: one warp per centre, l_max == L exactly.
 template <int T, int L, bool PRECISE, int MINB>
 void launch_paired(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
@@ -206,6 +215,8 @@ struct Variant {
     bool paired = false;   // paired-channel kernel (soap_paired_kernel), l_max == lmax exactly
     bool precise = false;  // paired: full-accuracy radial factors (float64 rows)
     const char* name = "";  // kernel and template arguments, for measurement records
+    CenterLauncher tail = nullptr;        // paired: soap_tail_kernel<lmax, maxt>
+    const void* (*tail_sym)() = nullptr;
 };
 
 #define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
@@ -253,7 +264,7 @@ const Variant kVariants[] = {
     Variant {                                                                                              \
         -1, T, 0, 0, 0, 8, L, MB, false, false, &launch_paired<T, L, PREC, MB>,                             \
             &paired_symbol<T, L, PREC, MB>, &launch_structure<L>, &structure_symbol<L>, true, PREC,         \
-            "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">"                                        \
+            "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch_tail<L, T>, &tail_symbol<L, T> \
     }
 
 // Paired-channel kernels: the default wherever they apply (n_max <= 8,
@@ -417,6 +428,8 @@ struct mdsoap_plan {
     const Variant* variant = nullptr;
     size_t center_smem = 0;
     size_t structure_smem = 0;
+    size_t tail_smem = 0;      // split tail kernel (tab.split_tail)
+    int64_t tail_chunk = 1 << 30; // centres per expansion / tail pair of launches (MDSOAP_TAIL_CHUNK)
     int64_t csize = 0;
     int64_t features = 0;
     bool timing = false;
@@ -479,6 +492,9 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
           "center kernel smem");
     check(cudaFuncSetAttribute(variant->structure_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
           "structure kernel smem");
+    if (variant->tail_sym)
+        check(cudaFuncSetAttribute(variant->tail_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+              "tail kernel smem");
     st.smem_configured = true;
 }
 
@@ -513,15 +529,39 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         st.work.pbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * features, "outer-average scratch");
         p.pbuf = st.work.pbuf.as<double>();
     }
-    if (tab.r_global) {
-        st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * tab.rsize, "coefficient scratch");
+    p.grid_begin = a0;
+    p.grid_end = a1;
+    if (tab.split_tail) {
+        // Expansion kernel, then tail kernel (soap_tail_kernel) on the raw-sum
+        // blocks it left in scratch; MDSOAP_TAIL_CHUNK alternates the two over
+        // chunks of centres instead (smaller scratch; measured slower on
+        // config 2, where one pair of launches is fastest).
+        const int64_t chunk = std::min<int64_t>(centers, tail_chunk);
+        st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(chunk, 1) * tab.rsize, "coefficient scratch");
         p.rbuf = st.work.rbuf.as<double>();
-    }
-    if (centers > 0) {
-        const int64_t grid = variant->pair ? centers : (centers + kWarps - 1) / kWarps;
-        variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
-        check(cudaGetLastError(), "centre kernel launch");
-        launches.fetch_add(1, std::memory_order_relaxed);
+        for (int64_t c0 = a0; c0 < a1; c0 += chunk) {
+            p.grid_begin = c0;
+            p.grid_end = std::min(a1, c0 + chunk);
+            const unsigned grid = (unsigned)((p.grid_end - c0 + kWarps - 1) / kWarps);
+            variant->center(dim3(grid), center_smem, stream, tab, p);
+            check(cudaGetLastError(), "centre kernel launch");
+            variant->tail(dim3(grid), tail_smem, stream, tab, p);
+            check(cudaGetLastError(), "tail kernel launch");
+            launches.fetch_add(2, std::memory_order_relaxed);
+        }
+        p.grid_begin = a0;
+        p.grid_end = a1;
+    } else {
+        if (tab.r_global) {
+            st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * tab.rsize, "coefficient scratch");
+            p.rbuf = st.work.rbuf.as<double>();
+        }
+        if (centers > 0) {
+            const int64_t grid = variant->pair ? centers : (centers + kWarps - 1) / kWarps;
+            variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
+            check(cudaGetLastError(), "centre kernel launch");
+            launches.fetch_add(1, std::memory_order_relaxed);
+        }
     }
     if (after_center) check(cudaEventRecord(after_center, stream), "timing event");
     if (average != MDSOAP_AVERAGE_OFF && s1 > s0) {
@@ -944,6 +984,16 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             plan->center_smem = shared + kWarps * (size_t)t.warp_bytes;
             plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? (size_t)t.csize * 8 : 0;
             plan->csize = t.csize;
+            // n_max == 8 tails in registers run as their own kernel (soap_tail_kernel).
+            // MDSOAP_SPLIT_TAIL=0 keeps them fused (measurement knob).
+            const char* split_env = std::getenv("MDSOAP_SPLIT_TAIL");
+            const bool split_allowed = !(split_env && split_env[0] == '0');
+            if (split_allowed && n == 8 && coef_species <= v.maxt && q.average != MDSOAP_AVERAGE_INNER && r_smem) {
+                t.split_tail = 1;
+                plan->tail_smem = (size_t)W * 64 * 8 + kWarps * (size_t)t.rsize * 8;
+                if (const char* chunk_env = std::getenv("MDSOAP_TAIL_CHUNK"))
+                    plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
+            }
             if (plan->center_smem > budget1 || plan->structure_smem > budget1)
                 return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
             *plan_out = plan.release();
@@ -1296,9 +1346,14 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
         p.out_row_begin = 0;
         p.center_begin = 0;
         p.center_end = N;
+        p.grid_begin = 0;
+        p.grid_end = N;
         if (N > 0) {
+            // One launch with the tail fused in (no scratch for a split tail here).
+            SoapTables fused = plan->tab;
+            fused.split_tail = 0;
             const int64_t grid = plan->variant->pair ? N : (N + kWarps - 1) / kWarps;
-            plan->variant->center(dim3((unsigned)grid), plan->center_smem, st, plan->tab, p);
+            plan->variant->center(dim3((unsigned)grid), plan->center_smem, st, fused, p);
             check(cudaGetLastError(), "centre kernel launch");
             plan->launches.fetch_add(1, std::memory_order_relaxed);
         }

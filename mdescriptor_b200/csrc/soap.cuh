@@ -63,6 +63,7 @@ struct SoapTables {
     int32_t compression;  // 0 off, 1 mu2, 2 mu1nu1, 3 crossover (paired kernel only when not 0)
     int32_t coef_species; // species of the coefficient block: n_species, or 1 for mu2
     int32_t weighted;     // 1: per-edge weights (weighting function, w0, or mu2 pooling); paired kernel only
+    int32_t split_tail;   // 1: the paired kernel stops after the flush; soap_tail_kernel finishes the centres
     int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)
     int32_t has_w0;       // the exact self pair takes weight w0
     double w_r0, w_c, w_d, w_m, w_0;
@@ -85,8 +86,10 @@ struct SoapPointers {
     double* pbuf;             // average outer: per-centre power spectra (block-local rows)
     double* rbuf;             // r_global: per-centre coefficient scratch (block-local rows)
     int64_t out_row_begin;    // average off: output row of centre c is c - out_row_begin
-    int64_t center_begin;
+    int64_t center_begin;     // first centre of the block (rows of cbuf / pbuf are relative to it)
     int64_t center_end;
+    int64_t grid_begin;       // paired / tail kernels: centres [grid_begin, grid_end) of this launch,
+    int64_t grid_end;         // rbuf rows relative to grid_begin
 };
 
 // Radial weight of one edge (soap_weight, cpp/src/standalone/soap.cpp:389-420,

@@ -150,8 +150,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     }
     constexpr int kShared = 256 + (L + 1) * 64 * 8;
     __syncthreads();
-    const int64_t center = p.center_begin + (int64_t)blockIdx.x * kWarps + warp;
-    if (center >= p.center_end) return;
+    const int64_t center = p.grid_begin + (int64_t)blockIdx.x * kWarps + warp;
+    if (center >= p.grid_end) return;
 
     unsigned char* region = smem + kShared + (size_t)warp * tab.warp_bytes;
     int* seg_prefix = reinterpret_cast<int*>(region);  // 40
@@ -170,7 +170,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     int32_t* ptype = reinterpret_cast<int32_t*>(pw + kPending);
     double* ybuf = reinterpret_cast<double*>(region + paired::kHeaderBytes);
     const int64_t local = center - p.center_begin;
-    double* R = tab.r_global ? p.rbuf + local * tab.rsize : reinterpret_cast<double*>(region + tab.r_offset);
+    double* R = tab.r_global ? p.rbuf + (center - p.grid_begin) * tab.rsize
+                             : reinterpret_cast<double*>(region + tab.r_offset);
 
     const BinView& bv = p.bins;
     const StructInfo& si = bv.info[bv.struct_of[center]];
@@ -494,6 +495,15 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         __syncwarp();
     }
 
+    if (tab.split_tail) {
+        // The tail runs as its own kernel (soap_tail_kernel): hand the raw
+        // sums over through global scratch, one contiguous block per centre.
+        const double2* src = reinterpret_cast<const double2*>(R);
+        double2* dst = reinterpret_cast<double2*>(p.rbuf + (center - p.grid_begin) * tab.rsize);
+        for (int i = lane; i < tab.rsize / 2; i += 32) dst[i] = src[i];
+        return;
+    }
+
     const int gq = lane >> 2, qq = lane & 3, R_rows = tab.rows;
     const bool n8 = n == 8;
     if (regs_tail) {
@@ -566,6 +576,48 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             mma::power_n8<L>(tab.power_pref, R, tab.rs, S, p.pbuf + local * tab.features, gq, qq);
         else
             mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, gq, qq);
+    }
+}
+
+// Tail of the paired kernel as a kernel of its own (n_max == 8, average off
+// or outer, at most MAXS species): one warp per centre stages the centre's
+// raw-sum block from global scratch into shared memory and runs the register
+// tail (beta transform + power spectrum on the fp64 tensor cores).  Split off
+// from the expansion it runs at the occupancy its few registers allow, so the
+// tensor-core latency is hidden by other warps instead of stalling the
+// expansion's warp.
+template <int L, int MAXS>
+__global__ void __launch_bounds__(kWarps * 32)
+soap_tail_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int S = tab.coef_species, n = tab.n_max;
+    double* bt = reinterpret_cast<double*>(smem);
+    for (int i = threadIdx.x; i < (L + 1) * 64; i += blockDim.x) {
+        const int l = i / 64, nn = (i / 8) % 8, k = i % 8;
+        bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
+    }
+    constexpr int kShared = (L + 1) * 64 * 8;
+    __syncthreads();
+    const int64_t center = p.grid_begin + (int64_t)blockIdx.x * kWarps + warp;
+    if (center >= p.grid_end) return;
+    const int64_t local = center - p.center_begin;
+    double* R = reinterpret_cast<double*>(smem + kShared) + (size_t)warp * tab.rsize;
+    const double2* src = reinterpret_cast<const double2*>(p.rbuf + (center - p.grid_begin) * tab.rsize);
+    double2* dst = reinterpret_cast<double2*>(R);
+    for (int i = lane; i < tab.rsize / 2; i += 32) dst[i] = src[i];
+    __syncwarp();
+    if (tab.average == 0) {
+        const int64_t row = center - p.out_row_begin;
+        if (tab.out_f64)
+            mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
+                                             static_cast<double*>(p.out) + row * tab.features, lane);
+        else
+            mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
+                                             static_cast<float*>(p.out) + row * tab.features, lane);
+    } else {
+        mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref, p.pbuf + local * tab.features,
+                                         lane);
     }
 }
 
