@@ -373,7 +373,7 @@ def main():
         soap.compute_device(view, out.data_ptr(), local, stream.cuda_stream)
     soap.check(local, stream.cuda_stream)
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    center_ms, bin_ms = [], []
+    center_ms, bin_ms, expansion_ms, tail_ms = [], [], [], []
     ranks.barrier()
     torch.cuda.synchronize(dev)
     launches0 = soap.launch_count()
@@ -386,6 +386,9 @@ def main():
         b, c, _ = soap.last_timing(local)
         bin_ms.append(b)
         center_ms.append(c)
+        x, t = soap.last_timing_split(local)
+        expansion_ms.append(x)
+        tail_ms.append(t)
     torch.cuda.synchronize(dev)
     sampler.end()
     ranks.barrier()
@@ -459,7 +462,8 @@ def main():
             "e2e": e2e,
             "gpu_launches": gpu_launches,
             "gpu_launches_per_step": launches_per_step,
-            "kernel_ms": {"bin": statistics.mean(bin_ms), "center": statistics.mean(center_ms)},
+            "kernel_ms": {"bin": statistics.mean(bin_ms), "center": statistics.mean(center_ms),
+                          "expansion": statistics.mean(expansion_ms), "tail": statistics.mean(tail_ms)},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved_gbs / hbm_peak, "traffic": traffic,
                          "kernel": kernel, "peak_source": hbm_src,

@@ -210,14 +210,21 @@ int mdsoap_plan_set_timing(mdsoap_plan* plan, int32_t enable);
 int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, double* center_ms,
                             double* structure_ms);
 
+/* The centre time of the last timed call split into the expansion kernel and
+ * the separate tail kernel (beta transform + power spectrum) that n_max = 8
+ * plans launch after it; tail_ms is 0 when the plan runs a fused tail
+ * (measurement support; no counterpart in the reference). */
+int mdsoap_plan_last_timing_split(mdsoap_plan* plan, int32_t device, double* expansion_ms, double* tail_ms);
+
 /* Number of kernels the plan has launched so far, over all devices and entry
  * points (measurement support; no counterpart in the reference).  A
  * benchmark reads it before and after its timed region to count its launches. */
 int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count);
 
-/* Name and template arguments of the centre kernel the plan launches, e.g.
- * "soap_paired_kernel<4, 6, false, 2>" (measurement support, for matching
- * profiler records; no counterpart in the reference).  Never NULL. */
+/* Name and template arguments of the centre kernel(s) the plan launches, e.g.
+ * "soap_paired_kernel<4, 6, false, 2> + soap_tail_kernel<6, 4>" (measurement
+ * support, for matching profiler records; no counterpart in the reference).
+ * Never NULL; valid while the plan lives. */
 const char* mdsoap_plan_kernel(const mdsoap_plan* plan);
 
 /* The engine's exp() for non-positive arguments (Tang's table-driven

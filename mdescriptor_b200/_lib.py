@@ -103,6 +103,8 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_pairs_copy.restype = ctypes.c_int
     lib.mdsoap_pairs_destroy.argtypes = [_P]
     lib.mdsoap_pairs_destroy.restype = None
+    lib.mdsoap_plan_last_timing_split.argtypes = [_P, ctypes.c_int32, _P, _P]
+    lib.mdsoap_plan_last_timing_split.restype = ctypes.c_int
     lib.mdsoap_plan_kernel.argtypes = [_P]
     lib.mdsoap_plan_kernel.restype = ctypes.c_char_p
     lib.mdsoap_compute.argtypes = [_P, ctypes.POINTER(BatchView), _P, _P, ctypes.c_int32, _P, _P]
@@ -146,6 +148,7 @@ EXPORTED = (
     "mdsoap_plan_feature_count",
     "mdsoap_plan_rows",
     "mdsoap_plan_kernel",
+    "mdsoap_plan_last_timing_split",
     "mdsoap_compute",
     "mdsoap_compute_device",
     "mdsoap_plan_check",

@@ -388,8 +388,9 @@ struct DeviceState {
     DeviceBytes out[2];
     PinnedBytes staging[2];
     bool smem_configured = false;
-    cudaEvent_t timing[4] = {nullptr, nullptr, nullptr, nullptr};
+    cudaEvent_t timing[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // bin | centre | tail | structure
     bool timed = false;  // the last device call recorded the timing events
+    bool split_timed = false;  // ... including the event between the expansion and tail kernels
     std::mutex mutex;
 
     ~DeviceState() {
@@ -429,6 +430,7 @@ struct mdsoap_plan {
     size_t center_smem = 0;
     size_t structure_smem = 0;
     size_t tail_smem = 0;      // split tail kernel (tab.split_tail)
+    std::string kernel_label;  // the kernel(s) a step launches after binning
     int64_t tail_chunk = 1 << 30; // centres per expansion / tail pair of launches (MDSOAP_TAIL_CHUNK)
     int64_t csize = 0;
     int64_t features = 0;
@@ -443,7 +445,8 @@ struct mdsoap_plan {
     void configure_smem(DeviceState& st);
     void bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream, unsigned* error);
     void run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, int64_t s1, int64_t a0, int64_t a1,
-                   void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center = nullptr);
+                   void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center = nullptr,
+                   cudaEvent_t after_expansion = nullptr);
     void shard_compute(int device, const mdsoap_batch& batch, int64_t s0, int64_t s1, char* out,
                        mdsoap_cancel_fn cancel, void* ctx, std::atomic<bool>& stop);
 };
@@ -510,7 +513,8 @@ void mdsoap_plan::bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream
 // Centres [a0, a1) = atoms of structures [s0, s1); rows go to `out` starting
 // at the block's first row.
 void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, int64_t s1, int64_t a0, int64_t a1,
-                            void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center) {
+                            void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center,
+                            cudaEvent_t after_expansion) {
     const int64_t centers = a1 - a0;
     const int64_t csize = tab.csize;
     SoapPointers p{};
@@ -545,6 +549,9 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             const unsigned grid = (unsigned)((p.grid_end - c0 + kWarps - 1) / kWarps);
             variant->center(dim3(grid), center_smem, stream, tab, p);
             check(cudaGetLastError(), "centre kernel launch");
+            // With one chunk, the event splits the timing into expansion and tail.
+            if (after_expansion && c0 == a0 && p.grid_end == a1)
+                check(cudaEventRecord(after_expansion, stream), "timing event");
             variant->tail(dim3(grid), tail_smem, stream, tab, p);
             check(cudaGetLastError(), "tail kernel launch");
             launches.fetch_add(2, std::memory_order_relaxed);
@@ -994,6 +1001,9 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                 if (const char* chunk_env = std::getenv("MDSOAP_TAIL_CHUNK"))
                     plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
             }
+            plan->kernel_label = v.name;
+            if (t.split_tail)
+                plan->kernel_label += " + soap_tail_kernel<" + std::to_string(L) + ", " + std::to_string(v.maxt) + ">";
             if (plan->center_smem > budget1 || plan->structure_smem > budget1)
                 return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
             *plan_out = plan.release();
@@ -1191,7 +1201,9 @@ int mdsoap_compute_device(mdsoap_plan* plan, const mdsoap_batch* batch, void* ou
         if (timed) check(cudaEventRecord(st.timing[1], s), "timing event");
         // Structure ranges are only needed for the averages; the device batch
         // is one block.
-        plan->run_block(st, db, 0, batch->structures, 0, batch->atoms, out, s, error, timed ? st.timing[2] : nullptr);
+        st.split_timed = timed && plan->tab.split_tail && plan->tail_chunk >= batch->atoms;
+        plan->run_block(st, db, 0, batch->structures, 0, batch->atoms, out, s, error, timed ? st.timing[2] : nullptr,
+                        timed ? st.timing[4] : nullptr);
         if (timed) check(cudaEventRecord(st.timing[3], s), "timing event");
         st.timed = timed;
         return MDSOAP_OK;
@@ -1404,7 +1416,30 @@ int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, d
 }
 
 const char* mdsoap_plan_kernel(const mdsoap_plan* plan) {
-    return plan && plan->variant ? plan->variant->name : "";
+    if (!plan || !plan->variant) return "";
+    return plan->kernel_label.empty() ? plan->variant->name : plan->kernel_label.c_str();
+}
+
+int mdsoap_plan_last_timing_split(mdsoap_plan* plan, int32_t device, double* expansion_ms, double* tail_ms) {
+    if (!plan) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        DeviceState& st = plan->state(device);
+        if (!st.timed) return fail(MDSOAP_INVALID_ARGUMENT, "no timed device call on this device");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        check(cudaEventSynchronize(st.timing[3]), "timing sync");
+        float a = 0, b = 0;
+        if (st.split_timed) {
+            check(cudaEventElapsedTime(&a, st.timing[1], st.timing[4]), "elapsed");
+            check(cudaEventElapsedTime(&b, st.timing[4], st.timing[2]), "elapsed");
+        } else {
+            check(cudaEventElapsedTime(&a, st.timing[1], st.timing[2]), "elapsed");
+        }
+        if (expansion_ms) *expansion_ms = a;
+        if (tail_ms) *tail_ms = b;
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    }
 }
 
 int mdsoap_plan_launch_count(const mdsoap_plan* plan, int64_t* count) {

@@ -158,6 +158,13 @@ class Soap:
                                               ctypes.byref(values, 8), ctypes.byref(values, 16)))
         return values[0], values[1], values[2]
 
+    def last_timing_split(self, device: int = 0) -> tuple[float, float]:
+        """(expansion_ms, tail_ms) of the last timed call (tail 0 for a fused tail)."""
+        values = (ctypes.c_double * 2)()
+        raise_for(lib.mdsoap_plan_last_timing_split(self._plan, int(device), ctypes.byref(values, 0),
+                                                    ctypes.byref(values, 8)))
+        return values[0], values[1]
+
     def check(self, device: int = 0, stream: int = 0) -> None:
         raise_for(lib.mdsoap_plan_check(self._plan, int(device), stream or None))
 
