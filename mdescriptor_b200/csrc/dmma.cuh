@@ -325,10 +325,13 @@ __device__ __forceinline__ void power_n8(const double* __restrict__ pref, const 
 //      species in the compression-off layout.
 // The coefficients of one degree are loaded once and shared by all pairs,
 // and every pair's product chain is independent of the others.
+// Degrees [l_lo, l_hi] are done, plus l_extra when it is >= 0 (several warps
+// can then share one centre's block, each with its own degrees).
 template <int L, int MAXS, class OutT>
 __device__ __forceinline__ void tail_regs_n8(const double* __restrict__ bt, const double* __restrict__ reg, int rs,
                                              int S, int compression, const double* __restrict__ pref,
-                                             OutT* __restrict__ out, int lane) {
+                                             OutT* __restrict__ out, int lane, int l_lo = 0, int l_hi = L,
+                                             int l_extra = -1) {
     const int g = lane >> 2, q = lane & 3;
     const int od = 8 * g + 2 * q;
     const int n2a = 2 * q, n2b = 2 * q + 1;
@@ -347,7 +350,8 @@ __device__ __forceinline__ void tail_regs_n8(const double* __restrict__ bt, cons
     // A runtime loop over l (one copy of the code); trip counts inside are
     // warp-uniform, the register arrays sized for the largest degree.
 #pragma unroll 1
-    for (int l = 0; l <= L; ++l) {
+    for (int li = l_lo; li <= l_hi + (l_extra >= 0 ? 1 : 0); ++li) {
+        const int l = li <= l_hi ? li : l_extra;
         const int KP = (2 * l + 1 + 3) & ~3, NK = KP / 4, MB = (KP + 7) / 8;
         int C0 = 0;
         for (int i = 0; i < l; ++i) C0 += (2 * i + 1 + 3) & ~3;

@@ -552,7 +552,7 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             // With one chunk, the event splits the timing into expansion and tail.
             if (after_expansion && c0 == a0 && p.grid_end == a1)
                 check(cudaEventRecord(after_expansion, stream), "timing event");
-            variant->tail(dim3(grid), tail_smem, stream, tab, p);
+            variant->tail(dim3((unsigned)(p.grid_end - c0)), tail_smem, stream, tab, p);  // one CTA per centre
             check(cudaGetLastError(), "tail kernel launch");
             launches.fetch_add(2, std::memory_order_relaxed);
         }
@@ -997,7 +997,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             const bool split_allowed = !(split_env && split_env[0] == '0');
             if (split_allowed && n == 8 && coef_species <= v.maxt && q.average != MDSOAP_AVERAGE_INNER && r_smem) {
                 t.split_tail = 1;
-                plan->tail_smem = (size_t)W * 64 * 8 + kWarps * (size_t)t.rsize * 8;
+                plan->tail_smem = (size_t)W * 64 * 8 + (size_t)t.rsize * 8;
                 if (const char* chunk_env = std::getenv("MDSOAP_TAIL_CHUNK"))
                     plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
             }

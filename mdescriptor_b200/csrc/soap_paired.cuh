@@ -580,15 +580,16 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
 }
 
 // Tail of the paired kernel as a kernel of its own (n_max == 8, average off
-// or outer, at most MAXS species): one warp per centre stages the centre's
-// raw-sum block from global scratch into shared memory and runs the register
-// tail (beta transform + power spectrum on the fp64 tensor cores).  Split off
-// from the expansion it runs at the occupancy its few registers allow, so the
-// tensor-core latency is hidden by other warps instead of stalling the
-// expansion's warp.
+// or outer, at most MAXS species): one CTA of four warps per centre stages the
+// centre's raw-sum block from global scratch into shared memory; warp w then
+// runs the register tail (beta transform + power spectrum on the fp64 tensor
+// cores) for the degrees of channel group w -- {L}, {L-1, 0}, {L-2, 1}, ...,
+// four groups of about equal tensor-core work for L = 5, 6 -- so a centre's
+// degrees proceed in parallel and more warps share an SM.
 template <int L, int MAXS>
 __global__ void __launch_bounds__(kWarps * 32)
 soap_tail_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
+    using P = paired::Layout<L>;
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int S = tab.coef_species, n = tab.n_max;
@@ -598,26 +599,27 @@ soap_tail_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
         bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
     }
     constexpr int kShared = (L + 1) * 64 * 8;
-    __syncthreads();
-    const int64_t center = p.grid_begin + (int64_t)blockIdx.x * kWarps + warp;
-    if (center >= p.grid_end) return;
+    const int64_t center = p.grid_begin + (int64_t)blockIdx.x;
+    if (center >= p.grid_end) return;  // uniform over the CTA
     const int64_t local = center - p.center_begin;
-    double* R = reinterpret_cast<double*>(smem + kShared) + (size_t)warp * tab.rsize;
+    double* R = reinterpret_cast<double*>(smem + kShared);
     const double2* src = reinterpret_cast<const double2*>(p.rbuf + (center - p.grid_begin) * tab.rsize);
     double2* dst = reinterpret_cast<double2*>(R);
-    for (int i = lane; i < tab.rsize / 2; i += 32) dst[i] = src[i];
-    __syncwarp();
+    for (int i = threadIdx.x; i < tab.rsize / 2; i += blockDim.x) dst[i] = src[i];
+    __syncthreads();
+    if (warp >= P::G) return;
+    const int la = P::la(warp), lb = P::lb(warp);
     if (tab.average == 0) {
         const int64_t row = center - p.out_row_begin;
         if (tab.out_f64)
             mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
-                                             static_cast<double*>(p.out) + row * tab.features, lane);
+                                       static_cast<double*>(p.out) + row * tab.features, lane, la, la, lb);
         else
             mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
-                                             static_cast<float*>(p.out) + row * tab.features, lane);
+                                       static_cast<float*>(p.out) + row * tab.features, lane, la, la, lb);
     } else {
         mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref, p.pbuf + local * tab.features,
-                                         lane);
+                                   lane, la, la, lb);
     }
 }
 
