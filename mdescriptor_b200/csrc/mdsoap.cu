@@ -181,13 +181,21 @@ const void* tail_symbol() {
     return reinterpret_cast<const void*>(&soap_tail_kernel<L, T>);
 }
 // Paired-channel kernel: one warp per centre, l_max == L exactly.
+// Plans with a split tail launch the instantiation without tail code (fewer registers).
 template <int T, int L, bool PRECISE, int MINB>
 void launch_paired(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_paired_kernel<T, L, PRECISE, MINB><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+    if (tab.split_tail)
+        soap_paired_kernel<T, L, PRECISE, MINB, true><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+    else
+        soap_paired_kernel<T, L, PRECISE, MINB, false><<<grid, kWarps * 32, smem, stream>>>(tab, p);
 }
 template <int T, int L, bool PRECISE, int MINB>
 const void* paired_symbol() {
-    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB>);
+    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB, false>);
+}
+template <int T, int L, bool PRECISE, int MINB>
+const void* paired_split_symbol() {
+    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB, true>);
 }
 template <int LMAX>
 void launch_structure(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const int64_t* offsets,
@@ -217,6 +225,7 @@ struct Variant {
     const char* name = "";  // kernel and template arguments, for measurement records
     CenterLauncher tail = nullptr;        // paired: soap_tail_kernel<lmax, maxt>
     const void* (*tail_sym)() = nullptr;
+    const void* (*split_sym)() = nullptr; // paired: the expansion kernel without tail code
 };
 
 #define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
@@ -264,7 +273,8 @@ const Variant kVariants[] = {
     Variant {                                                                                              \
         -1, T, 0, 0, 0, 8, L, MB, false, false, &launch_paired<T, L, PREC, MB>,                             \
             &paired_symbol<T, L, PREC, MB>, &launch_structure<L>, &structure_symbol<L>, true, PREC,         \
-            "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch_tail<L, T>, &tail_symbol<L, T> \
+            "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch_tail<L, T>, &tail_symbol<L, T>, \
+            &paired_split_symbol<T, L, PREC, MB>                                                          \
     }
 
 // Paired-channel kernels: the default wherever they apply (n_max <= 8,
@@ -498,6 +508,9 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
     if (variant->tail_sym)
         check(cudaFuncSetAttribute(variant->tail_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
               "tail kernel smem");
+    if (variant->split_sym)
+        check(cudaFuncSetAttribute(variant->split_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+              "centre kernel smem");
     st.smem_configured = true;
 }
 

@@ -129,7 +129,9 @@ __device__ __forceinline__ void harmonics_row(const SoapTables& tab, double x, d
 // One warp per centre.  MAXT species register banks per pass over the
 // neighbourhood; L = l_max exactly; PRECISE selects the radial-factor
 // accuracy (float64 rows need the full one); MINB resident CTAs per SM.
-template <int MAXT, int L, bool PRECISE, int MINB>
+// SPLIT: the kernel ends after the flush, handing the raw sums to
+// soap_tail_kernel (no tail code, so fewer registers).
+template <int MAXT, int L, bool PRECISE, int MINB, bool SPLIT = false>
 __global__ void __launch_bounds__(kWarps * 32, MINB)
 soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
     using P = paired::Layout<L>;
@@ -144,10 +146,11 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     double* etab = reinterpret_cast<double*>(smem);
     if (threadIdx.x < 32) etab[threadIdx.x] = kExp2Table[threadIdx.x];
     double* bt = reinterpret_cast<double*>(smem + 256);
-    for (int i = threadIdx.x; i < (L + 1) * 64; i += blockDim.x) {
-        const int l = i / 64, nn = (i / 8) % 8, k = i % 8;
-        bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
-    }
+    if (!SPLIT)
+        for (int i = threadIdx.x; i < (L + 1) * 64; i += blockDim.x) {
+            const int l = i / 64, nn = (i / 8) % 8, k = i % 8;
+            bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
+        }
     constexpr int kShared = 256 + (L + 1) * 64 * 8;
     __syncthreads();
     const int64_t center = p.grid_begin + (int64_t)blockIdx.x * kWarps + warp;
@@ -495,7 +498,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         __syncwarp();
     }
 
-    if (tab.split_tail) {
+    if (SPLIT || tab.split_tail) {
         // The tail runs as its own kernel (soap_tail_kernel): hand the raw
         // sums over through global scratch, one contiguous block per centre.
         const double2* src = reinterpret_cast<const double2*>(R);
