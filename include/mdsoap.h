@@ -21,7 +21,7 @@
 extern "C" {
 #endif
 
-#define MDSOAP_ABI_VERSION 2
+#define MDSOAP_ABI_VERSION 3
 
 /* Status codes.  They mirror the reference plugin's error classes
  * (cpp/cuda/include/mdescriptor/cuda/error.hpp:15-28 and
@@ -59,6 +59,9 @@ typedef enum {
     MDSOAP_WEIGHTING_EXP = 3    /* c / (d + exp(-x)) */
 } mdsoap_weighting;
 
+/* SoapOptions::radial_basis (src/mdescriptor/descriptors/_kernels/core.py:79-95). */
+typedef enum { MDSOAP_RADIAL_GTO = 0, MDSOAP_RADIAL_POLYNOMIAL = 1 } mdsoap_radial_basis;
+
 /* Descriptor parameters; the fields of the reference's SoapOptions for the
  * GTO basis (cpp/include/mdescriptor/descriptor.hpp:17-43, filled by
  * SoapKernel._ensure_native, _kernels/core.py:207-269). */
@@ -82,6 +85,17 @@ typedef struct {
     double weighting_d;            /* >= 0 */
     double weighting_m;            /* >= 0 */
     double weighting_w0;           /* >= 0 */
+    /* Radial basis (SoapOptions::radial_basis): 0 GTO (alphas / betas above),
+     * 1 polynomial on a quadrature grid (_basis_polynomial,
+     * src/mdescriptor/descriptors/_kernels/core.py:79-95): radial_grid and
+     * radial_weights [radial_grid_size] (nodes in [0, r_cut], positive
+     * weights), radial_values [n_max * radial_grid_size] (the orthonormal
+     * basis on the nodes, index n * grid_size + q). */
+    int32_t radial_basis;
+    int32_t radial_grid_size;      /* 2..128 */
+    const double* radial_grid;
+    const double* radial_weights;
+    const double* radial_values;
 } mdsoap_params;
 
 /* A flat batch with StructureBatch's layout (src/mdescriptor/core/input.py:20-131):

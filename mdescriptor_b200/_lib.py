@@ -15,7 +15,7 @@ from pathlib import Path
 # MDSOAP_LIBRARY may point at another build of the same ABI (e.g. a debug build).
 LIB_PATH = Path(os.environ.get("MDSOAP_LIBRARY") or Path(__file__).resolve().parent / "lib" / "libmdsoap.so")
 
-ABI_VERSION = 2  # MDSOAP_ABI_VERSION: layout of Params below
+ABI_VERSION = 3  # MDSOAP_ABI_VERSION: layout of Params below
 
 OK = 0
 INVALID_ARGUMENT = 1
@@ -58,6 +58,11 @@ class Params(ctypes.Structure):
         ("weighting_d", ctypes.c_double),
         ("weighting_m", ctypes.c_double),
         ("weighting_w0", ctypes.c_double),
+        ("radial_basis", ctypes.c_int32),
+        ("radial_grid_size", ctypes.c_int32),
+        ("radial_grid", _P),
+        ("radial_weights", _P),
+        ("radial_values", _P),
     ]
 
 

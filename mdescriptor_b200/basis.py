@@ -34,6 +34,31 @@ def basis_gto(r_cut: float, n_max: int, l_max: int) -> tuple[np.ndarray, np.ndar
     return alphas, betas
 
 
+def basis_polynomial(r_cut: float, n_max: int, nodes: int = 100) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Polynomial radial basis on a Gauss-Legendre grid (grid (Q,), weights (Q,),
+    values (n, Q)).
+
+    Restates ``_basis_polynomial`` (src/mdescriptor/descriptors/_kernels/core.py:79-95):
+    Q = 100 Gauss-Legendre nodes mapped to [0, r_cut]; the monomials
+    (r_cut - r)^(n + 3), n = 0..n_max-1, have the overlap
+    S_ij = 2 r_cut^(7+i+j) / ((5+i+j)(6+i+j)(7+i+j)) (i, j = 1..n_max), and the
+    orthonormal basis on the nodes is S^(-1/2) applied to the monomials.
+    """
+    x, w = np.polynomial.legendre.leggauss(nodes)
+    grid = 0.5 * r_cut * (x + 1.0)
+    weights = 0.5 * r_cut * w
+    overlap = np.empty((n_max, n_max), dtype=np.float64)
+    for i in range(1, n_max + 1):
+        for j in range(1, n_max + 1):
+            overlap[i - 1, j - 1] = (2.0 * r_cut ** (7 + i + j)) / ((5 + i + j) * (6 + i + j) * (7 + i + j))
+    values, vectors = np.linalg.eigh(overlap)
+    if np.any(values <= 0.0):
+        raise ValueError("could not normalize the SOAP polynomial radial basis")
+    betas = (vectors * (1.0 / np.sqrt(values))) @ vectors.T
+    powers = np.asarray([(r_cut - np.clip(grid, 0.0, r_cut)) ** (n + 3) for n in range(n_max)])
+    return grid, weights, betas @ powers
+
+
 def feature_count(n_species: int, n_max: int, l_max: int, compression: str = "off") -> int:
     """Features per row by compression mode (_kernels/core.py:272-284; soap.cpp:373-387)."""
     if compression == "mu2":

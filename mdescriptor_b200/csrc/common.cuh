@@ -11,6 +11,7 @@ namespace mdsoap {
 constexpr int kMaxSpecies = 64;
 constexpr int kMaxL = 20;
 constexpr int kMaxN = 32;
+constexpr int kMaxGrid = 128;  // polynomial basis quadrature nodes
 constexpr int kWarps = 4;             // warps per CTA of the centre kernel
 constexpr int kPending = 64;          // accepted-edge queue per warp (>= 2 * 32)
 constexpr int kRegionHeader = 544;    // per-warp candidate tables + chunk permutation (bytes)

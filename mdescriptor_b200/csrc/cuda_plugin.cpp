@@ -149,8 +149,9 @@ public:
         sigma_ = option(options_, "sigma", 1.0);
         if (n_max_ < 1 || n_max_ > 32 || l_max_ < 0 || l_max_ > 20 || r_cut_ <= 0.0 || sigma_ <= 0.0)
             throw std::invalid_argument("invalid CUDA SOAP parameters");
-        if (option(options_, "rbf", std::string("gto")) != "gto")
-            throw std::invalid_argument("unsupported CUDA SOAP radial basis");
+        const std::string rbf = option(options_, "rbf", std::string("gto"));
+        if (rbf != "gto" && rbf != "polynomial") throw std::invalid_argument("unsupported CUDA SOAP radial basis");
+        polynomial_ = rbf == "polynomial";
         // extended_descriptors_soap.cuh:819-828, 878-884: compression mode and
         // weighting function names.
         const py::dict compression = child_dict(options_, "compression");
@@ -204,11 +205,21 @@ public:
         f64_ = dtype == "float64";
         const py::dict payload = child_dict(options_, "_cuda_payload");
         const py::dict radial = child_dict(payload, "radial_basis");
-        alphas_ = flat_doubles(radial, "alphas");
-        betas_ = flat_doubles(radial, "betas");
         const size_t W = (size_t)l_max_ + 1;
-        if (alphas_.size() != W * n_max_ || betas_.size() != W * n_max_ * n_max_)
-            throw std::invalid_argument("CUDA SOAP GTO payload has an invalid shape");
+        if (polynomial_) {
+            // _cuda_payload of the polynomial basis (_kernels/core.py:343-349).
+            grid_ = flat_doubles(radial, "radial_grid");
+            grid_weights_ = flat_doubles(radial, "radial_weights");
+            grid_values_ = flat_doubles(radial, "radial_values");
+            if (grid_.size() < 2 || grid_weights_.size() != grid_.size() ||
+                grid_values_.size() != (size_t)n_max_ * grid_.size())
+                throw std::invalid_argument("CUDA SOAP polynomial payload has an invalid shape");
+        } else {
+            alphas_ = flat_doubles(radial, "alphas");
+            betas_ = flat_doubles(radial, "betas");
+            if (alphas_.size() != W * n_max_ || betas_.size() != W * n_max_ * n_max_)
+                throw std::invalid_argument("CUDA SOAP GTO payload has an invalid shape");
+        }
         mdsoap_params params{};
         params.n_species = (int32_t)species_.size();
         params.species = species_.data();
@@ -219,6 +230,11 @@ public:
         params.l_max = l_max_;
         params.alphas = alphas_.data();
         params.betas = betas_.data();
+        params.radial_basis = polynomial_ ? MDSOAP_RADIAL_POLYNOMIAL : MDSOAP_RADIAL_GTO;
+        params.radial_grid_size = (int32_t)grid_.size();
+        params.radial_grid = grid_.data();
+        params.radial_weights = grid_weights_.data();
+        params.radial_values = grid_values_.data();
         params.average = average_;
         params.output_dtype = f64_ ? MDSOAP_FLOAT64 : MDSOAP_FLOAT32;
         params.compression = compression_;
@@ -385,7 +401,8 @@ private:
     std::string name_;
     py::dict options_;
     std::vector<int32_t> species_;
-    std::vector<double> weights_, alphas_, betas_;
+    std::vector<double> weights_, alphas_, betas_, grid_, grid_weights_, grid_values_;
+    bool polynomial_ = false;
     int n_max_ = 8, l_max_ = 6, average_ = MDSOAP_AVERAGE_INNER;
     double r_cut_ = 6.0, sigma_ = 1.0;
     int compression_ = MDSOAP_COMPRESSION_OFF, weighting_function_ = MDSOAP_WEIGHTING_NONE;

@@ -189,6 +189,16 @@ void launch_paired(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables
     else
         soap_paired_kernel<T, L, PRECISE, MINB, false><<<grid, kWarps * 32, smem, stream>>>(tab, p);
 }
+// Polynomial radial basis: the paired kernel's POLY instantiation (full
+// accuracy exps, tail fused).
+template <int T, int L>
+void launch_poly(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_paired_kernel<T, L, true, 2, false, true><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <int T, int L>
+const void* poly_symbol() {
+    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, true, 2, false, true>);
+}
 template <int T, int L, bool PRECISE, int MINB>
 const void* paired_symbol() {
     return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB, false>);
@@ -289,6 +299,25 @@ const Variant kPairedVariants[] = {
     MDSOAP_PAIRED_VARIANT(4, 5, false, 2), MDSOAP_PAIRED_VARIANT(4, 5, true, 2),
     MDSOAP_PAIRED_VARIANT(4, 6, false, 2), MDSOAP_PAIRED_VARIANT(4, 6, true, 2),
 };
+
+#define MDSOAP_POLY_VARIANT(T, L)                                                                           \
+    Variant {                                                                                              \
+        -1, T, 0, 0, 0, 8, L, 2, false, false, &launch_poly<T, L>, &poly_symbol<T, L>, &launch_structure<L>, \
+            &structure_symbol<L>, true, true, "soap_paired_kernel<" #T ", " #L ", true, 2, false, true>"       \
+    }
+
+// Polynomial radial basis kernels (same applicability as the paired kernels).
+const Variant kPolyVariants[] = {
+    MDSOAP_POLY_VARIANT(4, 0), MDSOAP_POLY_VARIANT(4, 1), MDSOAP_POLY_VARIANT(4, 2), MDSOAP_POLY_VARIANT(4, 3),
+    MDSOAP_POLY_VARIANT(4, 4), MDSOAP_POLY_VARIANT(4, 5), MDSOAP_POLY_VARIANT(4, 6),
+};
+
+const Variant* poly_variant(int n_max, int l_max) {
+    if (n_max > 8 || n_max * (1 + (l_max + 1) / 2) > 32) return nullptr;
+    for (const Variant& v : kPolyVariants)
+        if (v.lmax == l_max) return &v;
+    return nullptr;
+}
 
 const Variant* paired_variant(int n_max, int l_max, bool precise) {
     if (n_max > 8 || n_max * (1 + (l_max + 1) / 2) > 32) return nullptr;
@@ -393,7 +422,7 @@ struct DeviceState {
     cudaStream_t copy = nullptr;
     cudaEvent_t computed[2] = {nullptr, nullptr};
     cudaEvent_t copied[2] = {nullptr, nullptr};
-    DeviceBytes items, betas, species, error;
+    DeviceBytes items, betas, species, error, poly;
     Workspace work;
     DeviceBytes out[2];
     PinnedBytes staging[2];
@@ -434,6 +463,7 @@ struct mdsoap_plan {
     double r_cut = 0, sigma = 0, cutoff = 0;
     std::vector<int32_t> species;
     std::vector<double> weights, alphas, betas;
+    std::vector<double> poly;  // polynomial basis: nodes [Q], weighted values [Q][n_max]
     std::vector<RadialItem> items;
     SoapTables tab{};
     const Variant* variant = nullptr;
@@ -487,6 +517,10 @@ DeviceState& mdsoap_plan::state(int device) {
     check(cudaMemcpy(st->betas.ptr, betas.data(), 8 * betas.size(), cudaMemcpyHostToDevice), "upload betas");
     st->species.reserve(4 * species.size(), "species");
     check(cudaMemcpy(st->species.ptr, species.data(), 4 * species.size(), cudaMemcpyHostToDevice), "upload species");
+    if (!poly.empty()) {
+        st->poly.reserve(8 * poly.size(), "polynomial basis");
+        check(cudaMemcpy(st->poly.ptr, poly.data(), 8 * poly.size(), cudaMemcpyHostToDevice), "upload polynomial basis");
+    }
     st->error.reserve(64, "error word");
     check(cudaMemset(st->error.ptr, 0, 64), "clear error word");
     configure_smem(*st);
@@ -535,6 +569,7 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
     p.bins = st.work.bins(error);
     p.items = st.items.as<RadialItem>();
     p.betas = st.betas.as<double>();
+    p.poly = st.poly.as<double>();
     p.out = out;
     p.out_row_begin = a0;
     p.center_begin = a0;
@@ -839,7 +874,26 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP weighting parameters");
     if (q.weighting_has_w0 && (!std::isfinite(q.weighting_w0) || q.weighting_w0 < 0.0))
         return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP w0 weighting");
-    if (!q.alphas || !q.betas) return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP radial basis size");
+    if (q.radial_basis != MDSOAP_RADIAL_GTO && q.radial_basis != MDSOAP_RADIAL_POLYNOMIAL)
+        return fail(MDSOAP_INVALID_ARGUMENT, "unsupported CUDA SOAP radial basis");
+    const bool polynomial = q.radial_basis == MDSOAP_RADIAL_POLYNOMIAL;
+    if (!polynomial && (!q.alphas || !q.betas)) return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP radial basis size");
+    // soap.cpp:1165-1192 polynomial basis checks; 128 nodes is this library's limit.
+    if (polynomial && (q.radial_grid_size < 2 || q.radial_grid_size > kMaxGrid || !q.radial_grid ||
+                       !q.radial_weights || !q.radial_values))
+        return fail(MDSOAP_INVALID_ARGUMENT, "invalid SOAP polynomial radial basis size");
+    if (polynomial) {
+        const int Q = q.radial_grid_size;
+        for (int i = 0; i < Q; ++i)
+            if (!std::isfinite(q.radial_grid[i]) || q.radial_grid[i] < 0.0 || q.radial_grid[i] > q.r_cut)
+                return fail(MDSOAP_INVALID_ARGUMENT, "SOAP polynomial radial grid must be finite and in range");
+        for (int i = 0; i < Q; ++i)
+            if (!std::isfinite(q.radial_weights[i]) || q.radial_weights[i] <= 0.0)
+                return fail(MDSOAP_INVALID_ARGUMENT, "SOAP polynomial radial weights must be positive and finite");
+        for (int i = 0; i < Q * q.n_max; ++i)
+            if (!std::isfinite(q.radial_values[i]))
+                return fail(MDSOAP_INVALID_ARGUMENT, "SOAP polynomial radial basis must be finite");
+    }
     for (int i = 0; i < q.n_species; ++i) {
         if (q.species[i] <= 0) return fail(MDSOAP_INVALID_ARGUMENT, "species must be positive atomic numbers");
         for (int j = 0; j < i; ++j)
@@ -864,8 +918,25 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             }
         }
         const int L = q.l_max, n = q.n_max, W = L + 1;
-        plan->alphas.assign(q.alphas, q.alphas + W * n);
-        plan->betas.assign(q.betas, q.betas + W * n * n);
+        if (polynomial) {
+            // The projection needs no beta transform and no pi^{3/2}: the plan
+            // carries identity betas and unit radial items for the shared tail.
+            plan->alphas.assign(W * n, 0.0);
+            plan->betas.assign(W * n * n, 0.0);
+            for (int l = 0; l < W; ++l)
+                for (int k = 0; k < n; ++k) plan->betas[(l * n + k) * n + k] = 1.0;
+            // prepare_soap (soap.cpp:555-569): wv[q][n] = weight_q grid_q^2 values[n][q].
+            const int Q = q.radial_grid_size;
+            plan->poly.assign(q.radial_grid, q.radial_grid + Q);
+            plan->poly.resize((size_t)Q * (n + 1));
+            for (int i = 0; i < Q; ++i) {
+                const double quad = q.radial_weights[i] * q.radial_grid[i] * q.radial_grid[i];
+                for (int k = 0; k < n; ++k) plan->poly[Q + (size_t)i * n + k] = quad * q.radial_values[(size_t)k * Q + i];
+            }
+        } else {
+            plan->alphas.assign(q.alphas, q.alphas + W * n);
+            plan->betas.assign(q.betas, q.betas + W * n * n);
+        }
         for (double v : plan->alphas)
             if (!std::isfinite(v)) return fail(MDSOAP_INVALID_ARGUMENT, "SOAP radial basis must be finite");
         for (double v : plan->betas)
@@ -924,7 +995,9 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         t.out_f64 = q.output_dtype == MDSOAP_FLOAT64;
         t.cutoff2 = plan->cutoff * plan->cutoff;
         const double pi = 3.141592653589793238462643383279502884;
-        t.soap_scale = pi * std::sqrt(pi);
+        t.soap_scale = polynomial ? 1.0 : pi * std::sqrt(pi);
+        t.grid_size = polynomial ? q.radial_grid_size : 0;
+        t.eta = eta;
         for (int l = 0; l <= L; ++l) {
             t.power_pref[l] = pi * std::sqrt(8.0 / (2.0 * l + 1.0));
             for (int m = 0; m <= l; ++m) {
@@ -950,13 +1023,15 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                 std::log(it.prefactor) - span < -690.0)
                 radial_normal = false;
         }
-        const Variant* paired = radial_normal ? paired_variant(n, L, q.output_dtype == MDSOAP_FLOAT64) : nullptr;
+        const Variant* paired = polynomial ? poly_variant(n, L)
+                                : radial_normal ? paired_variant(n, L, q.output_dtype == MDSOAP_FLOAT64)
+                                                : nullptr;
         const char* env = std::getenv("MDSOAP_VARIANT");
         const int want = env ? std::atoi(env) : -1;
         const Variant* picked = nullptr;
         if (paired && want <= 0) picked = paired;
         else picked = &pick_variant(n, L, paired ? want - 1 : want);
-        const bool needs_paired = t.weighted || q.compression != MDSOAP_COMPRESSION_OFF;
+        const bool needs_paired = t.weighted || q.compression != MDSOAP_COMPRESSION_OFF || polynomial;
         if (needs_paired && paired) picked = paired;
         if (paired && picked != paired && want > 0 && want - 1 >= 0) {
             // An index past the class list falls back to the default (the paired kernel).
@@ -976,13 +1051,15 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             t.rsize = coef_species * n * t.rs;
             t.n_magic = n == 1 ? 0u : (uint32_t)((1ull << 32) / (uint64_t)n + 1ull);
             const bool single_pass = t.type_groups == 1;
-            const size_t shared = 256 + (size_t)W * 64 * 8;
+            const size_t grid_bytes = polynomial ? ((size_t)t.grid_size * 9 * 8 + 15) & ~(size_t)15 : 0;
+            const size_t flir_bytes = polynomial ? (size_t)W * t.grid_size * 8 : 0;
+            const size_t shared = 256 + (size_t)W * 64 * 8 + grid_bytes;
             // paired::Layout<L>::ROW: G views of 2L+2 doubles, padded to = 2 (mod 4).
             const size_t views = (size_t)(1 + (L + 1) / 2) * (size_t)(2 * L + 2);
             const size_t row = views + (2 - views % 4 + 4) % 4;
             const size_t r_bytes = (size_t)t.rsize * 8;
             auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
-            auto walk = [&](int c) { return (size_t)paired::kHeaderBytes + (size_t)c * row * 8; };
+            auto walk = [&](int c) { return (size_t)paired::kHeaderBytes + (size_t)c * row * 8 + flir_bytes; };
             auto per_warp = [&](int c, bool r_in) {
                 if (!r_in) return align16(walk(c));
                 if (single_pass) return align16(std::max(walk(c), r_bytes));
@@ -1008,7 +1085,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             // MDSOAP_SPLIT_TAIL=0 keeps them fused (measurement knob).
             const char* split_env = std::getenv("MDSOAP_SPLIT_TAIL");
             const bool split_allowed = !(split_env && split_env[0] == '0');
-            if (split_allowed && n == 8 && coef_species <= v.maxt && q.average != MDSOAP_AVERAGE_INNER && r_smem) {
+            if (split_allowed && !polynomial && n == 8 && coef_species <= v.maxt && q.average != MDSOAP_AVERAGE_INNER && r_smem) {
                 t.split_tail = 1;
                 plan->tail_smem = (size_t)W * 64 * 8 + (size_t)t.rsize * 8;
                 if (const char* chunk_env = std::getenv("MDSOAP_TAIL_CHUNK"))
@@ -1024,8 +1101,8 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         }
         if (needs_paired)
             return fail(MDSOAP_INVALID_ARGUMENT,
-                        "SOAP weighting and compression run on the paired-channel kernel, which needs n_max <= 8, "
-                        "n_max (1 + (l_max + 1) / 2) <= 32 and l_max <= 6");
+                        "SOAP weighting, compression and the polynomial radial basis run on the paired-channel "
+                        "kernel, which needs n_max <= 8, n_max (1 + (l_max + 1) / 2) <= 32 and l_max <= 6");
         // The tensor-core kernel keeps a centre's whole coefficient block in
         // shared memory; when that does not fit, the class's scalar kernel runs.
         const mma::Layout lay = mma::layout(L, q.n_species * n);
@@ -1292,6 +1369,7 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
     const size_t o_items = take(sizeof(RadialItem) * plan->items.size());
     const size_t o_betas = take(8 * plan->betas.size());
     const size_t o_species = take(4 * plan->species.size());
+    const size_t o_poly = take(8 * plan->poly.size());
     const size_t o_error = take(sizeof(unsigned));
     const size_t o_info = take(sizeof(StructInfo) * (size_t)std::max<int64_t>(S, 1));
     const size_t o_struct = take(4 * (size_t)N);
@@ -1338,6 +1416,9 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
         check(cudaMemcpyAsync(base + o_species, plan->species.data(), 4 * plan->species.size(),
                               cudaMemcpyHostToDevice, st),
               "upload species");
+        if (!plan->poly.empty())
+            check(cudaMemcpyAsync(base + o_poly, plan->poly.data(), 8 * plan->poly.size(), cudaMemcpyHostToDevice, st),
+                  "upload polynomial basis");
         unsigned* error = reinterpret_cast<unsigned*>(base + o_error);
         check(cudaMemsetAsync(error, 0, sizeof(unsigned), st), "clear error word");
         BinView v;
@@ -1364,6 +1445,7 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
         p.bins = v;
         p.items = reinterpret_cast<RadialItem*>(base + o_items);
         p.betas = reinterpret_cast<double*>(base + o_betas);
+        p.poly = reinterpret_cast<double*>(base + o_poly);
         p.out = out;
         p.cbuf = o_cbuf ? reinterpret_cast<double*>(base + o_cbuf) : nullptr;
         p.pbuf = o_pbuf ? reinterpret_cast<double*>(base + o_pbuf) : nullptr;

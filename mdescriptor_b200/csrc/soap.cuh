@@ -64,6 +64,8 @@ struct SoapTables {
     int32_t coef_species; // species of the coefficient block: n_species, or 1 for mu2
     int32_t weighted;     // 1: per-edge weights (weighting function, w0, or mu2 pooling); paired kernel only
     int32_t split_tail;   // 1: the paired kernel stops after the flush; soap_tail_kernel finishes the centres
+    int32_t grid_size;    // polynomial basis: quadrature nodes (0 for the GTO basis)
+    double eta;           // 1 / (2 sigma^2)
     int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)
     int32_t has_w0;       // the exact self pair takes weight w0
     double w_r0, w_c, w_d, w_m, w_0;
@@ -90,6 +92,7 @@ struct SoapPointers {
     int64_t center_end;
     int64_t grid_begin;       // paired / tail kernels: centres [grid_begin, grid_end) of this launch,
     int64_t grid_end;         // rbuf rows relative to grid_begin
+    const double* poly;       // polynomial basis: nodes [Q], then weighted values wv [Q][n_max]
 };
 
 // Radial weight of one edge (soap_weight, cpp/src/standalone/soap.cpp:389-420,

@@ -131,7 +131,14 @@ __device__ __forceinline__ void harmonics_row(const SoapTables& tab, double x, d
 // accuracy (float64 rows need the full one); MINB resident CTAs per SM.
 // SPLIT: the kernel ends after the flush, handing the raw sums to
 // soap_tail_kernel (no tail code, so fewer registers).
-template <int MAXT, int L, bool PRECISE, int MINB, bool SPLIT = false>
+// POLY: polynomial radial basis (soap.cpp:450-492, 805-857): per edge, the
+// warp evaluates the modified-Bessel overlaps flir_l(r, q) on the quadrature
+// nodes (lanes over nodes, the reference's recurrence and operation order,
+// its clamp at 0), and each lane projects its two channels onto the weighted
+// basis: g_ln = 4 pi r^-l sum_q flir_l(r, q) wv[q][n] (4 pi at l = 0 for the
+// exact self pair).  The accumulation and the tail are the GTO path's, with
+// beta = identity and no pi^{3/2} (the plan uploads those).
+template <int MAXT, int L, bool PRECISE, int MINB, bool SPLIT = false, bool POLY = false>
 __global__ void __launch_bounds__(kWarps * 32, MINB)
 soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
     using P = paired::Layout<L>;
@@ -151,7 +158,18 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             const int l = i / 64, nn = (i / 8) % 8, k = i % 8;
             bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
         }
-    constexpr int kShared = 256 + (L + 1) * 64 * 8;
+    // POLY: nodes [Q] and weighted values [Q][8] (zero beyond n_max) after beta.
+    const int Q = POLY ? tab.grid_size : 0;
+    double* qnodes = bt + (L + 1) * 64;
+    double* qwv = qnodes + Q;
+    if (POLY) {
+        for (int i = threadIdx.x; i < Q; i += blockDim.x) qnodes[i] = p.poly[i];
+        for (int i = threadIdx.x; i < Q * 8; i += blockDim.x) {
+            const int qq = i / 8, nn = i % 8;
+            qwv[i] = nn < n ? p.poly[Q + qq * n + nn] : 0.0;
+        }
+    }
+    const int kShared = 256 + (L + 1) * 64 * 8 + (POLY ? ((Q * 9 * 8 + 15) & ~15) : 0);
     __syncthreads();
     const int64_t center = p.grid_begin + (int64_t)blockIdx.x * kWarps + warp;
     if (center >= p.grid_end) return;
@@ -172,6 +190,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     double* pw = pr2 + kPending;
     int32_t* ptype = reinterpret_cast<int32_t*>(pw + kPending);
     double* ybuf = reinterpret_cast<double*>(region + paired::kHeaderBytes);
+    // POLY: flir_l(r, q) of the current edge, [L+1][Q], after the harmonic rows.
+    double* flir = ybuf + tab.chunk * P::ROW;
     const int64_t local = center - p.center_begin;
     double* R = tab.r_global ? p.rbuf + (center - p.grid_begin) * tab.rsize
                              : reinterpret_cast<double*>(region + tab.r_offset);
@@ -250,6 +270,58 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 }
             }
         };
+        // POLY: radial factors of the lane's two channels for one edge (d2 = r^2).
+        auto poly_radial = [&](double d2, double& gA, double& gB) {
+            const double r = sqrt(d2);
+            const double eta = tab.eta;
+            __syncwarp();
+            for (int q = lane; q < Q; q += 32) {
+                const double x = qnodes[q];
+                if (r <= 1e-14) {
+                    flir[q] = exp_nonpositive(__dmul_rn(__dmul_rn(-eta, x), x), etab);
+                    for (int l = 1; l <= L; ++l) flir[l * Q + q] = 0.0;
+                    continue;
+                }
+                // polynomial_flir, soap.cpp:470-489 (operation order kept, no contraction).
+                const double pre = __ddiv_rn(0.25, __dmul_rn(__dmul_rn(eta, r), x));
+                const double dm = __dsub_rn(x, r), dp = __dadd_rn(x, r);
+                const double minus = exp_nonpositive(__dmul_rn(__dmul_rn(-eta, dm), dm), etab);
+                const double plus = exp_nonpositive(__dmul_rn(__dmul_rn(-eta, dp), dp), etab);
+                double v2 = __dmul_rn(pre, __dsub_rn(minus, plus));
+                flir[q] = v2;
+                if (L >= 1) {
+                    double v1 = __dmul_rn(pre, __dsub_rn(__dadd_rn(minus, plus), __dmul_rn(2.0, v2)));
+                    flir[Q + q] = v1;
+#pragma unroll
+                    for (int l = 2; l <= L; ++l) {
+                        const double v = fmax(0.0, __dsub_rn(v2, __dmul_rn(__dmul_rn(pre, 4.0 * l - 2.0), v1)));
+                        flir[l * Q + q] = v;
+                        v2 = v1;
+                        v1 = v;
+                    }
+                }
+            }
+            __syncwarp();
+            double sa = 0.0, sb = 0.0;
+            const double* fa = flir + lA * Q;
+            const double* fb = flir + (lB >= 0 ? lB : 0) * Q;
+            for (int q = 0; q < Q; ++q) {
+                const double w = qwv[q * 8 + k];
+                sa = fma(fa[q], w, sa);
+                sb = fma(fb[q], w, sb);
+            }
+            // scale 4 pi r^-l (soap.cpp:811-818): r^-l as the reference's running product.
+            constexpr double kFourPi = 12.566370614359172953850573533118;
+            const double inv = r <= 1e-14 ? 0.0 : 1.0 / r;
+            double pa = 1.0, pb = 1.0;
+            for (int l = 0; l < lA; ++l) pa *= inv;
+            for (int l = 0; l < (lB >= 0 ? lB : 0); ++l) pb *= inv;
+            const double scale_a = r <= 1e-14 ? (lA == 0 ? kFourPi : 0.0) : kFourPi * pa;
+            const double scale_b = r <= 1e-14 ? (lB == 0 ? kFourPi : 0.0) : kFourPi * pb;
+            gA = lane_on ? scale_a * sa : 0.0;
+            gB = (lane_on && lB >= 0) ? scale_b * sb : 0.0;
+        };
+
         auto process = [&](int count) {
             if (lane < count) paired::harmonics_row<L>(tab, pdx[lane], pdy[lane], pdz[lane], pr2[lane],
                                                        ybuf + lane * P::ROW);
@@ -277,8 +349,13 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 for (int i = run_start[TT]; i < end; ++i) {
                     const int ea = perm[i];
                     const double ua = pr2[ea];
-                    double gAa = scaled_exp<PRECISE>(nEA * ua, prefA, etab);
-                    double gBa = scaled_exp<PRECISE>(nEB * ua, prefB, etab);
+                    double gAa, gBa;
+                    if constexpr (POLY) {
+                        poly_radial(ua, gAa, gBa);
+                    } else {
+                        gAa = scaled_exp<PRECISE>(nEA * ua, prefA, etab);
+                        gBa = scaled_exp<PRECISE>(nEB * ua, prefB, etab);
+                    }
                     if (weighted) {
                         const double wa = pw[ea];
                         gAa *= wa;

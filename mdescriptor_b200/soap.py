@@ -15,7 +15,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import BatchView, CancelFn, Params, lib, raise_for
-from .basis import basis_gto, feature_count, graph_cutoff, labels
+from .basis import basis_gto, basis_polynomial, feature_count, graph_cutoff, labels
 
 
 def _contiguous(batch) -> tuple[np.ndarray, ...]:
@@ -45,15 +45,21 @@ class Soap:
     Parameters follow ``SoapKernel``: species (declared order), r_cut, n_max,
     l_max, sigma, average ("off" | "inner" | "outer"), dtype ("float32" |
     "float64"), species_weights (the ``compression["species_weighting"]``
-    mapping, optional).  ``alphas``/``betas`` default to the reference basis
-    construction (``basis_gto``); the plugin passes the adapter's payload.
+    mapping, optional), compression ("off" | "mu2" | "mu1nu1" | "crossover"),
+    weighting (the reference's weighting dict), rbf ("gto" | "polynomial").
+    ``alphas``/``betas`` (GTO) and ``radial_grid``/``radial_weights``/
+    ``radial_values`` (polynomial) default to the reference basis
+    constructions (``basis_gto``, ``basis_polynomial``); the plugin passes the
+    adapter's payload.
     """
 
     def __init__(self, species: Sequence[int], r_cut: float = 6.0, n_max: int = 8, l_max: int = 6,
                  sigma: float = 1.0, average: str = "inner", dtype: str = "float64",
                  species_weights: dict | Sequence[float] | None = None,
                  alphas: np.ndarray | None = None, betas: np.ndarray | None = None,
-                 compression: str = "off", weighting: dict | None = None) -> None:
+                 compression: str = "off", weighting: dict | None = None, rbf: str = "gto",
+                 radial_grid: np.ndarray | None = None, radial_weights: np.ndarray | None = None,
+                 radial_values: np.ndarray | None = None) -> None:
         self.species = tuple(int(z) for z in species)
         self.r_cut = float(r_cut)
         self.n_max = int(n_max)
@@ -65,10 +71,24 @@ class Soap:
         if dtype not in ("float32", "float64"):
             raise ValueError("dtype must be 'float32' or 'float64'")
         self.dtype = np.dtype(dtype)
-        if alphas is None or betas is None:
-            alphas, betas = basis_gto(self.r_cut, self.n_max, self.l_max)
-        self._alphas = np.ascontiguousarray(alphas, dtype=np.float64).ravel()
-        self._betas = np.ascontiguousarray(betas, dtype=np.float64).ravel()
+        if rbf not in ("gto", "polynomial"):
+            raise ValueError("rbf must be 'gto' or 'polynomial'")
+        self.rbf = rbf
+        if rbf == "gto":
+            if alphas is None or betas is None:
+                alphas, betas = basis_gto(self.r_cut, self.n_max, self.l_max)
+            self._alphas = np.ascontiguousarray(alphas, dtype=np.float64).ravel()
+            self._betas = np.ascontiguousarray(betas, dtype=np.float64).ravel()
+            self._grid = self._grid_weights = self._grid_values = np.zeros(0)
+        else:
+            if radial_grid is None or radial_weights is None or radial_values is None:
+                radial_grid, radial_weights, radial_values = basis_polynomial(self.r_cut, self.n_max)
+            self._grid = np.ascontiguousarray(radial_grid, dtype=np.float64).ravel()
+            self._grid_weights = np.ascontiguousarray(radial_weights, dtype=np.float64).ravel()
+            self._grid_values = np.ascontiguousarray(radial_values, dtype=np.float64).ravel()
+            if self._grid_weights.size != self._grid.size or self._grid_values.size != self.n_max * self._grid.size:
+                raise ValueError("invalid SOAP polynomial radial basis size")
+            self._alphas = self._betas = np.zeros(0)
         self._species = np.asarray(self.species, dtype=np.int32)
         if species_weights is None:
             self._weights = None
@@ -94,7 +114,11 @@ class Soap:
             _lib.COMPRESSION[compression], _lib.WEIGHTING[function], 1 if "w0" in self.weighting else 0,
             float(self.weighting.get("r0", 1.0)), float(self.weighting.get("c", 1.0)),
             float(self.weighting.get("d", 0.0)), float(self.weighting.get("m", 1.0)),
-            float(self.weighting.get("w0", 1.0)))
+            float(self.weighting.get("w0", 1.0)),
+            0 if rbf == "gto" else 1, int(self._grid.size),
+            self._grid.ctypes.data if self._grid.size else None,
+            self._grid_weights.ctypes.data if self._grid.size else None,
+            self._grid_values.ctypes.data if self._grid.size else None)
         handle = ctypes.c_void_p()
         raise_for(lib.mdsoap_plan_create(ctypes.byref(params), ctypes.byref(handle)))
         self._plan = handle
@@ -251,9 +275,13 @@ def options_from_payload(options: dict[str, Any]) -> dict[str, Any]:
     payload = options["_cuda_payload"]["radial_basis"]
     output = options.get("output") or {}
     compression = options.get("compression") or {}
+    rbf = options.get("rbf", "gto")
+    basis = (dict(alphas=payload["alphas"], betas=payload["betas"]) if rbf == "gto" else
+             dict(radial_grid=payload["radial_grid"], radial_weights=payload["radial_weights"],
+                  radial_values=payload["radial_values"]))
     return dict(species=options["species"], r_cut=options.get("r_cut", 6.0), n_max=options.get("n_max", 8),
                 l_max=options.get("l_max", 6), sigma=options.get("sigma", 1.0),
                 average=options.get("average", "inner"), dtype=output.get("dtype", "float64"),
                 species_weights=compression.get("species_weighting"),
                 compression=compression.get("mode", "off"), weighting=options.get("weighting"),
-                alphas=payload["alphas"], betas=payload["betas"])
+                rbf=rbf, **basis)

@@ -115,6 +115,43 @@ class _Checker:
         return offsets, atoms, shifts, displacements, distance2
 
 
+_RBF_TAIL = ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int] + [ctypes.c_double] * 5
+             + [ctypes.c_int, ctypes.c_int, _P, _P, _P, ctypes.c_int, _P])
+
+
+def _soap_rbf(checker, batch, species, r_cut, n_max, l_max, sigma, radial, average, species_weights,
+              num_threads, compression, weighting):
+    """<prefix>_soap_compute_rbf: radial = ("gto", alphas, betas) or
+    ("polynomial", grid, weights, values)."""
+    fn = getattr(checker.lib, f"{checker.prefix}_soap_compute_rbf")
+    fn.restype = ctypes.c_int
+    fn.argtypes = ([_P] * 5 + [ctypes.c_int64, _P, ctypes.c_int, _P, ctypes.c_double, ctypes.c_int,
+                               ctypes.c_int, ctypes.c_double, _P, _P] + _RBF_TAIL)
+    arrays = _batch_arrays(batch)
+    structures = len(arrays[4]) - 1
+    species = np.ascontiguousarray(species, dtype=np.int32)
+    rows = structures if average != "off" else int(arrays[4][-1])
+    out = np.zeros((rows, feature_count(len(species), n_max, l_max, compression)), np.float64)
+    weights = None if species_weights is None else np.ascontiguousarray(species_weights, np.float64)
+    kind, *tables = radial
+    tables = [np.ascontiguousarray(t, np.float64) for t in tables]
+    if kind == "gto":
+        alphas, betas = tables
+        basis = (_ptr(alphas), _ptr(betas))
+        rbf = (0, 0, None, None, None)
+    else:
+        grid, grid_weights, values = tables
+        basis = (None, None)
+        rbf = (1, int(grid.size), _ptr(grid), _ptr(grid_weights), _ptr(values))
+    status = fn(*map(_ptr, arrays), structures, _ptr(species), len(species),
+                None if weights is None else _ptr(weights), float(r_cut), int(n_max), int(l_max), float(sigma),
+                *basis, _AVERAGE[average], _COMPRESSION[compression], *_weighting_args(weighting), *rbf,
+                int(num_threads), _ptr(out))
+    if status:
+        raise ValueError(checker.error())
+    return out
+
+
 class OracleLib(_Checker):
     """The plain-C restatement (soap_oracle.c)."""
 
@@ -159,6 +196,12 @@ class OracleLib(_Checker):
             raise ValueError(self.error())
         return out
 
+    def soap_poly(self, batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values,
+                  average="off", species_weights=None, num_threads=0, compression="off", weighting=None):
+        """The polynomial radial basis (oracle_soap_compute_rbf)."""
+        return _soap_rbf(self, batch, species, r_cut, n_max, l_max, sigma, ("polynomial", grid, grid_weights, values),
+                         average, species_weights, num_threads, compression, weighting)
+
     def soap(self, batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average="off",
              species_weights=None, num_threads=0, compression="off", weighting=None):
         arrays = _batch_arrays(batch)
@@ -194,6 +237,12 @@ class RefLib(_Checker):
 
     def _graph_handle(self, arrays, structures, cutoff):
         return self._build(*map(_ptr, arrays), structures, cutoff, 1)
+
+    def soap_poly(self, batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values,
+                  average="off", species_weights=None, num_threads=0, compression="off", weighting=None):
+        """compute_soap with the polynomial radial basis (ref_soap_compute_rbf)."""
+        return _soap_rbf(self, batch, species, r_cut, n_max, l_max, sigma, ("polynomial", grid, grid_weights, values),
+                         average, species_weights, num_threads, compression, weighting)
 
     def soap_ex(self, batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average="off",
                 species_weights=None, num_threads=0, compression="off", weighting=None):

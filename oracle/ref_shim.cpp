@@ -78,14 +78,16 @@ int ref_soap_compute(
 
 // compute_soap with every SoapOptions field this engine covers: species
 // weights (NULL: 1.0 each), compression 0..3, weighting function 0..3 with
-// its parameters, w0.
-int ref_soap_compute_ex(
+// its parameters, w0, and the radial basis (0 GTO: alphas / betas; 1
+// polynomial: grid, weights and values [n][grid_size]).
+int ref_soap_compute_rbf(
     const int32_t* numbers, const double* positions, const double* cells,
     const int32_t* pbc, const int64_t* offsets, int64_t structures,
     const int32_t* species, int n_species, const double* species_weights, double r_cut, int n_max,
     int l_max, double sigma, const double* alphas, const double* betas, int average, int compression,
     int weighting_function, int weighting_has_w0, double weighting_r0, double weighting_c,
-    double weighting_d, double weighting_m, double weighting_w0, int num_threads, double* out) {
+    double weighting_d, double weighting_m, double weighting_w0, int radial_basis, int grid_size,
+    const double* grid, const double* grid_weights, const double* grid_values, int num_threads, double* out) {
     try {
         mdescriptor::SoapOptions options;
         options.species.assign(species, species + n_species);
@@ -93,10 +95,16 @@ int ref_soap_compute_ex(
         options.n_max = n_max;
         options.l_max = l_max;
         options.sigma = sigma;
-        options.radial_basis = 0;
-        const size_t count = static_cast<size_t>((l_max + 1) * n_max);
-        options.alphas.assign(alphas, alphas + count);
-        options.betas.assign(betas, betas + count * n_max);
+        options.radial_basis = radial_basis;
+        if (radial_basis == 0) {
+            const size_t count = static_cast<size_t>((l_max + 1) * n_max);
+            options.alphas.assign(alphas, alphas + count);
+            options.betas.assign(betas, betas + count * n_max);
+        } else {
+            options.radial_grid.assign(grid, grid + grid_size);
+            options.radial_weights.assign(grid_weights, grid_weights + grid_size);
+            options.radial_values.assign(grid_values, grid_values + static_cast<size_t>(grid_size) * n_max);
+        }
         if (species_weights)
             options.species_weights.assign(species_weights, species_weights + n_species);
         else
@@ -120,6 +128,19 @@ int ref_soap_compute_ex(
         g_error = error.what();
         return 1;
     }
+}
+
+int ref_soap_compute_ex(
+    const int32_t* numbers, const double* positions, const double* cells,
+    const int32_t* pbc, const int64_t* offsets, int64_t structures,
+    const int32_t* species, int n_species, const double* species_weights, double r_cut, int n_max,
+    int l_max, double sigma, const double* alphas, const double* betas, int average, int compression,
+    int weighting_function, int weighting_has_w0, double weighting_r0, double weighting_c,
+    double weighting_d, double weighting_m, double weighting_w0, int num_threads, double* out) {
+    return ref_soap_compute_rbf(numbers, positions, cells, pbc, offsets, structures, species, n_species,
+                                species_weights, r_cut, n_max, l_max, sigma, alphas, betas, average, compression,
+                                weighting_function, weighting_has_w0, weighting_r0, weighting_c, weighting_d,
+                                weighting_m, weighting_w0, 0, 0, nullptr, nullptr, nullptr, num_threads, out);
 }
 
 struct PairHandle {

@@ -360,6 +360,11 @@ typedef struct {
     double* normalization;      /* [(L+1)^2], l*width+m */
     double* radial_prefactors;  /* [(L+1)*n] */
     double* radial_exponents;   /* [(L+1)*n] */
+    int radial_basis;           /* 0 GTO, 1 polynomial */
+    int grid_size;              /* polynomial: quadrature nodes Q */
+    const double* grid;         /* [Q] */
+    double* weighted_values;    /* [Q][n]: weight_q grid_q^2 values[n][q] (soap.cpp:555-569) */
+    double eta;
 } soap_plan;
 
 /* Real regular solid harmonics r^l Y_lm, layout l^2 + (l-m) = cos m, l^2 + l = m0,
@@ -430,6 +435,31 @@ static int species_type(const soap_plan* plan, int32_t z) {
     return -1;
 }
 
+/* polynomial_flir (soap.cpp:450-492): the modified-spherical-Bessel overlap of
+ * a Gaussian at distance r with each quadrature node, by the reference's
+ * downward-stable recurrence clamped at zero; values [(L+1)][Q]. */
+static void polynomial_flir(const soap_plan* plan, double radius, double* values) {
+    const int Q = plan->grid_size, L = plan->l_max;
+    const double eta = plan->eta;
+    for (int i = 0; i < (L + 1) * Q; ++i) values[i] = 0.0;
+    for (int q = 0; q < Q; ++q) {
+        const double radial = plan->grid[q];
+        if (radius <= 1e-14) {
+            values[q] = exp(-eta * (radial * radial));
+            continue;
+        }
+        const double prefactor = 0.25 / (eta * radius * radial);
+        const double minus = exp(-eta * (radial - radius) * (radial - radius));
+        const double plus = exp(-eta * (radial + radius) * (radial + radius));
+        values[q] = prefactor * (minus - plus);
+        if (L >= 1) values[Q + q] = prefactor * (minus + plus - 2.0 * values[q]);
+        for (int l = 2; l <= L; ++l) {
+            const double v = values[(l - 2) * Q + q] - prefactor * (4.0 * l - 2.0) * values[(l - 1) * Q + q];
+            values[l * Q + q] = v > 0.0 ? v : 0.0;
+        }
+    }
+}
+
 /* calculate_coefficients (soap.cpp:701-931) for one centre of one structure. */
 static void center_coefficients(const soap_plan* plan, const int* atom_types, int64_t local,
                                 const pair_list* pairs, int64_t pair_begin, int64_t pair_end,
@@ -478,6 +508,42 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
         const int self = pairs->atoms[p] - structure_begin_index == local && sh[0] == 0 && sh[1] == 0 && sh[2] == 0;
         const int type = atom_types[pairs->atoms[p] - structure_begin_index];
         weight[j] = soap_weight(plan, sqrt(pairs->distance2[p]), self, type);
+    }
+    if (plan->radial_basis == 1) {
+        /* soap.cpp:799-857: integrand[type][lm][q] accumulated over the
+         * neighbours, then projected onto the weighted basis values. */
+        const int Q = plan->grid_size;
+        double* integrand = calloc((size_t)CT * H * Q, sizeof(double));
+        double* flir = malloc(sizeof(double) * (size_t)(L + 1) * Q);
+        for (int t = 0; t < CT; ++t) {
+            for (int64_t j = type_offsets[t]; j < type_offsets[t + 1]; ++j) {
+                const double radius = sqrt(pairs->distance2[order[j]]);
+                polynomial_flir(plan, radius, flir);
+                const double inverse = radius <= 1e-14 ? 0.0 : 1.0 / radius;
+                double inverse_power = 1.0;
+                for (int l = 0; l <= L; ++l) {
+                    const double scale = radius <= 1e-14 ? (l == 0 ? 4.0 * OR_PI * weight[j] : 0.0)
+                                                         : 4.0 * OR_PI * inverse_power * weight[j];
+                    for (int m = 0; m < 2 * l + 1; ++m) {
+                        const double factor = scale * harm[j * H + l * l + m];
+                        double* target = integrand + ((size_t)t * H + l * l + m) * Q;
+                        for (int q = 0; q < Q; ++q) target[q] += factor * flir[l * Q + q];
+                    }
+                    inverse_power *= inverse;
+                }
+            }
+            for (int l = 0; l <= L; ++l)
+                for (int nn = 0; nn < n; ++nn)
+                    for (int m = 0; m < 2 * l + 1; ++m) {
+                        const double* source = integrand + ((size_t)t * H + l * l + m) * Q;
+                        double sum = 0.0;
+                        for (int q = 0; q < Q; ++q) sum += source[q] * plan->weighted_values[q * n + nn];
+                        coefficients[(t * n + nn) * H + l * l + m] += sum;
+                    }
+        }
+        free(integrand);
+        free(flir);
+        return;
     }
     for (int t = 0; t < CT; ++t) {
         for (int l = 0; l <= L; ++l) {
@@ -575,19 +641,37 @@ int64_t oracle_soap_feature_count(int n_species, int n_max, int l_max) {
  * average: 0 off (rows = atoms), 1 inner, 2 outer (rows = structures).
  * species_weights may be NULL (all 1.0).  out is fp64 (rows, F).
  */
-int oracle_soap_compute_ex(const int32_t* numbers, const double* positions, const double* cells,
-                           const int32_t* pbc, const int64_t* offsets, int64_t structures,
-                           const int32_t* species, int n_species, const double* species_weights,
-                           double r_cut, int n_max, int l_max, double sigma, const double* alphas,
-                           const double* betas, int average, int compression, int weighting_function,
-                           int weighting_has_w0, double weighting_r0, double weighting_c, double weighting_d,
-                           double weighting_m, double weighting_w0, int num_threads, double* out) {
+int oracle_soap_compute_rbf(const int32_t* numbers, const double* positions, const double* cells,
+                            const int32_t* pbc, const int64_t* offsets, int64_t structures,
+                            const int32_t* species, int n_species, const double* species_weights,
+                            double r_cut, int n_max, int l_max, double sigma, const double* alphas,
+                            const double* betas, int average, int compression, int weighting_function,
+                            int weighting_has_w0, double weighting_r0, double weighting_c, double weighting_d,
+                            double weighting_m, double weighting_w0, int radial_basis, int grid_size,
+                            const double* grid, const double* grid_weights, const double* grid_values,
+                            int num_threads, double* out) {
     if (validate_batch(numbers, positions, cells, pbc, offsets, structures)) return 1;
     if (!isfinite(r_cut) || !isfinite(sigma) || r_cut <= 0.0 || sigma <= 0.0 || n_max < 1 || l_max < 0
         || l_max > 20 || n_species < 1 || n_species > 64 || average < 0 || average > 2 || compression < 0
-        || compression > 3 || weighting_function < 0 || weighting_function > 3)
+        || compression > 3 || weighting_function < 0 || weighting_function > 3 || radial_basis < 0
+        || radial_basis > 1)
         return fail("invalid SOAP parameters");
+    if (radial_basis == 1 && (grid_size < 2 || !grid || !grid_weights || !grid_values))
+        return fail("invalid SOAP polynomial radial basis size");
     soap_plan plan;
+    plan.radial_basis = radial_basis;
+    plan.grid_size = radial_basis == 1 ? grid_size : 0;
+    plan.grid = grid;
+    plan.eta = 1.0 / (2.0 * sigma * sigma);
+    plan.weighted_values = NULL;
+    if (radial_basis == 1) {
+        plan.weighted_values = malloc(sizeof(double) * (size_t)grid_size * n_max);
+        for (int q = 0; q < grid_size; ++q) {
+            const double quadrature = grid_weights[q] * grid[q] * grid[q];
+            for (int k = 0; k < n_max; ++k)
+                plan.weighted_values[q * n_max + k] = quadrature * grid_values[k * grid_size + q];
+        }
+    }
     plan.compression = compression;
     plan.weighting_function = weighting_function;
     plan.weighting_has_w0 = weighting_has_w0;
@@ -620,7 +704,7 @@ int oracle_soap_compute_ex(const int32_t* numbers, const double* positions, cons
     }
     const double eta = 1.0 / (2.0 * sigma * sigma);
     double eta_power = 1.0;
-    for (int l = 0; l <= l_max; ++l) {
+    for (int l = 0; l <= l_max && radial_basis == 0; ++l) {
         if (l > 0) eta_power *= eta;
         for (int k = 0; k < n_max; ++k) {
             const int i = l * n_max + k;
@@ -693,7 +777,21 @@ int oracle_soap_compute_ex(const int32_t* numbers, const double* positions, cons
     free(plan.normalization);
     free(plan.radial_prefactors);
     free(plan.radial_exponents);
+    free(plan.weighted_values);
     return status;
+}
+
+int oracle_soap_compute_ex(const int32_t* numbers, const double* positions, const double* cells,
+                           const int32_t* pbc, const int64_t* offsets, int64_t structures,
+                           const int32_t* species, int n_species, const double* species_weights,
+                           double r_cut, int n_max, int l_max, double sigma, const double* alphas,
+                           const double* betas, int average, int compression, int weighting_function,
+                           int weighting_has_w0, double weighting_r0, double weighting_c, double weighting_d,
+                           double weighting_m, double weighting_w0, int num_threads, double* out) {
+    return oracle_soap_compute_rbf(numbers, positions, cells, pbc, offsets, structures, species, n_species,
+                                   species_weights, r_cut, n_max, l_max, sigma, alphas, betas, average, compression,
+                                   weighting_function, weighting_has_w0, weighting_r0, weighting_c, weighting_d,
+                                   weighting_m, weighting_w0, 0, 0, NULL, NULL, NULL, num_threads, out);
 }
 
 /* compute_soap with compression off and no weighting function. */
@@ -728,6 +826,11 @@ int oracle_soap_rows(const int32_t* numbers, const double* positions, const doub
     plan.weighting_has_w0 = 0;
     plan.weighting_r0 = plan.weighting_c = plan.weighting_m = plan.weighting_w0 = 1.0;
     plan.weighting_d = 0.0;
+    plan.radial_basis = 0;
+    plan.grid_size = 0;
+    plan.grid = NULL;
+    plan.weighted_values = NULL;
+    plan.eta = 1.0 / (2.0 * sigma * sigma);
     plan.n_species = n_species;
     plan.n_max = n_max;
     plan.l_max = l_max;

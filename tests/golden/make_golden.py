@@ -107,6 +107,8 @@ ADAPTER_KWARGS = [
          weighting={"function": "poly", "r0": 6.0, "c": 1.0, "m": 2.0}),
     dict(species=[8, 1], r_cut=4.0, n_max=4, l_max=3, average="outer", compression={"mode": "mu2"},
          weighting={"function": "exp", "r0": 1.5, "c": 2.0, "d": 0.5, "w0": 0.25}),
+    dict(species=[1, 8], r_cut=4.0, n_max=4, l_max=3, average="off", rbf="polynomial",
+         compression={"mode": "crossover"}),
 ]
 
 

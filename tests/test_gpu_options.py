@@ -102,3 +102,28 @@ def test_weighting_needs_paired_kernel_shape():
     with pytest.raises(ValueError, match="paired-channel kernel"):
         Soap((13, 29), r_cut=5.0, n_max=8, l_max=8, average="off", dtype="float64", alphas=alphas, betas=betas,
              compression="mu2")
+
+
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+@pytest.mark.parametrize("compression", ["off", "mu2", "mu1nu1", "crossover"])
+def test_polynomial_basis(oracle, cuda_device, shape, compression):
+    """rbf="polynomial" on the paired kernel's POLY instantiation (per-edge
+    flir on the quadrature nodes) against the checker."""
+    from mdescriptor_b200.basis import basis_polynomial
+
+    species, r_cut, n_max, l_max, sigma = SHAPES[shape]
+    grid, grid_weights, values = basis_polynomial(r_cut, n_max)
+    batch = cluster_batch(17) if shape == "n8l6" else mixed_batch(21)
+    weights = list(np.linspace(0.6, 1.8, len(species)))
+    weighting = WEIGHTINGS["poly+w0"] if compression == "mu2" else None
+    for average in ("off", "inner", "outer"):
+        want = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values,
+                                average=average, species_weights=weights, compression=compression,
+                                weighting=weighting)
+        for dtype in ("float64", "float32"):
+            soap = Soap(species, r_cut=r_cut, n_max=n_max, l_max=l_max, sigma=sigma, average=average, dtype=dtype,
+                        species_weights=weights, compression=compression, weighting=weighting, rbf="polynomial",
+                        radial_grid=grid, radial_weights=grid_weights, radial_values=values)
+            assert soap.kernel().endswith("true, 2, false, true>")
+            got = soap.compute(batch, devices=[0])
+            assert_close(got, want, dtype)

@@ -63,7 +63,7 @@ def expected():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("index", [0, 1, 2, 3])
+@pytest.mark.parametrize("index", [0, 1, 2, 3, 4])
 def test_adapter_options_replayed_into_the_plugin(cuda_device, expected, index):
     plugin = load_plugin()
     name, options, kwargs = adapter_cases()[index]

@@ -78,3 +78,40 @@ def test_labels_follow_reference_layouts():
         "soap:compression=mu2,l=0,n1=0,n2=2")
     assert labels(species, n_max, l_max, "mu1nu1")[0] == "soap:compression=mu1nu1,z1=8,l=0,n1=0,n2=0"
     assert labels(species, n_max, l_max, "crossover")[-1] == "soap:z1=1,z2=1,l=2,n1=2,n2=2"
+
+
+@pytest.mark.parametrize("l_max", [0, 1, 3, 6])
+@pytest.mark.parametrize("compression", ["off", "mu2", "mu1nu1", "crossover"])
+def test_checker_matches_reference_polynomial_basis(oracle, l_max, compression):
+    """rbf="polynomial": the checker's flir recurrence, integrand and projection
+    (soap.cpp:450-492, 799-857) against compute_soap, with weighting and w0
+    (the exact self pair takes the r <= 1e-14 branch)."""
+    from oracle import RefLib
+    from mdescriptor_b200.basis import basis_polynomial
+
+    ref = RefLib()
+    species, r_cut, n_max, sigma = (1, 6, 8), 3.6, 4, 0.8
+    grid, grid_weights, values = basis_polynomial(r_cut, n_max)
+    batch = mixed_batch(31 + l_max)
+    for average in ("off", "inner", "outer"):
+        kwargs = dict(average=average, species_weights=np.array([1.0, 0.7, 1.9]), compression=compression,
+                      weighting={"function": "poly", "r0": 4.2, "c": 1.3, "m": 2.0, "w0": 0.3})
+        got = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values, **kwargs)
+        want = ref.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values, **kwargs)
+        assert got.shape == want.shape == (want.shape[0], feature_count(3, n_max, l_max, compression))
+        assert np.isfinite(want).all() and np.abs(want).max() > 0
+        err = max_rel_err(got, want, AGREE_FLOOR)
+        assert err <= AGREE_TOL, f"{compression}/{average}: {err:.3e}"
+
+
+def test_polynomial_basis_matches_reference_construction():
+    """basis_polynomial restates _basis_polynomial (_kernels/core.py:79-95): the
+    values are orthonormal under the quadrature weight r^2 (to the conditioning
+    of the monomial overlap, which grows quickly with n_max)."""
+    from mdescriptor_b200.basis import basis_polynomial
+
+    grid, weights, values = basis_polynomial(5.0, 4)
+    assert grid.shape == weights.shape == (100,) and values.shape == (4, 100)
+    assert grid.min() > 0.0 and grid.max() < 5.0
+    gram = (values * (weights * grid**2)) @ values.T
+    np.testing.assert_allclose(gram, np.eye(4), atol=1e-8)

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
     lib = ctypes.CDLL(str(_lib.LIB_PATH))
     for name in declared:
         assert hasattr(lib, name), name
-    assert _lib.lib.mdsoap_abi_version() == 2
+    assert _lib.lib.mdsoap_abi_version() == 3
 
 
 def test_plugin_module_attributes():
@@ -77,7 +77,8 @@ def test_unsupported_descriptors_and_options_raise_mapped_errors():
     with pytest.raises(ImportError, match="SOAP and NeighborList only"):
         plugin.create_backend("ACSF", {"species": [1, 8]})
     for key, value, match in [
-        ("rbf", "polynomial", "radial basis"),
+        ("rbf", "bessel", "radial basis"),
+        ("rbf", "polynomial", "polynomial payload"),
         ("compression", {"mode": "mu3"}, "compression"),
         ("weighting", {"function": "gauss", "r0": 3.0, "c": 1.0}, "weighting"),
         ("average", "median", "average"),
@@ -168,7 +169,8 @@ def test_adapter_options_fixture_matches_live_adapter():
             assert set(live) == set(options)
             for key in options:
                 if key == "_cuda_payload":
-                    for arr in ("alphas", "betas"):
+                    assert set(live[key]["radial_basis"]) == set(options[key]["radial_basis"])
+                    for arr in options[key]["radial_basis"]:
                         np.testing.assert_array_equal(live[key]["radial_basis"][arr],
                                                       options[key]["radial_basis"][arr])
                 else:
@@ -209,3 +211,27 @@ def test_golden_archives_load_without_pickle():
         with np.load(path) as archive:
             for key in archive.files:
                 assert archive[key].dtype != object, (path.name, key)
+
+
+def test_checker_reproduces_the_reference_public_api_for_every_adapter_case(oracle):
+    """The CPU checker, fed the adapter's own options and payload (GTO and
+    polynomial bases, compression, weighting), reproduces the reference's
+    public-API CPU rows committed beside them (float32 output)."""
+    from _util import assert_features_close
+    from mdescriptor_b200.soap import options_from_payload
+
+    expected = dict(np.load(ROOT / "tests" / "golden" / "adapter_expected.npz"))
+    batch = workloads.Batch(*(expected[f"input/{k}"] for k in ("numbers", "positions", "cells", "pbc", "offsets")))
+    for index, (_, options, _) in enumerate(adapter_cases()):
+        kw = options_from_payload(options)
+        weights = kw["species_weights"]
+        if weights is not None:
+            weights = [float(weights.get(str(z), weights.get(z, 1.0))) for z in kw["species"]]
+        common = dict(average=kw["average"], species_weights=weights, compression=kw["compression"],
+                      weighting=kw["weighting"])
+        args = (batch, kw["species"], kw["r_cut"], kw["n_max"], kw["l_max"], kw["sigma"])
+        if kw["rbf"] == "polynomial":
+            got = oracle.soap_poly(*args, kw["radial_grid"], kw["radial_weights"], kw["radial_values"], **common)
+        else:
+            got = oracle.soap(*args, kw["alphas"], kw["betas"], **common)
+        assert_features_close(got.astype(np.float32), expected[f"case{index}/values"], np.float32)
