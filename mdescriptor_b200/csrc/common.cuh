@@ -25,6 +25,7 @@ enum DeviceError : unsigned {
     kErrSingularCell = 8u,     // |det(cell)| < 1e-14 for a periodic structure
     kErrPairCapacity = 16u,    // neighbour CSR fill overran its counted capacity
     kErrExtendedRange = 32u,   // image-expanded structure beyond int32 atom indices
+    kErrTailTimeout = 64u,     // a tail kernel's bulk copy did not complete within its time limit
 };
 
 // Per-structure geometry and binning plan, written by bin_structures_kernel.

@@ -59,6 +59,7 @@ std::string device_error_text(unsigned bits) {
     if (bits & kErrWrapRange) return "periodic image range exceeds integer range";
     if (bits & kErrPairCapacity) return "neighbour list: a centre has more pairs than the GPU list holds (2048)";
     if (bits & kErrExtendedRange) return "neighbor extended atom index exceeds int32 range";
+    if (bits & kErrTailTimeout) return "tail kernel: a coefficient block copy did not complete in time";
     return "device error";
 }
 
@@ -427,6 +428,7 @@ struct DeviceState {
     DeviceBytes out[2];
     PinnedBytes staging[2];
     bool smem_configured = false;
+    int64_t tail_grid = 0;  // persistent tail kernel: resident CTAs on this device
     cudaEvent_t timing[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // bin | centre | tail | structure
     bool timed = false;  // the last device call recorded the timing events
     bool split_timed = false;  // ... including the event between the expansion and tail kernels
@@ -539,9 +541,22 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
           "center kernel smem");
     check(cudaFuncSetAttribute(variant->structure_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
           "structure kernel smem");
-    if (variant->tail_sym)
-        check(cudaFuncSetAttribute(variant->tail_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+    if (variant->tail_sym) {
+        // The tail kernel's mbarriers are static shared memory: the dynamic
+        // ceiling is what remains of the opt-in maximum.
+        cudaFuncAttributes attr{};
+        check(cudaFuncGetAttributes(&attr, variant->tail_sym()), "tail kernel attributes");
+        check(cudaFuncSetAttribute(variant->tail_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   optin - (int)attr.sharedSizeBytes),
               "tail kernel smem");
+        if (tab.split_tail) {
+            int per_sm = 0, sms = 0;
+            check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, variant->tail_sym(), kWarps * 32, tail_smem),
+                  "tail kernel occupancy");
+            check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, st.device), "SM count");
+            st.tail_grid = (int64_t)std::max(per_sm, 1) * sms;
+        }
+    }
     if (variant->split_sym)
         check(cudaFuncSetAttribute(variant->split_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
               "centre kernel smem");
@@ -600,7 +615,9 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             // With one chunk, the event splits the timing into expansion and tail.
             if (after_expansion && c0 == a0 && p.grid_end == a1)
                 check(cudaEventRecord(after_expansion, stream), "timing event");
-            variant->tail(dim3((unsigned)(p.grid_end - c0)), tail_smem, stream, tab, p);  // one CTA per centre
+            // Persistent tail: the resident CTAs stride over the block's centres.
+            const int64_t tail_ctas = std::min<int64_t>(p.grid_end - c0, std::max<int64_t>(st.tail_grid, 1));
+            variant->tail(dim3((unsigned)tail_ctas), tail_smem, stream, tab, p);
             check(cudaGetLastError(), "tail kernel launch");
             launches.fetch_add(2, std::memory_order_relaxed);
         }
@@ -1087,7 +1104,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             const bool split_allowed = !(split_env && split_env[0] == '0');
             if (split_allowed && !polynomial && n == 8 && coef_species <= v.maxt && q.average != MDSOAP_AVERAGE_INNER && r_smem) {
                 t.split_tail = 1;
-                plan->tail_smem = (size_t)W * 64 * 8 + (size_t)t.rsize * 8;
+                plan->tail_smem = (size_t)W * 64 * 8 + 2 * (size_t)t.rsize * 8;  // beta + two coefficient blocks
                 if (const char* chunk_env = std::getenv("MDSOAP_TAIL_CHUNK"))
                     plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
             }

@@ -31,6 +31,7 @@
 // the fp64 tensor cores are dmma.cuh's, as in soap_center_kernel.
 #pragma once
 
+#include "bulk_copy.cuh"
 #include "soap.cuh"
 
 namespace mdsoap {
@@ -660,17 +661,20 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
 }
 
 // Tail of the paired kernel as a kernel of its own (n_max == 8, average off
-// or outer, at most MAXS species): one CTA of four warps per centre stages the
-// centre's raw-sum block from global scratch into shared memory; warp w then
-// runs the register tail (beta transform + power spectrum on the fp64 tensor
-// cores) for the degrees of channel group w -- {L}, {L-1, 0}, {L-2, 1}, ...,
-// four groups of about equal tensor-core work for L = 5, 6 -- so a centre's
-// degrees proceed in parallel and more warps share an SM.
+// or outer, at most MAXS species).  Persistent: CTA b takes centres b,
+// b + gridDim.x, ...; each centre's raw-sum block arrives in shared memory by
+// one bulk (TMA) copy, double buffered, so the next centre's block is in
+// flight while the four warps work on this one.  Warp w runs the register
+// tail (beta transform + power spectrum on the fp64 tensor cores) for the
+// degrees of channel group w -- {L}, {L-1, 0}, {L-2, 1}, ..., four groups of
+// about equal tensor-core work for L = 5, 6.  A copy that does not complete
+// within a second sets kErrTailTimeout and ends the CTA.
 template <int L, int MAXS>
 __global__ void __launch_bounds__(kWarps * 32)
 soap_tail_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
     using P = paired::Layout<L>;
     extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bars[2];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int S = tab.coef_species, n = tab.n_max;
     double* bt = reinterpret_cast<double*>(smem);
@@ -679,27 +683,55 @@ soap_tail_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
         bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
     }
     constexpr int kShared = (L + 1) * 64 * 8;
-    const int64_t center = p.grid_begin + (int64_t)blockIdx.x;
-    if (center >= p.grid_end) return;  // uniform over the CTA
-    const int64_t local = center - p.center_begin;
-    double* R = reinterpret_cast<double*>(smem + kShared);
-    const double2* src = reinterpret_cast<const double2*>(p.rbuf + (center - p.grid_begin) * tab.rsize);
-    double2* dst = reinterpret_cast<double2*>(R);
-    for (int i = threadIdx.x; i < tab.rsize / 2; i += blockDim.x) dst[i] = src[i];
+    double* const rbuf = reinterpret_cast<double*>(smem + kShared);  // two blocks of rsize doubles
+    const uint32_t bytes = (uint32_t)tab.rsize * 8u;  // a multiple of 256 (row_stride)
+    const int64_t count = p.grid_end - p.grid_begin;
+    if (threadIdx.x == 0) {
+        bulk::barrier_init(&bars[0], 1);
+        bulk::barrier_init(&bars[1], 1);
+        bulk::barrier_init_fence();
+    }
     __syncthreads();
-    if (warp >= P::G) return;
-    const int la = P::la(warp), lb = P::lb(warp);
-    if (tab.average == 0) {
-        const int64_t row = center - p.out_row_begin;
-        if (tab.out_f64)
-            mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
-                                       static_cast<double*>(p.out) + row * tab.features, lane, la, la, lb);
-        else
-            mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
-                                       static_cast<float*>(p.out) + row * tab.features, lane, la, la, lb);
-    } else {
-        mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref, p.pbuf + local * tab.features,
-                                   lane, la, la, lb);
+    int64_t c = blockIdx.x;
+    if (threadIdx.x == 0 && c < count) {
+        bulk::arrive_expect(&bars[0], bytes);
+        bulk::load(rbuf, p.rbuf + c * tab.rsize, bytes, &bars[0]);
+    }
+    const int la = warp < P::G ? P::la(warp) : 0, lb = warp < P::G ? P::lb(warp) : -1;
+    for (int it = 0; c < count; ++it, c += gridDim.x) {
+        const int b = it & 1;
+        const int64_t next = c + gridDim.x;
+        // Buffer b^1 was last read in iteration it - 1, which ended in a barrier.
+        if (threadIdx.x == 0 && next < count) {
+            bulk::proxy_fence();
+            bulk::arrive_expect(&bars[b ^ 1], bytes);
+            bulk::load(rbuf + (b ^ 1) * tab.rsize, p.rbuf + next * tab.rsize, bytes, &bars[b ^ 1]);
+        }
+        const bool ok = bulk::wait(&bars[b], (uint32_t)(it >> 1) & 1u);
+        if (__syncthreads_or(!ok)) {
+            if (threadIdx.x == 0) {
+                atomicOr(p.bins.error, kErrTailTimeout);
+                if (next < count) bulk::wait(&bars[b ^ 1], (uint32_t)((it + 1) >> 1) & 1u);
+            }
+            return;
+        }
+        const double* R = rbuf + b * tab.rsize;
+        const int64_t center = p.grid_begin + c;
+        if (warp < P::G) {
+            if (tab.average == 0) {
+                const int64_t row = center - p.out_row_begin;
+                if (tab.out_f64)
+                    mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
+                                               static_cast<double*>(p.out) + row * tab.features, lane, la, la, lb);
+                else
+                    mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
+                                               static_cast<float*>(p.out) + row * tab.features, lane, la, la, lb);
+            } else {
+                mma::tail_regs_n8<L, MAXS>(bt, R, tab.rs, S, tab.compression, tab.power_pref,
+                                           p.pbuf + (center - p.center_begin) * tab.features, lane, la, la, lb);
+            }
+        }
+        __syncthreads();
     }
 }
 

@@ -435,6 +435,26 @@ static int species_type(const soap_plan* plan, int32_t z) {
     return -1;
 }
 
+/* Conditioning probe for tests: when set, every exponential of the polynomial
+ * basis is moved by one unit in the last place (up or down by a bit of its
+ * argument), so a test can measure how far last-bit differences between exp
+ * implementations travel through the reference's flir recurrence. */
+static int g_flir_exp_ulp = 0;
+
+void oracle_set_flir_exp_ulp(int enabled) { g_flir_exp_ulp = enabled; }
+
+static double flir_exp(double x) {
+    double v = exp(x);
+    if (g_flir_exp_ulp && v > 0.0) {
+        uint64_t a, b;
+        memcpy(&a, &x, sizeof a);
+        memcpy(&b, &v, sizeof b);
+        b = ((a >> 3) & 1) ? b + 1 : b - 1;
+        memcpy(&v, &b, sizeof v);
+    }
+    return v;
+}
+
 /* polynomial_flir (soap.cpp:450-492): the modified-spherical-Bessel overlap of
  * a Gaussian at distance r with each quadrature node, by the reference's
  * downward-stable recurrence clamped at zero; values [(L+1)][Q]. */
@@ -445,12 +465,12 @@ static void polynomial_flir(const soap_plan* plan, double radius, double* values
     for (int q = 0; q < Q; ++q) {
         const double radial = plan->grid[q];
         if (radius <= 1e-14) {
-            values[q] = exp(-eta * (radial * radial));
+            values[q] = flir_exp(-eta * (radial * radial));
             continue;
         }
         const double prefactor = 0.25 / (eta * radius * radial);
-        const double minus = exp(-eta * (radial - radius) * (radial - radius));
-        const double plus = exp(-eta * (radial + radius) * (radial + radius));
+        const double minus = flir_exp(-eta * (radial - radius) * (radial - radius));
+        const double plus = flir_exp(-eta * (radial + radius) * (radial + radius));
         values[q] = prefactor * (minus - plus);
         if (L >= 1) values[Q + q] = prefactor * (minus + plus - 2.0 * values[q]);
         for (int l = 2; l <= L; ++l) {

@@ -7,7 +7,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from _util import AGREE_FLOOR, AGREE_TOL, assert_features_close, max_rel_err
+from _util import AGREE_FLOOR, AGREE_TOL, F32_FLOOR, F32_TOL, assert_features_close, max_rel_err
 from mdescriptor_b200 import workloads
 from mdescriptor_b200.basis import basis_gto
 from mdescriptor_b200.soap import Soap
@@ -117,13 +117,27 @@ def test_polynomial_basis(oracle, cuda_device, shape, compression):
     weights = list(np.linspace(0.6, 1.8, len(species)))
     weighting = WEIGHTINGS["poly+w0"] if compression == "mu2" else None
     for average in ("off", "inner", "outer"):
-        want = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values,
-                                average=average, species_weights=weights, compression=compression,
-                                weighting=weighting)
+        kwargs = dict(average=average, species_weights=weights, compression=compression, weighting=weighting)
+        want = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values, **kwargs)
+        # The reference's upward flir recurrence amplifies last-bit differences
+        # of its exponentials (at n_max = 8 up to ~1e-6 relative at floor 1e-3
+        # and ~6e-4 at floor 1e-6); each bound is four times the spread the
+        # checker itself shows at that floor when every exponential moves by
+        # one ulp, and never below the usual bound for the dtype.
+        try:
+            oracle.lib.oracle_set_flir_exp_ulp(1)
+            moved = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values,
+                                     **kwargs)
+        finally:
+            oracle.lib.oracle_set_flir_exp_ulp(0)
+        bound = {"float64": max(AGREE_TOL, 4.0 * max_rel_err(moved, want, AGREE_FLOOR)),
+                 "float32": max(F32_TOL, 4.0 * max_rel_err(moved, want, F32_FLOOR))}
+        floor = {"float64": AGREE_FLOOR, "float32": F32_FLOOR}
         for dtype in ("float64", "float32"):
             soap = Soap(species, r_cut=r_cut, n_max=n_max, l_max=l_max, sigma=sigma, average=average, dtype=dtype,
                         species_weights=weights, compression=compression, weighting=weighting, rbf="polynomial",
                         radial_grid=grid, radial_weights=grid_weights, radial_values=values)
             assert soap.kernel().endswith("true, 2, false, true>")
             got = soap.compute(batch, devices=[0])
-            assert_close(got, want, dtype)
+            err = max_rel_err(got, want, floor[dtype])
+            assert err <= bound[dtype], f"{dtype} max rel err {err:.3e} > {bound[dtype]:.3e}"

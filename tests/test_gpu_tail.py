@@ -1,0 +1,63 @@
+"""The n_max = 8 tail as its own persistent kernel (soap_tail_kernel: bulk-copied,
+double-buffered coefficient blocks) against the tail fused into the expansion
+kernel (MDSOAP_SPLIT_TAIL=0) and against chunked expansion / tail launches
+(MDSOAP_TAIL_CHUNK): the same per-degree arithmetic in every mode, so the rows
+agree bit for bit, and with the CPU checker within the float tolerances."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from test_gpu_options import assert_close
+from mdescriptor_b200 import workloads
+from mdescriptor_b200.basis import basis_gto
+from mdescriptor_b200.soap import Soap
+
+pytestmark = pytest.mark.gpu
+
+SPECIES, R_CUT, N_MAX, L_MAX, SIGMA = (1, 6, 7, 8), 5.0, 8, 6, 1.0
+
+
+def make(average, dtype, compression="off"):
+    return Soap(SPECIES, r_cut=R_CUT, n_max=N_MAX, l_max=L_MAX, sigma=SIGMA, average=average, dtype=dtype,
+                compression=compression)
+
+
+@pytest.mark.parametrize("average", ["off", "outer"])
+@pytest.mark.parametrize("dtype", ["float32", "float64"])
+def test_split_fused_and_chunked_tails_agree(oracle, cuda_device, monkeypatch, average, dtype):
+    batch = workloads.config2(structures=12, seed=5)
+    split = make(average, dtype)
+    assert "soap_tail_kernel" in split.kernel()
+    want = split.compute(batch, devices=[0])
+    # Repeated calls reuse the device state (barriers re-initialised per launch).
+    assert np.array_equal(split.compute(batch, devices=[0]), want)
+
+    monkeypatch.setenv("MDSOAP_SPLIT_TAIL", "0")
+    fused = make(average, dtype)
+    assert "soap_tail_kernel" not in fused.kernel()
+    assert np.array_equal(fused.compute(batch, devices=[0]), want)
+    monkeypatch.delenv("MDSOAP_SPLIT_TAIL")
+
+    for chunk in ("37", "200"):  # ragged chunks; more centres than some grids
+        monkeypatch.setenv("MDSOAP_TAIL_CHUNK", chunk)
+        chunked = make(average, dtype)
+        assert np.array_equal(chunked.compute(batch, devices=[0]), want), chunk
+    monkeypatch.delenv("MDSOAP_TAIL_CHUNK")
+
+    alphas, betas = basis_gto(R_CUT, N_MAX, L_MAX)
+    ref = oracle.soap(batch, SPECIES, R_CUT, N_MAX, L_MAX, SIGMA, alphas, betas, average=average)
+    assert_close(want, ref, dtype)
+
+
+def test_split_tail_single_centre_and_empty(cuda_device):
+    """Fewer centres than resident CTAs (one structure of one atom) and an empty batch."""
+    soap = make("off", "float64")
+    one = workloads.Batch(np.array([8], np.int32), np.zeros((1, 3)), np.zeros((1, 3, 3)),
+                          np.zeros((1, 3), np.int32), np.array([0, 1], np.int64))
+    rows = soap.compute(one, devices=[0])
+    assert rows.shape == (1, soap.feature_count) and np.isfinite(rows).all() and rows.any()
+    empty = workloads.Batch(np.zeros(0, np.int32), np.zeros((0, 3)), np.zeros((0, 3, 3)),
+                            np.zeros((0, 3), np.int32), np.array([0], np.int64))
+    assert soap.compute(empty, devices=[0]).shape == (0, soap.feature_count)

@@ -115,3 +115,23 @@ def test_polynomial_basis_matches_reference_construction():
     assert grid.min() > 0.0 and grid.max() < 5.0
     gram = (values * (weights * grid**2)) @ values.T
     np.testing.assert_allclose(gram, np.eye(4), atol=1e-8)
+
+
+def test_flir_conditioning_probe(oracle):
+    """The probe that moves every polynomial-basis exponential by one ulp
+    changes the checker's rows by a small, nonzero amount, and switching it
+    off restores the reference-matching rows bit for bit."""
+    from mdescriptor_b200.basis import basis_polynomial
+
+    species, r_cut, n_max, l_max, sigma = (1, 6, 8), 3.6, 4, 3, 0.8
+    grid, grid_weights, values = basis_polynomial(r_cut, n_max)
+    batch = mixed_batch(5)
+    base = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values)
+    try:
+        oracle.lib.oracle_set_flir_exp_ulp(1)
+        moved = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values)
+    finally:
+        oracle.lib.oracle_set_flir_exp_ulp(0)
+    again = oracle.soap_poly(batch, species, r_cut, n_max, l_max, sigma, grid, grid_weights, values)
+    assert np.array_equal(again, base)
+    assert 0.0 < max_rel_err(moved, base, AGREE_FLOOR) < 1e-6
