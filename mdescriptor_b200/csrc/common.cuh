@@ -43,7 +43,8 @@ struct StructInfo {
     int32_t K[3];        // bin search half-width per axis
     int64_t atom_begin;
     int32_t atom_count;
-    int32_t pad_;
+    int32_t aligned;     // bins are axis-aligned boxes origin + [b, b+1) * extent / M (isolated, or
+                         // periodic with a diagonal cell of positive entries)
     int64_t bin_base;    // first bin_start entry of this structure
     double pre_cut2;     // prefilter radius^2: cutoff plus a margin far above fp64 rounding of any displacement
 };

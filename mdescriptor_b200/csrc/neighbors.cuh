@@ -137,6 +137,11 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
     }
     if (tid == 0) {
         si.periodic = periodic;
+        {
+            const double* c = b.cells + 9 * s;
+            si.aligned = !periodic || (c[1] == 0.0 && c[2] == 0.0 && c[3] == 0.0 && c[5] == 0.0 && c[6] == 0.0 &&
+                                       c[7] == 0.0 && c[0] > 0.0 && c[4] > 0.0 && c[8] > 0.0);
+        }
         si.atom_begin = begin;
         si.atom_count = (int32_t)count;
         si.bin_base = bin_base_of(begin, s);

@@ -498,16 +498,42 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     const int dy = row - (row / wy) * wy - Ky;
                     const int ey = cy + dy, ez = cz + dz;
                     int ty = 0, tz = 0, tx = 0, b0, b1;
+                    // Axis-aligned bins: drop rows whose box lies beyond the
+                    // prefilter sphere and trim the x range to the bins the
+                    // sphere reaches (the dropped candidates would all fail
+                    // the prefilter, so the survivors and their order are
+                    // unchanged).
+                    int rxlo = xlo, rxhi = xhi;
+                    if (si.aligned) {
+                        const double hx = si.extent[0] / Mx, hy = si.extent[1] / My, hz = si.extent[2] / Mz;
+                        const double cx_ = wpos[0] - si.origin[0], cy_ = wpos[1] - si.origin[1],
+                                     cz_ = wpos[2] - si.origin[2];
+                        const double eps = 1e-8 * (1.0 + si.extent[0] + si.extent[1] + si.extent[2] + fabs(cx_) +
+                                                   fabs(cy_) + fabs(cz_) + sqrt(pre2));
+                        auto gap = [&](double c, int e, double h) {
+                            const double lo = e * h, hi = (e + 1) * h;
+                            return fmax(0.0, (c < lo ? lo - c : (c > hi ? c - hi : 0.0)) - eps);
+                        };
+                        const double ry = gap(cy_, ey, hy), rz = gap(cz_, ez, hz);
+                        const double rem = pre2 - ry * ry - rz * rz;
+                        if (rem < 0.0) {
+                            valid = false;
+                        } else if (hx > 0.0) {
+                            const double reach = sqrt(rem) + eps;
+                            rxlo = max(xlo, (int)fmax(floor((cx_ - reach) / hx), (double)xlo - 1.0));
+                            rxhi = min(xhi, (int)fmin(floor((cx_ + reach) / hx), (double)xhi + 1.0));
+                        }
+                    }
                     if (periodic) {
                         ty = floor_div(ey, My);
                         tz = floor_div(ez, Mz);
                         tx = tx0 + xs;
-                        b0 = max(xlo, tx * Mx) - tx * Mx;
-                        b1 = min(xhi, tx * Mx + Mx - 1) - tx * Mx;
+                        b0 = max(rxlo, tx * Mx) - tx * Mx;
+                        b1 = min(rxhi, tx * Mx + Mx - 1) - tx * Mx;
                     } else {
-                        valid = ey >= 0 && ey < My && ez >= 0 && ez < Mz;
-                        b0 = max(xlo, 0);
-                        b1 = min(xhi, Mx - 1);
+                        valid = valid && ey >= 0 && ey < My && ez >= 0 && ez < Mz;
+                        b0 = max(rxlo, 0);
+                        b1 = min(rxhi, Mx - 1);
                     }
                     valid = valid && b0 <= b1;
                     if (valid) {
