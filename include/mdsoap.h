@@ -179,6 +179,25 @@ int mdsoap_compute_device(mdsoap_plan* plan, const mdsoap_batch* batch, void* ou
  * `device` since the last check (and clear it). */
 int mdsoap_plan_check(mdsoap_plan* plan, int32_t device, void* stream);
 
+/* Sparse rows.  The feature matrix in CSR form with exact zeros dropped,
+ * built on `device`: the batch (host arrays) is uploaded, the rows are
+ * computed into device memory, and a count pass, a prefix and a fill pass
+ * emit row offsets, column indices and values (columns ascending within a
+ * row), so only the nonzeros cross PCIe.  Values have the plan's output dtype;
+ * the result equals scipy.sparse.csr_matrix of the dense rows mdsoap_compute
+ * returns.  Device memory for the dense rows is allocated for the call and
+ * freed before it returns.
+ * Replaces: format_values(..., sparse=True) on the dense host matrix
+ * (src/mdescriptor/core/result.py:64-84) for OutputOptions(sparse=True). */
+typedef struct mdsoap_csr mdsoap_csr;
+int mdsoap_compute_csr(mdsoap_plan* plan, const mdsoap_batch* batch, int32_t device, mdsoap_csr** csr);
+/* Shape and number of stored values of a CSR result. */
+int mdsoap_csr_info(const mdsoap_csr* csr, int64_t* rows, int64_t* cols, int64_t* nnz);
+/* Copy out: indptr int64[rows + 1], indices int32[nnz], data [nnz] of the
+ * plan's output dtype. */
+int mdsoap_csr_copy(const mdsoap_csr* csr, int64_t* indptr, int32_t* indices, void* data);
+void mdsoap_csr_destroy(mdsoap_csr* csr);
+
 /* Size of the fixed device scratch area used by mdsoap_compute_device_noalloc:
  * 32 MiB, held by every GPU that loads this library until the process exits. */
 #define MDSOAP_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)

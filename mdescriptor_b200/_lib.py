@@ -118,6 +118,15 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_compute_device.restype = ctypes.c_int
     lib.mdsoap_plan_check.argtypes = [_P, ctypes.c_int32, _P]
     lib.mdsoap_plan_check.restype = ctypes.c_int
+    lib.mdsoap_compute_csr.argtypes = [_P, ctypes.POINTER(BatchView), ctypes.c_int32, ctypes.POINTER(_P)]
+    lib.mdsoap_compute_csr.restype = ctypes.c_int
+    lib.mdsoap_csr_info.argtypes = [_P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
+                                    ctypes.POINTER(ctypes.c_int64)]
+    lib.mdsoap_csr_info.restype = ctypes.c_int
+    lib.mdsoap_csr_copy.argtypes = [_P, _P, _P, _P]
+    lib.mdsoap_csr_copy.restype = ctypes.c_int
+    lib.mdsoap_csr_destroy.argtypes = [_P]
+    lib.mdsoap_csr_destroy.restype = None
     lib.mdsoap_compute_device_noalloc.argtypes = [_P, ctypes.POINTER(BatchView), _P, ctypes.c_int32, _P]
     lib.mdsoap_compute_device_noalloc.restype = ctypes.c_int
     lib.mdsoap_plan_set_timing.argtypes = [_P, ctypes.c_int32]
@@ -157,6 +166,10 @@ EXPORTED = (
     "mdsoap_compute",
     "mdsoap_compute_device",
     "mdsoap_plan_check",
+    "mdsoap_compute_csr",
+    "mdsoap_csr_info",
+    "mdsoap_csr_copy",
+    "mdsoap_csr_destroy",
     "mdsoap_compute_device_noalloc",
     "mdsoap_plan_set_timing",
     "mdsoap_plan_last_timing",

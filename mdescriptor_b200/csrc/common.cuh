@@ -59,7 +59,8 @@ struct BinView {
     int32_t* bin_start;      // [2*atoms + 8*structures] bin offsets (+1 sentinel per structure)
     int32_t* bin_cursor;     // same size, scatter cursors
     unsigned* error;         // device error word
-    double4* spos;           // [atoms] in `sorted` order: wrapped position (x, y, z) and species index (w);
+    double4* spos;           // [atoms] in `sorted` order: wrapped position (x, y, z) and
+                             // w = 128 * local atom id + species index + 1;
                              // may be null (then not written)
 };
 

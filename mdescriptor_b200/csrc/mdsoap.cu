@@ -9,6 +9,7 @@
 #include "soap_pair.cuh"
 #include "soap_paired.cuh"
 #include "neighbor_list.cuh"
+#include "csr.cuh"
 
 #include <cuda_runtime.h>
 
@@ -428,7 +429,8 @@ struct DeviceState {
     DeviceBytes out[2];
     PinnedBytes staging[2];
     bool smem_configured = false;
-    int64_t tail_grid = 0;  // persistent tail kernel: resident CTAs on this device
+    int64_t tail_grid = 0;    // persistent tail kernel: resident CTAs on this device
+    int64_t center_grid = 0;  // paired kernel: resident CTAs on this device (0: one CTA per kWarps centres)
     cudaEvent_t timing[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // bin | centre | tail | structure
     bool timed = false;  // the last device call recorded the timing events
     bool split_timed = false;  // ... including the event between the expansion and tail kernels
@@ -560,6 +562,18 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
     if (variant->split_sym)
         check(cudaFuncSetAttribute(variant->split_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
               "centre kernel smem");
+    // The paired kernel runs persistent: as many CTAs as fit on the device,
+    // each over a contiguous range of centres.  MDSOAP_PERSISTENT=0 launches
+    // one CTA per kWarps centres instead (measurement knob).
+    const char* persistent_env = std::getenv("MDSOAP_PERSISTENT");
+    if (variant->paired && !(persistent_env && persistent_env[0] == '0')) {
+        const void* sym = (tab.split_tail && variant->split_sym) ? variant->split_sym() : variant->center_sym();
+        int per_sm = 0, sms = 0;
+        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sym, kWarps * 32, center_smem),
+              "centre kernel occupancy");
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, st.device), "SM count");
+        st.center_grid = (int64_t)std::max(per_sm, 1) * sms;
+    }
     st.smem_configured = true;
 }
 
@@ -609,8 +623,9 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         for (int64_t c0 = a0; c0 < a1; c0 += chunk) {
             p.grid_begin = c0;
             p.grid_end = std::min(a1, c0 + chunk);
-            const unsigned grid = (unsigned)((p.grid_end - c0 + kWarps - 1) / kWarps);
-            variant->center(dim3(grid), center_smem, stream, tab, p);
+            int64_t grid = (p.grid_end - c0 + kWarps - 1) / kWarps;
+            if (st.center_grid > 0) grid = std::min(grid, st.center_grid);
+            variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
             check(cudaGetLastError(), "centre kernel launch");
             // With one chunk, the event splits the timing into expansion and tail.
             if (after_expansion && c0 == a0 && p.grid_end == a1)
@@ -629,7 +644,8 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             p.rbuf = st.work.rbuf.as<double>();
         }
         if (centers > 0) {
-            const int64_t grid = variant->pair ? centers : (centers + kWarps - 1) / kWarps;
+            int64_t grid = variant->pair ? centers : (centers + kWarps - 1) / kWarps;
+            if (variant->paired && st.center_grid > 0) grid = std::min(grid, st.center_grid);
             variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
             check(cudaGetLastError(), "centre kernel launch");
             launches.fetch_add(1, std::memory_order_relaxed);
@@ -1339,6 +1355,148 @@ int mdsoap_plan_check(mdsoap_plan* plan, int32_t device, void* stream) {
         return fail(f.status, f.message);
     }
 }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Sparse (CSR) rows.
+
+struct mdsoap_csr {
+    int64_t rows = 0, cols = 0, nnz = 0;
+    int32_t dtype = MDSOAP_FLOAT32;
+    std::vector<int64_t> indptr;
+    std::vector<int32_t> indices;
+    std::vector<unsigned char> data;
+};
+
+namespace {
+// Device bytes freed when the call ends.
+struct ScopedBytes : DeviceBytes {
+    ScopedBytes() = default;
+    ScopedBytes(const ScopedBytes&) = delete;
+    ScopedBytes& operator=(const ScopedBytes&) = delete;
+    ~ScopedBytes() { release(); }
+};
+
+template <class T>
+void csr_from_device_rows(mdsoap_plan* plan, const void* dense, int64_t rows, int64_t cols, cudaStream_t s,
+                          mdsoap_csr& csr) {
+    ScopedBytes counts, indptr, indices, data;
+    counts.reserve(8 * (size_t)rows, "CSR row counts");
+    const unsigned grid = (unsigned)std::min<int64_t>((rows + kWarps - 1) / kWarps, 65535);
+    csr_count_kernel<T><<<grid, kWarps * 32, 0, s>>>(static_cast<const T*>(dense), rows, cols, counts.as<int64_t>());
+    check(cudaGetLastError(), "CSR count kernel launch");
+    std::vector<int64_t> host_counts((size_t)rows);
+    check(cudaMemcpyAsync(host_counts.data(), counts.ptr, 8 * (size_t)rows, cudaMemcpyDeviceToHost, s),
+          "CSR row counts D2H");
+    check(cudaStreamSynchronize(s), "stream sync");
+    csr.indptr.assign((size_t)rows + 1, 0);
+    for (int64_t r = 0; r < rows; ++r) csr.indptr[(size_t)r + 1] = csr.indptr[(size_t)r] + host_counts[(size_t)r];
+    csr.nnz = csr.indptr[(size_t)rows];
+    csr.indices.resize((size_t)csr.nnz);
+    csr.data.resize((size_t)csr.nnz * sizeof(T));
+    if (csr.nnz > 0) {
+        indptr.reserve(8 * ((size_t)rows + 1), "CSR row offsets");
+        indices.reserve(4 * (size_t)csr.nnz, "CSR column indices");
+        data.reserve(sizeof(T) * (size_t)csr.nnz, "CSR values");
+        check(cudaMemcpyAsync(indptr.ptr, csr.indptr.data(), 8 * ((size_t)rows + 1), cudaMemcpyHostToDevice, s),
+              "CSR row offsets H2D");
+        csr_fill_kernel<T><<<grid, kWarps * 32, 0, s>>>(static_cast<const T*>(dense), rows, cols,
+                                                         indptr.as<int64_t>(), indices.as<int32_t>(), data.as<T>());
+        check(cudaGetLastError(), "CSR fill kernel launch");
+        check(cudaMemcpyAsync(csr.indices.data(), indices.ptr, 4 * (size_t)csr.nnz, cudaMemcpyDeviceToHost, s),
+              "CSR indices D2H");
+        check(cudaMemcpyAsync(csr.data.data(), data.ptr, sizeof(T) * (size_t)csr.nnz, cudaMemcpyDeviceToHost, s),
+              "CSR values D2H");
+        check(cudaStreamSynchronize(s), "stream sync");
+        plan->launches.fetch_add(1, std::memory_order_relaxed);
+    }
+    plan->launches.fetch_add(1, std::memory_order_relaxed);
+}
+}  // namespace
+
+extern "C" {
+
+int mdsoap_compute_csr(mdsoap_plan* plan, const mdsoap_batch* batch, int32_t device, mdsoap_csr** csr_out) {
+    if (!plan || !batch || !csr_out) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    *csr_out = nullptr;
+    try {
+        validate_host_batch(plan, *batch);
+        auto csr = std::make_unique<mdsoap_csr>();
+        const int64_t rows = mdsoap_plan_rows(plan, batch), cols = plan->features;
+        csr->rows = rows;
+        csr->cols = cols;
+        csr->dtype = plan->out_dtype;
+        csr->indptr.assign((size_t)rows + 1, 0);
+        DeviceState& st = plan->state(device);
+        if (batch->structures == 0 || rows == 0) {
+            *csr_out = csr.release();
+            return MDSOAP_OK;
+        }
+        std::lock_guard<std::mutex> lock(st.mutex);
+        check(cudaSetDevice(device), "cudaSetDevice");
+        cudaStream_t s = st.compute;
+        const int64_t S = batch->structures, N = batch->atoms;
+        ScopedBytes numbers, positions, cells, pbc, offsets, dense;
+        numbers.reserve(4 * (size_t)N, "batch numbers");
+        positions.reserve(24 * (size_t)N, "batch positions");
+        cells.reserve(72 * (size_t)S, "batch cells");
+        pbc.reserve(12 * (size_t)S, "batch pbc");
+        offsets.reserve(8 * ((size_t)S + 1), "batch offsets");
+        dense.reserve((size_t)rows * (size_t)cols * plan->out_elem(), "dense rows");
+        check(cudaMemcpyAsync(numbers.ptr, batch->numbers, 4 * (size_t)N, cudaMemcpyHostToDevice, s), "H2D numbers");
+        check(cudaMemcpyAsync(positions.ptr, batch->positions, 24 * (size_t)N, cudaMemcpyHostToDevice, s),
+              "H2D positions");
+        check(cudaMemcpyAsync(cells.ptr, batch->cells, 72 * (size_t)S, cudaMemcpyHostToDevice, s), "H2D cells");
+        check(cudaMemcpyAsync(pbc.ptr, batch->pbc, 12 * (size_t)S, cudaMemcpyHostToDevice, s), "H2D pbc");
+        check(cudaMemcpyAsync(offsets.ptr, batch->offsets, 8 * ((size_t)S + 1), cudaMemcpyHostToDevice, s),
+              "H2D offsets");
+        DeviceBatch db{numbers.as<int32_t>(), positions.as<double>(), cells.as<double>(), pbc.as<int32_t>(),
+                       offsets.as<int64_t>(), S, N};
+        unsigned* error = st.error.as<unsigned>();
+        plan->bin(st, db, s, error);
+        plan->run_block(st, db, 0, S, 0, N, dense.ptr, s, error);
+        unsigned bits = 0;
+        check(cudaMemcpyAsync(&bits, error, sizeof(unsigned), cudaMemcpyDeviceToHost, s), "read error word");
+        check(cudaStreamSynchronize(s), "stream sync");
+        if (bits) {
+            check(cudaMemset(error, 0, sizeof(unsigned)), "clear error word");
+            return fail(bits & (kErrUnknownSpecies | kErrMixedPbc | kErrSingularCell) ? MDSOAP_INVALID_ARGUMENT
+                                                                                      : MDSOAP_INTERNAL,
+                        device_error_text(bits));
+        }
+        if (plan->out_dtype == MDSOAP_FLOAT64)
+            csr_from_device_rows<double>(plan, dense.ptr, rows, cols, s, *csr);
+        else
+            csr_from_device_rows<float>(plan, dense.ptr, rows, cols, s, *csr);
+        *csr_out = csr.release();
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
+
+int mdsoap_csr_info(const mdsoap_csr* csr, int64_t* rows, int64_t* cols, int64_t* nnz) {
+    if (!csr) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    if (rows) *rows = csr->rows;
+    if (cols) *cols = csr->cols;
+    if (nnz) *nnz = csr->nnz;
+    return MDSOAP_OK;
+}
+
+int mdsoap_csr_copy(const mdsoap_csr* csr, int64_t* indptr, int32_t* indices, void* data) {
+    if (!csr || !indptr || ((!indices || !data) && csr->nnz > 0)) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    std::memcpy(indptr, csr->indptr.data(), 8 * csr->indptr.size());
+    if (csr->nnz > 0) {
+        std::memcpy(indices, csr->indices.data(), 4 * (size_t)csr->nnz);
+        std::memcpy(data, csr->data.data(), csr->data.size());
+    }
+    return MDSOAP_OK;
+}
+
+void mdsoap_csr_destroy(mdsoap_csr* csr) { delete csr; }
 
 }  // extern "C"
 

@@ -315,12 +315,15 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
     }
     if (v.spos == nullptr) return;
     __syncthreads();
-    // Wrapped positions and species in bin order (the centre kernels' prefilter reads them coalesced).
+    // Wrapped positions in bin order, with w = 128 j + species + 1 (j the
+    // structure-local atom id; exact in a double): the centre kernels'
+    // prefilter reads one coalesced record and learns both.
     for (int64_t p = tid; p < count; p += blockDim.x) {
-        const int64_t atom = begin + v.sorted[begin + p];
+        const int32_t j = v.sorted[begin + p];
+        const int64_t atom = begin + j;
         double w[3];
         wrapped_position(si, b.positions + 3 * atom, v.wrap + 3 * atom, w);
-        v.spos[begin + p] = make_double4(w[0], w[1], w[2], (double)v.type[atom]);
+        v.spos[begin + p] = make_double4(w[0], w[1], w[2], (double)((int64_t)j * 128 + v.type[atom] + 1));
     }
 }
 

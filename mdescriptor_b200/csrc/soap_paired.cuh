@@ -63,7 +63,7 @@ struct Layout {
 // Per-warp shared-memory region (bytes); the harmonic rows follow.
 constexpr int kSegBytes = 544;                     // seg_prefix[40] seg_start[32] seg_t[32] perm[32]
 constexpr int kSegOffBytes = 3 * 32 * 8;           // per-segment offset vectors
-constexpr int kPreQueue = 64;                      // prefilter survivors awaiting the exact test
+constexpr int kPreQueue = 96;                      // prefilter survivors awaiting the exact test
 constexpr int kPreBytes = 3 * kPreQueue * 4;
 constexpr int kEdgeBytes = kPending * (5 * 8 + 4); // dx dy dz r2 weight + species
 constexpr int kHeaderBytes = kSegBytes + kSegOffBytes + kPreBytes + kEdgeBytes;
@@ -172,8 +172,6 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     }
     const int kShared = 256 + (L + 1) * 64 * 8 + (POLY ? ((Q * 9 * 8 + 15) & ~15) : 0);
     __syncthreads();
-    const int64_t center = p.grid_begin + (int64_t)blockIdx.x * kWarps + warp;
-    if (center >= p.grid_end) return;
 
     unsigned char* region = smem + kShared + (size_t)warp * tab.warp_bytes;
     int* seg_prefix = reinterpret_cast<int*>(region);  // 40
@@ -193,6 +191,17 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     double* ybuf = reinterpret_cast<double*>(region + paired::kHeaderBytes);
     // POLY: flir_l(r, q) of the current edge, [L+1][Q], after the harmonic rows.
     double* flir = ybuf + tab.chunk * P::ROW;
+    // Centres: CTA b owns the contiguous range [c_lo, c_hi) of this launch
+    // and its warps stride through it, so the CTA's centres share a few
+    // structures whose bins, positions and sorted positions stay in L1.  A
+    // grid of resident CTAs makes the kernel persistent; a grid of one CTA
+    // per kWarps centres gives every warp one centre.
+    const int64_t total_centres = p.grid_end - p.grid_begin;
+    const int64_t per_cta = (total_centres + gridDim.x - 1) / gridDim.x;
+    const int64_t c_lo = p.grid_begin + (int64_t)blockIdx.x * per_cta;
+    const int64_t c_hi = min(p.grid_end, c_lo + per_cta);
+    auto run_centre = [&](const int64_t center) {
+    __syncwarp();  // the previous centre's tail reads are done before the walk reuses the region
     const int64_t local = center - p.center_begin;
     double* R = tab.r_global ? p.rbuf + (center - p.grid_begin) * tab.rsize
                              : reinterpret_cast<double*>(region + tab.r_offset);
@@ -378,8 +387,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         //   5. otherwise done.
         // Stage 1 runs whenever pcount >= chunk, so stage 2 starts with
         // pcount < chunk and the edge queue never exceeds chunk + 31 <= 63 <
-        // kPending; likewise stage 2 runs whenever qn >= 32, so stage 3 leaves
-        // at most 63 < kPreQueue survivors queued.
+        // kPending; likewise stage 2 runs whenever qn >= 32, so stage 3 (64
+        // candidates, two per lane) leaves at most 95 < kPreQueue survivors.
         int qn = 0;      // prefilter survivors queued (warp-uniform)
         int pcount = 0;  // accepted edges queued (warp-uniform)
         int round = 0;   // next segment index
@@ -420,9 +429,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0, w = 1.0;
                 int t = 0;
                 if (lane < count) {
-                    const int a = qa[lane], tp = qt[lane];
+                    const int j = qa[lane], tp = qt[lane];
                     t = qs[lane];
-                    const int j = bv.sorted[ab + a];
                     int nimg[3];
                     ok = accept_candidate(si, bv, p.positions, center, wi, j, (tp & 1023) - 512,
                                           ((tp >> 10) & 1023) - 512, ((tp >> 20) & 1023) - 512, tab.cutoff2, nimg,
@@ -445,45 +453,78 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     ptype[q] = pooled ? 0 : t - tb;
                 }
                 pcount += __popc(mask);
+                // Move the remaining survivors (up to 63) to the queue's front.
                 const int rem = qn - count;
-                int sa = 0, st = 0, ss = 0;
+                int sa0 = 0, st0 = 0, ss0 = 0, sa1 = 0, st1 = 0, ss1 = 0;
                 if (lane < rem) {
-                    sa = qa[count + lane];
-                    st = qt[count + lane];
-                    ss = qs[count + lane];
+                    sa0 = qa[count + lane];
+                    st0 = qt[count + lane];
+                    ss0 = qs[count + lane];
+                }
+                if (lane + 32 < rem) {
+                    sa1 = qa[count + 32 + lane];
+                    st1 = qt[count + 32 + lane];
+                    ss1 = qs[count + 32 + lane];
                 }
                 __syncwarp();
                 if (lane < rem) {
-                    qa[lane] = sa;
-                    qt[lane] = st;
-                    qs[lane] = ss;
+                    qa[lane] = sa0;
+                    qt[lane] = st0;
+                    qs[lane] = ss0;
+                }
+                if (lane + 32 < rem) {
+                    qa[32 + lane] = sa1;
+                    qt[32 + lane] = st1;
+                    qs[32 + lane] = ss1;
                 }
                 __syncwarp();
                 qn = rem;
             } else if (q0 < total) {
-                // Prefilter candidates q0 .. q0 + 31 of this round.
-                const int q = q0 + lane;
-                bool pass = false;
-                int a = 0, ty = 0, i = 0;
-                if (q < total) {
+                // Prefilter candidates q0 .. q0 + 63 of this round, two per
+                // lane (q0 + lane and q0 + 32 + lane): the two searches and
+                // the two position loads are independent, so their latencies
+                // overlap.  Survivors are queued in candidate order.
+                const int qA = q0 + lane, qB = q0 + 32 + lane;
+                bool passA = false, passB = false;
+                int aA = 0, tyA = 0, iA = 0, aB = 0, tyB = 0, iB = 0;  // a: local atom id
 #pragma unroll
-                    for (int step = 16; step > 0; step >>= 1)
-                        if (seg_prefix[i + step] <= q) i += step;
-                    a = seg_start[i] + (q - seg_prefix[i]);
-                    const double4 sp = bv.spos[ab + a];
-                    ty = (int)sp.w;
-                    const double dx = sp.x + seg_off[i], dy = sp.y + seg_off[32 + i], dz = sp.z + seg_off[64 + i];
-                    pass = (pooled || (ty >= tb && ty < te)) && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
+                for (int step = 16; step > 0; step >>= 1) {
+                    if (seg_prefix[iA + step] <= qA) iA += step;
+                    if (seg_prefix[iB + step] <= qB) iB += step;
                 }
-                const unsigned mask = __ballot_sync(0xffffffffu, pass);
-                if (pass) {
-                    const int slot = qn + __popc(mask & ((1u << lane) - 1u));
-                    qa[slot] = a;
-                    qt[slot] = seg_t[i];
-                    qs[slot] = ty;
+                if (qA < total) {
+                    const double4 sp = bv.spos[ab + seg_start[iA] + (qA - seg_prefix[iA])];
+                    const long long code = (long long)sp.w;
+                    tyA = (int)(code & 127) - 1;
+                    aA = (int)(code >> 7);
+                    const double dx = sp.x + seg_off[iA], dy = sp.y + seg_off[32 + iA], dz = sp.z + seg_off[64 + iA];
+                    passA = (pooled || (tyA >= tb && tyA < te)) && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
                 }
-                qn += __popc(mask);
-                q0 += 32;
+                if (qB < total) {
+                    const double4 sp = bv.spos[ab + seg_start[iB] + (qB - seg_prefix[iB])];
+                    const long long code = (long long)sp.w;
+                    tyB = (int)(code & 127) - 1;
+                    aB = (int)(code >> 7);
+                    const double dx = sp.x + seg_off[iB], dy = sp.y + seg_off[32 + iB], dz = sp.z + seg_off[64 + iB];
+                    passB = (pooled || (tyB >= tb && tyB < te)) && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
+                }
+                const unsigned maskA = __ballot_sync(0xffffffffu, passA);
+                const unsigned maskB = __ballot_sync(0xffffffffu, passB);
+                const unsigned lt = (1u << lane) - 1u;
+                if (passA) {
+                    const int slot = qn + __popc(maskA & lt);
+                    qa[slot] = aA;
+                    qt[slot] = seg_t[iA];
+                    qs[slot] = tyA;
+                }
+                if (passB) {
+                    const int slot = qn + __popc(maskA) + __popc(maskB & lt);
+                    qa[slot] = aB;
+                    qt[slot] = seg_t[iB];
+                    qs[slot] = tyB;
+                }
+                qn += __popc(maskA) + __popc(maskB);
+                q0 += 64;
                 __syncwarp();
             } else if (round < entries) {
                 // Segments round .. round + 31: one (y, z) bin row at one x image each.
@@ -684,6 +725,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         else
             mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, gq, qq);
     }
+    };
+    for (int64_t center = c_lo + warp; center < c_hi; center += kWarps) run_centre(center);
 }
 
 // Tail of the paired kernel as a kernel of its own (n_max == 8, average off

@@ -157,6 +157,28 @@ class Soap:
         raise_for(status)
         return out
 
+    def compute_csr(self, batch, device: int = 0):
+        """Sparse rows (C ABI ``mdsoap_compute_csr``): a ``scipy.sparse.csr_matrix``
+        with exact zeros dropped, equal to ``csr_matrix(self.compute(batch))``
+        (the ``OutputOptions(sparse=True)`` representation), built on the device
+        so that only the nonzeros cross PCIe."""
+        import scipy.sparse
+
+        arrays = _contiguous(batch)
+        view = host_view(arrays)
+        handle = ctypes.c_void_p()
+        raise_for(lib.mdsoap_compute_csr(self._plan, ctypes.byref(view), int(device), ctypes.byref(handle)))
+        try:
+            rows, cols, nnz = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+            raise_for(lib.mdsoap_csr_info(handle, ctypes.byref(rows), ctypes.byref(cols), ctypes.byref(nnz)))
+            indptr = np.empty(rows.value + 1, np.int64)
+            indices = np.empty(nnz.value, np.int32)
+            data = np.empty(nnz.value, self.dtype)
+            raise_for(lib.mdsoap_csr_copy(handle, indptr.ctypes.data, indices.ctypes.data, data.ctypes.data))
+        finally:
+            lib.mdsoap_csr_destroy(handle)
+        return scipy.sparse.csr_matrix((data, indices, indptr), shape=(rows.value, cols.value))
+
     def compute_device(self, view: BatchView, out_ptr: int, device: int = 0, stream: int = 0) -> None:
         """Enqueue the pipeline on device memory (C ABI ``mdsoap_compute_device``)."""
         raise_for(lib.mdsoap_compute_device(self._plan, ctypes.byref(view), out_ptr or None, int(device),

@@ -1,8 +1,10 @@
 """The n_max = 8 tail as its own persistent kernel (soap_tail_kernel: bulk-copied,
 double-buffered coefficient blocks) against the tail fused into the expansion
 kernel (MDSOAP_SPLIT_TAIL=0) and against chunked expansion / tail launches
-(MDSOAP_TAIL_CHUNK): the same per-degree arithmetic in every mode, so the rows
-agree bit for bit, and with the CPU checker within the float tolerances."""
+(MDSOAP_TAIL_CHUNK), and the persistent expansion kernel against one CTA per
+four centres (MDSOAP_PERSISTENT=0): the same per-centre arithmetic in every
+mode, so the rows agree bit for bit, and with the CPU checker within the float
+tolerances."""
 
 from __future__ import annotations
 
@@ -39,6 +41,10 @@ def test_split_fused_and_chunked_tails_agree(oracle, cuda_device, monkeypatch, a
     assert "soap_tail_kernel" not in fused.kernel()
     assert np.array_equal(fused.compute(batch, devices=[0]), want)
     monkeypatch.delenv("MDSOAP_SPLIT_TAIL")
+
+    monkeypatch.setenv("MDSOAP_PERSISTENT", "0")  # one CTA per four centres instead of resident CTAs
+    assert np.array_equal(make(average, dtype).compute(batch, devices=[0]), want)
+    monkeypatch.delenv("MDSOAP_PERSISTENT")
 
     for chunk in ("37", "200"):  # ragged chunks; more centres than some grids
         monkeypatch.setenv("MDSOAP_TAIL_CHUNK", chunk)
