@@ -1121,6 +1121,10 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             if (split_allowed && !polynomial && n == 8 && coef_species <= v.maxt && q.average != MDSOAP_AVERAGE_INNER && r_smem) {
                 t.split_tail = 1;
                 plan->tail_smem = (size_t)W * 64 * 8 + 2 * (size_t)t.rsize * 8;  // beta + two coefficient blocks
+                // The raw-sum scratch holds one block per centre of a chunk:
+                // chunks of at most 4 GiB (240 k centres for config 2's
+                // 17 KB blocks, so config 2 runs as one pair of launches).
+                plan->tail_chunk = std::max<int64_t>(4096, (int64_t)((4ull << 30) / (8ull * (uint64_t)t.rsize)));
                 if (const char* chunk_env = std::getenv("MDSOAP_TAIL_CHUNK"))
                     plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
             }
