@@ -182,6 +182,14 @@ template <int L, int T>
 const void* tail_symbol() {
     return reinterpret_cast<const void*>(&soap_tail_kernel<L, T>);
 }
+template <int L>
+void launch_tail_generic(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_tail_generic_kernel<L><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <int L>
+const void* tail_generic_symbol() {
+    return reinterpret_cast<const void*>(&soap_tail_generic_kernel<L>);
+}
 // Paired-channel kernel: one warp per centre, l_max == L exactly.
 // Plans with a split tail launch the instantiation without tail code (fewer registers).
 template <int T, int L, bool PRECISE, int MINB>
@@ -238,6 +246,8 @@ struct Variant {
     CenterLauncher tail = nullptr;        // paired: soap_tail_kernel<lmax, maxt>
     const void* (*tail_sym)() = nullptr;
     const void* (*split_sym)() = nullptr; // paired: the expansion kernel without tail code
+    CenterLauncher tail_generic = nullptr;  // paired: soap_tail_generic_kernel<lmax>
+    const void* (*tail_generic_sym)() = nullptr;
 };
 
 #define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
@@ -286,7 +296,7 @@ const Variant kVariants[] = {
         -1, T, 0, 0, 0, 8, L, MB, false, false, &launch_paired<T, L, PREC, MB>,                             \
             &paired_symbol<T, L, PREC, MB>, &launch_structure<L>, &structure_symbol<L>, true, PREC,         \
             "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch_tail<L, T>, &tail_symbol<L, T>, \
-            &paired_split_symbol<T, L, PREC, MB>                                                          \
+            &paired_split_symbol<T, L, PREC, MB>, &launch_tail_generic<L>, &tail_generic_symbol<L>        \
     }
 
 // Paired-channel kernels: the default wherever they apply (n_max <= 8,
@@ -544,16 +554,19 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
     check(cudaFuncSetAttribute(variant->structure_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
           "structure kernel smem");
     if (variant->tail_sym) {
-        // The tail kernel's mbarriers are static shared memory: the dynamic
+        // The tail kernels' static shared memory (the mbarriers): the dynamic
         // ceiling is what remains of the opt-in maximum.
-        cudaFuncAttributes attr{};
-        check(cudaFuncGetAttributes(&attr, variant->tail_sym()), "tail kernel attributes");
-        check(cudaFuncSetAttribute(variant->tail_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   optin - (int)attr.sharedSizeBytes),
-              "tail kernel smem");
+        for (const void* sym : {variant->tail_sym(), variant->tail_generic_sym()}) {
+            cudaFuncAttributes attr{};
+            check(cudaFuncGetAttributes(&attr, sym), "tail kernel attributes");
+            check(cudaFuncSetAttribute(sym, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       optin - (int)attr.sharedSizeBytes),
+                  "tail kernel smem");
+        }
         if (tab.split_tail) {
             int per_sm = 0, sms = 0;
-            check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, variant->tail_sym(), kWarps * 32, tail_smem),
+            const void* sym = tab.split_tail == 2 ? variant->tail_generic_sym() : variant->tail_sym();
+            check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sym, kWarps * 32, tail_smem),
                   "tail kernel occupancy");
             check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, st.device), "SM count");
             st.tail_grid = (int64_t)std::max(per_sm, 1) * sms;
@@ -632,7 +645,8 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
                 check(cudaEventRecord(after_expansion, stream), "timing event");
             // Persistent tail: the resident CTAs stride over the block's centres.
             const int64_t tail_ctas = std::min<int64_t>(p.grid_end - c0, std::max<int64_t>(st.tail_grid, 1));
-            variant->tail(dim3((unsigned)tail_ctas), tail_smem, stream, tab, p);
+            (tab.split_tail == 2 ? variant->tail_generic : variant->tail)(dim3((unsigned)tail_ctas), tail_smem,
+                                                                          stream, tab, p);
             check(cudaGetLastError(), "tail kernel launch");
             launches.fetch_add(2, std::memory_order_relaxed);
         }
@@ -1118,9 +1132,15 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             // MDSOAP_SPLIT_TAIL=0 keeps them fused (measurement knob).
             const char* split_env = std::getenv("MDSOAP_SPLIT_TAIL");
             const bool split_allowed = !(split_env && split_env[0] == '0');
-            if (split_allowed && !polynomial && n == 8 && coef_species <= v.maxt && q.average != MDSOAP_AVERAGE_INNER && r_smem) {
-                t.split_tail = 1;
-                plan->tail_smem = (size_t)W * 64 * 8 + 2 * (size_t)t.rsize * 8;  // beta + two coefficient blocks
+            const size_t generic_smem = (size_t)W * 64 * 8 + (size_t)kWarps * t.rsize * 8;  // beta + a block per warp
+            const bool regs = n == 8 && coef_species <= v.maxt;
+            if (split_allowed && !polynomial && q.average != MDSOAP_AVERAGE_INNER && r_smem &&
+                (regs || generic_smem <= budget1)) {
+                // Register tail (soap_tail_kernel) where the coefficients fit
+                // the register banks, else soap_tail_generic_kernel.
+                t.split_tail = regs ? 1 : 2;
+                plan->tail_smem = regs ? (size_t)W * 64 * 8 + 2 * (size_t)t.rsize * 8  // beta + two coefficient blocks
+                                       : generic_smem;
                 // The raw-sum scratch holds one block per centre of a chunk:
                 // chunks of at most 4 GiB (240 k centres for config 2's
                 // 17 KB blocks, so config 2 runs as one pair of launches).
@@ -1129,8 +1149,10 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                     plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
             }
             plan->kernel_label = v.name;
-            if (t.split_tail)
+            if (t.split_tail == 1)
                 plan->kernel_label += " + soap_tail_kernel<" + std::to_string(L) + ", " + std::to_string(v.maxt) + ">";
+            else if (t.split_tail == 2)
+                plan->kernel_label += " + soap_tail_generic_kernel<" + std::to_string(L) + ">";
             if (plan->center_smem > budget1 || plan->structure_smem > budget1)
                 return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
             *plan_out = plan.release();

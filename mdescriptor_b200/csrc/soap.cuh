@@ -63,7 +63,7 @@ struct SoapTables {
     int32_t compression;  // 0 off, 1 mu2, 2 mu1nu1, 3 crossover (paired kernel only when not 0)
     int32_t coef_species; // species of the coefficient block: n_species, or 1 for mu2
     int32_t weighted;     // 1: per-edge weights (weighting function, w0, or mu2 pooling); paired kernel only
-    int32_t split_tail;   // 1: the paired kernel stops after the flush; soap_tail_kernel finishes the centres
+    int32_t split_tail;   // the paired kernel stops after the flush; 1: soap_tail_kernel, 2: soap_tail_generic_kernel finishes the centres
     int32_t grid_size;    // polynomial basis: quadrature nodes (0 for the GTO basis)
     double eta;           // 1 / (2 sigma^2)
     int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)

@@ -127,6 +127,75 @@ __device__ __forceinline__ void harmonics_row(const SoapTables& tab, double x, d
 
 }  // namespace paired
 
+// Beta transform and power spectrum (or the inner-average block copy) of one
+// centre from its raw-sum block R in shared memory, one warp: the tail for
+// plans whose coefficients do not stay in registers (n_max < 8, more species
+// than register banks, average inner, compression through power_generic).
+// Used by the fused paired kernel and by soap_tail_generic_kernel.
+template <int L>
+__device__ __forceinline__ void tail_generic(const SoapTables& tab, const SoapPointers& p, double* R,
+                                             const double* bt, int64_t center, int lane) {
+    const int S = tab.coef_species, n = tab.n_max;
+    const int gq = lane >> 2, qq = lane & 3, R_rows = tab.rows;
+    const bool n8 = n == 8;
+    const int64_t local = center - p.center_begin;
+    if (n8)
+        mma::beta_n8<L>(bt, R, tab.rs, S, gq, qq);
+    else
+        mma::beta_mma<L>(bt, R, tab.rs, L, S, n, gq, qq);
+    __syncwarp();
+    const mma::FeatureMap fm{S, n, L, R_rows, tab.n_magic};
+    if (tab.average != 1 && (tab.compression == 2 || tab.compression == 3)) {
+        const int rs = tab.rs;
+        auto coef = [&](int t, int k, int l, int m) { return R[(t * n + k) * rs + mma::col_off(l) + m]; };
+        if (tab.average == 0) {
+            const int64_t row = center - p.out_row_begin;
+            if (tab.out_f64)
+                power_generic(coef, tab.power_pref, S, n, L, tab.compression,
+                              static_cast<double*>(p.out) + row * tab.features, lane);
+            else
+                power_generic(coef, tab.power_pref, S, n, L, tab.compression,
+                              static_cast<float*>(p.out) + row * tab.features, lane);
+        } else {
+            power_generic(coef, tab.power_pref, S, n, L, tab.compression, p.pbuf + local * tab.features, lane);
+        }
+        return;
+    }
+    if (tab.average == 0) {
+        const int64_t row = center - p.out_row_begin;
+        if (tab.out_f64) {
+            double* dst = static_cast<double*>(p.out) + row * tab.features;
+            if (n8)
+                mma::power_n8<L>(tab.power_pref, R, tab.rs, S, dst, gq, qq);
+            else
+                mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, dst, gq, qq);
+        } else {
+            float* dst = static_cast<float*>(p.out) + row * tab.features;
+            if (n8)
+                mma::power_n8<L>(tab.power_pref, R, tab.rs, S, dst, gq, qq);
+            else
+                mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, dst, gq, qq);
+        }
+    } else if (tab.average == 1) {
+        // The structure kernel's layout: [l][r][m], rows padded to 2l+2.
+        double* dst = p.cbuf + local * tab.csize;
+        for (int l = 0; l <= L; ++l) {
+            const int pad = 2 * l + 2;
+            double* dl = dst + cblock(S, n, l);
+            const double* src = R + mma::col_off(l);
+            for (int i = lane; i < R_rows * pad; i += 32) {
+                const int r = i / pad, m = i - r * pad;
+                dl[i] = m < 2 * l + 1 ? src[r * tab.rs + m] : 0.0;
+            }
+        }
+    } else {
+        if (n8)
+            mma::power_n8<L>(tab.power_pref, R, tab.rs, S, p.pbuf + local * tab.features, gq, qq);
+        else
+            mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, gq, qq);
+    }
+}
+
 // One warp per centre.  MAXT species register banks per pass over the
 // neighbourhood; L = l_max exactly; PRECISE selects the radial-factor
 // accuracy (float64 rows need the full one); MINB resident CTAs per SM.
@@ -801,6 +870,38 @@ soap_tail_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
             }
         }
         __syncthreads();
+    }
+}
+
+// Tail of the paired kernel as a kernel of its own for plans whose
+// coefficients do not stay in registers (tail_generic): n_max < 8, more
+// species than register banks, compression layouts through power_generic.
+// Without tail code the expansion kernel keeps a small instruction-cache
+// footprint.  Persistent: warp w of CTA b takes centres (b * kWarps + w) +
+// i * gridDim.x * kWarps, copying each raw-sum block into its own slice of
+// shared memory (coalesced 16-byte loads) before the tail.
+template <int L>
+__global__ void __launch_bounds__(kWarps * 32)
+soap_tail_generic_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n = tab.n_max;
+    double* bt = reinterpret_cast<double*>(smem);
+    for (int i = threadIdx.x; i < (L + 1) * 64; i += blockDim.x) {
+        const int l = i / 64, nn = (i / 8) % 8, k = i % 8;
+        bt[i] = (nn < n && k < n) ? tab.soap_scale * p.betas[((int64_t)l * n + nn) * n + k] : 0.0;
+    }
+    __syncthreads();
+    constexpr int kShared = (L + 1) * 64 * 8;
+    double* R = reinterpret_cast<double*>(smem + kShared) + (int64_t)warp * tab.rsize;
+    const int64_t count = p.grid_end - p.grid_begin;
+    for (int64_t c = (int64_t)blockIdx.x * kWarps + warp; c < count; c += (int64_t)gridDim.x * kWarps) {
+        const double2* src = reinterpret_cast<const double2*>(p.rbuf + c * tab.rsize);
+        double2* dst = reinterpret_cast<double2*>(R);
+        __syncwarp();
+        for (int i = lane; i < tab.rsize / 2; i += 32) dst[i] = src[i];
+        __syncwarp();
+        tail_generic<L>(tab, p, R, bt, p.grid_begin + c, lane);
     }
 }
 

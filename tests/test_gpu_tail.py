@@ -67,3 +67,38 @@ def test_split_tail_single_centre_and_empty(cuda_device):
     empty = workloads.Batch(np.zeros(0, np.int32), np.zeros((0, 3)), np.zeros((0, 3, 3)),
                             np.zeros((0, 3), np.int32), np.array([0], np.int64))
     assert soap.compute(empty, devices=[0]).shape == (0, soap.feature_count)
+
+
+@pytest.mark.parametrize("shape", [((1, 6, 7, 8, 16), 5.0, 6, 4, "off"),      # more species than banks
+                                   ((1, 8), 4.5, 4, 3, "off"),                # n_max < 8
+                                   ((1, 6, 8), 3.8, 6, 4, "mu1nu1"),          # power_generic layouts
+                                   ((1, 6, 8), 3.8, 8, 6, "crossover")])
+@pytest.mark.parametrize("average", ["off", "outer"])
+def test_generic_split_tail_matches_fused(oracle, cuda_device, monkeypatch, shape, average):
+    """Plans whose coefficients do not stay in registers hand their raw-sum
+    blocks to soap_tail_generic_kernel; the rows equal the fused kernel's bit
+    for bit (the same tail code on the same blocks) and the checker's."""
+    species, r_cut, n_max, l_max, compression = shape
+    batch = workloads.config4(structures=40, seed=9)
+    batch = workloads.Batch(np.where(np.isin(batch.numbers, species), batch.numbers, species[0]).astype(np.int32),
+                            batch.positions, batch.cells, batch.pbc, batch.offsets)
+
+    def make_plan():
+        return Soap(species, r_cut=r_cut, n_max=n_max, l_max=l_max, sigma=1.0, average=average, dtype="float64",
+                    compression=compression)
+
+    split = make_plan()
+    assert "soap_tail_generic_kernel" in split.kernel() or "soap_tail_kernel" in split.kernel()
+    want = split.compute(batch, devices=[0])
+    monkeypatch.setenv("MDSOAP_SPLIT_TAIL", "0")
+    fused = make_plan()
+    assert "soap_tail" not in fused.kernel()
+    assert np.array_equal(fused.compute(batch, devices=[0]), want)
+    monkeypatch.delenv("MDSOAP_SPLIT_TAIL")
+    monkeypatch.setenv("MDSOAP_TAIL_CHUNK", "29")
+    assert np.array_equal(make_plan().compute(batch, devices=[0]), want)
+    monkeypatch.delenv("MDSOAP_TAIL_CHUNK")
+    alphas, betas = basis_gto(r_cut, n_max, l_max)
+    ref = oracle.soap(batch, species, r_cut, n_max, l_max, 1.0, alphas, betas, average=average,
+                      compression=compression)
+    assert_close(want, ref, "float64")
