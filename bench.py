@@ -54,6 +54,8 @@ def parse_args():
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--local", default=None, choices=("SphericalExpansion", "SoapRadialSpectrum", "SoapPowerSpectrum"),
+                   help="time a local spherical spectrum (reference defaults) instead of SOAP; one GPU")
     return p.parse_args()
 
 
@@ -329,8 +331,54 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_local(args):
+    """One local spectrum (reference default options: cutoff 6, density width
+    0.3, max_radial 6, max_angular 4) through the C ABI with host buffers
+    (``mdsoap_local_compute``: upload, kernels and the float64 rows' D2H
+    inside the host clock), beside the reference's own C++/OpenMP
+    ``compute_spherical_expansion`` (oracle/_ref) on a bounded sample."""
+    from mdescriptor_b200 import workloads
+    from mdescriptor_b200.soap import LOCAL_KINDS, local_feature_count, local_spectrum
+
+    cfg = workloads.CONFIGS[args.config]
+    structures = args.structures or 64
+    batch = workloads.make(args.config, structures)
+    species = list(cfg.species)
+    for _ in range(max(1, args.warmup)):
+        local_spectrum(args.local, batch, species)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        local_spectrum(args.local, batch, species)
+    elapsed = time.perf_counter() - t0
+    line = {"metric": f"{args.local} atom-environments/sec", "value": batch.atoms * args.steps / elapsed,
+            "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True, "dtype": "f64",
+            "path": "mdsoap_local_compute (host buffers: H2D + bin + local_spectra_kernel + D2H per step)",
+            "config": {"workload": f"{cfg.name} x {structures} structures", "atoms": batch.atoms,
+                       "features": local_feature_count(args.local, species), "cutoff": 6.0, "density_width": 0.3,
+                       "max_radial": 6, "max_angular": 4, "output_dtype": "float64"}}
+    pkg = ROOT / "oracle" / "_ref" / "pkg"
+    if not args.no_cpu_baseline and list(pkg.glob("_native*.so")):
+        sys.path.insert(0, str(pkg))
+        import _native
+
+        threads = os.cpu_count() or 1
+        sample = workloads.make(args.config, max(4, min(structures, threads)), seed=workloads.SEED_BASE + 901)
+        t0 = time.perf_counter()
+        _native.compute_spherical_expansion(sample.numbers, sample.positions, sample.cells, sample.pbc,
+                                            sample.offsets, species, 6.0, 0.3, 6, 4, LOCAL_KINDS[args.local],
+                                            2.5, 1, 6.0, threads, None)
+        cpu_s = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": sample.atoms / cpu_s, "unit": UNIT, "cores": threads, "kind": "reference",
+                                "sample": f"{sample.structures} structures of {cfg.name}, {cpu_s:.2f} s wall"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.local:
+        run_local(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return

@@ -315,6 +315,40 @@ int mdsoap_pairs_copy(const mdsoap_pairs* pairs, double* records, double* values
 
 void mdsoap_pairs_destroy(mdsoap_pairs* pairs);
 
+/* Local spherical spectra: the featomic-style GTO expansion of a Gaussian
+ * atomic density (width `density_width`) with a cosine cutoff of width
+ * min(0.5, cutoff).  `kind` takes the reference's LocalDescriptorKind values:
+ * 0 SphericalExpansion, 2 SoapRadialSpectrum, 3 SoapPowerSpectrum.  Species
+ * are kept in declared order (not sorted), as the reference does. */
+#define MDSOAP_LOCAL_SPHERICAL_EXPANSION 0
+#define MDSOAP_LOCAL_RADIAL_SPECTRUM 2
+#define MDSOAP_LOCAL_POWER_SPECTRUM 3
+
+typedef struct mdsoap_local_params {
+    int32_t kind;
+    int32_t max_radial;  /* radial count = max_radial + 1, at most 16 */
+    int32_t max_angular; /* at most 8 (any value for the radial spectrum) */
+    int32_t n_species;
+    const int32_t* species;
+    double cutoff;
+    double density_width;
+} mdsoap_local_params;
+
+/* Feature count of one row: S*S*n*(L+1)^2 (expansion), S*S*n (radial
+ * spectrum), S(S+1)/2*S*(L+1)*n*n (power spectrum); -1 on invalid options
+ * (message in mdsoap_last_error).
+ * Replaces: local_descriptor_feature_count (cpp/src/standalone/spherical_expansion.cpp:115-121)
+ * and local_layout_feature_count (cpp/src/common/local_layout.hpp:115-130). */
+int64_t mdsoap_local_feature_count(const mdsoap_local_params* params);
+
+/* Rows float64[atoms][features] of a host batch computed on `device`, written
+ * into the caller's host buffer `out` (atoms * features doubles).
+ * Replaces: compute_spherical_expansion (cpp/src/standalone/spherical_expansion.cpp:124-206)
+ * and compute_local_descriptors_into, the reference plugin's local branch
+ * (cpp/cuda/src/backend.cu:590-624). */
+int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* batch, double* out,
+                         int32_t device);
+
 #ifdef __cplusplus
 }
 #endif

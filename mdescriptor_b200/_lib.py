@@ -66,6 +66,20 @@ class Params(ctypes.Structure):
     ]
 
 
+class LocalParams(ctypes.Structure):
+    """``mdsoap_local_params`` (include/mdsoap.h)."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("max_radial", ctypes.c_int32),
+        ("max_angular", ctypes.c_int32),
+        ("n_species", ctypes.c_int32),
+        ("species", ctypes.POINTER(ctypes.c_int32)),
+        ("cutoff", ctypes.c_double),
+        ("density_width", ctypes.c_double),
+    ]
+
+
 class BatchView(ctypes.Structure):
     _fields_ = [
         ("numbers", _P),
@@ -147,6 +161,10 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_graph_copy.restype = ctypes.c_int
     lib.mdsoap_graph_destroy.argtypes = [_P]
     lib.mdsoap_graph_destroy.restype = None
+    lib.mdsoap_local_feature_count.argtypes = [ctypes.POINTER(LocalParams)]
+    lib.mdsoap_local_feature_count.restype = ctypes.c_int64
+    lib.mdsoap_local_compute.argtypes = [ctypes.POINTER(LocalParams), ctypes.POINTER(BatchView), _P, ctypes.c_int32]
+    lib.mdsoap_local_compute.restype = ctypes.c_int
     return lib
 
 
@@ -184,6 +202,8 @@ EXPORTED = (
     "mdsoap_pairs_count",
     "mdsoap_pairs_copy",
     "mdsoap_pairs_destroy",
+    "mdsoap_local_feature_count",
+    "mdsoap_local_compute",
 )
 
 

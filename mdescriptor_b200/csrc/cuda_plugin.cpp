@@ -138,8 +138,28 @@ public:
             devices_ = device_list();
             return;
         }
+        if (name_ == "SphericalExpansion" || name_ == "SoapRadialSpectrum" || name_ == "SoapPowerSpectrum") {
+            // cpp/cuda/src/backend.cu:590-602 option names and defaults.
+            local_ = true;
+            species_ = option(options_, "species", std::vector<int32_t>{});
+            local_params_.kind = name_ == "SoapRadialSpectrum"  ? MDSOAP_LOCAL_RADIAL_SPECTRUM
+                                 : name_ == "SoapPowerSpectrum" ? MDSOAP_LOCAL_POWER_SPECTRUM
+                                                                : MDSOAP_LOCAL_SPHERICAL_EXPANSION;
+            local_params_.cutoff = option(options_, "cutoff", 6.0);
+            local_params_.density_width = option(options_, "density_width", 0.3);
+            local_params_.max_radial = option(options_, "max_radial", 6);
+            local_params_.max_angular = option(options_, "max_angular", 4);
+            local_params_.n_species = (int32_t)species_.size();
+            local_params_.species = species_.data();
+            features_ = mdsoap_local_feature_count(&local_params_);
+            if (features_ < 0) throw std::invalid_argument(mdsoap_last_error());
+            labels_ = labels_option();
+            devices_ = device_list();
+            return;
+        }
         if (name_ != "SOAP")
-            throw CudaUnavailable("this CUDA plugin implements SOAP and NeighborList only; '" + name_ +
+            throw CudaUnavailable("this CUDA plugin implements SOAP, NeighborList, SphericalExpansion, "
+                                  "SoapRadialSpectrum and SoapPowerSpectrum only; '" + name_ +
                                   "' has no CUDA backend here");
         species_ = option(options_, "species", std::vector<int32_t>{});
         if (species_.empty()) throw std::invalid_argument("SOAP species must not be empty");
@@ -272,7 +292,7 @@ public:
             py::gil_scoped_release release;
             guard.lock();
         }
-        if (closed_ || (plan_ == nullptr && !list_)) throw std::runtime_error("CUDA backend is closed");
+        if (closed_ || (plan_ == nullptr && !list_ && !local_)) throw std::runtime_error("CUDA backend is closed");
         auto numbers = py::array_t<int32_t, py::array::c_style | py::array::forcecast>::ensure(batch.attr("numbers"));
         auto positions = py::array_t<double, py::array::c_style | py::array::forcecast>::ensure(batch.attr("positions"));
         auto cells = py::array_t<double, py::array::c_style | py::array::forcecast>::ensure(batch.attr("cells"));
@@ -292,6 +312,7 @@ public:
         }
         mdsoap_batch view{numbers.data(), positions.data(), cells.data(), pbc.data(), offsets.data(), structures, atoms};
         if (list_) return compute_list(view, structures, control);
+        if (local_) return compute_local(view, offsets, structures, control);
         const int64_t rows = average_ == MDSOAP_AVERAGE_OFF ? atoms : structures;
         py::array values = f64_ ? py::array(py::array_t<double>({(py::ssize_t)rows, (py::ssize_t)features_}))
                                 : py::array(py::array_t<float>({(py::ssize_t)rows, (py::ssize_t)features_}));
@@ -354,6 +375,35 @@ public:
         return std::move(result);
     }
 
+    // Local spectra: float64 atom rows (cpp/cuda/src/backend.cu:590-624).
+    py::object compute_local(const mdsoap_batch& view, const py::array_t<int64_t>& offsets, int64_t structures,
+                             py::object control) {
+        py::array_t<double> values({(py::ssize_t)view.atoms, (py::ssize_t)features_});
+        int status;
+        {
+            py::gil_scoped_release release;
+            status = mdsoap_local_compute(&local_params_, &view, values.mutable_data(),
+                                          devices_.empty() ? 0 : devices_[0]);
+        }
+        if (status != MDSOAP_OK) throw_status(status);
+        if (!control.is_none()) {
+            if (py::cast<bool>(control.attr("cancelled")()))
+                throw CudaCancelledError("descriptor computation was cancelled");
+            if (py::hasattr(control, "mark_completed"))
+                for (int64_t s = 0; s < structures; ++s) control.attr("mark_completed")();
+        }
+        py::array_t<int64_t> row_offsets(structures + 1);
+        std::copy(offsets.data(), offsets.data() + structures + 1, row_offsets.mutable_data());
+        py::dict result;
+        result["values"] = values;
+        result["_mdescriptor_owned_values"] = true;
+        result["level"] = "atom";
+        result["row_offsets"] = row_offsets;
+        result["labels"] = labels_;
+        result["metadata"] = metadata();
+        return std::move(result);
+    }
+
     py::object predict(py::object, py::object) {
         throw std::invalid_argument("CUDA prediction supports NEP and DPA4C only");
     }
@@ -381,6 +431,7 @@ public:
         if (!closed_) {
             closed_ = true;
             list_ = false;
+            local_ = false;
             if (plan_) mdsoap_plan_destroy(plan_);
             plan_ = nullptr;
         }
@@ -411,6 +462,8 @@ private:
     bool f64_ = true;
     bool list_ = false, list_full_ = true, list_self_ = false;  // NeighborList backend
     double list_cutoff_ = 6.0;
+    bool local_ = false;  // SphericalExpansion / SoapRadialSpectrum / SoapPowerSpectrum backend
+    mdsoap_local_params local_params_{};
     int64_t features_ = 0;
     py::list labels_;
     std::vector<int32_t> devices_;

@@ -10,6 +10,7 @@
 #include "soap_paired.cuh"
 #include "neighbor_list.cuh"
 #include "csr.cuh"
+#include "local_spectra.cuh"
 
 #include <cuda_runtime.h>
 
@@ -61,6 +62,7 @@ std::string device_error_text(unsigned bits) {
     if (bits & kErrPairCapacity) return "neighbour list: a centre has more pairs than the GPU list holds (2048)";
     if (bits & kErrExtendedRange) return "neighbor extended atom index exceeds int32 range";
     if (bits & kErrTailTimeout) return "tail kernel: a coefficient block copy did not complete in time";
+    if (bits & kErrLocalSeries) return "local descriptor radial integral overflow";
     return "device error";
 }
 
@@ -2050,5 +2052,293 @@ int mdsoap_graph_copy(const mdsoap_graph* graph, int64_t* offsets, int32_t* atom
 }
 
 void mdsoap_graph_destroy(mdsoap_graph* graph) { delete graph; }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Local spherical spectra (SphericalExpansion, SoapRadialSpectrum,
+// SoapPowerSpectrum): host tables and driver.
+
+namespace {
+
+struct LocalHostTables {
+    int n = 0, lc = 0;
+    double c = 0, gf = 0, log_gf = 0;
+    std::vector<double> g, log_cg, gratio, ppow, ortho;
+};
+
+double checked_gamma(double x) {
+    const double v = std::tgamma(x);
+    if (!std::isfinite(v) || v <= 0.0) raise(MDSOAP_INVALID_ARGUMENT, "local descriptor radial basis is numerically singular");
+    return v;
+}
+
+// S^(-1/2) of the symmetric overlap matrix by the classical Jacobi method:
+// each step zeroes the largest off-diagonal entry (rotation angle
+// 0.5 atan2(2 a_pq, a_qq - a_pp)), until it is below 1e-15 or after 100 n^2
+// steps; result = V diag(lambda)^(-1/2) V^T.  The pivot order, the angle
+// formula and the stopping rule are those of the reference's
+// inverse_symmetric_sqrt (cpp/src/common/rotational_math.hpp:15-72): the
+// orthonormalisation carries the solver's rounding amplified by the overlap's
+// condition number, and the same sequence of rotations reproduces the
+// reference's radial basis to the last bit.
+std::vector<double> inverse_sqrt_spd(std::vector<double> a, int n) {
+    std::vector<double> v((size_t)n * n, 0.0);
+    for (int i = 0; i < n; ++i) v[(size_t)i * n + i] = 1.0;
+    for (int step = 0; step < 100 * n * n; ++step) {
+        int p = 0, q = n > 1 ? 1 : 0;
+        double largest = 0.0;
+        for (int i = 0; i < n; ++i)
+            for (int j = i + 1; j < n; ++j)
+                if (std::abs(a[(size_t)i * n + j]) > largest) {
+                    largest = std::abs(a[(size_t)i * n + j]);
+                    p = i;
+                    q = j;
+                }
+        if (largest < 1e-15) break;
+        const double angle = 0.5 * std::atan2(2.0 * a[(size_t)p * n + q], a[(size_t)q * n + q] - a[(size_t)p * n + p]);
+        const double c = std::cos(angle), s = std::sin(angle);
+        for (int k = 0; k < n; ++k) {
+            const double akp = a[(size_t)k * n + p], akq = a[(size_t)k * n + q];
+            a[(size_t)k * n + p] = c * akp - s * akq;
+            a[(size_t)k * n + q] = s * akp + c * akq;
+        }
+        for (int k = 0; k < n; ++k) {
+            const double apk = a[(size_t)p * n + k], aqk = a[(size_t)q * n + k];
+            a[(size_t)p * n + k] = c * apk - s * aqk;
+            a[(size_t)q * n + k] = s * apk + c * aqk;
+        }
+        for (int k = 0; k < n; ++k) {
+            const double vkp = v[(size_t)k * n + p], vkq = v[(size_t)k * n + q];
+            v[(size_t)k * n + p] = c * vkp - s * vkq;
+            v[(size_t)k * n + q] = s * vkp + c * vkq;
+        }
+    }
+    std::vector<double> r((size_t)n * n, 0.0);
+    for (int i = 0; i < n; ++i)
+        for (int j = 0; j < n; ++j)
+            for (int k = 0; k < n; ++k)
+                r[(size_t)i * n + j] += v[(size_t)i * n + k] * v[(size_t)j * n + k] / std::sqrt(a[(size_t)k * n + k]);
+    for (double x : r)
+        if (!std::isfinite(x)) raise(MDSOAP_INVALID_ARGUMENT, "radial overlap matrix is singular, lower max_radial");
+    return r;
+}
+
+// GTO radial basis of the local spectra (GtoRadialBasis, local_spherical_common.hpp:181-253):
+// widths sigma_n = r_c max(sqrt n, 1) / n_radial, overlap of the normalised
+// r^n exp(-r^2 / 2 sigma_n^2) functions, orthonormalisation N_n S^(-1/2);
+// density factors of prepare_density (:240-253).
+LocalHostTables local_tables(const mdsoap_local_params& p, int lc) {
+    LocalHostTables t;
+    const int n = p.max_radial + 1;
+    t.n = n;
+    t.lc = lc;
+    const double radius = p.cutoff;
+    std::vector<double> width(n), norm(n);
+    t.g.resize(n);
+    for (int k = 0; k < n; ++k) {
+        width[k] = radius * std::max(std::sqrt((double)k), 1.0) / n;
+        t.g[k] = 1.0 / (2.0 * width[k] * width[k]);
+        norm[k] = std::sqrt(2.0 / (std::pow(width[k], 2 * k + 3) * checked_gamma(k + 1.5)));
+    }
+    std::vector<double> overlap((size_t)n * n);
+    for (int a = 0; a < n; ++a)
+        for (int b = a; b < n; ++b) {
+            const double s1 = width[a], s2 = width[b];
+            const double e = 0.5 * (3.0 + a + b);
+            const double value = std::pow(0.5 / (s1 * s1) + 0.5 / (s2 * s2), -e) / (std::pow(s1, a) * std::pow(s2, b)) *
+                                 checked_gamma(e) /
+                                 (std::pow(s1 * s2, 1.5) * std::sqrt(checked_gamma(a + 1.5) * checked_gamma(b + 1.5)));
+            overlap[(size_t)a * n + b] = overlap[(size_t)b * n + a] = value;
+        }
+    const std::vector<double> inv = inverse_sqrt_spd(overlap, n);
+    t.ortho.resize((size_t)n * n);
+    for (int a = 0; a < n; ++a)
+        for (int b = 0; b < n; ++b) t.ortho[(size_t)a * n + b] = norm[a] * inv[(size_t)a * n + b];
+    const double w2 = p.density_width * p.density_width;
+    t.c = 1.0 / (2.0 * w2);
+    t.gf = std::pow(3.141592653589793238462643383279502884 / w2, 0.75);
+    t.log_gf = std::log(t.gf);
+    t.log_cg.resize(n);
+    for (int k = 0; k < n; ++k) t.log_cg[k] = std::log(t.c + t.g[k]);
+    t.gratio.resize((size_t)(lc + 1) * n);
+    t.ppow.resize((size_t)(lc + 1) * n);
+    for (int l = 0; l <= lc; ++l) {
+        const double gb = checked_gamma(l + 1.5);
+        for (int k = 0; k < n; ++k) {
+            const double a = 0.5 * (k + l + 3.0);
+            t.gratio[(size_t)l * n + k] = checked_gamma(a) / gb;
+            t.ppow[(size_t)l * n + k] = std::pow(t.c + t.g[k], -a);
+        }
+    }
+    return t;
+}
+
+void validate_local(const mdsoap_local_params* p) {
+    if (!p) raise(MDSOAP_INVALID_ARGUMENT, "null argument");
+    // local_common.hpp:12-21 (validate_options)
+    if (!std::isfinite(p->cutoff) || p->cutoff <= 0.0 || !std::isfinite(p->density_width) || p->density_width <= 0.0 ||
+        p->max_radial < 0 || p->max_angular < 0)
+        raise(MDSOAP_INVALID_ARGUMENT, "invalid local descriptor descriptor parameters");
+    if (p->kind != MDSOAP_LOCAL_SPHERICAL_EXPANSION && p->kind != MDSOAP_LOCAL_RADIAL_SPECTRUM &&
+        p->kind != MDSOAP_LOCAL_POWER_SPECTRUM)
+        raise(MDSOAP_INVALID_ARGUMENT, "unknown local descriptor kind");
+    if (p->n_species <= 0 || !p->species) raise(MDSOAP_INVALID_ARGUMENT, "species must not be empty");
+    for (int i = 0; i < p->n_species; ++i) {
+        if (p->species[i] <= 0) raise(MDSOAP_INVALID_ARGUMENT, "species must be positive atomic numbers");
+        for (int j = 0; j < i; ++j)
+            if (p->species[j] == p->species[i]) raise(MDSOAP_INVALID_ARGUMENT, "species must be unique");
+    }
+    if (p->max_radial + 1 > kLocalMaxN)
+        raise(MDSOAP_INVALID_ARGUMENT, "max_radial above the GPU local spectra limit (15)");
+    if (p->max_angular > kLocalMaxL && p->kind != MDSOAP_LOCAL_RADIAL_SPECTRUM)
+        raise(MDSOAP_INVALID_ARGUMENT, "max_angular above the GPU local spectra limit (8)");
+}
+
+int64_t local_features(const mdsoap_local_params& p) {
+    const int64_t S = p.n_species, n = p.max_radial + 1, A = p.max_angular + 1;
+    if (p.kind == MDSOAP_LOCAL_RADIAL_SPECTRUM) return S * S * n;
+    if (p.kind == MDSOAP_LOCAL_POWER_SPECTRUM) return S * (S + 1) / 2 * S * A * n * n;
+    return S * S * n * A * A;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t mdsoap_local_feature_count(const mdsoap_local_params* params) {
+    try {
+        validate_local(params);
+        return local_features(*params);
+    } catch (const Failure& f) {
+        fail(f.status, f.message);
+        return -1;
+    }
+}
+
+int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* batch, double* out, int32_t device) {
+    if (!params || !batch) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        validate_local(params);
+        validate_host_batch(nullptr, *batch);
+        const int64_t atoms = batch->atoms, S = batch->structures;
+        const int64_t features = local_features(*params);
+        for (int64_t a = 0; a < atoms; ++a) {
+            bool known = false;
+            for (int i = 0; i < params->n_species; ++i) known = known || params->species[i] == batch->numbers[a];
+            if (!known) raise(MDSOAP_INVALID_ARGUMENT, "batch contains an atomic number outside calculator species");
+        }
+        if (atoms == 0 || S == 0) return MDSOAP_OK;
+        if (!out) raise(MDSOAP_INVALID_ARGUMENT, "null output");
+        if (features > 2147483647LL) raise(MDSOAP_INVALID_ARGUMENT, "local descriptor feature count exceeds int32");
+        const int lc = params->kind == MDSOAP_LOCAL_RADIAL_SPECTRUM ? 0 : params->max_angular;
+        const LocalLayout lay = local_layout(params->n_species, params->max_radial + 1, lc);
+        int warps = 4;
+        while (warps > 1 && lay.bytes_per_warp * warps > 200 * 1024) --warps;
+        if (lay.bytes_per_warp * warps > 227 * 1024)
+            raise(MDSOAP_INVALID_ARGUMENT, "local descriptor shape needs more shared memory than a GPU block holds");
+        const LocalHostTables ht = local_tables(*params, lc);
+
+        int count = 0;
+        const cudaError_t probe_err = cudaGetDeviceCount(&count);
+        if (probe_err != cudaSuccess || count == 0)
+            raise(MDSOAP_DEVICE_UNAVAILABLE, std::string("no CUDA device available: ") + cudaGetErrorString(probe_err));
+        if (device < 0 || device >= count) raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device index out of range");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        cudaStream_t stream = nullptr;
+        check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "stream");
+        struct StreamGuard {
+            cudaStream_t s;
+            ~StreamGuard() { cudaStreamDestroy(s); }
+        } guard{stream};
+        Workspace w;
+        struct WorkGuard {
+            Workspace& w;
+            ~WorkGuard() { w.release(); }
+        } wguard{w};
+        DeviceBytes error, species, tables, rows;
+        struct BytesGuard {
+            std::vector<DeviceBytes*> list;
+            ~BytesGuard() {
+                for (auto* b : list) b->release();
+            }
+        } bguard{{&error, &species, &tables, &rows}};
+        w.numbers.reserve(4 * atoms, "numbers");
+        w.positions.reserve(24 * atoms, "positions");
+        w.cells.reserve(72 * S, "cells");
+        w.pbc.reserve(12 * S, "pbc");
+        w.offsets.reserve(8 * (S + 1), "offsets");
+        check(cudaMemcpyAsync(w.numbers.ptr, batch->numbers, 4 * atoms, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.positions.ptr, batch->positions, 24 * atoms, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.cells.ptr, batch->cells, 72 * S, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.pbc.ptr, batch->pbc, 12 * S, cudaMemcpyHostToDevice, stream), "H2D");
+        check(cudaMemcpyAsync(w.offsets.ptr, batch->offsets, 8 * (S + 1), cudaMemcpyHostToDevice, stream), "H2D");
+        species.reserve(4 * params->n_species, "species");
+        check(cudaMemcpyAsync(species.ptr, params->species, 4 * params->n_species, cudaMemcpyHostToDevice, stream),
+              "H2D");
+        const int n = ht.n;
+        std::vector<double> packed;
+        for (const auto* part : {&ht.g, &ht.log_cg, &ht.gratio, &ht.ppow, &ht.ortho})
+            packed.insert(packed.end(), part->begin(), part->end());
+        tables.reserve(8 * packed.size(), "local tables");
+        check(cudaMemcpyAsync(tables.ptr, packed.data(), 8 * packed.size(), cudaMemcpyHostToDevice, stream), "H2D");
+        error.reserve(64, "error");
+        check(cudaMemsetAsync(error.ptr, 0, 64, stream), "memset");
+        w.reserve_bins(atoms, S);
+        DeviceBatch db{w.numbers.as<int32_t>(), w.positions.as<double>(), w.cells.as<double>(), w.pbc.as<int32_t>(),
+                       w.offsets.as<int64_t>(), S, atoms};
+        bin_structures_kernel<<<(unsigned)S, 256, 0, stream>>>(db, w.bins(error.as<unsigned>()), params->cutoff,
+                                                               species.as<int32_t>(), params->n_species);
+        check(cudaGetLastError(), "bin kernel");
+        LocalTables t;
+        t.kind = params->kind;
+        t.n = n;
+        t.lc = lc;
+        t.l_out = params->max_angular;
+        t.species = params->n_species;
+        t.features = (int)features;
+        t.cutoff = params->cutoff;
+        t.cutoff2 = params->cutoff * params->cutoff;
+        t.c = ht.c;
+        t.gf = ht.gf;
+        t.log_gf = ht.log_gf;
+        const double* tb = tables.as<double>();
+        t.g = tb;
+        t.log_cg = tb + n;
+        t.gratio = tb + 2 * n;
+        t.ppow = t.gratio + (size_t)(lc + 1) * n;
+        t.ortho = t.ppow + (size_t)(lc + 1) * n;
+        // Rows in chunks of centres (at most 512 MiB of device rows at a time).
+        const size_t row_bytes = 8 * (size_t)features;
+        const int64_t chunk =
+            std::max<int64_t>(warps, std::min<int64_t>(atoms, (int64_t)((512ull << 20) / row_bytes)));
+        rows.reserve(row_bytes * (size_t)std::min<int64_t>(chunk, atoms), "local rows");
+        const size_t smem = lay.bytes_per_warp * warps;
+        check(cudaFuncSetAttribute(local_spectra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+              "smem attribute");
+        for (int64_t a0 = 0; a0 < atoms; a0 += chunk) {
+            const int64_t a1 = std::min<int64_t>(atoms, a0 + chunk);
+            const unsigned grid = (unsigned)((a1 - a0 + warps - 1) / warps);
+            local_spectra_kernel<<<grid, 32 * warps, smem, stream>>>(t, db.positions, w.bins(error.as<unsigned>()),
+                                                                     a0, a1, rows.as<double>());
+            check(cudaGetLastError(), "local spectra kernel");
+            check(cudaMemcpyAsync(out + a0 * features, rows.ptr, row_bytes * (size_t)(a1 - a0), cudaMemcpyDeviceToHost,
+                                  stream),
+                  "D2H rows");
+            check(cudaStreamSynchronize(stream), "sync");
+        }
+        unsigned bits = 0;
+        check(cudaMemcpy(&bits, error.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "error word");
+        if (bits)
+            raise(bits & (kErrMixedPbc | kErrSingularCell | kErrUnknownSpecies | kErrLocalSeries) ? MDSOAP_INVALID_ARGUMENT
+                                                                                                 : MDSOAP_INTERNAL,
+                  device_error_text(bits));
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
 
 }  // extern "C"

@@ -14,7 +14,7 @@ from typing import Any, Callable, Sequence
 import numpy as np
 
 from . import _lib
-from ._lib import BatchView, CancelFn, Params, lib, raise_for
+from ._lib import BatchView, CancelFn, LocalParams, Params, last_error, lib, raise_for
 from .basis import basis_gto, basis_polynomial, feature_count, graph_cutoff, labels
 
 
@@ -269,6 +269,46 @@ def neighbor_list(batch, cutoff: float, full_neighbor_list: bool = True, self_pa
     finally:
         lib.mdsoap_pairs_destroy(handle)
     return records, values, row_offsets
+
+
+LOCAL_KINDS = {"SphericalExpansion": 0, "SoapRadialSpectrum": 2, "SoapPowerSpectrum": 3}
+
+
+def _local_params(name: str, species: Sequence[int], cutoff: float, density_width: float, max_radial: int,
+                  max_angular: int) -> tuple[LocalParams, np.ndarray]:
+    if name not in LOCAL_KINDS:
+        raise ValueError(f"unknown local spectrum {name!r}; expected one of {sorted(LOCAL_KINDS)}")
+    sp = np.ascontiguousarray(np.asarray(tuple(int(z) for z in species), dtype=np.int32))
+    params = LocalParams(LOCAL_KINDS[name], int(max_radial), int(max_angular), int(sp.shape[0]),
+                         sp.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), float(cutoff), float(density_width))
+    return params, sp
+
+
+def local_feature_count(name: str, species: Sequence[int], max_radial: int = 6, max_angular: int = 4) -> int:
+    """Row width of a local spectrum (C ABI ``mdsoap_local_feature_count``;
+    cpp/src/common/local_layout.hpp:115-130)."""
+    params, _keep = _local_params(name, species, 6.0, 0.3, max_radial, max_angular)
+    count = int(lib.mdsoap_local_feature_count(ctypes.byref(params)))
+    if count < 0:
+        raise ValueError(last_error())
+    return count
+
+
+def local_spectrum(name: str, batch, species: Sequence[int], cutoff: float = 6.0, density_width: float = 0.3,
+                   max_radial: int = 6, max_angular: int = 4, device: int = 0) -> np.ndarray:
+    """SphericalExpansion, SoapRadialSpectrum or SoapPowerSpectrum rows
+    float64[atoms, F] on the GPU (C ABI ``mdsoap_local_compute``), the values
+    of the reference's ``compute_spherical_expansion``
+    (cpp/src/standalone/spherical_expansion.cpp:124-206) for the same options."""
+    params, _keep = _local_params(name, species, cutoff, density_width, max_radial, max_angular)
+    count = int(lib.mdsoap_local_feature_count(ctypes.byref(params)))
+    if count < 0:
+        raise ValueError(last_error())
+    arrays = _contiguous(batch)
+    view = host_view(arrays)
+    out = np.zeros((int(arrays[4][-1]), count), np.float64)
+    raise_for(lib.mdsoap_local_compute(ctypes.byref(params), ctypes.byref(view), out.ctypes.data, int(device)))
+    return out
 
 
 def probe_fp64_fma(device: int = 0) -> float:

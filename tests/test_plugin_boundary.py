@@ -74,8 +74,18 @@ def test_backend_construction_touches_no_gpu_and_compute_fails_loudly():
 def test_unsupported_descriptors_and_options_raise_mapped_errors():
     plugin = load_plugin()
     name, options, _ = adapter_cases()[0]
-    with pytest.raises(ImportError, match="SOAP and NeighborList only"):
+    with pytest.raises(ImportError, match="SOAP, NeighborList, SphericalExpansion"):
         plugin.create_backend("ACSF", {"species": [1, 8]})
+    # local spectra: reference option names, defaults and layout
+    # (cpp/cuda/src/backend.cu:108-131, 590-602)
+    for local, features in [("SphericalExpansion", 2 * 2 * 7 * 25), ("SoapRadialSpectrum", 2 * 2 * 7),
+                            ("SoapPowerSpectrum", 3 * 2 * 5 * 49)]:
+        backend = plugin.create_backend(local, {"species": [1, 8]})
+        assert backend.feature_count == features
+        backend.close()
+        backend.close()
+    with pytest.raises(ValueError):
+        plugin.create_backend("SphericalExpansion", {"species": [1, 8], "density_width": -1.0})
     for key, value, match in [
         ("rbf", "bessel", "radial basis"),
         ("rbf", "polynomial", "polynomial payload"),
