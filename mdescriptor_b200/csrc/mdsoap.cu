@@ -20,6 +20,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <exception>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -2067,6 +2068,22 @@ struct LocalHostTables {
     std::vector<double> g, log_cg, gratio, ppow, ortho;
 };
 
+struct LocalStaging {
+    std::mutex mutex;
+    PinnedBytes stage[2];
+};
+
+LocalStaging& local_staging(int device) {
+    // Never destroyed: freeing pinned memory after the CUDA runtime has shut
+    // down at process exit is not allowed.
+    static std::mutex registry_mutex;
+    static auto* registry = new std::map<int, std::unique_ptr<LocalStaging>>();
+    std::lock_guard<std::mutex> lock(registry_mutex);
+    auto& slot = (*registry)[device];
+    if (!slot) slot = std::make_unique<LocalStaging>();
+    return *slot;
+}
+
 double checked_gamma(double x) {
     const double v = std::tgamma(x);
     if (!std::isfinite(v) || v <= 0.0) raise(MDSOAP_INVALID_ARGUMENT, "local descriptor radial basis is numerically singular");
@@ -2308,25 +2325,70 @@ int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* 
         t.gratio = tb + 2 * n;
         t.ppow = t.gratio + (size_t)(lc + 1) * n;
         t.ortho = t.ppow + (size_t)(lc + 1) * n;
-        // Rows in chunks of centres (at most 512 MiB of device rows at a time).
+        // Rows in blocks of centres (about MDSOAP_BLOCK_BYTES of rows each),
+        // double buffered: block i's kernel runs while the host copies block
+        // i-1 out of its pinned staging buffer into the caller's rows.  A
+        // pinned `out` receives the D2H directly.
         const size_t row_bytes = 8 * (size_t)features;
-        const int64_t chunk =
-            std::max<int64_t>(warps, std::min<int64_t>(atoms, (int64_t)((512ull << 20) / row_bytes)));
-        rows.reserve(row_bytes * (size_t)std::min<int64_t>(chunk, atoms), "local rows");
+        const int64_t chunk = std::max<int64_t>(
+            warps, std::min<int64_t>(atoms, (int64_t)((size_t)block_bytes_target() / row_bytes)));
+        const size_t block_bytes = row_bytes * (size_t)std::min<int64_t>(chunk, atoms);
+        const bool direct = is_pinned(out);
+        DeviceBytes rows2;
+        struct RowsGuard {
+            DeviceBytes& r;
+            ~RowsGuard() { r.release(); }
+        } rguard{rows2};
+        // Pinned staging is allocated once per device and kept until exit
+        // (pinning host pages costs more than the copy it speeds up); calls on
+        // one device take turns on it.
+        LocalStaging& staging = local_staging(device);
+        std::lock_guard<std::mutex> staging_lock(staging.mutex);
+        PinnedBytes* stage = staging.stage;
+        DeviceBytes* rowbuf[2] = {&rows, &rows2};
+        rows.reserve(block_bytes, "local rows");
+        if (atoms > chunk) rows2.reserve(block_bytes, "local rows");
+        if (!direct) {
+            stage[0].reserve(block_bytes);
+            if (atoms > chunk) stage[1].reserve(block_bytes);
+        }
+        cudaEvent_t done[2] = {nullptr, nullptr};
+        struct EventGuard {
+            cudaEvent_t* e;
+            ~EventGuard() {
+                for (int i = 0; i < 2; ++i)
+                    if (e[i]) cudaEventDestroy(e[i]);
+            }
+        } eguard{done};
+        for (int i = 0; i < 2; ++i) check(cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming), "event");
         const size_t smem = lay.bytes_per_warp * warps;
         check(cudaFuncSetAttribute(local_spectra_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
               "smem attribute");
-        for (int64_t a0 = 0; a0 < atoms; a0 += chunk) {
+        auto drain = [&](int slot, int64_t b0, int64_t b1) {
+            check(cudaEventSynchronize(done[slot]), "sync");
+            if (!direct)
+                parallel_copy(reinterpret_cast<char*>(out + b0 * features), static_cast<const char*>(stage[slot].ptr),
+                              row_bytes * (size_t)(b1 - b0));
+        };
+        int64_t prev0 = -1, prev1 = -1;
+        int slot = 0;
+        for (int64_t a0 = 0; a0 < atoms; a0 += chunk, slot ^= 1) {
             const int64_t a1 = std::min<int64_t>(atoms, a0 + chunk);
             const unsigned grid = (unsigned)((a1 - a0 + warps - 1) / warps);
             local_spectra_kernel<<<grid, 32 * warps, smem, stream>>>(t, db.positions, w.bins(error.as<unsigned>()),
-                                                                     a0, a1, rows.as<double>());
+                                                                     a0, a1, rowbuf[slot]->as<double>());
             check(cudaGetLastError(), "local spectra kernel");
-            check(cudaMemcpyAsync(out + a0 * features, rows.ptr, row_bytes * (size_t)(a1 - a0), cudaMemcpyDeviceToHost,
+            void* dst = direct ? static_cast<void*>(out + a0 * features) : stage[slot].ptr;
+            check(cudaMemcpyAsync(dst, rowbuf[slot]->ptr, row_bytes * (size_t)(a1 - a0), cudaMemcpyDeviceToHost,
                                   stream),
                   "D2H rows");
-            check(cudaStreamSynchronize(stream), "sync");
+            check(cudaEventRecord(done[slot], stream), "event record");
+            if (prev0 >= 0) drain(slot ^ 1, prev0, prev1);
+            prev0 = a0;
+            prev1 = a1;
         }
+        if (prev0 >= 0) drain(slot ^ 1, prev0, prev1);
+        check(cudaStreamSynchronize(stream), "sync");
         unsigned bits = 0;
         check(cudaMemcpy(&bits, error.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "error word");
         if (bits)
