@@ -229,7 +229,9 @@ void mdsoap_csr_destroy(mdsoap_csr* csr);
  *    call's contents; everything that must start at zero is cleared by each
  *    call.  Calls whose GPU work overlaps (different streams or threads)
  *    race on the array: serialise them.
- *  - The call waits for its work on `stream` and returns device-detected input
+ *  - Every call blocks: after queueing its kernels it copies the error word
+ *    back to the host and calls cudaStreamSynchronize(stream), so it returns
+ *    only once its work on `stream` has finished, with device-detected input
  *    errors (unknown species, mixed pbc, singular cell) as its status. */
 int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, void* out, int32_t device,
                                   void* stream);

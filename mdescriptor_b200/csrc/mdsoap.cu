@@ -5,9 +5,7 @@
 // there, so building a plan touches no GPU (the reference's construction-time
 // contract, tests/test_cuda_backend.py:266-279).
 #include "../../include/mdsoap.h"
-#include "soap_mma.cuh"
-#include "soap_pair.cuh"
-#include "soap_paired.cuh"
+#include "launchers.cuh"
 #include "neighbor_list.cuh"
 #include "csr.cuh"
 #include "local_spectra.cuh"
@@ -146,89 +144,8 @@ struct Workspace {
     }
 };
 
-using CenterLauncher = void (*)(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);
-using StructureLauncher = void (*)(dim3, size_t, cudaStream_t, const SoapTables&, const int64_t*, int64_t, int64_t,
-                                   const double*, const double*, void*, int64_t);
-
-template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX, int MINB>
-void launch_center(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX, MINB><<<grid, kWarps * 32, smem, stream>>>(tab, p);
-}
-template <int MAXT, int L0, int L1, int L2, int NMAX, int LMAX, int MINB>
-const void* center_symbol() {
-    return reinterpret_cast<const void*>(&soap_center_kernel<MAXT, L0, L1, L2, NMAX, LMAX, MINB>);
-}
-// Two-warp variant: one CTA of 64 threads per centre (grid = centres).
-template <int MAXT, int LA, int LB1, int LB2, int NMAX, int LMAX, int MINB>
-void launch_pair(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_pair_kernel<MAXT, LA, LB1, LB2, NMAX, LMAX, MINB><<<grid, 64, smem, stream>>>(tab, p);
-}
-template <int MAXT, int LA, int LB1, int LB2, int NMAX, int LMAX, int MINB>
-const void* pair_symbol() {
-    return reinterpret_cast<const void*>(&soap_pair_kernel<MAXT, LA, LB1, LB2, NMAX, LMAX, MINB>);
-}
-// fp64 tensor-core kernel: one warp per centre, n_max <= 8.
-template <int LMAX, int MINB>
-void launch_mma(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_mma_kernel<LMAX, MINB><<<grid, kWarps * 32, smem, stream>>>(tab, p);
-}
-template <int LMAX, int MINB>
-const void* mma_symbol() {
-    return reinterpret_cast<const void*>(&soap_mma_kernel<LMAX, MINB>);
-}
-// Split tail of the paired kernel: one warp per centre.
-template <int L, int T>
-void launch_tail(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_tail_kernel<L, T><<<grid, kWarps * 32, smem, stream>>>(tab, p);
-}
-template <int L, int T>
-const void* tail_symbol() {
-    return reinterpret_cast<const void*>(&soap_tail_kernel<L, T>);
-}
-template <int L>
-void launch_tail_generic(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_tail_generic_kernel<L><<<grid, kWarps * 32, smem, stream>>>(tab, p);
-}
-template <int L>
-const void* tail_generic_symbol() {
-    return reinterpret_cast<const void*>(&soap_tail_generic_kernel<L>);
-}
-// Paired-channel kernel: one warp per centre, l_max == L exactly.
-// Plans with a split tail launch the instantiation without tail code (fewer registers).
-template <int T, int L, bool PRECISE, int MINB>
-void launch_paired(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    if (tab.split_tail)
-        soap_paired_kernel<T, L, PRECISE, MINB, true><<<grid, kWarps * 32, smem, stream>>>(tab, p);
-    else
-        soap_paired_kernel<T, L, PRECISE, MINB, false><<<grid, kWarps * 32, smem, stream>>>(tab, p);
-}
-// Polynomial radial basis: the paired kernel's POLY instantiation (full
-// accuracy exps, tail fused).
-template <int T, int L>
-void launch_poly(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
-    soap_paired_kernel<T, L, true, 2, false, true><<<grid, kWarps * 32, smem, stream>>>(tab, p);
-}
-template <int T, int L>
-const void* poly_symbol() {
-    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, true, 2, false, true>);
-}
-template <int T, int L, bool PRECISE, int MINB>
-const void* paired_symbol() {
-    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB, false>);
-}
-template <int T, int L, bool PRECISE, int MINB>
-const void* paired_split_symbol() {
-    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB, true>);
-}
-template <int LMAX>
-void launch_structure(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const int64_t* offsets,
-                      int64_t s0, int64_t s1, const double* cbuf, const double* pbuf, void* out, int64_t row0) {
-    soap_structure_kernel<LMAX><<<grid, kWarps * 32, smem, stream>>>(tab, offsets, s0, s1, cbuf, pbuf, out, row0);
-}
-template <int LMAX>
-const void* structure_symbol() {
-    return reinterpret_cast<const void*>(&soap_structure_kernel<LMAX>);
-}
+using launch::CenterLauncher;
+using launch::StructureLauncher;
 
 // Kernel variants.  Slot lengths bound 2l+1 of the channels a lane owns per
 // pass: channels are sorted by l descending, 32 per slot, and with n_max <= 8
@@ -237,8 +154,6 @@ const void* structure_symbol() {
 // registers per thread (MINB resident CTAs per SM).
 struct Variant {
     int cls, maxt, l0, l1, l2, nmax, lmax, minb;
-    bool pair;  // two warps per centre (soap_pair_kernel), channel slots A | B1 B2
-    bool mma;   // fp64 tensor-core kernel (soap_mma_kernel)
     CenterLauncher center;
     const void* (*center_sym)();
     StructureLauncher structure;
@@ -253,53 +168,33 @@ struct Variant {
     const void* (*tail_generic_sym)() = nullptr;
 };
 
-#define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                        \
-    Variant {                                                                                             \
-        CLS, T, A, B, C, N, L, MB, false, false, &launch_center<T, A, B, C, N, L, MB>,                      \
-            &center_symbol<T, A, B, C, N, L, MB>, &launch_structure<L>, &structure_symbol<L>, false, false, \
-            "soap_center_kernel<" #T ", " #A ", " #B ", " #C ", " #N ", " #L ", " #MB ">"                   \
-    }
-#define MDSOAP_PAIR_VARIANT(CLS, T, A, B, C, N, L, MB)                                                   \
-    Variant {                                                                                             \
-        CLS, T, A, B, C, N, L, MB, true, false, &launch_pair<T, A, B, C, N, L, MB>,                         \
-            &pair_symbol<T, A, B, C, N, L, MB>,                                                           \
-            &launch_structure<L>, &structure_symbol<L>, false, false,                                     \
-            "soap_pair_kernel<" #T ", " #A ", " #B ", " #C ", " #N ", " #L ", " #MB ">"                     \
+#define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                           \
+    Variant {                                                                                                \
+        CLS, T, A, B, C, N, L, MB, &launch::center<T, A, B, C, N, L, MB>,                                    \
+            &launch::center_symbol<T, A, B, C, N, L, MB>, &launch::structure<L>, &launch::structure_symbol<L>, \
+            false, false, "soap_center_kernel<" #T ", " #A ", " #B ", " #C ", " #N ", " #L ", " #MB ">"        \
     }
 
-#define MDSOAP_MMA_VARIANT(CLS, L, MB)                                                                  \
-    Variant {                                                                                             \
-        CLS, 0, 0, 0, 0, 8, L, MB, false, true, &launch_mma<L, MB>, &mma_symbol<L, MB>, &launch_structure<L>, \
-            &structure_symbol<L>, false, false, "soap_mma_kernel<" #L ", " #MB ">"                          \
-    }
-
-// First entry of each class is the default.  Defaults chosen by measurement
-// on B200 (config shapes 1-5): the one-warp scalar-expansion kernel with the
-// tensor-core tail; the two-warp pair kernels and the all-tensor-core kernel
-// (soap_mma_kernel) are alternatives (MDSOAP_VARIANT=k).
+// First entry of each class is the default (chosen by measurement on B200,
+// config shapes 1-5); the other member trades species register banks against
+// resident CTAs (MDSOAP_VARIANT=k).
 const Variant kVariants[] = {
     MDSOAP_VARIANT(0, 4, 7, 0, 0, 8, 3, 3),         // n <= 8, l <= 3
     MDSOAP_VARIANT(0, 8, 7, 0, 0, 8, 3, 2),
-    MDSOAP_MMA_VARIANT(0, 3, 2),
     MDSOAP_VARIANT(1, 3, 9, 1, 0, 8, 4, 3),         // n <= 8, l == 4
     MDSOAP_VARIANT(1, 6, 9, 1, 0, 8, 4, 2),
-    MDSOAP_MMA_VARIANT(1, 4, 2),
     MDSOAP_VARIANT(2, 4, 13, 5, 0, 8, 6, 2),        // n <= 8, l in 5..6
-    MDSOAP_PAIR_VARIANT(2, 4, 13, 9, 0, 8, 6, 6),
-    MDSOAP_PAIR_VARIANT(2, 3, 13, 9, 0, 8, 6, 6),
-    MDSOAP_MMA_VARIANT(2, 6, 2),
     MDSOAP_VARIANT(3, 2, 17, 9, 1, 8, 8, 2),        // n <= 8, l in 7..8
-    MDSOAP_PAIR_VARIANT(3, 2, 17, 13, 5, 8, 8, 6),
-    MDSOAP_MMA_VARIANT(3, 8, 2),
     MDSOAP_VARIANT(4, 1, 41, 0, 0, 32, 20, 1),  // any n <= 32, l <= 20
 };
 
-#define MDSOAP_PAIRED_VARIANT(T, L, PREC, MB)                                                              \
-    Variant {                                                                                              \
-        -1, T, 0, 0, 0, 8, L, MB, false, false, &launch_paired<T, L, PREC, MB>,                             \
-            &paired_symbol<T, L, PREC, MB>, &launch_structure<L>, &structure_symbol<L>, true, PREC,         \
-            "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch_tail<L, T>, &tail_symbol<L, T>, \
-            &paired_split_symbol<T, L, PREC, MB>, &launch_tail_generic<L>, &tail_generic_symbol<L>        \
+#define MDSOAP_PAIRED_VARIANT(T, L, PREC, MB)                                                                \
+    Variant {                                                                                                \
+        -1, T, 0, 0, 0, 8, L, MB, &launch::paired<T, L, PREC, MB>, &launch::paired_symbol<T, L, PREC, MB>,   \
+            &launch::structure<L>, &launch::structure_symbol<L>, true, PREC,                                 \
+            "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch::tail<L, T>,                   \
+            &launch::tail_symbol<L, T>, &launch::paired_split_symbol<T, L, PREC, MB>,                        \
+            &launch::tail_generic<L>, &launch::tail_generic_symbol<L>                                        \
     }
 
 // Paired-channel kernels: the default wherever they apply (n_max <= 8,
@@ -315,10 +210,10 @@ const Variant kPairedVariants[] = {
     MDSOAP_PAIRED_VARIANT(4, 6, false, 2), MDSOAP_PAIRED_VARIANT(4, 6, true, 2),
 };
 
-#define MDSOAP_POLY_VARIANT(T, L)                                                                           \
-    Variant {                                                                                              \
-        -1, T, 0, 0, 0, 8, L, 2, false, false, &launch_poly<T, L>, &poly_symbol<T, L>, &launch_structure<L>, \
-            &structure_symbol<L>, true, true, "soap_paired_kernel<" #T ", " #L ", true, 2, false, true>"       \
+#define MDSOAP_POLY_VARIANT(T, L)                                                                            \
+    Variant {                                                                                                \
+        -1, T, 0, 0, 0, 8, L, 2, &launch::poly<T, L>, &launch::poly_symbol<T, L>, &launch::structure<L>,     \
+            &launch::structure_symbol<L>, true, true, "soap_paired_kernel<" #T ", " #L ", true, 2, false, true>" \
     }
 
 // Polynomial radial basis kernels (same applicability as the paired kernels).
@@ -351,13 +246,6 @@ int variant_class(int n_max, int l_max) {
     return 4;
 }
 
-// First scalar (non tensor-core) member of a class.
-const Variant& scalar_variant(int cls) {
-    for (const Variant& v : kVariants)
-        if (v.cls == cls && !v.mma) return v;
-    return kVariants[sizeof(kVariants) / sizeof(kVariants[0]) - 1];
-}
-
 // The want-th member of the class of (n_max, l_max), or its first member
 // when `want` is out of range.
 const Variant& pick_variant(int n_max, int l_max, int want) {
@@ -370,31 +258,6 @@ const Variant& pick_variant(int n_max, int l_max, int want) {
         if (k++ == want) return v;
     }
     return *first;
-}
-
-// Channel order for the kernels: the one-warp kernel takes channels sorted
-// by l descending, 32 per slot; the pair kernel takes three padded slots of
-// 32 (padding has l = -1): A = {L, L-1, 1, 0} (warp A), B1 = {L-2 .. L-5}
-// and B2 = the rest (warp B), which bounds each slot's 2l+1 by the variant's
-// slot lengths and balances the two warps.
-std::vector<RadialItem> order_items(const std::vector<RadialItem>& by_l, int l_max, int n_max, bool pair) {
-    if (!pair) return by_l;
-    std::vector<RadialItem> out(96, RadialItem{0.0, 0.0, -1, 0});
-    auto put = [&](int slot, const std::vector<int>& ls) {
-        int pos = 32 * slot;
-        for (int l : ls)
-            for (const RadialItem& it : by_l)
-                if (it.l == l) out[pos++] = it;
-    };
-    const int L = l_max;
-    std::vector<int> a{L, L - 1, 1, 0}, b1, b2;
-    for (int l = L - 2; l >= 2 && l >= L - 5; --l) b1.push_back(l);
-    for (int l = L - 6; l >= 2; --l) b2.push_back(l);
-    put(0, a);
-    put(1, b1);
-    put(2, b2);
-    (void)n_max;
-    return out;
 }
 
 // fp64 FMA throughput probe: kProbeChains independent dependent-FMA chains per
@@ -661,7 +524,7 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             p.rbuf = st.work.rbuf.as<double>();
         }
         if (centers > 0) {
-            int64_t grid = variant->pair ? centers : (centers + kWarps - 1) / kWarps;
+            int64_t grid = (centers + kWarps - 1) / kWarps;
             if (variant->paired && st.center_grid > 0) grid = std::min(grid, st.center_grid);
             variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
             check(cudaGetLastError(), "centre kernel launch");
@@ -1165,37 +1028,27 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             return fail(MDSOAP_INVALID_ARGUMENT,
                         "SOAP weighting, compression and the polynomial radial basis run on the paired-channel "
                         "kernel, which needs n_max <= 8, n_max (1 + (l_max + 1) / 2) <= 32 and l_max <= 6");
-        // The tensor-core kernel keeps a centre's whole coefficient block in
-        // shared memory; when that does not fit, the class's scalar kernel runs.
-        const mma::Layout lay = mma::layout(L, q.n_species * n);
-        const size_t mma_smem = (size_t)lay.shared + kWarps * (size_t)lay.warp_bytes;
-        if (picked->mma && mma_smem > 227 * 1024) picked = &scalar_variant(picked->cls);
-        const Variant& v = *picked;
-        // Tables of the scalar kernels (the tensor-core kernel shares csize/hp).
-        const Variant& sv = v.mma ? scalar_variant(v.cls) : v;
-        plan->variant = &v;
-        plan->items = order_items(plan->items, L, n, sv.pair);
-        if (sv.pair) t.items = (int32_t)plan->items.size();
+        const Variant& sv = *picked;
+        plan->variant = &sv;
         const int ns = (sv.l0 > 0) + (sv.l1 > 0) + (sv.l2 > 0);
         const int slots = (t.items + 31) / 32;
-        t.slot_groups = sv.pair ? 1 : (slots + ns - 1) / ns;
+        t.slot_groups = (slots + ns - 1) / ns;
         t.type_groups = (q.n_species + sv.maxt - 1) / sv.maxt;
         const bool single_pass = t.slot_groups == 1 && t.type_groups == 1;
         // One-warp scalar kernels with n_max <= 8 finish on the tensor cores:
         // row-strided coefficient block, padded 8 x 8 beta table in shared memory.
-        const bool mma_tail = !sv.pair && sv.nmax <= 8;
+        const bool mma_tail = sv.nmax <= 8;
         const size_t beta_bytes = mma_tail ? (size_t)W * 64 * 8 : (size_t)W * n * n * 8;
         t.beta_in_smem = mma_tail || beta_bytes <= 32768;
         // CTA-shared: 32-entry exp table (256 B) + optional beta copy.
         const size_t beta_smem = 256 + (t.beta_in_smem ? ((beta_bytes + 15) & ~(size_t)15) : 0);
         t.csize = q.n_species * n * W * (W + 1);
         t.hp = W * (W + 1);
-        t.rs = (mma_tail || v.mma) ? mma::row_stride(L) : 0;
+        t.rs = mma_tail ? mma::row_stride(L) : 0;
         t.rsize = mma_tail ? q.n_species * n * t.rs : t.csize;
         t.n_magic = n == 1 ? 0u : (uint32_t)((1ull << 32) / (uint64_t)n + 1ull);
         const size_t r_bytes = (size_t)t.rsize * 8;
-        const size_t pend = sv.pair ? (size_t)kPairHeader + (size_t)kPairPending * 36
-                                   : kRegionHeader + (size_t)kPending * 36;
+        const size_t pend = kRegionHeader + (size_t)kPending * 36;
         auto region_a = [&](int chunk) { return pend + ((size_t)chunk * t.hp + 48) * 8; };
         auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
         auto per_warp = [&](int chunk, bool r_in_smem) {
@@ -1216,32 +1069,11 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             chunk = 32;
             while (chunk > 8 && beta_smem + kWarps * per_warp(chunk, false) > budget) chunk -= 8;
         }
-        if (sv.pair) {
-            // One region per CTA (one centre), no beta copy; offsets relative
-            // to the queue (after the exp table and the header).
-            t.beta_in_smem = 0;
-            auto cta = [&](int c, bool r_in) { return 256 + per_warp(c, r_in); };
-            chunk = 32;
-            r_smem = true;
-            while (chunk > 8 && cta(chunk, true) > budget) chunk -= 8;
-            if (cta(chunk, true) > budget1) r_smem = false;
-            t.chunk = chunk;
-            t.r_global = r_smem ? 0 : 1;
-            t.warp_bytes = (int32_t)per_warp(chunk, r_smem);
-            t.r_offset = (r_smem && !single_pass) ? (int32_t)(align16(region_a(chunk)) - kPairHeader) : 0;
-            plan->center_smem = cta(chunk, r_smem);
-        } else {
         t.chunk = chunk;
         t.r_global = r_smem ? 0 : 1;
         t.warp_bytes = (int32_t)per_warp(chunk, r_smem);
         t.r_offset = (r_smem && !single_pass) ? (int32_t)align16(region_a(chunk)) : 0;
         plan->center_smem = beta_smem + kWarps * (size_t)t.warp_bytes;
-        }
-        if (v.mma) {
-            t.r_global = 0;
-            t.warp_bytes = lay.warp_bytes;
-            plan->center_smem = mma_smem;
-        }
         plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? (size_t)t.csize * 8 : 0;
         plan->csize = t.csize;
         if (plan->center_smem > budget1 || plan->structure_smem > budget1)
@@ -1562,39 +1394,39 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
                                   void* stream) {
     if (!plan || !batch) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
     if (batch->structures < 0 || batch->atoms < 0) return fail(MDSOAP_INVALID_ARGUMENT, "invalid structure batch");
-    const int64_t S = batch->structures, N = batch->atoms;
-    // Scratch layout (each piece 256-byte aligned).
-    size_t off = 0;
-    auto take = [&](size_t bytes) {
-        const size_t at = off;
-        off = align256(off + std::max<size_t>(bytes, 1));
-        return at;
-    };
-    const size_t o_items = take(sizeof(RadialItem) * plan->items.size());
-    const size_t o_betas = take(8 * plan->betas.size());
-    const size_t o_species = take(4 * plan->species.size());
-    const size_t o_poly = take(8 * plan->poly.size());
-    const size_t o_error = take(sizeof(unsigned));
-    const size_t o_info = take(sizeof(StructInfo) * (size_t)std::max<int64_t>(S, 1));
-    const size_t o_struct = take(4 * (size_t)N);
-    const size_t o_type = take(4 * (size_t)N);
-    const size_t o_bin = take(4 * (size_t)N);
-    const size_t o_wrap = take(12 * (size_t)N);
-    const size_t o_sorted = take(4 * (size_t)N);
-    const size_t o_spos = take(32 * (size_t)N);
-    const size_t bins = (size_t)(2 * N + 8 * S + 8);
-    const size_t o_bstart = take(4 * bins);
-    const size_t o_bcursor = take(4 * bins);
-    size_t o_cbuf = 0, o_pbuf = 0, o_rbuf = 0;
-    if (plan->average == MDSOAP_AVERAGE_INNER) o_cbuf = take(8 * (size_t)N * (size_t)plan->csize);
-    if (plan->average == MDSOAP_AVERAGE_OUTER) o_pbuf = take(8 * (size_t)N * (size_t)plan->features);
-    if (plan->tab.r_global) o_rbuf = take(8 * (size_t)N * (size_t)plan->tab.rsize);
-    if (off > MDSOAP_NOALLOC_SCRATCH_BYTES)
-        return fail(MDSOAP_CAPACITY_OVERFLOW,
-                    "batch needs " + std::to_string(off) + " bytes of scratch; the no-allocation entry point holds " +
-                        std::to_string((size_t)MDSOAP_NOALLOC_SCRATCH_BYTES) + " bytes (split the batch)");
-    if (N > 2147483647LL) return fail(MDSOAP_INVALID_ARGUMENT, "neighbor atom index exceeds int32 range");
     try {
+        const int64_t S = batch->structures, N = batch->atoms;
+        // Scratch layout (each piece 256-byte aligned).
+        size_t off = 0;
+        auto take = [&](size_t bytes) {
+            const size_t at = off;
+            off = align256(off + std::max<size_t>(bytes, 1));
+            return at;
+        };
+        const size_t o_items = take(sizeof(RadialItem) * plan->items.size());
+        const size_t o_betas = take(8 * plan->betas.size());
+        const size_t o_species = take(4 * plan->species.size());
+        const size_t o_poly = take(8 * plan->poly.size());
+        const size_t o_error = take(sizeof(unsigned));
+        const size_t o_info = take(sizeof(StructInfo) * (size_t)std::max<int64_t>(S, 1));
+        const size_t o_struct = take(4 * (size_t)N);
+        const size_t o_type = take(4 * (size_t)N);
+        const size_t o_bin = take(4 * (size_t)N);
+        const size_t o_wrap = take(12 * (size_t)N);
+        const size_t o_sorted = take(4 * (size_t)N);
+        const size_t o_spos = take(32 * (size_t)N);
+        const size_t bins = (size_t)(2 * N + 8 * S + 8);
+        const size_t o_bstart = take(4 * bins);
+        const size_t o_bcursor = take(4 * bins);
+        size_t o_cbuf = 0, o_pbuf = 0, o_rbuf = 0;
+        if (plan->average == MDSOAP_AVERAGE_INNER) o_cbuf = take(8 * (size_t)N * (size_t)plan->csize);
+        if (plan->average == MDSOAP_AVERAGE_OUTER) o_pbuf = take(8 * (size_t)N * (size_t)plan->features);
+        if (plan->tab.r_global) o_rbuf = take(8 * (size_t)N * (size_t)plan->tab.rsize);
+        if (off > MDSOAP_NOALLOC_SCRATCH_BYTES)
+            return fail(MDSOAP_CAPACITY_OVERFLOW,
+                        "batch needs " + std::to_string(off) + " bytes of scratch; the no-allocation entry point holds " +
+                            std::to_string((size_t)MDSOAP_NOALLOC_SCRATCH_BYTES) + " bytes (split the batch)");
+        if (N > 2147483647LL) return fail(MDSOAP_INVALID_ARGUMENT, "neighbor atom index exceeds int32 range");
         int count = 0;
         if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
             cudaGetLastError();
@@ -1663,7 +1495,7 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
             // One launch with the tail fused in (no scratch for a split tail here).
             SoapTables fused = plan->tab;
             fused.split_tail = 0;
-            const int64_t grid = plan->variant->pair ? N : (N + kWarps - 1) / kWarps;
+            const int64_t grid = (N + kWarps - 1) / kWarps;
             plan->variant->center(dim3((unsigned)grid), plan->center_smem, st, fused, p);
             check(cudaGetLastError(), "centre kernel launch");
             plan->launches.fetch_add(1, std::memory_order_relaxed);
@@ -1684,6 +1516,8 @@ int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, 
         return MDSOAP_OK;
     } catch (const Failure& f) {
         return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
     }
 }
 
@@ -2344,6 +2178,13 @@ int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* 
         // one device take turns on it.
         LocalStaging& staging = local_staging(device);
         std::lock_guard<std::mutex> staging_lock(staging.mutex);
+        // Destroyed before staging_lock: on any exit (an exception included)
+        // the stream drains first, so no D2H queued below still writes into
+        // the staging buffers once another call on this device takes them.
+        struct DrainGuard {
+            cudaStream_t s;
+            ~DrainGuard() { cudaStreamSynchronize(s); }
+        } drain{stream};
         PinnedBytes* stage = staging.stage;
         DeviceBytes* rowbuf[2] = {&rows, &rows2};
         rows.reserve(block_bytes, "local rows");

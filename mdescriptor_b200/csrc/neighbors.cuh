@@ -76,6 +76,9 @@ __device__ __forceinline__ void wrapped_position(const StructInfo& si, const dou
     }
 }
 
+// Translation units that only instantiate the centre kernels (k_*.cu) leave
+// out the non-template kernels, which the host translation unit defines.
+#ifndef MDSOAP_NO_GRAPH_KERNELS
 // ---------------------------------------------------------------------------
 // Kernel 1: per structure (one CTA each): geometry plan, species lookup, and a
 // deterministic counting sort of its atoms into bins.
@@ -327,6 +330,8 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
     }
 }
 
+#endif  // MDSOAP_NO_GRAPH_KERNELS
+
 // ---------------------------------------------------------------------------
 // Exact displacement of image n of atom gj seen from centre gi; returns d2.
 __device__ __forceinline__ double exact_pair(const StructInfo& si, const double* __restrict__ pos,
@@ -417,6 +422,7 @@ __device__ __forceinline__ bool accept_candidate(const StructInfo& si, const Bin
     return d2 <= cutoff2;
 }
 
+#ifndef MDSOAP_NO_GRAPH_KERNELS
 // ---------------------------------------------------------------------------
 // Neighbour-graph export: count then fill (warp per centre).
 __global__ void graph_count_kernel(const double* __restrict__ pos, BinView v, int64_t atoms, double cutoff2,
@@ -470,5 +476,6 @@ __global__ void graph_fill_kernel(const double* __restrict__ pos, BinView v, int
         cursor += __popc(mask);
     });
 }
+#endif  // MDSOAP_NO_GRAPH_KERNELS
 
 }  // namespace mdsoap

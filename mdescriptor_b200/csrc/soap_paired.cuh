@@ -847,10 +847,17 @@ soap_tail_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
         }
         const bool ok = bulk::wait(&bars[b], (uint32_t)(it >> 1) & 1u);
         if (__syncthreads_or(!ok)) {
+            // Before the CTA hands its shared memory back, give each copy it
+            // issued one more bounded wait: the one that timed out and the one
+            // for the next centre.  A copy still outstanding after both waits
+            // (two further seconds) is left in flight; the error word already
+            // tells the host that this launch's rows are invalid.
             if (threadIdx.x == 0) {
                 atomicOr(p.bins.error, kErrTailTimeout);
+                bulk::wait(&bars[b], (uint32_t)(it >> 1) & 1u);
                 if (next < count) bulk::wait(&bars[b ^ 1], (uint32_t)((it + 1) >> 1) & 1u);
             }
+            __syncthreads();
             return;
         }
         const double* R = rbuf + b * tab.rsize;

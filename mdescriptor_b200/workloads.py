@@ -2,8 +2,11 @@
 
 No public dataset backs the benchmark; these generators stand in for it with
 the stated cell shapes, atom counts, species weights and minimum distances.
-Config k draws from ``numpy.random.default_rng(20261201 + k)`` unless a seed
-is given.  Positions are float64 and never wrapped into the cell.
+Configs 1-4 draw from ``numpy.random.default_rng(20261201 + k)`` unless a
+seed is given.  Config 5 (16.8 M atoms) uses a per-structure stream of the
+C generator in csrc/synth.c instead, so that each rank of a sharded run can
+make its own slice of the one batch in well under a second.  Positions are
+float64 and never wrapped into the cell.
 """
 
 from __future__ import annotations
@@ -159,14 +162,67 @@ def config4(structures=16384, seed=None):
     return Batch(numbers, positions, cells, pbc, offsets)
 
 
-def config5(structures=65536, seed=None):
-    rng = np.random.default_rng(SEED_BASE + 5 if seed is None else seed)
-    return _cubic_batch(rng, structures, 256, 16.0, (1, 6, 8), (0.5, 0.3, 0.2), 0.9)
+_SYNTH = None
+
+
+def _synth_lib():
+    global _SYNTH
+    if _SYNTH is None:
+        import ctypes
+        from pathlib import Path
+
+        path = Path(__file__).resolve().parent / "lib" / "libmdsynth.so"
+        if not path.is_file():
+            raise RuntimeError(f"{path} is missing: run python -m mdescriptor_b200.build")
+        lib = ctypes.CDLL(str(path))
+        lib.mdsynth_cubic.restype = ctypes.c_int
+        lib.mdsynth_cubic.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                      ctypes.c_double, ctypes.c_double, ctypes.c_int32, ctypes.c_void_p,
+                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]
+        _SYNTH = lib
+    return _SYNTH
+
+
+def streamed_cubic_batch(seed, first, structures, atoms, side, species, weights, d_min):
+    """Structures [first, first + structures) of a batch of cubic periodic
+    cells whose structure s draws only from the stream of (seed, s)
+    (csrc/synth.c): any slice equals the same range of the whole batch, so a
+    sharded run makes only its own part."""
+    species = np.ascontiguousarray(species, np.int32)
+    weights = np.ascontiguousarray(weights, np.float64)
+    numbers = np.empty(structures * atoms, np.int32)
+    positions = np.empty((structures * atoms, 3), np.float64)
+    rc = _synth_lib().mdsynth_cubic(seed, first, structures, atoms, side, d_min, len(species),
+                                    species.ctypes.data, weights.ctypes.data, numbers.ctypes.data,
+                                    positions.ctypes.data, 1 << 20)
+    if rc != 0:
+        raise RuntimeError("synthetic cell too dense for its minimum distance")
+    cells = np.broadcast_to(np.eye(3) * side, (structures, 3, 3)).copy()
+    pbc = np.ones((structures, 3), np.int32)
+    offsets = np.arange(structures + 1, dtype=np.int64) * atoms
+    return Batch(numbers, positions, cells, pbc, offsets)
+
+
+def config5(structures=65536, seed=None, first=0):
+    """Structures [first, first + structures) of the config-5 batch (65 536
+    periodic 16 A cells x 256 atoms, species 1/6/8 drawn 0.5/0.3/0.2, 0.9 A
+    minimum image distance), per-structure streams (csrc/synth.c)."""
+    return streamed_cubic_batch(SEED_BASE + 5 if seed is None else seed, first, structures, 256, 16.0,
+                                (1, 6, 8), (0.5, 0.3, 0.2), 0.9)
 
 
 GENERATORS = {1: config1, 2: config2, 3: config3, 4: config4, 5: config5}
 
 
-def make(config: int, structures: int | None = None, seed: int | None = None) -> Batch:
+def make(config: int, structures: int | None = None, seed: int | None = None, first: int = 0) -> Batch:
+    """Config `config`'s batch (or its first `structures` structures).  For
+    config 5, `first` selects structures [first, first + structures) of the
+    one seeded batch; the other configs draw a whole batch from one stream
+    and take no offset."""
     generator = GENERATORS[config]
-    return generator(seed=seed) if structures is None else generator(structures=structures, seed=seed)
+    kwargs = {} if structures is None else {"structures": structures}
+    if config == 5:
+        kwargs["first"] = first
+    elif first:
+        raise ValueError("only config 5 supports a structure offset")
+    return generator(seed=seed, **kwargs)

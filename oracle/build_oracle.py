@@ -19,13 +19,24 @@ Two things are built here, neither of which is part of the product:
     container, to run the reference's unchanged Python API when generating
     golden fixtures and when checking the drop-in plugin boundary.
 
-The reference tree is only present in the build container; on a machine
-without it the ``_ref`` step is skipped and the prebuilt files are used.
+* ``baseline/_ref/mdescriptor/`` -- the reference's Python package, staged
+  from ``src/mdescriptor`` with the ``_native`` build above beside it (the
+  offline ``pip install --target baseline/_ref`` of the reference fails here:
+  its build backend needs ``setuptools_scm`` and ``scipy-openblas32``, neither
+  of which is installed).  Its unchanged public API is what the GPU tests and
+  ``bench.py``'s API-path figure drive, with ``MDESCRIPTOR_CUDA_PLUGIN_DIR``
+  pointing at this repository's plugin.  The model weight files are left out
+  (no SOAP path reads them).
+
+The reference tree is only present in the build container, named by the
+``MDSOAP_REFERENCE_ROOT`` environment variable; without it the reference steps
+are skipped (with a message) and the prebuilt files are used.
 """
 
 from __future__ import annotations
 
 import os
+import shutil
 import subprocess
 import sys
 import sysconfig
@@ -34,7 +45,7 @@ from pathlib import Path
 
 ORACLE_DIR = Path(__file__).resolve().parent
 REF_OUT = ORACLE_DIR / "_ref"
-DEFAULT_REFERENCE_ROOT = "/root/reference"
+BASELINE_REF = ORACLE_DIR.parent / "baseline" / "_ref"
 
 # CMakeLists.txt:92-120 (MDESCRIPTOR_CPP_SOURCES)
 _NATIVE_SOURCES = [
@@ -77,8 +88,17 @@ _REF_FLAGS = ["-std=c++17", "-O3", "-DNDEBUG", "-fopenmp", "-fPIC"]
 
 
 def reference_root() -> Path | None:
-    root = Path(os.environ.get("MDSOAP_REFERENCE_ROOT", DEFAULT_REFERENCE_ROOT))
-    return root if (root / "cpp" / "src" / "standalone" / "soap.cpp").is_file() else None
+    """The reference source tree named by MDSOAP_REFERENCE_ROOT, or None when
+    the variable is unset; a set variable that names no reference tree is an
+    error."""
+    value = os.environ.get("MDSOAP_REFERENCE_ROOT")
+    if not value:
+        return None
+    root = Path(value)
+    if not (root / "cpp" / "src" / "standalone" / "soap.cpp").is_file():
+        raise RuntimeError(f"MDSOAP_REFERENCE_ROOT={value} is not a reference source tree "
+                           "(cpp/src/standalone/soap.cpp missing)")
+    return root
 
 
 def _run(cmd: list[str]) -> None:
@@ -146,12 +166,30 @@ def build_ref_native(root: Path, force: bool = False) -> Path:
     return target
 
 
+def stage_reference_package(root: Path, native: Path) -> Path:
+    """Copy the reference's Python package into baseline/_ref with its compiled
+    ``_native`` beside it (weights and caches left out)."""
+    dest = BASELINE_REF / "mdescriptor"
+    if dest.exists():
+        shutil.rmtree(dest)
+    shutil.copytree(root / "src" / "mdescriptor", dest,
+                    ignore=shutil.ignore_patterns("__pycache__", "*.pyc", "*.pt", "nep89*.txt"))
+    # The source placeholder would shadow nothing once the extension sits beside it,
+    # but remove it so that the compiled module is the only candidate.
+    (dest / "_native.py").unlink(missing_ok=True)
+    shutil.copy2(native, dest / native.name)
+    return dest
+
+
 def build_all(force: bool = False) -> None:
     build_c_oracle(force)
     root = reference_root()
-    if root is not None:
-        build_ref_soap(root, force)
-        build_ref_native(root, force)
+    if root is None:
+        print("build_oracle: MDSOAP_REFERENCE_ROOT is unset; using the prebuilt oracle/_ref and baseline/_ref")
+        return
+    build_ref_soap(root, force)
+    native = build_ref_native(root, force)
+    stage_reference_package(root, native)
 
 
 if __name__ == "__main__":

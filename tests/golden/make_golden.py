@@ -29,6 +29,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -156,8 +157,11 @@ def capture_adapter_options(SOAP, StructureBatch, OutputOptions, ExecutionOption
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference-root", default="/root/reference")
+    parser.add_argument("--reference-root", default=os.environ.get("MDSOAP_REFERENCE_ROOT"),
+                        help="reference source tree (default: $MDSOAP_REFERENCE_ROOT)")
     args = parser.parse_args()
+    if not args.reference_root:
+        parser.error("name the reference source tree with --reference-root or MDSOAP_REFERENCE_ROOT")
     root = Path(args.reference_root)
     SOAP, StructureBatch, OutputOptions, ExecutionOptions, basis_gto = import_reference(root)
     from oracle import RefLib

@@ -23,6 +23,7 @@ tolerances (``tolerance`` = rtol, atol).
 from __future__ import annotations
 
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -30,7 +31,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REFERENCE = Path("/root/reference")
+if not os.environ.get("MDSOAP_REFERENCE_ROOT"):
+    raise SystemExit("set MDSOAP_REFERENCE_ROOT to the reference source tree")
+REFERENCE = Path(os.environ["MDSOAP_REFERENCE_ROOT"])
 sys.path.insert(0, str(ROOT))
 
 from mdescriptor_b200 import workloads  # noqa: E402

@@ -303,13 +303,13 @@ def test_multi_device_sharding_matches_single(cuda_device):
     np.testing.assert_array_equal(single, multi)
 
 
-@pytest.mark.parametrize("config,variant", [(c, k) for c in (1, 2, 3, 4) for k in (1, 2, 3)])
+@pytest.mark.parametrize("config,variant", [(c, k) for c in (1, 2, 3, 4) for k in (1, 2)])
 def test_alternative_kernel_variants_match(cuda_device, monkeypatch, config, variant):
-    """Every alternative kernel of a class (selected with MDSOAP_VARIANT: other
-    register-bank splits, the two-warp pair kernels, the all-tensor-core
-    kernel; an index past the class gives the default) matches the default
-    kernel's features within the agreement bound of two fp64 implementations
-    that sum in different orders."""
+    """Every alternative kernel of a class (selected with MDSOAP_VARIANT: the
+    scalar centre kernel where the paired kernel is the default, other
+    register-bank splits; an index past the class gives the default) matches
+    the default kernel's features within the agreement bound of two fp64
+    implementations that sum in different orders."""
     name = f"cfg{config}"
     meta = CFG_META[name]
     batch = batch_from(CFG, f"{name}/input")

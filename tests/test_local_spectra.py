@@ -2,7 +2,7 @@
 SoapPowerSpectrum) on the GPU against the reference's own values.
 
 * the checker is the reference's compiled ``compute_spherical_expansion``
-  (oracle/_ref/pkg/_native), pinned to the reference's own committed goldens
+  (the staged reference package in baseline/_ref), pinned to the reference's own committed goldens
   for this family (its CPU output and the Featomic 0.6.6 external golden);
 * committed fixtures (tests/golden/local_spectra.npz, made by
   tests/golden/make_local_golden.py): the reference goldens and seeded
@@ -26,6 +26,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+from _reference import reference_native
 from _util import F64_FLOOR, F64_TOL, max_rel_err
 from mdescriptor_b200 import workloads
 from mdescriptor_b200.soap import LOCAL_KINDS, local_feature_count, local_spectrum
@@ -34,7 +35,6 @@ LOCAL_TOL, LOCAL_FLOOR = F64_TOL, F64_FLOOR
 
 ROOT = Path(__file__).resolve().parents[1]
 GOLDEN = ROOT / "tests" / "golden" / "local_spectra.npz"
-NATIVE_PKG = ROOT / "oracle" / "_ref" / "pkg"
 NAMES = {v: k for k, v in LOCAL_KINDS.items()}
 
 
@@ -47,33 +47,6 @@ def golden_cases():
 def golden_batch(data, name):
     return workloads.Batch(data[f"{name}/numbers"], data[f"{name}/positions"], data[f"{name}/cells"],
                            data[f"{name}/pbc"], data[f"{name}/offsets"])
-
-
-def reference_native():
-    """The reference's compiled ``_native`` module.  A pybind module loads once
-    per process, so it is imported as ``mdescriptor._native`` wherever the
-    reference package is importable (the plugin-boundary tests import it that
-    way) and as a top-level module elsewhere (the GPU box)."""
-    if not list(NATIVE_PKG.glob("_native*.so")):
-        pytest.skip("reference _native build not present")
-    for key in ("mdescriptor._native", "_native"):
-        if key in sys.modules:
-            return sys.modules[key]
-    reference_src = Path("/root/reference") / "src"
-    if (reference_src / "mdescriptor").is_dir():
-        if str(reference_src) not in sys.path:
-            sys.path.insert(0, str(reference_src))
-        import mdescriptor  # noqa: PLC0415
-
-        if str(NATIVE_PKG) not in mdescriptor.__path__:
-            mdescriptor.__path__.insert(0, str(NATIVE_PKG))
-        from mdescriptor import _native  # noqa: PLC0415
-
-        return _native
-    sys.path.insert(0, str(NATIVE_PKG))
-    import _native  # noqa: PLC0415
-
-    return _native
 
 
 def native_values(nat, b, species, cutoff, width, nr, na, kind):

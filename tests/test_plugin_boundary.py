@@ -8,9 +8,9 @@
   adapter maps (src/mdescriptor/core/errors.py:83-113);
 * building a backend touches no GPU, and computing without one raises
   CudaUnavailable (ImportError) -- never a silent CPU result;
-* when the reference tree and its ``_native`` build are present, the
-  reference's own public API, pointed at the plugin through
-  MDESCRIPTOR_CUDA_PLUGIN_DIR, reaches it and reports device_unavailable.
+* when the reference package is staged (baseline/_ref), the reference's own
+  public API, pointed at the plugin through MDESCRIPTOR_CUDA_PLUGIN_DIR,
+  reaches it and reports device_unavailable.
 """
 
 from __future__ import annotations
@@ -24,11 +24,10 @@ import numpy as np
 import pytest
 
 from _plugin import PLUGIN_DIR, adapter_cases, load_plugin
+from _reference import reference_package
 from mdescriptor_b200 import _lib, workloads
 
 ROOT = Path(__file__).resolve().parents[1]
-REFERENCE = Path("/root/reference")
-NATIVE_PKG = ROOT / "oracle" / "_ref" / "pkg"
 
 
 def test_library_exports_every_declared_symbol():
@@ -131,15 +130,7 @@ def test_labels_follow_declared_species_order():
 
 
 def _reference_api():
-    if not (REFERENCE / "src" / "mdescriptor").is_dir() or not list(NATIVE_PKG.glob("_native*.so")):
-        pytest.skip("reference tree or its _native build not present")
-    if str(REFERENCE / "src") not in sys.path:
-        sys.path.insert(0, str(REFERENCE / "src"))
-    import mdescriptor
-
-    if str(NATIVE_PKG) not in mdescriptor.__path__:
-        mdescriptor.__path__.insert(0, str(NATIVE_PKG))
-    return mdescriptor
+    return reference_package()
 
 
 def test_adapter_options_fixture_matches_live_adapter():
