@@ -5,6 +5,8 @@ Two things are built here, neither of which is part of the product:
 * ``oracle/liboracle_soap.so`` -- the plain-C restatement of the reference's
   SOAP hot path (``oracle/soap_oracle.c``).  It travels with the repository
   snapshot and is what the GPU parity tests and ``smoke()`` check against.
+  ``oracle/liboracle_soap_ext.so`` is the same source with its SOAP stage in
+  extended precision: the exact-value yardstick for float64 parity.
 * ``oracle/_ref/`` -- the reference's own CPU path compiled from its sources
   where they lie (never copied into this repository):
   - ``libref_soap.so``: ``cpp/src/standalone/soap.cpp``,
@@ -115,12 +117,18 @@ def _stale(target: Path, sources: list[Path]) -> bool:
 
 
 def build_c_oracle(force: bool = False) -> Path:
-    """Compile the plain-C restatement (no FMA contraction, like the reference build)."""
+    """Compile the plain-C restatement (no FMA contraction, like the reference
+    build), and the same source with its SOAP stage in x87 extended precision
+    (liboracle_soap_ext.so, -DORACLE_EXTENDED): the exact-value yardstick of
+    the float64 parity tests."""
     source = ORACLE_DIR / "soap_oracle.c"
     target = ORACLE_DIR / "liboracle_soap.so"
+    flags = ["gcc", "-std=c11", "-O2", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared", "-Wall"]
     if force or _stale(target, [source]):
-        _run(["gcc", "-std=c11", "-O2", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared",
-              str(source), "-o", str(target), "-lm"])
+        _run([*flags, str(source), "-o", str(target), "-lm"])
+    extended = ORACLE_DIR / "liboracle_soap_ext.so"
+    if force or _stale(extended, [source]):
+        _run([*flags, "-DORACLE_EXTENDED", str(source), "-o", str(extended), "-lm"])
     return target
 
 

@@ -221,6 +221,17 @@ class OracleLib(_Checker):
         return out
 
 
+class ExtendedLib(OracleLib):
+    """The same restatement with its SOAP stage in x87 extended precision
+    (liboracle_soap_ext.so, built with -DORACLE_EXTENDED): the exact value of
+    the reference's algorithm on the same double graph and constants, up to
+    ~1e-16 relative.  The float64 parity tests measure every double
+    implementation's distance to it."""
+
+    def __init__(self, path: Path | None = None) -> None:
+        super().__init__(path or ORACLE_DIR / "liboracle_soap_ext.so")
+
+
 class RefLib(_Checker):
     """The reference's own CPU path, compiled from its sources into oracle/_ref."""
 

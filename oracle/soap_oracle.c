@@ -19,6 +19,18 @@
  * to the reference's and the features agree to rounding.  Only tests/,
  * __graft_entry__.smoke() and bench.py's CPU-baseline leg load this library;
  * the product never does.
+ *
+ * Extended-precision build (-DORACLE_EXTENDED, liboracle_soap_ext.so): the
+ * SOAP stage -- harmonics, radial factors, neighbour sums, beta transform,
+ * power spectrum, averages -- runs in x87 extended precision (long double,
+ * 64-bit significand, unit roundoff 5.4e-20) on the same double inputs: the
+ * same double neighbour graph (displacements and squared distances), the
+ * same double plan constants (radial prefactors and exponents, harmonic
+ * normalisation, beta, power prefactors) and the same statements.  Its rows
+ * are the exact value of the reference's algorithm for those inputs up to
+ * ~1e-16 relative, 2^11 times closer than any double evaluation: the
+ * yardstick the tests use to measure how far double implementations (the
+ * reference's, this checker's, the GPU's) each stray from it.
  */
 #include <math.h>
 #include <stdint.h>
@@ -27,6 +39,15 @@
 
 #ifdef _OPENMP
 #include <omp.h>
+#endif
+
+/* Arithmetic type of the SOAP stage (see the header comment). */
+#ifdef ORACLE_EXTENDED
+typedef long double oreal;
+#define OEXP expl
+#else
+typedef double oreal;
+#define OEXP exp
 #endif
 
 #define OR_PI 3.141592653589793238462643383279502884
@@ -369,15 +390,15 @@ typedef struct {
 
 /* Real regular solid harmonics r^l Y_lm, layout l^2 + (l-m) = cos m, l^2 + l = m0,
  * l^2 + (l+m) = sin m (soap.cpp:101-216, generic Cartesian recurrence). */
-static void solid_harmonics(const soap_plan* plan, double x, double y, double z, double r2,
-                            double* real, double* imag, double* result) {
+static void solid_harmonics(const soap_plan* plan, oreal x, oreal y, oreal z, oreal r2,
+                            oreal* real, oreal* imag, oreal* result) {
     const int L = plan->l_max, w = plan->width;
     for (int i = 0; i < w * w; ++i) real[i] = imag[i] = 0.0;
     real[0] = 1.0;
     for (int m = 0; m <= L; ++m) {
         if (m > 0) {
             const double factor = -(2.0 * m - 1.0);
-            const double pr = real[(m - 1) * w + (m - 1)], pi = imag[(m - 1) * w + (m - 1)];
+            const oreal pr = real[(m - 1) * w + (m - 1)], pi = imag[(m - 1) * w + (m - 1)];
             real[m * w + m] = factor * (x * pr - y * pi);
             imag[m * w + m] = factor * (x * pi + y * pr);
         }
@@ -483,21 +504,21 @@ static void polynomial_flir(const soap_plan* plan, double radius, double* values
 /* calculate_coefficients (soap.cpp:701-931) for one centre of one structure. */
 static void center_coefficients(const soap_plan* plan, const int* atom_types, int64_t local,
                                 const pair_list* pairs, int64_t pair_begin, int64_t pair_end,
-                                int64_t structure_begin_index, double* coefficients,
-                                double* scratch) {
+                                int64_t structure_begin_index, oreal* coefficients,
+                                oreal* scratch) {
     const int S = plan->n_species, n = plan->n_max, L = plan->l_max, H = plan->harmonics;
     const int w = plan->width;
     const int64_t count = pair_end - pair_begin;
     const int pooled = plan->compression == 1;  /* mu2: one density over all species */
     const int CT = pooled ? 1 : S;
-    memset(coefficients, 0, sizeof(double) * (size_t)CT * n * H);
+    memset(coefficients, 0, sizeof(oreal) * (size_t)CT * n * H);
     /* scratch layout */
     int64_t* order = (int64_t*)scratch;
-    double* harm = scratch + count;                 /* [count][H] */
-    double* weight = harm + count * H;              /* [count] */
-    double* real = weight + count;
-    double* imag = real + w * w;
-    double* hs = imag + w * w;                      /* [2L+1] */
+    oreal* harm = scratch + count;                  /* [count][H] */
+    oreal* weight = harm + count * H;               /* [count] */
+    oreal* real = weight + count;
+    oreal* imag = real + w * w;
+    oreal* hs = imag + w * w;                       /* [2L+1] */
     int64_t type_offsets[65];
     int64_t cursor[64];
     for (int t = 0; t <= S; ++t) type_offsets[t] = 0;
@@ -518,8 +539,8 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
     for (int64_t j = 0; j < count; ++j) {
         const int64_t p = order[j];
         const double* d = pairs->displacements + 3 * p;
-        solid_harmonics(plan, d[0], d[1], d[2], d[0] * d[0] + d[1] * d[1] + d[2] * d[2], real, imag,
-                        harm + j * H);
+        const oreal x = d[0], y = d[1], z = d[2];
+        solid_harmonics(plan, x, y, z, x * x + y * y + z * z, real, imag, harm + j * H);
     }
     for (int64_t j = 0; j < count; ++j) {
         /* NeighborView::exact_self (neighbor.cpp:683-689): the centre itself, image 0 */
@@ -572,13 +593,13 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
                 const int ri = l * n + k;
                 for (int m = 0; m < mc; ++m) hs[m] = 0.0;
                 for (int64_t j = type_offsets[t]; j < type_offsets[t + 1]; ++j) {
-                    const double radial = plan->radial_prefactors[ri]
-                                          * exp(-plan->radial_exponents[ri] * pairs->distance2[order[j]]);
+                    const oreal radial = plan->radial_prefactors[ri]
+                                         * OEXP(-(oreal)plan->radial_exponents[ri] * pairs->distance2[order[j]]);
                     for (int m = 0; m < mc; ++m) hs[m] += radial * harm[j * H + off + m] * weight[j];
                 }
                 for (int nn = 0; nn < n; ++nn) {
                     const double beta = plan->betas[(l * n + nn) * n + k];
-                    double* dest = coefficients + (t * n + nn) * H + off;
+                    oreal* dest = coefficients + (t * n + nn) * H + off;
                     for (int m = 0; m < mc; ++m) dest[m] += plan->soap_scale * beta * hs[m];
                 }
             }
@@ -587,21 +608,21 @@ static void center_coefficients(const soap_plan* plan, const int* atom_types, in
 }
 
 /* power spectrum in every compression layout (soap.cpp:933-1017) */
-static void power_spectrum(const soap_plan* plan, const double* c, double* out) {
+static void power_spectrum(const soap_plan* plan, const oreal* c, oreal* out) {
     const int S = plan->n_species, n = plan->n_max, L = plan->l_max, H = plan->harmonics;
     int64_t f = 0;
     if (plan->compression == 1) { /* mu2: one pooled density, l -> n1 -> n2 >= n1 */
         for (int l = 0; l <= L; ++l)
             for (int n1 = 0; n1 < n; ++n1)
                 for (int n2 = n1; n2 < n; ++n2) {
-                    double sum = 0.0;
+                    oreal sum = 0.0;
                     for (int m = 0; m < 2 * l + 1; ++m) sum += c[n1 * H + l * l + m] * c[n2 * H + l * l + m];
                     out[f++] = plan->power_prefactors[l] * sum;
                 }
         return;
     }
     if (plan->compression == 2) { /* mu1nu1: species x species-summed density, all n2 */
-        double* summed = calloc((size_t)n * H, sizeof(double));
+        oreal* summed = calloc((size_t)n * H, sizeof(oreal));
         for (int t = 0; t < S; ++t)
             for (int k = 0; k < n; ++k)
                 for (int i = 0; i < H; ++i) summed[k * H + i] += c[(t * n + k) * H + i];
@@ -609,7 +630,7 @@ static void power_spectrum(const soap_plan* plan, const double* c, double* out) 
             for (int l = 0; l <= L; ++l)
                 for (int n1 = 0; n1 < n; ++n1)
                     for (int n2 = 0; n2 < n; ++n2) {
-                        double sum = 0.0;
+                        oreal sum = 0.0;
                         for (int m = 0; m < 2 * l + 1; ++m)
                             sum += c[(t * n + n1) * H + l * l + m] * summed[n2 * H + l * l + m];
                         out[f++] = plan->power_prefactors[l] * sum;
@@ -622,7 +643,7 @@ static void power_spectrum(const soap_plan* plan, const double* c, double* out) 
             for (int l = 0; l <= L; ++l)
                 for (int n1 = 0; n1 < n; ++n1)
                     for (int n2 = n1; n2 < n; ++n2) {
-                        double sum = 0.0;
+                        oreal sum = 0.0;
                         for (int m = 0; m < 2 * l + 1; ++m)
                             sum += c[(t * n + n1) * H + l * l + m] * c[(t * n + n2) * H + l * l + m];
                         out[f++] = plan->power_prefactors[l] * sum;
@@ -635,9 +656,9 @@ static void power_spectrum(const soap_plan* plan, const double* c, double* out) 
                 const double pref = plan->power_prefactors[l];
                 for (int n1 = 0; n1 < n; ++n1)
                     for (int n2 = (t1 == t2 ? n1 : 0); n2 < n; ++n2) {
-                        const double* a = c + (t1 * n + n1) * H + l * l;
-                        const double* b = c + (t2 * n + n2) * H + l * l;
-                        double sum = 0.0;
+                        const oreal* a = c + (t1 * n + n1) * H + l * l;
+                        const oreal* b = c + (t2 * n + n2) * H + l * l;
+                        oreal sum = 0.0;
                         for (int m = 0; m < 2 * l + 1; ++m) sum += a[m] * b[m];
                         out[f++] = pref * sum;
                     }
@@ -748,10 +769,10 @@ int oracle_soap_compute_rbf(const int32_t* numbers, const double* positions, con
         pair_list pairs = {0};
         int64_t* counts = malloc(sizeof(int64_t) * ((size_t)atoms + 1));
         int* types = malloc(sizeof(int) * ((size_t)atoms + 1));
-        double* coefficients = malloc(sizeof(double) * (size_t)csize);
-        double* accumulated = calloc((size_t)csize, sizeof(double));
-        double* power = malloc(sizeof(double) * (size_t)F);
-        double* power_sum = calloc((size_t)F, sizeof(double));
+        oreal* coefficients = malloc(sizeof(oreal) * (size_t)csize);
+        oreal* accumulated = calloc((size_t)csize, sizeof(oreal));
+        oreal* power = malloc(sizeof(oreal) * (size_t)F);
+        oreal* power_sum = calloc((size_t)F, sizeof(oreal));
         int local_status = structure_graph(positions, cells + 9 * s, pbc + 3 * s, begin, end, cutoff,
                                            0, NULL, 0, &pairs, counts);
         for (int64_t i = 0; i < atoms && !local_status; ++i) {
@@ -761,11 +782,12 @@ int oracle_soap_compute_rbf(const int32_t* numbers, const double* positions, con
         int64_t max_count = 0;
         for (int64_t i = 0; i < atoms && !local_status; ++i)
             if (counts[i + 1] - counts[i] > max_count) max_count = counts[i + 1] - counts[i];
-        double* scratch = malloc(sizeof(double) * (size_t)(max_count * (plan.harmonics + 3) + 4 * w * w + 64));
+        oreal* scratch = malloc(sizeof(oreal) * (size_t)(max_count * (plan.harmonics + 3) + 4 * w * w + 64));
         for (int64_t i = 0; i < atoms && !local_status; ++i) {
             center_coefficients(&plan, types, i, &pairs, counts[i], counts[i + 1], 0, coefficients, scratch);
             if (average == 0) {
-                power_spectrum(&plan, coefficients, out + (begin + i) * F);
+                power_spectrum(&plan, coefficients, power);
+                for (int64_t k = 0; k < F; ++k) out[(begin + i) * F + k] = (double)power[k];
             } else if (average == 1) {
                 for (int64_t k = 0; k < csize; ++k) accumulated[k] += coefficients[k];
             } else {
@@ -778,9 +800,10 @@ int oracle_soap_compute_rbf(const int32_t* numbers, const double* positions, con
                 const double inverse = 1.0 / (double)atoms;
                 for (int64_t k = 0; k < csize; ++k) accumulated[k] *= inverse;
             }
-            power_spectrum(&plan, accumulated, out + s * F);
+            power_spectrum(&plan, accumulated, power);
+            for (int64_t k = 0; k < F; ++k) out[s * F + k] = (double)power[k];
         } else if (!local_status && average == 2) {
-            for (int64_t k = 0; k < F; ++k) out[s * F + k] = atoms > 0 ? power_sum[k] / (double)atoms : 0.0;
+            for (int64_t k = 0; k < F; ++k) out[s * F + k] = atoms > 0 ? (double)(power_sum[k] / (double)atoms) : 0.0;
         }
         free(scratch);
         free(counts);
@@ -914,12 +937,15 @@ int oracle_soap_rows(const int32_t* numbers, const double* positions, const doub
         int64_t max_count = 0;
         for (int64_t i = 0; i < wanted && !status; ++i)
             if (counts[i + 1] - counts[i] > max_count) max_count = counts[i + 1] - counts[i];
-        double* coefficients = malloc(sizeof(double) * (size_t)csize);
-        double* scratch = malloc(sizeof(double) * (size_t)(max_count * (plan.harmonics + 3) + 4 * w * w + 64));
+        oreal* coefficients = malloc(sizeof(oreal) * (size_t)csize);
+        oreal* power = malloc(sizeof(oreal) * (size_t)F);
+        oreal* scratch = malloc(sizeof(oreal) * (size_t)(max_count * (plan.harmonics + 3) + 4 * w * w + 64));
         for (int64_t i = 0; i < wanted && !status; ++i) {
             center_coefficients(&plan, types, subset[i], &pairs, counts[i], counts[i + 1], 0, coefficients, scratch);
-            power_spectrum(&plan, coefficients, out + slot[i] * F);
+            power_spectrum(&plan, coefficients, power);
+            for (int64_t k = 0; k < F; ++k) out[slot[i] * F + k] = (double)power[k];
         }
+        free(power);
         free(scratch);
         free(coefficients);
         free(counts);

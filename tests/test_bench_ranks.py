@@ -1,9 +1,9 @@
 """bench.py's multi-rank logic on CPU: world_size-2 ``gloo`` ranks.
 
-The SOAP path shards by structure with no data exchange, so the only
-collectives are the barrier and the max / sum reductions around the timed
-regions; these tests run exactly those helpers on two processes, plus the
-reference arm's "rank 0 alone works" rule.
+The SOAP path shards one batch by structure with no data exchange, so the
+only collectives are the barrier and the max / sum reductions around the
+timed regions; these tests run exactly those helpers on two processes, plus
+the shard arithmetic and the reference arm's "rank 0 alone works" rule.
 """
 
 from __future__ import annotations
@@ -39,7 +39,7 @@ def _worker(rank, world, port, queue):
         total_ms = ranks.max(local_ms)
         atoms_all = ranks.sum(local_atoms)
         value = bench.job_throughput(atoms_all, 4, total_ms)
-        queue.put((rank, ranks.world, total_ms, atoms_all, value, bench.rank_seed(2, rank)))
+        queue.put((rank, ranks.world, total_ms, atoms_all, value, bench.shard_range(65536, rank, world)))
     finally:
         ranks.close()
 
@@ -62,7 +62,37 @@ def test_two_gloo_ranks_take_max_time_and_sum_units():
     assert t0 == t1 == 20.0                       # max over ranks
     assert a0 == a1 == 228                        # units of all ranks
     assert v0 == v1 == pytest.approx(228 * 4 / 0.020)
-    assert s0 != s1                               # each rank owns its own batch
+    assert s0 == (0, 32768) and s1 == (32768, 65536)  # one batch, contiguous shards
+
+
+def test_shards_cover_the_batch_once_and_slice_the_one_seeded_batch():
+    import numpy as np
+
+    from mdescriptor_b200 import workloads
+
+    for world in (1, 2, 3, 4, 8):
+        ranges = [bench.shard_range(65536, r, world) for r in range(world)]
+        assert ranges[0][0] == 0 and ranges[-1][1] == 65536
+        assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+    whole = workloads.make(5, 12)
+    for world in (2, 3):
+        parts = [bench.shard_batch(5, 12, r, world) for r in range(world)]
+        np.testing.assert_array_equal(np.concatenate([p.positions for p in parts]), whole.positions)
+        np.testing.assert_array_equal(np.concatenate([p.numbers for p in parts]), whole.numbers)
+    small = [bench.shard_batch(1, 8, r, 2) for r in range(2)]
+    np.testing.assert_array_equal(np.concatenate([p.positions for p in small]), workloads.make(1, 8).positions)
+
+
+def test_e2e_slice_respects_the_host_budget(monkeypatch):
+    from mdescriptor_b200 import workloads
+
+    batch = workloads.make(5, 64)
+    monkeypatch.setattr(bench, "host_memory_available", lambda: 64 << 30)
+    row_bytes = 256 * 2100 * 4  # one structure's float32 rows
+    assert bench.e2e_structures(batch, row_bytes, 1) == 64          # the whole shard fits
+    assert bench.e2e_structures(batch, row_bytes, 1, cap_bytes=10 * row_bytes) == 10
+    monkeypatch.setattr(bench, "host_memory_available", lambda: 4 * 8 * 5 * row_bytes)
+    assert bench.e2e_structures(batch, row_bytes, 8) == 5            # a quarter of the host, shared by 8 ranks
 
 
 def test_single_process_ranks_are_identity():
@@ -70,8 +100,9 @@ def test_single_process_ranks_are_identity():
         os.environ.pop(key, None)
     ranks = bench.Ranks("gloo")
     assert (ranks.rank, ranks.world, ranks.group) == (0, 1, None)
-    assert ranks.max(3.5) == 3.5 and ranks.sum(7) == 7.0
+    assert ranks.max(3.5) == 3.5 and ranks.sum(7) == 7.0 and ranks.min(2.0) == 2.0
     ranks.barrier()
+    ranks.host_barrier()
     ranks.close()
 
 
