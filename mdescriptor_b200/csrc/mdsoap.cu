@@ -2184,7 +2184,7 @@ int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* 
         struct DrainGuard {
             cudaStream_t s;
             ~DrainGuard() { cudaStreamSynchronize(s); }
-        } drain{stream};
+        } drain_guard{stream};
         PinnedBytes* stage = staging.stage;
         DeviceBytes* rowbuf[2] = {&rows, &rows2};
         rows.reserve(block_bytes, "local rows");
