@@ -487,9 +487,14 @@ def api_path_throughput(cfg, batch, steps, local, ranks, sampler):
     if str(ref) not in sys.path:
         sys.path.insert(0, str(ref))
     from mdescriptor import ExecutionOptions, OutputOptions, StructureBatch
+    from mdescriptor._cuda_loader import load_cuda_plugin
     from mdescriptor.descriptors import SOAP
 
     import torch
+
+    # The reference loads its CUDA plugin on request (its own tests and
+    # benchmarks call this loader, which honours MDESCRIPTOR_CUDA_PLUGIN_DIR).
+    load_cuda_plugin()
 
     sb = StructureBatch(batch.numbers, batch.positions, batch.cells, batch.pbc, batch.offsets,
                         tuple(f"s{i}" for i in range(batch.structures)))

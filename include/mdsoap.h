@@ -269,6 +269,16 @@ const char* mdsoap_plan_kernel(const mdsoap_plan* plan);
  * reference, whose CPU path calls std::exp, soap.cpp:895-896). */
 int mdsoap_probe_exp(int32_t device, const double* x, int64_t count, double* ours, double* cuda_exp);
 
+/* Failure-detection probe (test support; no counterpart in the reference):
+ * launches one thread that arms an mbarrier for a bulk copy it never issues
+ * and waits for it with the tail kernel's own bounded wait (limit_ns, at most
+ * 2 s).  The wait runs out, the kernel sets the tail-timeout bit of its error
+ * word and returns; the call then reports MDSOAP_INTERNAL ("tail kernel: a
+ * coefficient block copy did not complete in time"), as mdsoap_compute does
+ * when a real copy stalls.  Nothing is left in flight, so the device stays
+ * usable.  MDSOAP_OK would mean the wait did not run out. */
+int mdsoap_probe_bounded_wait(int32_t device, uint64_t limit_ns);
+
 /* Measured fp64 FMA throughput of `device` in TFLOP/s (2 flops per FMA) from a
  * register-resident FMA chain kernel over every SM (measurement support; no
  * counterpart in the reference).  Used as the roofline denominator of the

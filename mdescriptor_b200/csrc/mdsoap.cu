@@ -11,6 +11,7 @@
 #include "local_spectra.cuh"
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <atomic>
@@ -65,6 +66,30 @@ std::string device_error_text(unsigned bits) {
     return "device error";
 }
 
+// Injected allocation failure, for the out-of-memory tests: with
+// MDSOAP_TEST_FAIL_ALLOC=<bytes> set, every engine device allocation of at
+// least that many bytes returns cudaErrorMemoryAllocation without calling
+// cudaMalloc, so the OUT_OF_MEMORY path (status, plugin exception, adapter
+// error code) is exercised on the host, with no real exhaustion of a GPU.
+cudaError_t engine_malloc(void** ptr, size_t bytes) {
+    if (const char* env = std::getenv("MDSOAP_TEST_FAIL_ALLOC")) {
+        const long long limit = std::atoll(env);
+        if (limit > 0 && bytes >= (size_t)limit) {
+            *ptr = nullptr;
+            return cudaErrorMemoryAllocation;
+        }
+    }
+    return cudaMalloc(ptr, bytes);
+}
+
+// Host-side NVTX range (upload, binning, expansion, tail, D2H), closed at scope exit.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
+
 // Grow-only device buffer.
 struct DeviceBytes {
     void* ptr = nullptr;
@@ -75,7 +100,7 @@ struct DeviceBytes {
         ptr = nullptr;
         size = 0;
         const size_t rounded = std::max<size_t>(bytes + bytes / 8, 256);
-        check(cudaMalloc(&ptr, rounded), what);
+        check(engine_malloc(&ptr, rounded), what);
         size = rounded;
     }
     template <class T>
@@ -290,6 +315,21 @@ __global__ void exp_probe_kernel(const double* __restrict__ x, int64_t count, do
     }
 }
 
+// The tail kernel's bounded wait made to run out: one thread arms an mbarrier
+// for 16 bytes of copies and issues none, so the phase cannot complete; the
+// wait (bulk::wait, the tail kernel's own) gives up after limit_ns and the
+// kernel sets kErrTailTimeout, exactly as the tail kernel does.  No copy is
+// ever in flight, so the shared memory is free when the CTA exits.
+__global__ void bounded_wait_probe_kernel(unsigned* error, uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        bulk::barrier_init(&bar, 1);
+        bulk::barrier_init_fence();
+        bulk::arrive_expect(&bar, 16u);
+        if (!bulk::wait(&bar, 0u, limit_ns)) atomicOr(error, kErrTailTimeout);
+    }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -458,6 +498,7 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
 
 void mdsoap_plan::bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream, unsigned* error) {
     if (b.structures == 0) return;
+    NvtxRange range("mdsoap bin");
     st.work.reserve_bins(b.atoms, b.structures);
     bin_structures_kernel<<<(unsigned)b.structures, 256, 0, stream>>>(b, st.work.bins(error), cutoff,
                                                                        st.species.as<int32_t>(), n_species);
@@ -504,13 +545,17 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             p.grid_end = std::min(a1, c0 + chunk);
             int64_t grid = (p.grid_end - c0 + kWarps - 1) / kWarps;
             if (st.center_grid > 0) grid = std::min(grid, st.center_grid);
-            variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
-            check(cudaGetLastError(), "centre kernel launch");
+            {
+                NvtxRange range("mdsoap expansion");
+                variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
+                check(cudaGetLastError(), "centre kernel launch");
+            }
             // With one chunk, the event splits the timing into expansion and tail.
             if (after_expansion && c0 == a0 && p.grid_end == a1)
                 check(cudaEventRecord(after_expansion, stream), "timing event");
             // Persistent tail: the resident CTAs stride over the block's centres.
             const int64_t tail_ctas = std::min<int64_t>(p.grid_end - c0, std::max<int64_t>(st.tail_grid, 1));
+            NvtxRange range("mdsoap tail");
             (tab.split_tail == 2 ? variant->tail_generic : variant->tail)(dim3((unsigned)tail_ctas), tail_smem,
                                                                           stream, tab, p);
             check(cudaGetLastError(), "tail kernel launch");
@@ -526,6 +571,7 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         if (centers > 0) {
             int64_t grid = (centers + kWarps - 1) / kWarps;
             if (variant->paired && st.center_grid > 0) grid = std::min(grid, st.center_grid);
+            NvtxRange range("mdsoap expansion");
             variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
             check(cudaGetLastError(), "centre kernel launch");
             launches.fetch_add(1, std::memory_order_relaxed);
@@ -647,6 +693,7 @@ void mdsoap_plan::shard_compute(int device, const mdsoap_batch& batch, int64_t s
     std::vector<int64_t> offsets(structures + 1);
     for (int64_t s = 0; s <= structures; ++s) offsets[s] = batch.offsets[s0 + s] - a_begin;
     cudaStream_t cs = st.compute;
+    NvtxRange upload_range("mdsoap upload");
     if (atoms > 0) {
         check(cudaMemcpyAsync(w.numbers.ptr, batch.numbers + a_begin, 4 * atoms, cudaMemcpyHostToDevice, cs), "H2D numbers");
         check(cudaMemcpyAsync(w.positions.ptr, batch.positions + 3 * a_begin, 24 * atoms, cudaMemcpyHostToDevice, cs),
@@ -713,10 +760,12 @@ void mdsoap_plan::shard_compute(int device, const mdsoap_batch& batch, int64_t s
         check(cudaEventRecord(st.computed[i % 2], cs), "record compute");
         if (i >= 1) finish(i - 1);
         check(cudaStreamWaitEvent(st.copy, st.computed[i % 2], 0), "wait compute");
-        if (bytes)
+        if (bytes) {
+            NvtxRange range("mdsoap D2H");
             check(cudaMemcpyAsync(direct ? dst : st.staging[i % 2].ptr, st.out[i % 2].ptr, bytes, cudaMemcpyDeviceToHost,
                                   st.copy),
                   "D2H output");
+        }
         check(cudaEventRecord(st.copied[i % 2], st.copy), "record copy");
         pending[i] = {bytes, dst};
     }
@@ -1602,6 +1651,33 @@ int mdsoap_probe_exp(int32_t device, const double* x, int64_t count, double* our
         return MDSOAP_OK;
     } catch (const Failure& f) {
         return fail(f.status, f.message);
+    }
+}
+
+int mdsoap_probe_bounded_wait(int32_t device, uint64_t limit_ns) {
+    if (limit_ns == 0 || limit_ns > 2000000000ull)
+        return fail(MDSOAP_INVALID_ARGUMENT, "limit_ns must be in (0, 2 s]");
+    try {
+        int devices = 0;
+        if (cudaGetDeviceCount(&devices) != cudaSuccess || device < 0 || device >= devices)
+            raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device unavailable");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        DeviceBytes word;
+        word.reserve(sizeof(unsigned), "error word");
+        check(cudaMemset(word.ptr, 0, sizeof(unsigned)), "clear error word");
+        bounded_wait_probe_kernel<<<1, 32>>>(word.as<unsigned>(), limit_ns);
+        check(cudaGetLastError(), "probe launch");
+        unsigned bits = 0;
+        check(cudaMemcpy(&bits, word.ptr, sizeof(unsigned), cudaMemcpyDeviceToHost), "read error word");
+        if (bits)
+            return fail(bits & (kErrUnknownSpecies | kErrMixedPbc | kErrSingularCell) ? MDSOAP_INVALID_ARGUMENT
+                                                                                      : MDSOAP_INTERNAL,
+                        device_error_text(bits));
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
     }
 }
 

@@ -19,7 +19,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from _plugin import PLUGIN_DIR, load_plugin
+from _plugin import PLUGIN_DIR
 from _reference import reference_package
 from _util import assert_features_close
 from mdescriptor_b200 import workloads
@@ -41,10 +41,14 @@ def api(monkeypatch, cuda_device):
     reference_package()
     monkeypatch.setenv("MDESCRIPTOR_CUDA_PLUGIN_DIR", str(PLUGIN_DIR))
     monkeypatch.setenv("MDSOAP_DEVICES", str(cuda_device))
-    load_plugin()
     import mdescriptor
     from mdescriptor import ExecutionOptions, OutputOptions, StructureBatch
+    from mdescriptor._cuda_loader import load_cuda_plugin
     from mdescriptor.descriptors import SOAP
+
+    # The reference's own loader (what its tests and benchmarks call); it
+    # accepts a plugin already imported from the same directory.
+    assert load_cuda_plugin() == PLUGIN_DIR.resolve()
 
     return mdescriptor, SOAP, StructureBatch, OutputOptions, ExecutionOptions
 
