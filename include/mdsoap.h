@@ -246,9 +246,10 @@ int mdsoap_plan_last_timing(mdsoap_plan* plan, int32_t device, double* bin_ms, d
                             double* structure_ms);
 
 /* The centre time of the last timed call split into the expansion kernel and
- * the separate tail kernel (beta transform + power spectrum) that n_max = 8
- * plans launch after it; tail_ms is 0 when the plan runs a fused tail
- * (measurement support; no counterpart in the reference). */
+ * the separate tail kernel (beta transform + power spectrum) that split-tail
+ * plans launch after it, each summed over the chunks of centres the call ran
+ * as expansion / tail launch pairs; tail_ms is 0 when the plan runs a fused
+ * tail (measurement support; no counterpart in the reference). */
 int mdsoap_plan_last_timing_split(mdsoap_plan* plan, int32_t device, double* expansion_ms, double* tail_ms);
 
 /* Number of kernels the plan has launched so far, over all devices and entry

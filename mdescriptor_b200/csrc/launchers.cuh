@@ -133,6 +133,18 @@ const void* structure_symbol() {
     template void tail_generic<L>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);           \
     template const void* tail_generic_symbol<L>();
 
+// Expansion kernels and the register tail with T species register banks
+// (plans with fewer species than the default four banks).
+#define MDSOAP_INSTANTIATE_PAIRED_BANKS(T, L)                                                                     \
+    template void paired<T, L, false, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);    \
+    template void paired<T, L, true, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);     \
+    template const void* paired_symbol<T, L, false, 2>();                                                         \
+    template const void* paired_symbol<T, L, true, 2>();                                                          \
+    template const void* paired_split_symbol<T, L, false, 2>();                                                   \
+    template const void* paired_split_symbol<T, L, true, 2>();                                                    \
+    template void tail<L, T>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);                \
+    template const void* tail_symbol<L, T>();
+
 #endif  // MDSOAP_LAUNCH_DEFINITIONS
 
 }  // namespace launch

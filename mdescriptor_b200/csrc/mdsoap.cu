@@ -233,6 +233,8 @@ const Variant kPairedVariants[] = {
     MDSOAP_PAIRED_VARIANT(4, 4, false, 2), MDSOAP_PAIRED_VARIANT(4, 4, true, 2),
     MDSOAP_PAIRED_VARIANT(4, 5, false, 2), MDSOAP_PAIRED_VARIANT(4, 5, true, 2),
     MDSOAP_PAIRED_VARIANT(4, 6, false, 2), MDSOAP_PAIRED_VARIANT(4, 6, true, 2),
+    // Fewer register banks for plans with fewer species (fewer registers).
+    MDSOAP_PAIRED_VARIANT(3, 6, false, 2), MDSOAP_PAIRED_VARIANT(3, 6, true, 2),
 };
 
 #define MDSOAP_POLY_VARIANT(T, L)                                                                            \
@@ -254,11 +256,20 @@ const Variant* poly_variant(int n_max, int l_max) {
     return nullptr;
 }
 
-const Variant* paired_variant(int n_max, int l_max, bool precise) {
+// The paired kernel for (n_max, l_max) with the fewest species register banks
+// that still hold all `species` of the coefficient block in one pass (the
+// four-bank kernel, in several passes, beyond that).
+const Variant* paired_variant(int n_max, int l_max, bool precise, int species) {
     if (n_max > 8 || n_max * (1 + (l_max + 1) / 2) > 32) return nullptr;
-    for (const Variant& v : kPairedVariants)
-        if (v.lmax == l_max && v.precise == precise) return &v;
-    return nullptr;
+    const Variant* best = nullptr;
+    for (const Variant& v : kPairedVariants) {
+        if (v.lmax != l_max || v.precise != precise) continue;
+        const bool fits = v.maxt >= species;
+        if (!best) best = &v;
+        else if (fits && (best->maxt < species || v.maxt < best->maxt)) best = &v;
+        else if (!fits && best->maxt < species && v.maxt > best->maxt) best = &v;
+    }
+    return best;
 }
 
 int variant_class(int n_max, int l_max) {
@@ -347,9 +358,13 @@ struct DeviceState {
     bool smem_configured = false;
     int64_t tail_grid = 0;    // persistent tail kernel: resident CTAs on this device
     int64_t center_grid = 0;  // paired kernel: resident CTAs on this device (0: one CTA per kWarps centres)
-    cudaEvent_t timing[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // bin | centre | tail | structure
+    cudaEvent_t timing[4] = {nullptr, nullptr, nullptr, nullptr};  // bin | centre | tail | structure
     bool timed = false;  // the last device call recorded the timing events
-    bool split_timed = false;  // ... including the event between the expansion and tail kernels
+    // Split-tail plans: per chunk of centres, an event after its expansion
+    // launch and one after its tail launch (the timed call used the first
+    // split_marks of them).
+    std::vector<cudaEvent_t> marks;
+    size_t split_marks = 0;
     std::mutex mutex;
 
     ~DeviceState() {
@@ -371,6 +386,8 @@ struct DeviceState {
         for (auto& e : copied)
             if (e) cudaEventDestroy(e);
         for (auto& e : timing)
+            if (e) cudaEventDestroy(e);
+        for (auto& e : marks)
             if (e) cudaEventDestroy(e);
         if (compute) cudaStreamDestroy(compute);
         if (copy) cudaStreamDestroy(copy);
@@ -406,7 +423,7 @@ struct mdsoap_plan {
     void bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream, unsigned* error);
     void run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, int64_t s1, int64_t a0, int64_t a1,
                    void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center = nullptr,
-                   cudaEvent_t after_expansion = nullptr);
+                   bool mark_chunks = false);
     void shard_compute(int device, const mdsoap_batch& batch, int64_t s0, int64_t s1, char* out,
                        mdsoap_cancel_fn cancel, void* ctx, std::atomic<bool>& stop);
 };
@@ -510,7 +527,7 @@ void mdsoap_plan::bin(DeviceState& st, const DeviceBatch& b, cudaStream_t stream
 // at the block's first row.
 void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, int64_t s1, int64_t a0, int64_t a1,
                             void* out, cudaStream_t stream, unsigned* error, cudaEvent_t after_center,
-                            cudaEvent_t after_expansion) {
+                            bool mark_chunks) {
     const int64_t centers = a1 - a0;
     const int64_t csize = tab.csize;
     SoapPointers p{};
@@ -540,6 +557,17 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         const int64_t chunk = std::min<int64_t>(centers, tail_chunk);
         st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(chunk, 1) * tab.rsize, "coefficient scratch");
         p.rbuf = st.work.rbuf.as<double>();
+        st.split_marks = 0;
+        // Timing: an event after each expansion launch and after each tail launch.
+        auto mark = [&]() {
+            if (!mark_chunks) return;
+            if (st.split_marks == st.marks.size()) {
+                cudaEvent_t e = nullptr;
+                check(cudaEventCreate(&e), "timing event");
+                st.marks.push_back(e);
+            }
+            check(cudaEventRecord(st.marks[st.split_marks++], stream), "timing event");
+        };
         for (int64_t c0 = a0; c0 < a1; c0 += chunk) {
             p.grid_begin = c0;
             p.grid_end = std::min(a1, c0 + chunk);
@@ -550,15 +578,14 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
                 variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
                 check(cudaGetLastError(), "centre kernel launch");
             }
-            // With one chunk, the event splits the timing into expansion and tail.
-            if (after_expansion && c0 == a0 && p.grid_end == a1)
-                check(cudaEventRecord(after_expansion, stream), "timing event");
+            mark();
             // Persistent tail: the resident CTAs stride over the block's centres.
             const int64_t tail_ctas = std::min<int64_t>(p.grid_end - c0, std::max<int64_t>(st.tail_grid, 1));
             NvtxRange range("mdsoap tail");
             (tab.split_tail == 2 ? variant->tail_generic : variant->tail)(dim3((unsigned)tail_ctas), tail_smem,
                                                                           stream, tab, p);
             check(cudaGetLastError(), "tail kernel launch");
+            mark();
             launches.fetch_add(2, std::memory_order_relaxed);
         }
         p.grid_begin = a0;
@@ -986,7 +1013,9 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                 radial_normal = false;
         }
         const Variant* paired = polynomial ? poly_variant(n, L)
-                                : radial_normal ? paired_variant(n, L, q.output_dtype == MDSOAP_FLOAT64)
+                                : radial_normal ? paired_variant(n, L, q.output_dtype == MDSOAP_FLOAT64,
+                                                                 q.compression == MDSOAP_COMPRESSION_MU2 ? 1
+                                                                                                         : q.n_species)
                                                 : nullptr;
         const char* env = std::getenv("MDSOAP_VARIANT");
         const int want = env ? std::atoi(env) : -1;
@@ -1073,16 +1102,16 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             *plan_out = plan.release();
             return MDSOAP_OK;
         }
-        if (needs_paired)
+        if (polynomial)
             return fail(MDSOAP_INVALID_ARGUMENT,
-                        "SOAP weighting, compression and the polynomial radial basis run on the paired-channel "
-                        "kernel, which needs n_max <= 8, n_max (1 + (l_max + 1) / 2) <= 32 and l_max <= 6");
+                        "the SOAP polynomial radial basis runs on the paired-channel kernel, which needs "
+                        "n_max <= 8, n_max (1 + (l_max + 1) / 2) <= 32 and l_max <= 6");
         const Variant& sv = *picked;
         plan->variant = &sv;
         const int ns = (sv.l0 > 0) + (sv.l1 > 0) + (sv.l2 > 0);
         const int slots = (t.items + 31) / 32;
         t.slot_groups = (slots + ns - 1) / ns;
-        t.type_groups = (q.n_species + sv.maxt - 1) / sv.maxt;
+        t.type_groups = (coef_species + sv.maxt - 1) / sv.maxt;
         const bool single_pass = t.slot_groups == 1 && t.type_groups == 1;
         // One-warp scalar kernels with n_max <= 8 finish on the tensor cores:
         // row-strided coefficient block, padded 8 x 8 beta table in shared memory.
@@ -1091,13 +1120,14 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         t.beta_in_smem = mma_tail || beta_bytes <= 32768;
         // CTA-shared: 32-entry exp table (256 B) + optional beta copy.
         const size_t beta_smem = 256 + (t.beta_in_smem ? ((beta_bytes + 15) & ~(size_t)15) : 0);
-        t.csize = q.n_species * n * W * (W + 1);
+        t.csize = coef_species * n * W * (W + 1);
         t.hp = W * (W + 1);
         t.rs = mma_tail ? mma::row_stride(L) : 0;
-        t.rsize = mma_tail ? q.n_species * n * t.rs : t.csize;
+        t.rsize = mma_tail ? coef_species * n * t.rs : t.csize;
         t.n_magic = n == 1 ? 0u : (uint32_t)((1ull << 32) / (uint64_t)n + 1ull);
         const size_t r_bytes = (size_t)t.rsize * 8;
-        const size_t pend = kRegionHeader + (size_t)kPending * 36;
+        // Pending edges: dx dy dz r2 weight (doubles) + species (int32).
+        const size_t pend = kRegionHeader + (size_t)kPending * 44;
         auto region_a = [&](int chunk) { return pend + ((size_t)chunk * t.hp + 48) * 8; };
         auto align16 = [](size_t x) { return (x + 15) & ~(size_t)15; };
         auto per_warp = [&](int chunk, bool r_in_smem) {
@@ -1234,9 +1264,9 @@ int mdsoap_compute_device(mdsoap_plan* plan, const mdsoap_batch* batch, void* ou
         if (timed) check(cudaEventRecord(st.timing[1], s), "timing event");
         // Structure ranges are only needed for the averages; the device batch
         // is one block.
-        st.split_timed = timed && plan->tab.split_tail && plan->tail_chunk >= batch->atoms;
+        st.split_marks = 0;
         plan->run_block(st, db, 0, batch->structures, 0, batch->atoms, out, s, error, timed ? st.timing[2] : nullptr,
-                        timed ? st.timing[4] : nullptr);
+                        timed);
         if (timed) check(cudaEventRecord(st.timing[3], s), "timing event");
         st.timed = timed;
         return MDSOAP_OK;
@@ -1609,12 +1639,23 @@ int mdsoap_plan_last_timing_split(mdsoap_plan* plan, int32_t device, double* exp
         if (!st.timed) return fail(MDSOAP_INVALID_ARGUMENT, "no timed device call on this device");
         check(cudaSetDevice(device), "cudaSetDevice");
         check(cudaEventSynchronize(st.timing[3]), "timing sync");
-        float a = 0, b = 0;
-        if (st.split_timed) {
-            check(cudaEventElapsedTime(&a, st.timing[1], st.timing[4]), "elapsed");
-            check(cudaEventElapsedTime(&b, st.timing[4], st.timing[2]), "elapsed");
+        double a = 0, b = 0;
+        if (st.split_marks >= 2) {
+            // Chunk i: expansion from the previous mark (the centre-phase start
+            // for the first chunk) to marks[2i], tail from marks[2i] to marks[2i+1].
+            cudaEvent_t prev = st.timing[1];
+            for (size_t i = 0; i + 1 < st.split_marks; i += 2) {
+                float x = 0, y = 0;
+                check(cudaEventElapsedTime(&x, prev, st.marks[i]), "elapsed");
+                check(cudaEventElapsedTime(&y, st.marks[i], st.marks[i + 1]), "elapsed");
+                a += x;
+                b += y;
+                prev = st.marks[i + 1];
+            }
         } else {
-            check(cudaEventElapsedTime(&a, st.timing[1], st.timing[2]), "elapsed");
+            float x = 0;
+            check(cudaEventElapsedTime(&x, st.timing[1], st.timing[2]), "elapsed");
+            a = x;
         }
         if (expansion_ms) *expansion_ms = a;
         if (tail_ms) *tail_ms = b;

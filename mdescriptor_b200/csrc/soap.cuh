@@ -373,7 +373,7 @@ __device__ __forceinline__ void power_spectrum_warp(const SoapTables& tab, const
 template <int NMAX>
 __device__ __forceinline__ void beta_transform_warp(const SoapTables& tab, const double* __restrict__ beta,
                                                     double* __restrict__ R, int lane, int nthreads = 32) {
-    const int S = tab.n_species, n = tab.n_max, L = tab.l_max;
+    const int S = tab.coef_species, n = tab.n_max, L = tab.l_max;
     for (int l = 0; l <= L; ++l) {
         const int len = 2 * l + 1, pad = 2 * l + 2;
         const int cols = S * len;
@@ -515,7 +515,12 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     extern __shared__ __align__(16) unsigned char smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int S = tab.n_species, n = tab.n_max, H = tab.hp;
+    // S: species of the coefficient block (1 when mu2 pools them all into one
+    // density, soap.cpp:613-615); per-edge weights when a weighting function,
+    // w0 or the mu2 pooling asks for them (soap_weight, soap.cpp:389-420).
+    const int S = tab.coef_species, n = tab.n_max, H = tab.hp;
+    const bool pooled = tab.compression == 1;
+    const bool weighted = tab.weighted != 0;
     const int beta_count = (tab.l_max + 1) * n * n;
     // CTA-shared: exp table (32 doubles), then beta (optional).
     double* etab = reinterpret_cast<double*>(smem);
@@ -551,7 +556,8 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     double* pdz = pdy + kPending;
     double* pr2 = pdz + kPending;
     int32_t* ptype = reinterpret_cast<int32_t*>(pr2 + kPending);
-    double* ybuf = reinterpret_cast<double*>(region + kRegionHeader + kPending * 36);
+    double* pw = reinterpret_cast<double*>(region + kRegionHeader + kPending * 36);
+    double* ybuf = reinterpret_cast<double*>(region + kRegionHeader + kPending * 44);
     const int64_t local = center - p.center_begin;
     double* R = tab.r_global ? p.rbuf + local * tab.rsize : reinterpret_cast<double*>(region + tab.r_offset);
 
@@ -644,21 +650,22 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     constexpr int TT = decltype(bank)::value;
                     const int end = run_start[TT + 1];
                     if (run_start[TT] == end) return;
-                    const double w = tab.species_weight[tb + TT];
+                    // The pooled density carries each edge's species weight.
+                    const double w = pooled ? 1.0 : tab.species_weight[tb + TT];
                     int i = run_start[TT];
                     // Two edges per step: more independent exp() chains in flight.
                     for (; i + 1 < end; i += 2) {
                         const int ea = perm[i], eb = perm[i + 1];
                         double ga0, ga1, ga2, gb0, gb1, gb2;
-                        radial(ea, w, ga0, ga1, ga2);
-                        radial(eb, w, gb0, gb1, gb2);
+                        radial(ea, weighted ? w * pw[ea] : w, ga0, ga1, ga2);
+                        radial(eb, weighted ? w * pw[eb] : w, gb0, gb1, gb2);
                         accumulate(bank, ga0, ga1, ga2, ea * H);
                         accumulate(bank, gb0, gb1, gb2, eb * H);
                     }
                     if (i < end) {
                         const int ea = perm[i];
                         double ga0, ga1, ga2;
-                        radial(ea, w, ga0, ga1, ga2);
+                        radial(ea, weighted ? w * pw[ea] : w, ga0, ga1, ga2);
                         accumulate(bank, ga0, ga1, ga2, ea * H);
                     }
                 });
@@ -669,14 +676,19 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             for_each_candidate_flat(si, bv, center, lane, seg_prefix, seg_start, seg_t,
                                     [&](bool valid, int j, int tx, int ty, int tz) {
                 int nimg[3];
-                double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0;
+                double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0, ew = 1.0;
                 int t = -1;
                 bool ok = false;
                 if (valid) {
                     t = bv.type[si.atom_begin + j];
-                    if (t >= tb && t < te)
+                    if (pooled || (t >= tb && t < te))
                         ok = accept_candidate(si, bv, p.positions, center, wi, j, tx, ty, tz, tab.cutoff2, nimg,
                                               dx, dy, dz, d2);
+                    if (ok && weighted) {
+                        ew = soap_edge_weight(tab, d2, si.atom_begin + j == center && nimg[0] == 0 && nimg[1] == 0 &&
+                                                           nimg[2] == 0);
+                        if (pooled) ew *= tab.species_weight[t];
+                    }
                 }
                 const unsigned mask = __ballot_sync(0xffffffffu, ok);
                 if (ok) {
@@ -685,7 +697,8 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     pdy[q] = dy;
                     pdz[q] = dz;
                     pr2[q] = d2;
-                    ptype[q] = t - tb;
+                    pw[q] = ew;
+                    ptype[q] = pooled ? 0 : t - tb;
                 }
                 pcount += __popc(mask);
                 // Drain whole chunks; the queue holds < chunk entries between
@@ -694,13 +707,14 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     __syncwarp();
                     process(chunk);
                     const int rem = pcount - chunk;
-                    double sx = 0.0, sy = 0.0, sz = 0.0, sr = 0.0;
+                    double sx = 0.0, sy = 0.0, sz = 0.0, sr = 0.0, sw = 1.0;
                     int st = 0;
                     if (lane < rem) {
                         sx = pdx[chunk + lane];
                         sy = pdy[chunk + lane];
                         sz = pdz[chunk + lane];
                         sr = pr2[chunk + lane];
+                        sw = pw[chunk + lane];
                         st = ptype[chunk + lane];
                     }
                     __syncwarp();
@@ -709,6 +723,7 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                         pdy[lane] = sy;
                         pdz[lane] = sz;
                         pr2[lane] = sr;
+                        pw[lane] = sw;
                         ptype[lane] = st;
                     }
                     __syncwarp();
@@ -753,12 +768,32 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         }
     }
 
+    // mu1nu1 and crossover rows (soap.cpp:933-996): one feature per lane over
+    // the layout, from the transformed coefficients.
+    auto compressed_rows = [&](auto coef) {
+        if (tab.average == 0) {
+            const int64_t row = center - p.out_row_begin;
+            if (tab.out_f64)
+                power_generic(coef, tab.power_pref, S, n, tab.l_max, tab.compression,
+                              static_cast<double*>(p.out) + row * tab.features, lane);
+            else
+                power_generic(coef, tab.power_pref, S, n, tab.l_max, tab.compression,
+                              static_cast<float*>(p.out) + row * tab.features, lane);
+        } else {
+            power_generic(coef, tab.power_pref, S, n, tab.l_max, tab.compression, p.pbuf + local * tab.features,
+                          lane);
+        }
+    };
+    const bool compressed = tab.average != 1 && (tab.compression == 2 || tab.compression == 3);
     if constexpr (kMmaTail) {
         const int g = lane >> 2, q = lane & 3, L = tab.l_max, R_rows = tab.rows;
         mma::beta_mma<LMAX>(beta, R, tab.rs, L, S, n, g, q);
         __syncwarp();
         const mma::FeatureMap fm{S, n, L, R_rows, tab.n_magic};
-        if (tab.average == 0) {
+        if (compressed) {
+            const int rs = tab.rs;
+            compressed_rows([&](int t, int k, int l, int m) { return R[(t * n + k) * rs + mma::col_off(l) + m]; });
+        } else if (tab.average == 0) {
             const int64_t row = center - p.out_row_begin;
             if (tab.out_f64)
                 mma::power_mma<LMAX>(fm, tab.power_pref, R, tab.rs, static_cast<double*>(p.out) + row * tab.features,
@@ -785,7 +820,9 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     } else {
     beta_transform_warp<NMAX>(tab, beta, R, lane);
     __syncwarp();
-    if (tab.average == 0) {
+    if (compressed) {
+        compressed_rows([&](int t, int k, int l, int m) { return R[cblock(S, n, l) + (t * n + k) * (2 * l + 2) + m]; });
+    } else if (tab.average == 0) {
         const int64_t row = center - p.out_row_begin;
         if (tab.out_f64)
             power_spectrum_warp<LMAX>(tab, R, static_cast<double*>(p.out) + row * tab.features, lane);

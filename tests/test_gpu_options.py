@@ -1,6 +1,7 @@
 """GPU parity of compression layouts and radial weighting (paired-channel
-kernel) against the CPU checker, which tests/test_oracle_options.py pins to
-the reference's own compute_soap."""
+kernel and, for the shapes outside it, the centre kernel) against the CPU
+checker, which tests/test_oracle_options.py pins to the reference's own
+compute_soap."""
 
 from __future__ import annotations
 
@@ -95,13 +96,55 @@ def test_config2_rows_with_weighting(oracle, cuda_device):
         assert_features_close(got, want, "float32")
 
 
-def test_weighting_needs_paired_kernel_shape():
-    """Shapes outside the paired kernel (here l_max = 8) reject weighting and
-    compression with a clear error instead of computing something else."""
-    alphas, betas = basis_gto(5.0, 8, 8)
+# Shapes outside the paired-channel kernel: the one-warp centre kernel with
+# the tensor-core tail (n_max <= 8, l_max 8, config 3's shape) and with the
+# scalar tail (n_max > 8).
+CENTER_SHAPES = {
+    "n8l8": ((1, 6, 8), 4.5, 8, 8, 1.0),
+    "n10l4": ((1, 6, 8), 6.0, 10, 4, 1.0),
+}
+
+
+@pytest.mark.parametrize("shape", sorted(CENTER_SHAPES))
+@pytest.mark.parametrize("compression", ["off", "mu2", "mu1nu1", "crossover"])
+def test_center_kernel_compression_and_weighting(oracle, cuda_device, shape, compression):
+    """Compression layouts, radial weighting (with w0) and species weights on
+    the centre kernel, every average, both dtypes, against the checker."""
+    species, r_cut, n_max, l_max, sigma = CENTER_SHAPES[shape]
+    alphas, betas = basis_gto(r_cut, n_max, l_max)
+    batch = mixed_batch(31)
+    weights = list(np.linspace(0.6, 1.8, len(species)))
+    cases = (("off", None), ("outer", WEIGHTINGS["poly+w0"]), ("inner", WEIGHTINGS["pow"]), ("off", WEIGHTINGS["exp"]),
+             ("off", WEIGHTINGS["w0"]))
+    for average, weighting in cases:
+        want = oracle.soap(batch, species, r_cut, n_max, l_max, sigma, alphas, betas, average=average,
+                           species_weights=weights, compression=compression, weighting=weighting)
+        for dtype in ("float64", "float32"):
+            soap = Soap(species, r_cut=r_cut, n_max=n_max, l_max=l_max, sigma=sigma, average=average, dtype=dtype,
+                        species_weights=weights, alphas=alphas, betas=betas, compression=compression,
+                        weighting=weighting)
+            assert "soap_center_kernel" in soap.kernel()
+            got = soap.compute(batch, devices=[0])
+            if dtype == "float32":
+                assert_features_close(got, want, dtype)
+            else:
+                # The agreement bound, widened for the worse-conditioned radial
+                # bases of larger n_max (|beta| up to 6e3 here).
+                bound = AGREE_TOL * max(1.0, float(np.abs(betas).max()) / 2e3)
+                err = max_rel_err(got, want, AGREE_FLOOR)
+                assert err <= bound, f"float64 max rel err {err:.3e} > {bound:.3e}"
+
+
+def test_polynomial_basis_needs_paired_kernel_shape():
+    """The polynomial radial basis runs on the paired kernel only: other
+    shapes (here l_max = 8) reject it with a clear error instead of computing
+    something else."""
+    from mdescriptor_b200.basis import basis_polynomial
+
+    grid, grid_weights, values = basis_polynomial(5.0, 8)
     with pytest.raises(ValueError, match="paired-channel kernel"):
-        Soap((13, 29), r_cut=5.0, n_max=8, l_max=8, average="off", dtype="float64", alphas=alphas, betas=betas,
-             compression="mu2")
+        Soap((13, 29), r_cut=5.0, n_max=8, l_max=8, average="off", dtype="float64", rbf="polynomial",
+             radial_grid=grid, radial_weights=grid_weights, radial_values=values)
 
 
 @pytest.mark.parametrize("shape", sorted(SHAPES))
