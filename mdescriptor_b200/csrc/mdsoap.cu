@@ -1014,8 +1014,9 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         }
         const Variant* paired = polynomial ? poly_variant(n, L)
                                 : radial_normal ? paired_variant(n, L, q.output_dtype == MDSOAP_FLOAT64,
-                                                                 q.compression == MDSOAP_COMPRESSION_MU2 ? 1
-                                                                                                         : q.n_species)
+                                                                 (q.compression == MDSOAP_COMPRESSION_MU2 ? 1
+                                                                                                          : q.n_species) *
+                                                                     (q.output_dtype == MDSOAP_FLOAT64 ? 2 : 1))
                                                 : nullptr;
         const char* env = std::getenv("MDSOAP_VARIANT");
         const int want = env ? std::atoi(env) : -1;
@@ -1033,7 +1034,11 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         if (picked->paired) {
             const Variant& v = *picked;
             plan->variant = &v;
-            t.type_groups = (coef_species + v.maxt - 1) / v.maxt;
+            // The full-accuracy (float64-row) instantiations keep every
+            // species' neighbour sum as two partial sums: half-length sums,
+            // the accuracy class of the reference's two-lane SIMD reduction.
+            t.ksplit = v.precise ? 2 : 1;
+            t.type_groups = (coef_species + v.maxt / t.ksplit - 1) / (v.maxt / t.ksplit);
             t.slot_groups = 1;
             t.beta_in_smem = 1;
             t.csize = coef_species * n * W * (W + 1);
@@ -1077,7 +1082,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
             const char* split_env = std::getenv("MDSOAP_SPLIT_TAIL");
             const bool split_allowed = !(split_env && split_env[0] == '0');
             const size_t generic_smem = (size_t)W * 64 * 8 + (size_t)kWarps * t.rsize * 8;  // beta + a block per warp
-            const bool regs = n == 8 && coef_species <= v.maxt;
+            const bool regs = n == 8 && coef_species * t.ksplit <= v.maxt;
             if (split_allowed && !polynomial && q.average != MDSOAP_AVERAGE_INNER && r_smem &&
                 (regs || generic_smem <= budget1)) {
                 // Register tail (soap_tail_kernel) where the coefficients fit
@@ -1111,6 +1116,7 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         const int ns = (sv.l0 > 0) + (sv.l1 > 0) + (sv.l2 > 0);
         const int slots = (t.items + 31) / 32;
         t.slot_groups = (slots + ns - 1) / ns;
+        t.ksplit = 1;
         t.type_groups = (coef_species + sv.maxt - 1) / sv.maxt;
         const bool single_pass = t.slot_groups == 1 && t.type_groups == 1;
         // One-warp scalar kernels with n_max <= 8 finish on the tensor cores:

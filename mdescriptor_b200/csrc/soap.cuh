@@ -65,6 +65,7 @@ struct SoapTables {
     int32_t weighted;     // 1: per-edge weights (weighting function, w0, or mu2 pooling); paired kernel only
     int32_t split_tail;   // the paired kernel stops after the flush; 1: soap_tail_kernel, 2: soap_tail_generic_kernel finishes the centres
     int32_t grid_size;    // polynomial basis: quadrature nodes (0 for the GTO basis)
+    int32_t ksplit;       // paired kernel: partial sums per species neighbour sum (2 in its float64 instantiations)
     double eta;           // 1 / (2 sigma^2)
     int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)
     int32_t has_w0;       // the exact self pair takes weight w0

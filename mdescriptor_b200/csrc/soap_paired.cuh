@@ -283,7 +283,14 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const int chunk = tab.chunk;
     // Beta transform and power spectrum in registers (n_max == 8, the whole
     // coefficient block in one pass of banks, per-centre rows).
-    const bool regs_tail = n == 8 && S <= MAXT && tab.average != 1;
+    // Split sums (PRECISE instantiations, i.e. float64 rows): each species'
+    // neighbour sum is kept as two partial sums over alternate accepted
+    // edges, in two register banks, added at the flush -- half-length sums,
+    // as the reference's two-lane SIMD reduction forms them
+    // (soap.cpp:905-912); a pass then holds MAXT / 2 species.
+    constexpr int ks = PRECISE ? 2 : 1;
+    constexpr int spp = MAXT / ks;
+    const bool regs_tail = n == 8 && S * ks <= MAXT && tab.average != 1;
 
     // This lane's channel pair: group g of radial index k.
     const int g = lane / n, k = lane - (lane / n) * n;
@@ -322,8 +329,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const int entries = wy * (2 * Kz + 1) * nxs;
     const double pre2 = si.pre_cut2;
 
-    for (int tb = 0; tb < S; tb += MAXT) {
-        const int te = min(S, tb + MAXT);
+    for (int tb = 0; tb < S; tb += spp) {
+        const int te = min(S, tb + spp);
         double acc[MAXT][P::W];
 #pragma unroll
         for (int t = 0; t < MAXT; ++t)
@@ -460,6 +467,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         // candidates, two per lane) leaves at most 95 < kPreQueue survivors.
         int qn = 0;      // prefilter survivors queued (warp-uniform)
         int pcount = 0;  // accepted edges queued (warp-uniform)
+        int naccepted = 0;  // accepted edges of this pass so far (split sums: bank parity)
         int round = 0;   // next segment index
         int q0 = 0, total = 0;
         while (true) {
@@ -513,15 +521,17 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 }
                 const unsigned mask = __ballot_sync(0xffffffffu, ok);
                 if (ok) {
-                    const int q = pcount + __popc(mask & ((1u << lane) - 1u));
+                    const int rank = __popc(mask & ((1u << lane) - 1u));
+                    const int q = pcount + rank;
                     pdx[q] = dx;
                     pdy[q] = dy;
                     pdz[q] = dz;
                     pr2[q] = d2;
                     pw[q] = w;
-                    ptype[q] = pooled ? 0 : t - tb;
+                    ptype[q] = (pooled ? 0 : t - tb) * ks + ((naccepted + rank) & (ks - 1));
                 }
                 pcount += __popc(mask);
+                naccepted += __popc(mask);
                 // Move the remaining survivors (up to 63) to the queue's front.
                 const int rem = qn - count;
                 int sa0 = 0, st0 = 0, ss0 = 0, sa1 = 0, st1 = 0, ss1 = 0;
@@ -687,18 +697,21 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             const int colA = mma::col_off(lA);
             const int colB = lB >= 0 ? mma::col_off(lB) - split : 0;
             const int padA = mma::kpad(lA), padB = lB >= 0 ? mma::kpad(lB) : 0;
-#pragma unroll
-            for (int tt = 0; tt < MAXT; ++tt) {
-                const int t = tb + tt;
-                if (t < te) {
+            static_for<0, MAXT>([&](auto bank) {
+                constexpr int tt = decltype(bank)::value;
+                // Bank tt holds species tb + tt / ks (partial sum tt % ks).
+                const int t = tb + tt / ks;
+                if (tt % ks == 0 && t < te) {
                     const double w = pooled ? 1.0 : tab.species_weight[t];
                     double* row = R + (t * n + k) * tab.rs;
 #pragma unroll
                     for (int m = 0; m < P::W; ++m) {
+                        double v = acc[tt][m];
+                        if constexpr (ks == 2 && tt + 1 < MAXT) v += acc[tt + 1][m];
                         if (m < split)
-                            row[colA + m] = w * acc[tt][m];
+                            row[colA + m] = w * v;
                         else if (lB >= 0)
-                            row[colB + m] = w * acc[tt][m];
+                            row[colB + m] = w * v;
                     }
                     // The register tail never reads the padding (tail_regs_n8 masks it).
                     if (!regs_tail) {
@@ -707,7 +720,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                             for (int m = 2 * lB + 1; m < padB; ++m) row[colB + split + m] = 0.0;
                     }
                 }
-            }
+            });
         }
         __syncwarp();
     }
