@@ -26,6 +26,7 @@ namespace mdsoap {
 constexpr int kLocalMaxL = 8;   // largest max_angular of the kernel
 constexpr int kLocalMaxN = 16;  // largest radial count (max_radial + 1)
 constexpr unsigned kErrLocalSeries = 128u;  // 1F1 series overflowed (the reference throws)
+constexpr int kLocalRecip = 256;             // series terms with a tabulated 1 / ((b + k - 1) k)
 
 enum LocalKind : int { kLocalSphericalExpansion = 0, kLocalRadialSpectrum = 2, kLocalPowerSpectrum = 3 };
 
@@ -46,6 +47,7 @@ struct LocalTables {
     const double* gratio;  // [(lc+1) n] Gamma(a) / Gamma(b)
     const double* ppow;    // [(lc+1) n] (c + g_n)^(-a)
     const double* ortho;   // [n][n] normalisation * S^(-1/2)
+    const double* recip;   // [(lc+1)][kLocalRecip]: 1 / ((l + 1.5 + k - 1) k), index k (entry 0 unused)
 };
 
 struct LocalLayout {
@@ -72,13 +74,21 @@ __host__ __device__ inline LocalLayout local_layout(int species, int n, int lc) 
     return L;
 }
 
-// 1F1(a; b; x) by its power series for x >= 0, with the stopping rule and
-// operation order of hyp1f1_series (local_spherical_common.hpp:33-47).
-__device__ inline double local_hyp1f1_series(double a, double b, double x, bool& overflow) {
+// 1F1(a; b; x) by its power series for x >= 0, with the stopping rule of
+// hyp1f1_series (local_spherical_common.hpp:33-47).  The term ratio
+// (a + k - 1) x / ((b + k - 1) k) multiplies by the tabulated, correctly
+// rounded reciprocal of its exact denominator (a half-integer times an
+// integer) instead of dividing: one multiply for the division's reciprocal
+// iteration, at most one more rounding per term.
+__device__ inline double local_hyp1f1_series(double a, double b, double x, const double* __restrict__ recip,
+                                             bool& overflow) {
     double sum = 1.0;
     double term = 1.0;
     for (int k = 1; k < 10000; ++k) {
-        term = __dmul_rn(term, __ddiv_rn(__dmul_rn(a + (double)k - 1.0, x), __dmul_rn(b + (double)k - 1.0, (double)k)));
+        const double num = __dmul_rn(a + (double)k - 1.0, x);
+        const double ratio = k < kLocalRecip ? __dmul_rn(num, __ldg(recip + k))
+                                             : __ddiv_rn(num, __dmul_rn(b + (double)k - 1.0, (double)k));
+        term = __dmul_rn(term, ratio);
         sum = __dadd_rn(sum, term);
         if (fabs(term) <= __dmul_rn(fabs(sum), 2e-15)) break;
         if (!isfinite(sum)) {
@@ -162,6 +172,14 @@ __device__ inline void local_harmonics(double x, double y, double z, int lmax, d
     }
 }
 
+// Degree l of harmonic index h = l^2 + l + m (h < 81): floor(sqrt(h)).
+__device__ __forceinline__ int degree_of(int h) {
+    int l = (int)sqrtf((float)h);
+    l += (l + 1) * (l + 1) <= h;
+    l -= l * l > h;
+    return l;
+}
+
 // Smooth cosine cutoff of width min(0.5, cutoff) (cutoff_value, :445-454).
 __device__ inline double local_cutoff_value(double d, double rc) {
     if (d >= rc) return 0.0;
@@ -193,7 +211,7 @@ __device__ inline void local_radial(const LocalTables& t, int l, double d, doubl
             lg = __dadd_rn(lg, __dmul_rn(__dsub_rn(a, b), log(z)));
             raw[k] = __dmul_rn(exp(lg), asym);
         } else {
-            const double s = local_hyp1f1_series(a, b, z, overflow);
+            const double s = local_hyp1f1_series(a, b, z, t.recip + l * kLocalRecip, overflow);
             raw[k] = __dmul_rn(__dmul_rn(__dmul_rn(__ldg(t.gratio + l * t.n + k), s), __ldg(t.ppow + l * t.n + k)),
                                factor);
         }
@@ -269,8 +287,7 @@ __global__ void __launch_bounds__(128) local_spectra_kernel(LocalTables t, const
             double* bank = coef + ty * L.nH;
             for (int i = lane; i < L.nH; i += 32) {
                 const int k = i / L.H, h = i - k * L.H;
-                int l = 0;
-                while ((l + 1) * (l + 1) <= h) ++l;
+                const int l = degree_of(h);
                 bank[i] = __dadd_rn(bank[i], __dmul_rn(r[l * t.n + k], y[h]));
             }
         }

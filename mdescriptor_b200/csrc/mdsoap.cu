@@ -2254,6 +2254,12 @@ int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* 
         std::vector<double> packed;
         for (const auto* part : {&ht.g, &ht.log_cg, &ht.gratio, &ht.ppow, &ht.ortho})
             packed.insert(packed.end(), part->begin(), part->end());
+        // Reciprocals of the 1F1 series denominators (l + 1.5 + k - 1) k, exact
+        // products, correctly rounded by the host division.
+        const size_t recip_at = packed.size();
+        for (int l = 0; l <= lc; ++l)
+            for (int k = 0; k < kLocalRecip; ++k)
+                packed.push_back(k == 0 ? 0.0 : 1.0 / (((double)l + 1.5 + (double)k - 1.0) * (double)k));
         tables.reserve(8 * packed.size(), "local tables");
         check(cudaMemcpyAsync(tables.ptr, packed.data(), 8 * packed.size(), cudaMemcpyHostToDevice, stream), "H2D");
         error.reserve(64, "error");
@@ -2282,6 +2288,7 @@ int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* 
         t.gratio = tb + 2 * n;
         t.ppow = t.gratio + (size_t)(lc + 1) * n;
         t.ortho = t.ppow + (size_t)(lc + 1) * n;
+        t.recip = tb + recip_at;
         // Rows in blocks of centres (about MDSOAP_BLOCK_BYTES of rows each),
         // double buffered: block i's kernel runs while the host copies block
         // i-1 out of its pinned staging buffer into the caller's rows.  A
