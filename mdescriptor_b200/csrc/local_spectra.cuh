@@ -48,6 +48,7 @@ struct LocalTables {
     const double* ppow;    // [(lc+1) n] (c + g_n)^(-a)
     const double* ortho;   // [n][n] normalisation * S^(-1/2)
     const double* recip;   // [(lc+1)][kLocalRecip]: 1 / ((l + 1.5 + k - 1) k), index k (entry 0 unused)
+    const double* ynorm;   // [l(l+1)/2 + m], m <= l <= lc: (-1)^m N_lm, times sqrt 2 for m > 0
 };
 
 struct LocalLayout {
@@ -112,62 +113,56 @@ __device__ inline double local_hyp1f1_asymptotic(double a, double b, double x) {
 }
 
 // Real spherical harmonics of a displacement in the reference's layout
-// (index l^2 + l + m), restating real_spherical_harmonics_into (:376-443):
-// normalised associated Legendre recurrence in cos(theta), and the cos/sin
-// of m*phi by the three-term Chebyshev recurrence.
-__device__ inline void local_harmonics(double x, double y, double z, int lmax, double* out) {
+// (index l^2 + l + m; real_spherical_harmonics_into, :376-443, defines the
+// values).  Evaluated here as regular solid harmonics of the unit direction
+// by the Cartesian recurrence the SOAP kernels use (Y_l^m = N_lm r^l P_l^m
+// (cos m phi, sin m phi) with P_mm = -(2m - 1)(x P - y P'), then
+// P_lm = ((2l - 1) z P_{l-1,m} - (l + m - 1) r^2 P_{l-2,m}) / (l - m) at
+// r = 1), with the reference's sign convention folded into the host table
+// ynorm[l(l+1)/2 + m] = (-1)^m N_lm (times sqrt 2 for m > 0).  The direction
+// is normalised as the reference does (length below 1e-6: the z axis).
+__device__ inline void local_harmonics(const LocalTables& t, double x, double y, double z, int lmax, double* out) {
     const double norm = sqrt(__dadd_rn(__dadd_rn(__dmul_rn(x, x), __dmul_rn(y, y)), __dmul_rn(z, z)));
-    double dx, dy, dz;
+    double ux, uy, uz;
     if (norm < 1e-6) {
-        dx = 0.0;
-        dy = 0.0;
-        dz = 1.0;
+        ux = 0.0;
+        uy = 0.0;
+        uz = 1.0;
     } else {
-        dx = __ddiv_rn(x, norm);
-        dy = __ddiv_rn(y, norm);
-        dz = __ddiv_rn(z, norm);
+        ux = __ddiv_rn(x, norm);
+        uy = __ddiv_rn(y, norm);
+        uz = __ddiv_rn(z, norm);
     }
-    constexpr double kInvSqrt2Pi = 0.398942280401432677939946059934;
-    constexpr double kSqrt3 = 1.732050807568877293527446341505872;
-    constexpr double kSqrt3Over2 = 1.224744871391589049098642;
-    constexpr double kSqrt2 = 1.41421356237309504880168872420969808;
-    double P[(kLocalMaxL + 1) * (kLocalMaxL + 2) / 2];
-    auto at = [&](int l, int m) -> double& { return P[m + l * (l + 1) / 2]; };
-    const double xy = hypot(dx, dy);
-    const double ct = dz, st = xy;
-    at(0, 0) = kInvSqrt2Pi;
-    if (lmax > 0) {
-        at(1, 0) = __dmul_rn(__dmul_rn(ct, kSqrt3), kInvSqrt2Pi);
-        double value = __dmul_rn(__dmul_rn(-kSqrt3Over2, st), kInvSqrt2Pi);
-        at(1, 1) = value;
-        for (int l = 2; l <= lmax; ++l) {
-            for (int m = 0; m < l - 1; ++m) {
-                const double ls = (double)(l * l), lm1s = (double)((l - 1) * (l - 1)), ms = (double)(m * m);
-                const double A = sqrt(__ddiv_rn(__dsub_rn(__dmul_rn(4.0, ls), 1.0), __dsub_rn(ls, ms)));
-                const double B = -sqrt(__ddiv_rn(__dsub_rn(lm1s, ms), __dsub_rn(__dmul_rn(4.0, lm1s), 1.0)));
-                at(l, m) = __dmul_rn(A, __dadd_rn(__dmul_rn(ct, at(l - 1, m)), __dmul_rn(B, at(l - 2, m))));
-            }
-            at(l, l - 1) = __dmul_rn(__dmul_rn(ct, sqrt(2.0 * l + 1.0)), value);
-            value = __dmul_rn(value, __dmul_rn(-sqrt(__dadd_rn(1.0, __ddiv_rn(0.5, (double)l))), st));
-            at(l, l) = value;
+    double dr = 1.0, di = 0.0;  // P_mm (cos and sin parts)
+    for (int m = 0; m <= lmax; ++m) {
+        if (m > 0) {
+            const double f = -(2.0 * m - 1.0);
+            const double nr = f * (ux * dr - uy * di);
+            const double ni = f * (ux * di + uy * dr);
+            dr = nr;
+            di = ni;
         }
-    }
-    for (int l = 0; l <= lmax; ++l) out[l * l + l] = __ddiv_rn(at(l, 0), kSqrt2);
-    const double eps = 2.220446049250313e-16;
-    const double cphi = xy > eps ? __ddiv_rn(dx, xy) : 1.0;
-    const double sphi = xy > eps ? __ddiv_rn(dy, xy) : 0.0;
-    double cprev = 1.0, sprev = 0.0, ccur = -cphi, scur = sphi;
-    const double m2c = -2.0 * cphi;
-    for (int m = 1; m <= lmax; ++m) {
-        const double sm = __dsub_rn(__dmul_rn(m2c, sprev), scur);
-        const double cm = __dsub_rn(__dmul_rn(m2c, cprev), ccur);
-        scur = sprev;
-        sprev = sm;
-        ccur = cprev;
-        cprev = cm;
-        for (int l = m; l <= lmax; ++l) {
-            out[l * l + l + m] = __dmul_rn(at(l, m), cm);
-            out[l * l + l - m] = __dmul_rn(at(l, m), sm);
+        auto store = [&](int l, double re, double im) {
+            const double nrm = __ldg(t.ynorm + l * (l + 1) / 2 + m);
+            out[l * l + l + m] = nrm * re;
+            if (m > 0) out[l * l + l - m] = nrm * im;
+        };
+        store(m, dr, di);
+        if (m < lmax) {
+            const double c = (2.0 * m + 1.0) * uz;
+            double pr2 = dr, pi2 = di, pr1 = c * dr, pi1 = c * di;
+            store(m + 1, pr1, pi1);
+            for (int l = m + 2; l <= lmax; ++l) {
+                const double a = (2.0 * l - 1.0) / (double)(l - m) * uz;
+                const double b = (double)(l + m - 1) / (double)(l - m);
+                const double nr = fma(a, pr1, -b * pr2);
+                const double ni = fma(a, pi1, -b * pi2);
+                pr2 = pr1;
+                pi2 = pi1;
+                pr1 = nr;
+                pi1 = ni;
+                store(l, nr, ni);
+            }
         }
     }
 }
@@ -274,7 +269,7 @@ __global__ void __launch_bounds__(128) local_spectra_kernel(LocalTables t, const
             if (scaling == 0.0) ty = -1;
             etype[lane] = ty;
             if (ty >= 0) {
-                local_harmonics(dx, dy, dz, t.lc, ys + lane * L.ystride);
+                local_harmonics(t, dx, dy, dz, t.lc, ys + lane * L.ystride);
                 for (int l = 0; l <= t.lc; ++l) local_radial(t, l, d, scaling, rs + lane * L.rstride + l * t.n, overflow);
             }
         }

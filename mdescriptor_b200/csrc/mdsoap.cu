@@ -2260,6 +2260,17 @@ int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* 
         for (int l = 0; l <= lc; ++l)
             for (int k = 0; k < kLocalRecip; ++k)
                 packed.push_back(k == 0 ? 0.0 : 1.0 / (((double)l + 1.5 + (double)k - 1.0) * (double)k));
+        // Harmonic normalisation sqrt((2l+1)/(4 pi) (l-m)!/(l+m)!), times sqrt 2
+        // for m > 0, with the reference's sign (-1)^m.
+        const size_t ynorm_at = packed.size();
+        for (int l = 0; l <= lc; ++l)
+            for (int m = 0; m <= l; ++m) {
+                const double pi = 3.141592653589793238462643383279502884;
+                double v = std::sqrt((2.0 * l + 1.0) / (4.0 * pi) *
+                                     std::exp(std::lgamma(l - m + 1.0) - std::lgamma(l + m + 1.0)));
+                if (m > 0) v *= 1.414213562373095048801688724209698079;
+                packed.push_back(m % 2 ? -v : v);
+            }
         tables.reserve(8 * packed.size(), "local tables");
         check(cudaMemcpyAsync(tables.ptr, packed.data(), 8 * packed.size(), cudaMemcpyHostToDevice, stream), "H2D");
         error.reserve(64, "error");
@@ -2289,6 +2300,7 @@ int mdsoap_local_compute(const mdsoap_local_params* params, const mdsoap_batch* 
         t.ppow = t.gratio + (size_t)(lc + 1) * n;
         t.ortho = t.ppow + (size_t)(lc + 1) * n;
         t.recip = tb + recip_at;
+        t.ynorm = tb + ynorm_at;
         // Rows in blocks of centres (about MDSOAP_BLOCK_BYTES of rows each),
         // double buffered: block i's kernel runs while the host copies block
         // i-1 out of its pinned staging buffer into the caller's rows.  A
