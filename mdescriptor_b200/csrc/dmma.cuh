@@ -40,14 +40,19 @@ __host__ __device__ constexpr int y_stride(int L) {
     return stride4(need);
 }
 
+// The warp-collective mma.sync is volatile asm: a plain asm statement is a
+// pure function of its operands to the compiler, which may then move it into a
+// branch taken by only some lanes (a consumer of its result under a
+// lane-dependent condition), where the instruction's all-lanes requirement
+// fails and the products come out wrong.
 __device__ __forceinline__ void dmma8(double& c0, double& c1, double a0, double b0) {
-    asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
         : "+d"(c0), "+d"(c1)
         : "d"(a0), "d"(b0));
 }
 __device__ __forceinline__ void dmma16(double& c0, double& c1, double& c2, double& c3, double a0, double a1,
                                        double b0) {
-    asm("mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+    asm volatile("mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
         : "+d"(c0), "+d"(c1), "+d"(c2), "+d"(c3)
         : "d"(a0), "d"(a1), "d"(b0));
 }

@@ -137,8 +137,8 @@ __device__ inline void local_harmonics(const LocalTables& t, double x, double y,
     for (int m = 0; m <= lmax; ++m) {
         if (m > 0) {
             const double f = -(2.0 * m - 1.0);
-            const double nr = f * (ux * dr - uy * di);
-            const double ni = f * (ux * di + uy * dr);
+            const double nr = f * fma(ux, dr, -__dmul_rn(uy, di));
+            const double ni = f * fma(ux, di, __dmul_rn(uy, dr));
             dr = nr;
             di = ni;
         }

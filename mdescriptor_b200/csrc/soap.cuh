@@ -106,7 +106,9 @@ __device__ __forceinline__ double soap_edge_weight(const SoapTables& tab, double
         const double ratio = distance / tab.w_r0;
         if (tab.weight_fn == 1) {
             value = distance > tab.w_r0 ? 0.0
-                                        : tab.w_c * pow(1.0 + 2.0 * ratio * ratio * ratio - 3.0 * ratio * ratio, tab.w_m);
+                                        : tab.w_c * pow(__dsub_rn(__dadd_rn(1.0, __dmul_rn(__dmul_rn(__dmul_rn(2.0, ratio), ratio), ratio)),
+                                                                  __dmul_rn(__dmul_rn(3.0, ratio), ratio)),
+                                                        tab.w_m);
         } else if (tab.weight_fn == 2) {
             value = tab.w_c / (tab.w_d + pow(ratio, tab.w_m));
         } else {
@@ -129,8 +131,8 @@ __device__ __forceinline__ void solid_harmonics(const SoapTables& tab, double x,
     for (int m = 0; m <= L; ++m) {
         if (m > 0) {
             const double f = -(2.0 * m - 1.0);
-            const double nr = f * (x * dr - y * di);
-            const double ni = f * (x * di + y * dr);
+            const double nr = f * fma(x, dr, -__dmul_rn(y, di));
+            const double ni = f * fma(x, di, __dmul_rn(y, dr));
             dr = nr;
             di = ni;
         }
@@ -181,8 +183,8 @@ __device__ __forceinline__ void solid_harmonics_fixed(const SoapTables& tab, dou
     for (int m = 0; m <= L; ++m) {
         if (m > 0) {
             const double f = -(2.0 * m - 1.0);
-            const double nr = f * (x * dr - y * di);
-            const double ni = f * (x * di + y * dr);
+            const double nr = f * fma(x, dr, -__dmul_rn(y, di));
+            const double ni = f * fma(x, di, __dmul_rn(y, dr));
             dr = nr;
             di = ni;
         }

@@ -82,8 +82,8 @@ __device__ __forceinline__ void harmonics_row(const SoapTables& tab, double x, d
         constexpr int m = decltype(mc)::value;
         if constexpr (m > 0) {
             const double f = -(2.0 * m - 1.0);
-            const double nr = f * (x * dr - y * di);
-            const double ni = f * (x * di + y * dr);
+            const double nr = f * fma(x, dr, -__dmul_rn(y, di));
+            const double ni = f * fma(x, di, __dmul_rn(y, dr));
             dr = nr;
             di = ni;
         }
@@ -734,8 +734,6 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         return;
     }
 
-    const int gq = lane >> 2, qq = lane & 3, R_rows = tab.rows;
-    const bool n8 = n == 8;
     if (regs_tail) {
         // Coefficients stay in registers from the beta transform to the power spectrum.
         if (tab.average == 0) {
@@ -752,61 +750,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         }
         return;
     }
-    if (n8)
-        mma::beta_n8<L>(bt, R, tab.rs, S, gq, qq);
-    else
-        mma::beta_mma<L>(bt, R, tab.rs, L, S, n, gq, qq);
-    __syncwarp();
-    const mma::FeatureMap fm{S, n, L, R_rows, tab.n_magic};
-    if (tab.average != 1 && (tab.compression == 2 || tab.compression == 3)) {
-        const int rs = tab.rs;
-        auto coef = [&](int t, int k, int l, int m) { return R[(t * n + k) * rs + mma::col_off(l) + m]; };
-        if (tab.average == 0) {
-            const int64_t row = center - p.out_row_begin;
-            if (tab.out_f64)
-                power_generic(coef, tab.power_pref, S, n, L, tab.compression,
-                              static_cast<double*>(p.out) + row * tab.features, lane);
-            else
-                power_generic(coef, tab.power_pref, S, n, L, tab.compression,
-                              static_cast<float*>(p.out) + row * tab.features, lane);
-        } else {
-            power_generic(coef, tab.power_pref, S, n, L, tab.compression, p.pbuf + local * tab.features, lane);
-        }
-        return;
-    }
-    if (tab.average == 0) {
-        const int64_t row = center - p.out_row_begin;
-        if (tab.out_f64) {
-            double* dst = static_cast<double*>(p.out) + row * tab.features;
-            if (n8)
-                mma::power_n8<L>(tab.power_pref, R, tab.rs, S, dst, gq, qq);
-            else
-                mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, dst, gq, qq);
-        } else {
-            float* dst = static_cast<float*>(p.out) + row * tab.features;
-            if (n8)
-                mma::power_n8<L>(tab.power_pref, R, tab.rs, S, dst, gq, qq);
-            else
-                mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, dst, gq, qq);
-        }
-    } else if (tab.average == 1) {
-        // The structure kernel's layout: [l][r][m], rows padded to 2l+2.
-        double* dst = p.cbuf + local * tab.csize;
-        for (int l = 0; l <= L; ++l) {
-            const int pad = 2 * l + 2;
-            double* dl = dst + cblock(S, n, l);
-            const double* src = R + mma::col_off(l);
-            for (int i = lane; i < R_rows * pad; i += 32) {
-                const int r = i / pad, m = i - r * pad;
-                dl[i] = m < 2 * l + 1 ? src[r * tab.rs + m] : 0.0;
-            }
-        }
-    } else {
-        if (n8)
-            mma::power_n8<L>(tab.power_pref, R, tab.rs, S, p.pbuf + local * tab.features, gq, qq);
-        else
-            mma::power_mma<L>(fm, tab.power_pref, R, tab.rs, p.pbuf + local * tab.features, gq, qq);
-    }
+    tail_generic<L>(tab, p, R, bt, center, lane);
     };
     for (int64_t center = c_lo + warp; center < c_hi; center += kWarps) run_centre(center);
 }
