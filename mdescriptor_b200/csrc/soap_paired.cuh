@@ -61,12 +61,13 @@ struct Layout {
 };
 
 // Per-warp shared-memory region (bytes); the harmonic rows follow.
-constexpr int kSegBytes = 544;                     // seg_prefix[40] seg_start[32] seg_t[32] perm[32]
+constexpr int kSegBytes = 544;                     // seg_prefix[40] seg_start[32] seg_t[32], 128 B spare
 constexpr int kSegOffBytes = 3 * 32 * 8;           // per-segment offset vectors
 constexpr int kPreQueue = 96;                      // prefilter survivors awaiting the exact test
 constexpr int kPreBytes = 3 * kPreQueue * 4;
 constexpr int kEdgeBytes = kPending * (5 * 8 + 4); // dx dy dz r2 weight + species
-constexpr int kHeaderBytes = kSegBytes + kSegOffBytes + kPreBytes + kEdgeBytes;
+constexpr int kSortBytes = 32 * 2 * 8;             // r2 and weight of a chunk's edges in bank order
+constexpr int kHeaderBytes = kSegBytes + kSegOffBytes + kPreBytes + kEdgeBytes + kSortBytes;
 static_assert(kHeaderBytes % 16 == 0, "harmonic rows must start 16-byte aligned");
 
 // Real regular solid harmonics of one displacement into the paired row
@@ -246,7 +247,6 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     int* seg_prefix = reinterpret_cast<int*>(region);  // 40
     int* seg_start = seg_prefix + 40;                   // 32
     int* seg_t = seg_start + 32;                        // 32
-    int* perm = seg_t + 32;                             // 32
     double* seg_off = reinterpret_cast<double*>(region + paired::kSegBytes);  // [3][32]
     int* qa = reinterpret_cast<int*>(region + paired::kSegBytes + paired::kSegOffBytes);
     int* qt = qa + paired::kPreQueue;
@@ -257,6 +257,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     double* pr2 = pdz + kPending;
     double* pw = pr2 + kPending;
     int32_t* ptype = reinterpret_cast<int32_t*>(pw + kPending);
+    double* sr2 = reinterpret_cast<double*>(region + paired::kHeaderBytes - paired::kSortBytes);
+    double* sw = sr2 + 32;
     double* ybuf = reinterpret_cast<double*>(region + paired::kHeaderBytes);
     // POLY: flir_l(r, q) of the current edge, [L+1][Q], after the harmonic rows.
     double* flir = ybuf + tab.chunk * P::ROW;
@@ -409,9 +411,9 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         };
 
         auto process = [&](int count) {
-            if (lane < count) paired::harmonics_row<L>(tab, pdx[lane], pdy[lane], pdz[lane], pr2[lane],
-                                                       ybuf + lane * P::ROW);
-            // Stable counting sort of the chunk by species bank.
+            // Stable counting sort of the chunk by species bank; each edge's
+            // harmonic row, r^2 and weight go to its rank, so a bank's edges
+            // are consecutive rows.
             const int mine = lane < count ? ptype[lane] : MAXT;
             const unsigned lt = (1u << lane) - 1u;
             int run_start[MAXT + 1];
@@ -423,7 +425,11 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 if (mine == tt) rank = run_start[tt] + __popc(msk & lt);
                 run_start[tt + 1] = run_start[tt] + __popc(msk);
             }
-            if (lane < count) perm[rank] = lane;
+            if (lane < count) {
+                paired::harmonics_row<L>(tab, pdx[lane], pdy[lane], pdz[lane], pr2[lane], ybuf + rank * P::ROW);
+                sr2[rank] = pr2[lane];
+                sw[rank] = pw[lane];
+            }
             __syncwarp();
             const bool weighted = tab.weighted != 0;
             // One edge per step: two independent exp chains per lane are
@@ -432,9 +438,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             static_for<0, MAXT>([&](auto bank) {
                 constexpr int TT = decltype(bank)::value;
                 const int end = run_start[TT + 1];
-                for (int i = run_start[TT]; i < end; ++i) {
-                    const int ea = perm[i];
-                    const double ua = pr2[ea];
+                for (int ea = run_start[TT]; ea < end; ++ea) {
+                    const double ua = sr2[ea];
                     double gAa, gBa;
                     if constexpr (POLY) {
                         poly_radial(ua, gAa, gBa);
@@ -443,7 +448,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                         gBa = scaled_exp<PRECISE>(nEB * ua, prefB, etab);
                     }
                     if (weighted) {
-                        const double wa = pw[ea];
+                        const double wa = sw[ea];
                         gAa *= wa;
                         gBa *= wa;
                     }
