@@ -236,6 +236,20 @@ void mdsoap_csr_destroy(mdsoap_csr* csr);
 int mdsoap_compute_device_noalloc(mdsoap_plan* plan, const mdsoap_batch* batch, void* out, int32_t device,
                                   void* stream);
 
+/* Page-locked host buffers for result rows, recycled across calls (no
+ * counterpart in the reference; used by the plugin for the rows it returns).
+ * Rows written into such a buffer by mdsoap_compute leave the GPU by a direct
+ * D2H, and a recycled buffer's pages are already resident, so neither the
+ * staging copy nor first-touch page faults of a fresh pageable array are paid.
+ * acquire: a buffer of at least `bytes` from the idle pool (a cached one at
+ * most twice as large) or newly page-locked; MDSOAP_OUT_OF_MEMORY when the
+ * host refuses to lock more memory.  release: back to the idle pool, which
+ * keeps at most MDSOAP_HOST_POOL_BYTES (environment, default 4 GiB; 0
+ * disables the pool's caching) and unlocks the rest.  Buffers are never
+ * unlocked at process exit.  Thread-safe. */
+int mdsoap_host_buffer_acquire(size_t bytes, void** ptr);
+void mdsoap_host_buffer_release(void* ptr);
+
 /* Per-kernel CUDA-event timing of mdsoap_compute_device calls (measurement
  * support; no counterpart in the reference).  While enabled, each device call
  * records events around its binning, centre and structure kernels on the

@@ -191,6 +191,8 @@ EXPORTED = (
     "mdsoap_csr_copy",
     "mdsoap_csr_destroy",
     "mdsoap_compute_device_noalloc",
+    "mdsoap_host_buffer_acquire",
+    "mdsoap_host_buffer_release",
     "mdsoap_plan_set_timing",
     "mdsoap_plan_last_timing",
     "mdsoap_plan_launch_count",

@@ -284,6 +284,24 @@ public:
 
     int64_t feature_count() const { return features_; }
 
+    // Result rows in a recycled page-locked buffer (mdsoap_host_buffer_acquire):
+    // the rows arrive by a direct D2H into resident pages, and the buffer goes
+    // back to the pool when the array is freed.  Buffers above 1 GiB, or when
+    // the host refuses to lock more memory, are ordinary NumPy arrays.
+    py::array result_array(int64_t rows) {
+        const size_t elem = f64_ ? 8 : 4;
+        const size_t bytes = (size_t)rows * (size_t)features_ * elem;
+        void* buffer = nullptr;
+        if (bytes > 0 && bytes <= ((size_t)1 << 30) && mdsoap_host_buffer_acquire(bytes, &buffer) == MDSOAP_OK) {
+            py::capsule owner(buffer, [](void* p) { mdsoap_host_buffer_release(p); });
+            const std::vector<py::ssize_t> shape{(py::ssize_t)rows, (py::ssize_t)features_};
+            if (f64_) return py::array_t<double>(shape, static_cast<double*>(buffer), owner);
+            return py::array_t<float>(shape, static_cast<float*>(buffer), owner);
+        }
+        if (f64_) return py::array_t<double>({(py::ssize_t)rows, (py::ssize_t)features_});
+        return py::array_t<float>({(py::ssize_t)rows, (py::ssize_t)features_});
+    }
+
     py::object compute(py::object batch, py::object control) {
         std::unique_lock<std::mutex> guard(mutex_, std::defer_lock);
         {
@@ -314,8 +332,7 @@ public:
         if (list_) return compute_list(view, structures, control);
         if (local_) return compute_local(view, offsets, structures, control);
         const int64_t rows = average_ == MDSOAP_AVERAGE_OFF ? atoms : structures;
-        py::array values = f64_ ? py::array(py::array_t<double>({(py::ssize_t)rows, (py::ssize_t)features_}))
-                                : py::array(py::array_t<float>({(py::ssize_t)rows, (py::ssize_t)features_}));
+        py::array values = result_array(rows);
         void* out = values.mutable_data();
         CancelContext context{control};
         int status;
@@ -330,7 +347,12 @@ public:
         }
         py::dict result;
         result["values"] = values;
-        result["_mdescriptor_owned_values"] = true;
+        // The adapter takes an array without its snapshot copy only when the
+        // array owns its data (core/result.py:31-50); rows in a recycled
+        // page-locked buffer are copied out by the adapter (its block
+        // combiner copies every multi-block result anyway), and the buffer
+        // goes back to the pool.
+        result["_mdescriptor_owned_values"] = values.owndata();
         result["level"] = average_ == MDSOAP_AVERAGE_OFF ? "atom" : "structure";
         if (average_ == MDSOAP_AVERAGE_OFF) {
             py::array_t<int64_t> row_offsets(structures + 1);

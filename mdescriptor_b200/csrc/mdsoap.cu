@@ -14,6 +14,7 @@
 #include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
+#include <unordered_map>
 #include <atomic>
 #include <cmath>
 #include <cstdlib>
@@ -1726,6 +1727,82 @@ int mdsoap_probe_bounded_wait(int32_t device, uint64_t limit_ns) {
     } catch (const std::exception& e) {
         return fail(MDSOAP_INTERNAL, e.what());
     }
+}
+
+namespace {
+
+// Idle page-locked result buffers, by capacity.  Never destroyed: unlocking
+// memory after the CUDA runtime has shut down at process exit is not allowed.
+struct HostPool {
+    std::mutex mutex;
+    std::multimap<size_t, void*> idle;           // capacity -> buffer
+    std::unordered_map<void*, size_t> capacity;  // every buffer handed out or idle
+    size_t idle_bytes = 0;
+};
+
+HostPool& host_pool() {
+    static HostPool* pool = new HostPool();
+    return *pool;
+}
+
+size_t host_pool_limit() {
+    const char* env = std::getenv("MDSOAP_HOST_POOL_BYTES");
+    return env ? (size_t)std::strtoull(env, nullptr, 10) : ((size_t)4 << 30);
+}
+
+}  // namespace
+
+int mdsoap_host_buffer_acquire(size_t bytes, void** ptr) {
+    if (!ptr) return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    *ptr = nullptr;
+    try {
+        HostPool& pool = host_pool();
+        const size_t want = std::max<size_t>(bytes, 1);
+        {
+            std::lock_guard<std::mutex> lock(pool.mutex);
+            auto it = pool.idle.lower_bound(want);
+            if (it != pool.idle.end() && it->first <= 2 * want) {
+                *ptr = it->second;
+                pool.idle_bytes -= it->first;
+                pool.idle.erase(it);
+                return MDSOAP_OK;
+            }
+        }
+        // Capacity rounded up to 2 MiB so that nearby sizes share buffers.
+        const size_t cap = (want + ((size_t)2 << 20) - 1) & ~(((size_t)2 << 20) - 1);
+        void* p = nullptr;
+        const cudaError_t err = cudaMallocHost(&p, cap);
+        if (err != cudaSuccess) {
+            cudaGetLastError();
+            return fail(MDSOAP_OUT_OF_MEMORY, std::string("page-locked result buffer: ") + cudaGetErrorString(err));
+        }
+        std::lock_guard<std::mutex> lock(pool.mutex);
+        pool.capacity[p] = cap;
+        *ptr = p;
+        return MDSOAP_OK;
+    } catch (const std::exception& e) {
+        return fail(MDSOAP_INTERNAL, e.what());
+    }
+}
+
+void mdsoap_host_buffer_release(void* ptr) {
+    if (!ptr) return;
+    HostPool& pool = host_pool();
+    void* unlock = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(pool.mutex);
+        auto it = pool.capacity.find(ptr);
+        if (it == pool.capacity.end()) return;  // not ours
+        const size_t cap = it->second;
+        if (pool.idle_bytes + cap <= host_pool_limit()) {
+            pool.idle.emplace(cap, ptr);
+            pool.idle_bytes += cap;
+        } else {
+            pool.capacity.erase(it);
+            unlock = ptr;
+        }
+    }
+    if (unlock) cudaFreeHost(unlock);
 }
 
 int mdsoap_probe_fp64_fma(int32_t device, double* tflops) {

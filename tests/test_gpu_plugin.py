@@ -75,7 +75,9 @@ def test_adapter_options_replayed_into_the_plugin(cuda_device, expected, index):
 
     values = result["values"]
     assert isinstance(values, np.ndarray) and values.dtype == np.float32 and values.flags.c_contiguous
-    assert result["_mdescriptor_owned_values"] is True
+    # owned (no snapshot copy in the adapter) exactly when NumPy owns the rows;
+    # rows in a recycled page-locked buffer are not
+    assert result["_mdescriptor_owned_values"] is bool(values.flags.owndata)
     assert values.shape[1] == backend.feature_count == options["_cuda_feature_count"]
     assert_features_close(values, expected[f"case{index}/values"], np.float32)
     if kwargs["average"] == "off":
@@ -176,3 +178,36 @@ def test_devices_environment_variable(cuda_device, expected, monkeypatch):
     assert np.array_equal(backend.compute(batch, None)["values"], reference)
     backend.close()
     assert os.environ["MDSOAP_DEVICES"] == str(cuda_device)
+
+
+@pytest.mark.gpu
+def test_recycled_page_locked_result_buffers(cuda_device, expected, monkeypatch):
+    """The plugin returns rows in recycled page-locked buffers
+    (mdsoap_host_buffer_acquire): a result the caller still holds is never
+    handed out again, a freed one is reused, results stay writable NumPy
+    arrays, and with the pool's cache disabled the rows are the same."""
+    import gc
+
+    plugin = load_plugin()
+    name, options, _ = adapter_cases()[0]
+    batch = Batch(expected)
+    backend = plugin.create_backend(name, options)
+    first = backend.compute(batch, None)["values"]
+    snapshot = first.copy()
+    held = [backend.compute(batch, None)["values"] for _ in range(3)]
+    for values in held:
+        assert values.ctypes.data != first.ctypes.data
+        assert np.array_equal(values, snapshot)
+    assert np.array_equal(first, snapshot)  # untouched by the later calls
+    address = held[0].ctypes.data
+    del held
+    gc.collect()
+    reused = backend.compute(batch, None)["values"]
+    assert np.array_equal(reused, snapshot)
+    assert reused.ctypes.data in (address, first.ctypes.data) or reused.base is not None
+    reused[0, 0] = 1.0  # writable
+    monkeypatch.setenv("MDSOAP_HOST_POOL_BYTES", "0")
+    del reused
+    gc.collect()
+    assert np.array_equal(backend.compute(batch, None)["values"], snapshot)
+    backend.close()
