@@ -47,6 +47,8 @@ struct StructInfo {
                          // periodic with a diagonal cell of positive entries)
     int64_t bin_base;    // first bin_start entry of this structure
     double pre_cut2;     // prefilter radius^2: cutoff plus a margin far above fp64 rounding of any displacement
+    double in_cut2;      // inner radius^2: cutoff minus the same margin; an approximate d^2 below it implies the
+                         // reference's exact d^2 is within the cutoff
 };
 
 struct BinView {

@@ -93,8 +93,10 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
     __shared__ int32_t flags;
     __shared__ int32_t scan_carry;
     __shared__ int32_t warp_sums[32];
+    __shared__ int32_t any_wrapped;
 
     if (tid == 0) {
+        any_wrapped = 0;
         const int32_t* p = b.pbc + 3 * s;
         const bool periodic = p[0] == 1 && p[1] == 1 && p[2] == 1;
         const bool isolated = p[0] == 0 && p[1] == 0 && p[2] == 0;
@@ -216,6 +218,10 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
         const double Z = 2.0 * amax + (bmax + 4.0) * cellsum;
         const double pre = cutoff + 1e-11 * (Z + cutoff);
         si.pre_cut2 = pre * pre * (1.0 + 1e-14);
+        // Inner radius: a displacement of approximate length below it lies
+        // within the cutoff by the reference's arithmetic as well.
+        const double inner = fmax(0.0, cutoff - 1e-11 * (Z + cutoff));
+        si.in_cut2 = inner * inner * (1.0 - 1e-14);
         v.info[s] = si;
     }
     __syncthreads();
@@ -246,6 +252,7 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
                 bin[c] = min(si.M[c] - 1, max(0, (int)floor(u)));
             }
         }
+        if (wrap[0] != 0 || wrap[1] != 0 || wrap[2] != 0) any_wrapped = 1;
         const int id = bin[0] + si.M[0] * (bin[1] + si.M[1] * bin[2]);
         v.bin_of[atom] = id;
         v.wrap[3 * atom] = wrap[0];
@@ -295,6 +302,10 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
         __syncthreads();
     }
     for (int i = tid; i < Mtot; i += blockDim.x) v.bin_cursor[bb + i] = v.bin_start[bb + i];
+    // The inner radius certifies a pair only when every atom lies inside the
+    // cell (then the image range admits every image within the cutoff);
+    // otherwise no candidate is certified.
+    if (tid == 0 && any_wrapped) v.info[s].in_cut2 = -1.0;
     __syncthreads();
     for (int64_t a = tid; a < count; a += blockDim.x) {
         const int pos = atomicAdd(&v.bin_cursor[bb + v.bin_of[begin + a]], 1);

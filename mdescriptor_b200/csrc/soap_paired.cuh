@@ -65,7 +65,11 @@ constexpr int kSegBytes = 544;                     // seg_prefix[40] seg_start[3
 constexpr int kSegOffBytes = 3 * 32 * 8;           // per-segment offset vectors
 constexpr int kPreQueue = 96;                      // prefilter survivors awaiting the exact test
 constexpr int kPreBytes = 3 * kPreQueue * 4;
-constexpr int kEdgeBytes = kPending * (5 * 8 + 4); // dx dy dz r2 weight + species
+// Accepted-edge queue: below chunk (<= 32) entries before a prefilter round,
+// which may append 64 direct edges (float32 plans), or before an exact test
+// (32 more).
+constexpr int kPendingPaired = 96;
+constexpr int kEdgeBytes = kPendingPaired * (5 * 8 + 4); // dx dy dz r2 weight + species
 constexpr int kSortBytes = 32 * 2 * 8;             // r2 and weight of a chunk's edges in bank order
 constexpr int kHeaderBytes = kSegBytes + kSegOffBytes + kPreBytes + kEdgeBytes + kSortBytes;
 static_assert(kHeaderBytes % 16 == 0, "harmonic rows must start 16-byte aligned");
@@ -252,11 +256,11 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     int* qt = qa + paired::kPreQueue;
     int* qs = qt + paired::kPreQueue;
     double* pdx = reinterpret_cast<double*>(region + paired::kSegBytes + paired::kSegOffBytes + paired::kPreBytes);
-    double* pdy = pdx + kPending;
-    double* pdz = pdy + kPending;
-    double* pr2 = pdz + kPending;
-    double* pw = pr2 + kPending;
-    int32_t* ptype = reinterpret_cast<int32_t*>(pw + kPending);
+    double* pdy = pdx + paired::kPendingPaired;
+    double* pdz = pdy + paired::kPendingPaired;
+    double* pr2 = pdz + paired::kPendingPaired;
+    double* pw = pr2 + paired::kPendingPaired;
+    int32_t* ptype = reinterpret_cast<int32_t*>(pw + paired::kPendingPaired);
     double* sr2 = reinterpret_cast<double*>(region + paired::kHeaderBytes - paired::kSortBytes);
     double* sw = sr2 + 32;
     double* ybuf = reinterpret_cast<double*>(region + paired::kHeaderBytes);
@@ -329,7 +333,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const int nxs = periodic ? floor_div(xhi, Mx) - tx0 + 1 : 1;
     const int wy = 2 * Ky + 1;
     const int entries = wy * (2 * Kz + 1) * nxs;
-    const double pre2 = si.pre_cut2;
+    const double pre2 = si.pre_cut2, in2 = si.in_cut2;
 
     for (int tb = 0; tb < S; tb += spp) {
         const int te = min(S, tb + spp);
@@ -481,25 +485,34 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 const int count = min(pcount, chunk);
                 __syncwarp();
                 process(count);
+                // Move the rest (up to 63 edges) to the queue's front.
                 const int rem = pcount - count;
-                double sx = 0.0, sy = 0.0, sz = 0.0, sr = 0.0, sw = 0.0;
-                int st = 0;
-                if (lane < rem) {
-                    sx = pdx[count + lane];
-                    sy = pdy[count + lane];
-                    sz = pdz[count + lane];
-                    sr = pr2[count + lane];
-                    sw = pw[count + lane];
-                    st = ptype[count + lane];
+                double sx[2], sy[2], sz[2], sr[2], swt[2];
+                int st[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i = lane + 32 * h;
+                    if (i < rem) {
+                        sx[h] = pdx[count + i];
+                        sy[h] = pdy[count + i];
+                        sz[h] = pdz[count + i];
+                        sr[h] = pr2[count + i];
+                        swt[h] = pw[count + i];
+                        st[h] = ptype[count + i];
+                    }
                 }
                 __syncwarp();
-                if (lane < rem) {
-                    pdx[lane] = sx;
-                    pdy[lane] = sy;
-                    pdz[lane] = sz;
-                    pr2[lane] = sr;
-                    pw[lane] = sw;
-                    ptype[lane] = st;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int i = lane + 32 * h;
+                    if (i < rem) {
+                        pdx[i] = sx[h];
+                        pdy[i] = sy[h];
+                        pdz[i] = sz[h];
+                        pr2[i] = sr[h];
+                        pw[i] = swt[h];
+                        ptype[i] = st[h];
+                    }
                 }
                 __syncwarp();
                 pcount = rem;
@@ -571,6 +584,15 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 const int qA = q0 + lane, qB = q0 + 32 + lane;
                 bool passA = false, passB = false;
                 int aA = 0, tyA = 0, iA = 0, aB = 0, tyB = 0, iB = 0;  // a: local atom id
+                // Float32 plans take candidates whose prefilter d^2 lies below
+                // the inner radius straight into the edge queue, with the
+                // prefilter's displacement (a few 1e-16 relative from the
+                // reference's): their membership in the pair set is certain,
+                // and float32 rows do not see the displacement's last bits.
+                // The rest go through the exact test.
+                constexpr bool kDirect = !PRECISE && !POLY;
+                bool dirA = false, dirB = false;
+                double xA = 0.0, yA = 0.0, zA = 0.0, rA = 0.0, xB = 0.0, yB = 0.0, zB = 0.0, rB = 0.0;
 #pragma unroll
                 for (int step = 16; step > 0; step >>= 1) {
                     if (seg_prefix[iA + step] <= qA) iA += step;
@@ -581,20 +603,53 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     const long long code = (long long)sp.w;
                     tyA = (int)(code & 127) - 1;
                     aA = (int)(code >> 7);
-                    const double dx = sp.x + seg_off[iA], dy = sp.y + seg_off[32 + iA], dz = sp.z + seg_off[64 + iA];
-                    passA = (pooled || (tyA >= tb && tyA < te)) && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
+                    xA = sp.x + seg_off[iA];
+                    yA = sp.y + seg_off[32 + iA];
+                    zA = sp.z + seg_off[64 + iA];
+                    rA = fma(zA, zA, fma(yA, yA, xA * xA));
+                    passA = (pooled || (tyA >= tb && tyA < te)) && rA <= pre2;
+                    dirA = kDirect && passA && rA <= in2;
                 }
                 if (qB < total) {
                     const double4 sp = bv.spos[ab + seg_start[iB] + (qB - seg_prefix[iB])];
                     const long long code = (long long)sp.w;
                     tyB = (int)(code & 127) - 1;
                     aB = (int)(code >> 7);
-                    const double dx = sp.x + seg_off[iB], dy = sp.y + seg_off[32 + iB], dz = sp.z + seg_off[64 + iB];
-                    passB = (pooled || (tyB >= tb && tyB < te)) && fma(dz, dz, fma(dy, dy, dx * dx)) <= pre2;
+                    xB = sp.x + seg_off[iB];
+                    yB = sp.y + seg_off[32 + iB];
+                    zB = sp.z + seg_off[64 + iB];
+                    rB = fma(zB, zB, fma(yB, yB, xB * xB));
+                    passB = (pooled || (tyB >= tb && tyB < te)) && rB <= pre2;
+                    dirB = kDirect && passB && rB <= in2;
+                }
+                const unsigned lt = (1u << lane) - 1u;
+                if constexpr (kDirect) {
+                    // Direct edges, in candidate order, after the queued ones.
+                    const unsigned dA = __ballot_sync(0xffffffffu, dirA);
+                    const unsigned dB = __ballot_sync(0xffffffffu, dirB);
+                    auto push = [&](int slot, int a, int ty, int seg, double x, double y, double z, double r) {
+                        double w = 1.0;
+                        if (tab.weighted) {
+                            const bool self = ab + a == center && seg_t[seg] == (512 | (512 << 10) | (512 << 20));
+                            w = soap_edge_weight(tab, r, self);
+                            if (pooled) w *= tab.species_weight[ty];
+                        }
+                        pdx[slot] = x;
+                        pdy[slot] = y;
+                        pdz[slot] = z;
+                        pr2[slot] = r;
+                        pw[slot] = w;
+                        ptype[slot] = pooled ? 0 : ty - tb;
+                    };
+                    if (dirA) push(pcount + __popc(dA & lt), aA, tyA, iA, xA, yA, zA, rA);
+                    if (dirB) push(pcount + __popc(dA) + __popc(dB & lt), aB, tyB, iB, xB, yB, zB, rB);
+                    pcount += __popc(dA) + __popc(dB);
+                    naccepted += __popc(dA) + __popc(dB);
+                    passA = passA && !dirA;
+                    passB = passB && !dirB;
                 }
                 const unsigned maskA = __ballot_sync(0xffffffffu, passA);
                 const unsigned maskB = __ballot_sync(0xffffffffu, passB);
-                const unsigned lt = (1u << lane) - 1u;
                 if (passA) {
                     const int slot = qn + __popc(maskA & lt);
                     qa[slot] = aA;

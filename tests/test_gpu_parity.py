@@ -65,14 +65,14 @@ def test_graph_reference_golden_inputs(oracle, cuda_device):
         assert_graph_bit_exact(neighbor_graph(batch, cutoff, cuda_device), oracle.graph(batch, cutoff))
 
 
-def random_mixed_batch(seed, structures=6):
+def random_mixed_batch(seed, structures=6, frac_range=(-0.4, 1.4)):
     rng = np.random.default_rng(seed)
     numbers, positions, cells, pbc, offsets = [], [], [], [], [0]
     for s in range(structures):
         n = 0 if s == 3 else int(rng.integers(1, 40))
         periodic = s % 3 != 2
         cell = np.diag(rng.uniform(3.0, 9.0, 3)) + np.triu(rng.uniform(-1.5, 1.5, (3, 3)), 1)
-        frac = rng.uniform(-0.4, 1.4, (n, 3))  # unwrapped: some atoms outside the cell
+        frac = rng.uniform(*frac_range, (n, 3))  # by default unwrapped: some atoms outside the cell
         positions.append(frac @ cell)
         numbers.append(rng.choice([1, 6, 8], n).astype(np.int32))
         cells.append(cell if periodic else np.zeros((3, 3)))
@@ -197,6 +197,32 @@ def test_species_weights(oracle, cuda_device):
     got = soap_for(meta, "off", "float64", species_weights=weights, alphas=CFG["cfg4/alphas"],
                    betas=CFG["cfg4/betas"]).compute(batch, devices=[cuda_device])
     assert max_rel_err(got, expected, 1e-3) <= 1e-9
+
+
+@pytest.mark.parametrize("frac_range", [(-0.4, 1.4), (0.0, 0.999)], ids=["unwrapped", "inside"])
+@pytest.mark.parametrize("seed", range(3))
+def test_float32_rows_certified_pairs(oracle, cuda_device, seed, frac_range):
+    """float32 plans take candidates well inside the cutoff without the exact
+    test when every atom of a structure lies inside its cell: random triclinic
+    cells (some with atoms outside the cell), isolated and empty structures,
+    radial weighting with a self weight, species-pooled compression."""
+    from test_oracle_options import WEIGHTINGS
+
+    batch = random_mixed_batch(seed, structures=8, frac_range=frac_range)
+    species = (1, 6, 8)
+    weights = [0.7, 1.3, 1.9]
+    for n_max, l_max, r_cut in ((8, 6, 4.0), (4, 3, 3.6)):
+        alphas, betas = basis_gto(r_cut, n_max, l_max)
+        for compression, weighting in (("off", None), ("mu2", WEIGHTINGS["poly+w0"]),
+                                       ("crossover", WEIGHTINGS["w0"])):
+            for average in ("off", "outer"):
+                want = oracle.soap(batch, species, r_cut, n_max, l_max, 0.8, alphas, betas, average=average,
+                                   species_weights=weights, compression=compression, weighting=weighting)
+                soap = Soap(species, r_cut=r_cut, n_max=n_max, l_max=l_max, sigma=0.8, average=average,
+                            dtype="float32", species_weights=weights, alphas=alphas, betas=betas,
+                            compression=compression, weighting=weighting)
+                assert "soap_paired_kernel" in soap.kernel()
+                assert_features_close(soap.compute(batch, devices=[cuda_device]), want, "float32")
 
 
 @pytest.mark.parametrize("l_max,n_max", [(0, 1), (1, 3), (2, 2), (5, 7), (7, 6), (9, 4), (12, 3), (6, 12)])
