@@ -78,6 +78,51 @@ def dist_env():
     return rank, world, local
 
 
+def smi_device_id(local: int) -> str:
+    """nvidia-smi's identifier of CUDA device `local`: the CUDA_VISIBLE_DEVICES
+    entry when that is set (an index or a UUID, both of which --id accepts),
+    else the index itself."""
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "").strip()
+    if visible:
+        entries = [e.strip() for e in visible.split(",") if e.strip()]
+        if local < len(entries):
+            return entries[local]
+    return str(local)
+
+
+def parse_cpulist(text: str) -> set[int]:
+    """CPUs of a sysfs cpulist ("0-15,32-47")."""
+    cpus: set[int] = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def bind_to_gpu_node(pci_address: str, sysfs: Path = Path("/sys")) -> dict:
+    """Restrict this process to the CPUs of its GPU's NUMA node, so that the
+    page-locked host buffers it touches first (rows, staging) are allocated on
+    the node the GPU's PCIe link attaches to.  A GPU without a node (-1, as in
+    single-node guests) or an unreadable sysfs leaves the affinity as it is."""
+    try:
+        node = int((sysfs / "bus/pci/devices" / pci_address / "numa_node").read_text())
+    except (OSError, ValueError):
+        return {"numa_node": None, "cpus": "unchanged (no sysfs record)"}
+    if node < 0:
+        return {"numa_node": None, "cpus": "unchanged (single node)"}
+    try:
+        text = (sysfs / f"devices/system/node/node{node}/cpulist").read_text().strip()
+        cpus = parse_cpulist(text) & os.sched_getaffinity(0)
+    except (OSError, ValueError):
+        return {"numa_node": node, "cpus": "unchanged (no cpulist)"}
+    if not cpus:
+        return {"numa_node": node, "cpus": "unchanged (no allowed CPU on the node)"}
+    os.sched_setaffinity(0, cpus)
+    return {"numa_node": node, "cpus": text}
+
+
 # Structures of each config's full batch (BASELINE configs 1-5), and atoms per
 # structure where that is fixed.
 DEFAULT_STRUCTURES = {1: 64, 2: 1024, 3: 8, 4: 16384, 5: 65536}
@@ -219,8 +264,8 @@ class ClockSampler:
               "clocks_event_reasons.sw_power_cap")
     NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, device: int):
-        self.device = device
+    def __init__(self, device: str):
+        self.device = device  # nvidia-smi --id value
         self.proc = None
         self.samples: list[tuple[float, str]] = []
         self.windows: list[list[float]] = []
@@ -526,9 +571,16 @@ def main():
         return
     import torch
 
-    _, _, local = dist_env()
+    _, world_env, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    host_binding = None
+    if world_env > 1:
+        # Several ranks share the host: keep each one's page-locked buffers on
+        # its GPU's NUMA node (N = 1 keeps every core for the CPU baseline).
+        props = torch.cuda.get_device_properties(local)
+        host_binding = bind_to_gpu_node(
+            f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0")
     ranks = Ranks("nccl", dev)
     rank, world = ranks.rank, ranks.world
 
@@ -556,7 +608,7 @@ def main():
     atoms_all = ranks.sum(batch.atoms)
     structures_all = ranks.sum(batch.structures)
 
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(smi_device_id(local))
     sampler.start()
 
     # ---- device-resident value
@@ -720,6 +772,8 @@ def main():
         }
         if sharder is not None:
             line["sharder_check"] = sharder
+        if host_binding is not None:
+            line["config"]["host_binding"] = host_binding
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, args)
         print(json.dumps(line), flush=True)

@@ -124,3 +124,35 @@ def test_clock_summary_keeps_only_samples_inside_timed_windows():
     assert summary["sm_mhz"] == 1850.0 and summary["sm_max_mhz"] == 1965.0
     assert summary["reasons"] == ["sw_power_cap"]
     assert bench.summarize_clocks(samples, [[10.0, 11.0]]) is None
+
+
+def test_ranks_bind_to_their_gpus_numa_node(tmp_path, monkeypatch):
+    """Each rank of a multi-GPU run restricts itself to the CPUs of its GPU's
+    NUMA node (read from a fake sysfs tree here); a node of -1 or a missing
+    record leaves the affinity alone."""
+    assert bench.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    allowed = sorted(os.sched_getaffinity(0))
+    dev = tmp_path / "bus/pci/devices/0000:18:00.0"
+    dev.mkdir(parents=True)
+    node = tmp_path / "devices/system/node/node1"
+    node.mkdir(parents=True)
+    (node / "cpulist").write_text(f"{allowed[0]}-{allowed[0]}\n")
+    calls = []
+    monkeypatch.setattr(bench.os, "sched_setaffinity", lambda pid, cpus: calls.append(set(cpus)))
+
+    (dev / "numa_node").write_text("1\n")
+    assert bench.bind_to_gpu_node("0000:18:00.0", tmp_path) == {"numa_node": 1, "cpus": f"{allowed[0]}-{allowed[0]}"}
+    assert calls == [{allowed[0]}]
+
+    (dev / "numa_node").write_text("-1\n")
+    assert bench.bind_to_gpu_node("0000:18:00.0", tmp_path)["numa_node"] is None
+    assert bench.bind_to_gpu_node("0000:99:00.0", tmp_path)["numa_node"] is None
+    assert len(calls) == 1
+
+
+def test_clock_sampler_follows_visible_devices(monkeypatch):
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES", raising=False)
+    assert bench.smi_device_id(3) == "3"
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "5,GPU-0a1b2c3d-0000-1111-2222-333344445555")
+    assert bench.smi_device_id(0) == "5"
+    assert bench.smi_device_id(1) == "GPU-0a1b2c3d-0000-1111-2222-333344445555"
