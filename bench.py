@@ -483,12 +483,13 @@ def run_local(args):
 def device_memory_fit(soap, cfg, batch, rows, elem, dev) -> tuple[int, dict]:
     """Largest leading slice of this rank's shard whose device working set fits:
     the rows, the engine's per-atom workspace (inputs, bins, sorted positions),
-    the split tail's raw-sum chunk and the L2 flush buffer, with 2 GiB spare."""
+    the split tail's raw-sum chunk and edge slots (4 GiB each at most) and
+    the L2 flush buffer, with 2 GiB spare."""
     import torch
 
     free, total = torch.cuda.mem_get_info(dev)
     per_atom = rows / max(batch.atoms, 1) * soap.feature_count * elem + 160
-    fixed = (5 << 30) + L2_FLUSH_BYTES + (2 << 30)
+    fixed = (9 << 30) + L2_FLUSH_BYTES + (2 << 30)
     fit_atoms = int(max(0, free - fixed) // per_atom)
     structures = batch.structures
     if fit_atoms < batch.atoms:

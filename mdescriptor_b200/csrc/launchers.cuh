@@ -31,6 +31,18 @@ const void* paired_symbol();
 template <int T, int L, bool PRECISE, int MINB>
 const void* paired_split_symbol();
 
+// Edge-list split of the SPLIT path: the walk-only kernel (no channel code,
+// one instantiation per accuracy) and the expansion-only kernel.
+constexpr int kWalkMinBlocks = 4;
+template <bool PRECISE>
+void paired_walk(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p);
+template <bool PRECISE>
+const void* paired_walk_symbol();
+template <int T, int L, bool PRECISE, int MINB>
+void paired_expand(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p);
+template <int T, int L, bool PRECISE, int MINB>
+const void* paired_expand_symbol();
+
 // Polynomial radial basis: the paired kernel's POLY instantiation
 // (full-accuracy radial factors, tail fused).
 template <int T, int L>
@@ -82,6 +94,23 @@ const void* paired_split_symbol() {
     return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB, true>);
 }
 
+template <bool PRECISE>
+void paired_walk(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_paired_kernel<1, 0, PRECISE, kWalkMinBlocks, true, false, 1><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <bool PRECISE>
+const void* paired_walk_symbol() {
+    return reinterpret_cast<const void*>(&soap_paired_kernel<1, 0, PRECISE, kWalkMinBlocks, true, false, 1>);
+}
+template <int T, int L, bool PRECISE, int MINB>
+void paired_expand(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
+    soap_paired_kernel<T, L, PRECISE, MINB, true, false, 2><<<grid, kWarps * 32, smem, stream>>>(tab, p);
+}
+template <int T, int L, bool PRECISE, int MINB>
+const void* paired_expand_symbol() {
+    return reinterpret_cast<const void*>(&soap_paired_kernel<T, L, PRECISE, MINB, true, false, 2>);
+}
+
 template <int T, int L>
 void poly(dim3 grid, size_t smem, cudaStream_t stream, const SoapTables& tab, const SoapPointers& p) {
     soap_paired_kernel<T, L, true, 2, false, true><<<grid, kWarps * 32, smem, stream>>>(tab, p);
@@ -126,6 +155,10 @@ const void* structure_symbol() {
     template const void* paired_symbol<4, L, true, 2>();                                                          \
     template const void* paired_split_symbol<4, L, false, 2>();                                                   \
     template const void* paired_split_symbol<4, L, true, 2>();                                                    \
+    template void paired_expand<4, L, false, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
+    template void paired_expand<4, L, true, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
+    template const void* paired_expand_symbol<4, L, false, 2>();                                                  \
+    template const void* paired_expand_symbol<4, L, true, 2>();                                                   \
     template void poly<4, L>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);                \
     template const void* poly_symbol<4, L>();                                                                     \
     template void tail<L, 4>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);                \
@@ -142,6 +175,10 @@ const void* structure_symbol() {
     template const void* paired_symbol<T, L, true, 2>();                                                          \
     template const void* paired_split_symbol<T, L, false, 2>();                                                   \
     template const void* paired_split_symbol<T, L, true, 2>();                                                    \
+    template void paired_expand<T, L, false, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
+    template void paired_expand<T, L, true, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
+    template const void* paired_expand_symbol<T, L, false, 2>();                                                  \
+    template const void* paired_expand_symbol<T, L, true, 2>();                                                   \
     template void tail<L, T>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);                \
     template const void* tail_symbol<L, T>();
 

@@ -136,9 +136,11 @@ struct Workspace {
     DeviceBytes numbers, positions, cells, pbc, offsets;
     DeviceBytes info, struct_of, type, bin_of, wrap, sorted, bin_start, bin_cursor, spos;
     DeviceBytes cbuf, pbuf, rbuf;
+    DeviceBytes edges, edge_info, edge_count;  // edge-list split: per-centre edge slots of a chunk
     void release() {
         for (DeviceBytes* b : {&numbers, &positions, &cells, &pbc, &offsets, &info, &struct_of, &type, &bin_of,
-                               &wrap, &sorted, &bin_start, &bin_cursor, &spos, &cbuf, &pbuf, &rbuf})
+                               &wrap, &sorted, &bin_start, &bin_cursor, &spos, &cbuf, &pbuf, &rbuf, &edges,
+                               &edge_info, &edge_count})
             b->release();
     }
     BinView bins(unsigned* error) {
@@ -192,6 +194,10 @@ struct Variant {
     const void* (*split_sym)() = nullptr; // paired: the expansion kernel without tail code
     CenterLauncher tail_generic = nullptr;  // paired: soap_tail_generic_kernel<lmax>
     const void* (*tail_generic_sym)() = nullptr;
+    CenterLauncher walk = nullptr;          // paired: walk-only kernel (edge-list split)
+    const void* (*walk_sym)() = nullptr;
+    CenterLauncher expand = nullptr;        // paired: expansion-only kernel (edge-list split)
+    const void* (*expand_sym)() = nullptr;
 };
 
 #define MDSOAP_VARIANT(CLS, T, A, B, C, N, L, MB)                                                           \
@@ -220,7 +226,9 @@ const Variant kVariants[] = {
             &launch::structure<L>, &launch::structure_symbol<L>, true, PREC,                                 \
             "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch::tail<L, T>,                   \
             &launch::tail_symbol<L, T>, &launch::paired_split_symbol<T, L, PREC, MB>,                        \
-            &launch::tail_generic<L>, &launch::tail_generic_symbol<L>                                        \
+            &launch::tail_generic<L>, &launch::tail_generic_symbol<L>, &launch::paired_walk<PREC>,           \
+            &launch::paired_walk_symbol<PREC>, &launch::paired_expand<T, L, PREC, MB>,                       \
+            &launch::paired_expand_symbol<T, L, PREC, MB>                                                    \
     }
 
 // Paired-channel kernels: the default wherever they apply (n_max <= 8,
@@ -359,6 +367,8 @@ struct DeviceState {
     bool smem_configured = false;
     int64_t tail_grid = 0;    // persistent tail kernel: resident CTAs on this device
     int64_t center_grid = 0;  // paired kernel: resident CTAs on this device (0: one CTA per kWarps centres)
+    int64_t walk_grid = 0;    // edge-list split: resident CTAs of the walk-only kernel
+    int64_t expand_grid = 0;  // edge-list split: resident CTAs of the expansion-only kernel
     cudaEvent_t timing[4] = {nullptr, nullptr, nullptr, nullptr};  // bin | centre | tail | structure
     bool timed = false;  // the last device call recorded the timing events
     // Split-tail plans: per chunk of centres, an event after its expansion
@@ -408,6 +418,7 @@ struct mdsoap_plan {
     size_t center_smem = 0;
     size_t structure_smem = 0;
     size_t tail_smem = 0;      // split tail kernel (tab.split_tail)
+    size_t walk_smem = 0;      // edge-list split: walk-only kernel (tab.edge_cap > 0)
     std::string kernel_label;  // the kernel(s) a step launches after binning
     int64_t tail_chunk = 1 << 30; // centres per expansion / tail pair of launches (MDSOAP_TAIL_CHUNK)
     int64_t csize = 0;
@@ -499,6 +510,20 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
     if (variant->split_sym)
         check(cudaFuncSetAttribute(variant->split_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
               "centre kernel smem");
+    if (tab.edge_cap > 0) {
+        int per_sm = 0, sms = 0;
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, st.device), "SM count");
+        check(cudaFuncSetAttribute(variant->walk_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+              "walk kernel smem");
+        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, variant->walk_sym(), kWarps * 32, walk_smem),
+              "walk kernel occupancy");
+        st.walk_grid = (int64_t)std::max(per_sm, 1) * sms;
+        check(cudaFuncSetAttribute(variant->expand_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+              "expansion kernel smem");
+        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, variant->expand_sym(), kWarps * 32, center_smem),
+              "expansion kernel occupancy");
+        st.expand_grid = (int64_t)std::max(per_sm, 1) * sms;
+    }
     // The paired kernel runs persistent: as many CTAs as fit on the device,
     // each over a contiguous range of centres.  MDSOAP_PERSISTENT=0 launches
     // one CTA per kWarps centres instead (measurement knob).
@@ -569,12 +594,38 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             }
             check(cudaEventRecord(st.marks[st.split_marks++], stream), "timing event");
         };
+        const bool edge_lists = tab.edge_cap > 0;
+        if (edge_lists) {
+            const size_t slots = (size_t)std::max<int64_t>(chunk, 1);
+            st.work.edges.reserve(slots * (size_t)tab.edge_cap * sizeof(double4), "edge slots");
+            st.work.edge_info.reserve(slots * (size_t)tab.edge_cap * sizeof(int32_t), "edge slots");
+            st.work.edge_count.reserve(slots * sizeof(int32_t), "edge counts");
+            p.edges = st.work.edges.as<double4>();
+            p.edge_info = st.work.edge_info.as<int32_t>();
+            p.edge_count = st.work.edge_count.as<int32_t>();
+        }
         for (int64_t c0 = a0; c0 < a1; c0 += chunk) {
             p.grid_begin = c0;
             p.grid_end = std::min(a1, c0 + chunk);
-            int64_t grid = (p.grid_end - c0 + kWarps - 1) / kWarps;
+            const int64_t one_per_warp = (p.grid_end - c0 + kWarps - 1) / kWarps;
+            int64_t grid = one_per_warp;
             if (st.center_grid > 0) grid = std::min(grid, st.center_grid);
-            {
+            if (edge_lists) {
+                // Walk (edges to the slots), expansion from the slots, then
+                // the fused kernel over the centres whose slot overflowed.
+                NvtxRange range("mdsoap walk + expansion");
+                SoapTables walk_tab = tab;
+                walk_tab.warp_bytes = paired::kHeaderBytes;
+                variant->walk(dim3((unsigned)std::min(one_per_warp, std::max<int64_t>(st.walk_grid, 1))), walk_smem,
+                              stream, walk_tab, p);
+                check(cudaGetLastError(), "walk kernel launch");
+                variant->expand(dim3((unsigned)std::min(one_per_warp, std::max<int64_t>(st.expand_grid, 1))),
+                                center_smem, stream, tab, p);
+                check(cudaGetLastError(), "expansion kernel launch");
+                variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
+                check(cudaGetLastError(), "centre kernel launch");
+                launches.fetch_add(2, std::memory_order_relaxed);
+            } else {
                 NvtxRange range("mdsoap expansion");
                 variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
                 check(cudaGetLastError(), "centre kernel launch");
@@ -591,6 +642,9 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
         }
         p.grid_begin = a0;
         p.grid_end = a1;
+        p.edges = nullptr;
+        p.edge_info = nullptr;
+        p.edge_count = nullptr;
     } else {
         if (tab.r_global) {
             st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * tab.rsize, "coefficient scratch");
@@ -1095,10 +1149,28 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                 // chunks of at most 4 GiB (240 k centres for config 2's
                 // 17 KB blocks, so config 2 runs as one pair of launches).
                 plan->tail_chunk = std::max<int64_t>(4096, (int64_t)((4ull << 30) / (8ull * (uint64_t)t.rsize)));
+                // Edge-list split: a walk-only kernel writes each centre's
+                // accepted edges (36 B each) to a slot of edge_cap edges, an
+                // expansion-only kernel reads them, and the fused kernel
+                // redoes the centres whose slot overflowed.  Slots of a
+                // chunk take at most 4 GiB too.  MDSOAP_EDGE_CAP sets the
+                // slot size (0: walk and expansion in one kernel).
+                int64_t cap = 0;
+                if (const char* cap_env = std::getenv("MDSOAP_EDGE_CAP")) cap = std::max<int64_t>(0, std::atoll(cap_env));
+                if (cap > 0 && v.walk && v.expand) {
+                    t.edge_cap = (int32_t)std::min<int64_t>(cap, 1 << 20);
+                    plan->walk_smem = 256 + 64 * 8 + (size_t)kWarps * paired::kHeaderBytes;
+                    const int64_t slot_bytes = (int64_t)t.edge_cap * (int64_t)(sizeof(double4) + sizeof(int32_t)) + 4;
+                    plan->tail_chunk = std::min<int64_t>(plan->tail_chunk,
+                                                         std::max<int64_t>(4096, (int64_t)(4ull << 30) / slot_bytes));
+                }
                 if (const char* chunk_env = std::getenv("MDSOAP_TAIL_CHUNK"))
                     plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
             }
             plan->kernel_label = v.name;
+            if (t.edge_cap > 0)
+                plan->kernel_label = std::string("soap_paired_kernel<1, 0, ") + (v.precise ? "true" : "false") +
+                                     ", 4, walk> + " + v.name + " (edge lists)";
             if (t.split_tail == 1)
                 plan->kernel_label += " + soap_tail_kernel<" + std::to_string(L) + ", " + std::to_string(v.maxt) + ">";
             else if (t.split_tail == 2)

@@ -66,6 +66,7 @@ struct SoapTables {
     int32_t split_tail;   // the paired kernel stops after the flush; 1: soap_tail_kernel, 2: soap_tail_generic_kernel finishes the centres
     int32_t grid_size;    // polynomial basis: quadrature nodes (0 for the GTO basis)
     int32_t ksplit;       // paired kernel: partial sums per species neighbour sum (2 in its float64 instantiations)
+    int32_t edge_cap;     // edge-list split of the SPLIT path: accepted edges per centre slot (0: not used)
     double eta;           // 1 / (2 sigma^2)
     int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)
     int32_t has_w0;       // the exact self pair takes weight w0
@@ -94,6 +95,10 @@ struct SoapPointers {
     int64_t grid_begin;       // paired / tail kernels: centres [grid_begin, grid_end) of this launch,
     int64_t grid_end;         // rbuf rows relative to grid_begin
     const double* poly;       // polynomial basis: nodes [Q], then weighted values wv [Q][n_max]
+    // Edge-list split (tab.edge_cap > 0): slot c = centre grid_begin + c.
+    double4* edges;           // [slots][edge_cap] accepted edges (dx, dy, dz, r^2) in walk order
+    int32_t* edge_info;       // [slots][edge_cap] species | exact-self flag << 16
+    int32_t* edge_count;      // [slots] accepted edges (above edge_cap: slot overflowed)
 };
 
 // Radial weight of one edge (soap_weight, cpp/src/standalone/soap.cpp:389-420,

@@ -213,7 +213,17 @@ __device__ __forceinline__ void tail_generic(const SoapTables& tab, const SoapPo
 // basis: g_ln = 4 pi r^-l sum_q flir_l(r, q) wv[q][n] (4 pi at l = 0 for the
 // exact self pair).  The accumulation and the tail are the GTO path's, with
 // beta = identity and no pi^{3/2} (the plan uploads those).
-template <int MAXT, int L, bool PRECISE, int MINB, bool SPLIT = false, bool POLY = false>
+// MODE (edge-list split of the SPLIT path, for plans with tab.edge_cap > 0):
+//   0  walk and expansion in one kernel; when p.edge_count is set, only the
+//      centres whose accepted edges overflowed their slot (count > edge_cap);
+//   1  walk only: each centre's accepted edges, in walk order, go to its
+//      slot of p.edges / p.edge_info (species | exact-self flag << 16) and
+//      their number to p.edge_count;
+//   2  expansion only: the edges come from the slots MODE 1 filled (centres
+//      with an overflowed slot are left to MODE 0).
+// The edges reach the expansion in the same order either way, so the three
+// give the same rows bit for bit.
+template <int MAXT, int L, bool PRECISE, int MINB, bool SPLIT = false, bool POLY = false, int MODE = 0>
 __global__ void __launch_bounds__(kWarps * 32, MINB)
 soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p) {
     using P = paired::Layout<L>;
@@ -277,6 +287,14 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const int64_t c_hi = min(p.grid_end, c_lo + per_cta);
     auto run_centre = [&](const int64_t center) {
     __syncwarp();  // the previous centre's tail reads are done before the walk reuses the region
+    const int64_t slot = center - p.grid_begin;  // edge-list slot of this centre
+    int nedges = 0;                              // MODE 2: accepted edges in the slot
+    if constexpr (MODE == 0) {
+        if (p.edge_count && p.edge_count[slot] <= tab.edge_cap) return;
+    } else if constexpr (MODE == 2) {
+        nedges = p.edge_count[slot];
+        if (nedges > tab.edge_cap) return;
+    }
     const int64_t local = center - p.center_begin;
     double* R = tab.r_global ? p.rbuf + (center - p.grid_begin) * tab.rsize
                              : reinterpret_cast<double*>(region + tab.r_offset);
@@ -286,7 +304,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const int wi[3] = {bv.wrap[3 * center], bv.wrap[3 * center + 1], bv.wrap[3 * center + 2]};
     double wpos[3];
     wrapped_position(si, p.positions + 3 * center, bv.wrap + 3 * center, wpos);
-    const int chunk = tab.chunk;
+    const int chunk = MODE == 1 ? 32 : tab.chunk;
     // Beta transform and power spectrum in registers (n_max == 8, the whole
     // coefficient block in one pass of banks, per-centre rows).
     // Split sums (PRECISE instantiations, i.e. float64 rows): each species'
@@ -335,8 +353,11 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const int entries = wy * (2 * Kz + 1) * nxs;
     const double pre2 = si.pre_cut2, in2 = si.in_cut2;
 
-    for (int tb = 0; tb < S; tb += spp) {
-        const int te = min(S, tb + spp);
+    // The walk-only kernel takes every species in one pass.
+    const int pass_species = MODE == 1 ? max(S, 1) : spp;
+    int written = 0;  // MODE 1: accepted edges of this centre so far
+    for (int tb = 0; tb < S; tb += pass_species) {
+        const int te = min(S, tb + pass_species);
         double acc[MAXT][P::W];
 #pragma unroll
         for (int t = 0; t < MAXT; ++t)
@@ -415,6 +436,19 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         };
 
         auto process = [&](int count) {
+            if constexpr (MODE == 1) {
+                // Walk only: the chunk goes to the centre's slot (beyond
+                // edge_cap only counted: the centre is then redone by MODE 0).
+                const int e = written + lane;
+                if (lane < count && e < tab.edge_cap) {
+                    const int64_t at = slot * tab.edge_cap + e;
+                    p.edges[at] = make_double4(pdx[lane], pdy[lane], pdz[lane], pr2[lane]);
+                    p.edge_info[at] = ptype[lane];
+                }
+                written += count;
+                __syncwarp();
+                return;
+            }
             // Stable counting sort of the chunk by species bank; each edge's
             // harmonic row, r^2 and weight go to its rank, so a bank's edges
             // are consecutive rows.
@@ -479,8 +513,17 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         int naccepted = 0;  // accepted edges of this pass so far (split sums: bank parity)
         int round = 0;   // next segment index
         int q0 = 0, total = 0;
+        int fetched = 0;  // MODE 2: edges of the slot read so far
+        // MODE 2: the lane's edge of the next batch of 32, loaded one batch
+        // ahead so that the load overlaps the processing of the current one.
+        double4 next_d = make_double4(0.0, 0.0, 0.0, 0.0);
+        int next_info = 0;
+        if (MODE == 2 && lane < nedges) {
+            next_d = p.edges[slot * tab.edge_cap + lane];
+            next_info = p.edge_info[slot * tab.edge_cap + lane];
+        }
         while (true) {
-            const bool walk_done = q0 >= total && round >= entries;
+            const bool walk_done = MODE == 2 ? fetched >= nedges : (q0 >= total && round >= entries);
             if (pcount >= chunk || (walk_done && qn == 0 && pcount > 0)) {
                 const int count = min(pcount, chunk);
                 __syncwarp();
@@ -516,7 +559,40 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 }
                 __syncwarp();
                 pcount = rem;
-            } else if (qn >= 32 || (walk_done && qn > 0)) {
+            } else if (MODE == 2 && fetched < nedges) {
+                // Next 32 edges of the slot, this pass's species, in order.
+                const int e = fetched + lane;
+                bool ok = false;
+                const double4 d = next_d;
+                const int info = next_info;
+                const int t = info & 0xffff;
+                const bool self = (info >> 16) != 0;
+                if (e < nedges) ok = pooled || (t >= tb && t < te);
+                if (e + 32 < nedges) {
+                    next_d = p.edges[slot * tab.edge_cap + e + 32];
+                    next_info = p.edge_info[slot * tab.edge_cap + e + 32];
+                }
+                const unsigned mask = __ballot_sync(0xffffffffu, ok);
+                if (ok) {
+                    const int rank = __popc(mask & ((1u << lane) - 1u));
+                    const int q = pcount + rank;
+                    double w = 1.0;
+                    if (tab.weighted) {
+                        w = soap_edge_weight(tab, d.w, self);
+                        if (pooled) w *= tab.species_weight[t];
+                    }
+                    pdx[q] = d.x;
+                    pdy[q] = d.y;
+                    pdz[q] = d.z;
+                    pr2[q] = d.w;
+                    pw[q] = w;
+                    ptype[q] = (pooled ? 0 : t - tb) * ks + ((naccepted + rank) & (ks - 1));
+                }
+                pcount += __popc(mask);
+                naccepted += __popc(mask);
+                fetched += 32;
+                __syncwarp();
+            } else if (MODE != 2 && (qn >= 32 || (walk_done && qn > 0))) {
                 // Exact test of queued survivors [0, count): the reference's geometry.
                 const int count = min(qn, 32);
                 __syncwarp();
@@ -530,7 +606,11 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     ok = accept_candidate(si, bv, p.positions, center, wi, j, (tp & 1023) - 512,
                                           ((tp >> 10) & 1023) - 512, ((tp >> 20) & 1023) - 512, tab.cutoff2, nimg,
                                           dx, dy, dz, d2);
-                    if (ok && tab.weighted) {
+                    if (MODE == 1) {
+                        // Species and the exact-self flag; the expansion forms the weight.
+                        if (ok && tab.weighted && ab + j == center && nimg[0] == 0 && nimg[1] == 0 && nimg[2] == 0)
+                            t |= 1 << 16;
+                    } else if (ok && tab.weighted) {
                         w = soap_edge_weight(tab, d2,
                                              ab + j == center && nimg[0] == 0 && nimg[1] == 0 && nimg[2] == 0);
                         // The pooled density carries each neighbour's species weight.
@@ -546,7 +626,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     pdz[q] = dz;
                     pr2[q] = d2;
                     pw[q] = w;
-                    ptype[q] = (pooled ? 0 : t - tb) * ks + ((naccepted + rank) & (ks - 1));
+                    ptype[q] = MODE == 1 ? t : (pooled ? 0 : t - tb) * ks + ((naccepted + rank) & (ks - 1));
                 }
                 pcount += __popc(mask);
                 naccepted += __popc(mask);
@@ -576,7 +656,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 }
                 __syncwarp();
                 qn = rem;
-            } else if (q0 < total) {
+            } else if (MODE != 2 && q0 < total) {
                 // Prefilter candidates q0 .. q0 + 63 of this round, two per
                 // lane (q0 + lane and q0 + 32 + lane): the two searches and
                 // the two position loads are independent, so their latencies
@@ -627,19 +707,24 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     // Direct edges, in candidate order, after the queued ones.
                     const unsigned dA = __ballot_sync(0xffffffffu, dirA);
                     const unsigned dB = __ballot_sync(0xffffffffu, dirB);
-                    auto push = [&](int slot, int a, int ty, int seg, double x, double y, double z, double r) {
+                    auto push = [&](int at, int a, int ty, int seg, double x, double y, double z, double r) {
                         double w = 1.0;
+                        int info = ty;
                         if (tab.weighted) {
                             const bool self = ab + a == center && seg_t[seg] == (512 | (512 << 10) | (512 << 20));
-                            w = soap_edge_weight(tab, r, self);
-                            if (pooled) w *= tab.species_weight[ty];
+                            if (MODE == 1) {
+                                info |= self ? 1 << 16 : 0;
+                            } else {
+                                w = soap_edge_weight(tab, r, self);
+                                if (pooled) w *= tab.species_weight[ty];
+                            }
                         }
-                        pdx[slot] = x;
-                        pdy[slot] = y;
-                        pdz[slot] = z;
-                        pr2[slot] = r;
-                        pw[slot] = w;
-                        ptype[slot] = pooled ? 0 : ty - tb;
+                        pdx[at] = x;
+                        pdy[at] = y;
+                        pdz[at] = z;
+                        pr2[at] = r;
+                        pw[at] = w;
+                        ptype[at] = MODE == 1 ? info : (pooled ? 0 : ty - tb);
                     };
                     if (dirA) push(pcount + __popc(dA & lt), aA, tyA, iA, xA, yA, zA, rA);
                     if (dirB) push(pcount + __popc(dA) + __popc(dB & lt), aB, tyB, iB, xB, yB, zB, rB);
@@ -665,7 +750,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 qn += __popc(maskA) + __popc(maskB);
                 q0 += 64;
                 __syncwarp();
-            } else if (round < entries) {
+            } else if (MODE != 2 && round < entries) {
                 // Segments round .. round + 31: one (y, z) bin row at one x image each.
                 const int e = round + lane;
                 bool valid = e < entries;
@@ -753,7 +838,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         // Flush the raw sums times the species weight: row (t, k), degree l
         // at columns col_off(l) .. + kpad(l), padding written as 0 where the
         // tail reads it.
-        if (lane_on) {
+        if (MODE != 1 && lane_on) {
             const int colA = mma::col_off(lA);
             const int colB = lB >= 0 ? mma::col_off(lB) - split : 0;
             const int padA = mma::kpad(lA), padB = lB >= 0 ? mma::kpad(lB) : 0;
@@ -785,6 +870,10 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         __syncwarp();
     }
 
+    if constexpr (MODE == 1) {
+        if (lane == 0) p.edge_count[slot] = written;
+        return;
+    }
     if (SPLIT || tab.split_tail) {
         // The tail runs as its own kernel (soap_tail_kernel): hand the raw
         // sums over through global scratch, one contiguous block per centre.
