@@ -62,7 +62,8 @@ struct BinView {
     int32_t* bin_cursor;     // same size, scatter cursors
     unsigned* error;         // device error word
     double4* spos;           // [atoms] in `sorted` order: wrapped position (x, y, z) and
-                             // w = 128 * local atom id + species index + 1;
+                             // w = the int64 128 * local atom id + species index + 1,
+                             // its bits stored as they are (__longlong_as_double);
                              // may be null (then not written)
 };
 

@@ -329,15 +329,16 @@ __global__ void bin_structures_kernel(DeviceBatch b, BinView v, double cutoff,
     }
     if (v.spos == nullptr) return;
     __syncthreads();
-    // Wrapped positions in bin order, with w = 128 j + species + 1 (j the
-    // structure-local atom id; exact in a double): the centre kernels'
-    // prefilter reads one coalesced record and learns both.
+    // Wrapped positions in bin order, with w holding the bits of the int64
+    // 128 j + species + 1 (j the structure-local atom id): the centre
+    // kernels' prefilter reads one coalesced record and learns both, with no
+    // conversion.
     for (int64_t p = tid; p < count; p += blockDim.x) {
         const int32_t j = v.sorted[begin + p];
         const int64_t atom = begin + j;
         double w[3];
         wrapped_position(si, b.positions + 3 * atom, v.wrap + 3 * atom, w);
-        v.spos[begin + p] = make_double4(w[0], w[1], w[2], (double)((int64_t)j * 128 + v.type[atom] + 1));
+        v.spos[begin + p] = make_double4(w[0], w[1], w[2], __longlong_as_double((int64_t)j * 128 + v.type[atom] + 1));
     }
 }
 

@@ -514,6 +514,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         int round = 0;   // next segment index
         int q0 = 0, total = 0;
         int fetched = 0;  // MODE 2: edges of the slot read so far
+        int seg_first = 0x7fffffff;  // first candidate of non-empty segment `lane` of this round
         // MODE 2: the lane's edge of the next batch of 32, loaded one batch
         // ahead so that the load overlaps the processing of the current one.
         double4 next_d = make_double4(0.0, 0.0, 0.0, 0.0);
@@ -673,14 +674,22 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 constexpr bool kDirect = !PRECISE && !POLY;
                 bool dirA = false, dirB = false;
                 double xA = 0.0, yA = 0.0, zA = 0.0, rA = 0.0, xB = 0.0, yB = 0.0, zB = 0.0, rB = 0.0;
-#pragma unroll
-                for (int step = 16; step > 0; step >>= 1) {
-                    if (seg_prefix[iA + step] <= qA) iA += step;
-                    if (seg_prefix[iB + step] <= qB) iB += step;
+                {
+                    // Segment of each candidate: the non-empty segments have
+                    // strictly increasing starts, so candidate q belongs to
+                    // segment #{starts <= q} - 1.  Bit d of (hi:lo) marks a
+                    // segment starting at q0 + d; lane i holds segment i's start.
+                    const int d = seg_first - q0;
+                    const unsigned lo = __reduce_or_sync(0xffffffffu, (d >= 0 && d < 32) ? 1u << d : 0u);
+                    const unsigned hi = __reduce_or_sync(0xffffffffu, (d >= 32 && d < 64) ? 1u << (d - 32) : 0u);
+                    const int before = __popc(__ballot_sync(0xffffffffu, d < 0)) - 1;
+                    const unsigned upto = 0xffffffffu >> (31 - lane);
+                    iA = before + __popc(lo & upto);
+                    iB = before + __popc(lo) + __popc(hi & upto);
                 }
                 if (qA < total) {
                     const double4 sp = bv.spos[ab + seg_start[iA] + (qA - seg_prefix[iA])];
-                    const long long code = (long long)sp.w;
+                    const long long code = __double_as_longlong(sp.w);
                     tyA = (int)(code & 127) - 1;
                     aA = (int)(code >> 7);
                     xA = sp.x + seg_off[iA];
@@ -692,7 +701,7 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 }
                 if (qB < total) {
                     const double4 sp = bv.spos[ab + seg_start[iB] + (qB - seg_prefix[iB])];
-                    const long long code = (long long)sp.w;
+                    const long long code = __double_as_longlong(sp.w);
                     tyB = (int)(code & 127) - 1;
                     aB = (int)(code >> 7);
                     xB = sp.x + seg_off[iB];
@@ -822,14 +831,20 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 total = __shfl_sync(0xffffffffu, incl, 31);
                 q0 = 0;
                 round += 32;
+                // Only the non-empty segments are kept, in order.
+                const unsigned nonempty = __ballot_sync(0xffffffffu, len > 0);
+                const int at = __popc(nonempty & ((1u << lane) - 1u));
                 __syncwarp();
-                seg_prefix[lane] = incl - len;
-                seg_start[lane] = start;
-                seg_t[lane] = tpack;
-                seg_off[lane] = ox;
-                seg_off[32 + lane] = oy;
-                seg_off[64 + lane] = oz;
+                if (len > 0) {
+                    seg_prefix[at] = incl - len;
+                    seg_start[at] = start;
+                    seg_t[at] = tpack;
+                    seg_off[at] = ox;
+                    seg_off[32 + at] = oy;
+                    seg_off[64 + at] = oz;
+                }
                 __syncwarp();
+                seg_first = lane < __popc(nonempty) ? seg_prefix[lane] : 0x7fffffff;
             } else {
                 break;
             }
