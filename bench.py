@@ -412,8 +412,8 @@ def run_reference(args):
         lib.soap(batch, cfg.species, cfg.r_cut, cfg.n_max, cfg.l_max, cfg.sigma, alphas, betas, cfg.average,
                  num_threads=threads)
         times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = batch.atoms * args.steps / total
+    elapsed = sum(times)
+    value = batch.atoms * args.steps / elapsed
     # The GPU arm's config (same workload and shapes); the CPU arm times a
     # bounded sample of it each step, described in cpu_baseline.sample.
     total = args.structures or DEFAULT_STRUCTURES[args.config]
@@ -427,7 +427,7 @@ def run_reference(args):
               f"{args.config} per step")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded generators with the config's shapes; no public dataset)",
         "config": ours_config,

@@ -156,3 +156,20 @@ def test_clock_sampler_follows_visible_devices(monkeypatch):
     monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "5,GPU-0a1b2c3d-0000-1111-2222-333344445555")
     assert bench.smi_device_id(0) == "5"
     assert bench.smi_device_id(1) == "GPU-0a1b2c3d-0000-1111-2222-333344445555"
+
+
+def test_reference_arm_line_is_consistent():
+    """The reference arm's ms_per_step is the time of one timed step of its
+    sample: value x ms_per_step equals the sample's atoms."""
+    import json
+    import re
+
+    if not (ROOT / "oracle" / "_ref" / "libref_soap.so").exists() and not (ROOT / "oracle" / "liboracle_soap.so").exists():
+        pytest.skip("no CPU checker built")
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--config", "1",
+                          "--steps", "1", "--warmup", "0"], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    structures, atoms = map(int, re.match(r"(\d+) structures x (\d+) atoms", line["cpu_baseline"]["sample"]).groups())
+    assert line["impl"] == "reference" and line["steps"] == 1
+    assert abs(line["value"] * line["ms_per_step"] / 1e3 - structures * atoms) <= 0.01 * structures * atoms
