@@ -155,10 +155,10 @@ const void* structure_symbol() {
     template const void* paired_symbol<4, L, true, 2>();                                                          \
     template const void* paired_split_symbol<4, L, false, 2>();                                                   \
     template const void* paired_split_symbol<4, L, true, 2>();                                                    \
-    template void paired_expand<4, L, false, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
-    template void paired_expand<4, L, true, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
-    template const void* paired_expand_symbol<4, L, false, 2>();                                                  \
-    template const void* paired_expand_symbol<4, L, true, 2>();                                                   \
+    template void paired_expand<1, L, false, 3>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
+    template void paired_expand<2, L, true, 3>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
+    template const void* paired_expand_symbol<1, L, false, 3>();                                                  \
+    template const void* paired_expand_symbol<2, L, true, 3>();                                                   \
     template void poly<4, L>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);                \
     template const void* poly_symbol<4, L>();                                                                     \
     template void tail<L, 4>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);                \
@@ -175,10 +175,6 @@ const void* structure_symbol() {
     template const void* paired_symbol<T, L, true, 2>();                                                          \
     template const void* paired_split_symbol<T, L, false, 2>();                                                   \
     template const void* paired_split_symbol<T, L, true, 2>();                                                    \
-    template void paired_expand<T, L, false, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
-    template void paired_expand<T, L, true, 2>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&); \
-    template const void* paired_expand_symbol<T, L, false, 2>();                                                  \
-    template const void* paired_expand_symbol<T, L, true, 2>();                                                   \
     template void tail<L, T>(dim3, size_t, cudaStream_t, const SoapTables&, const SoapPointers&);                \
     template const void* tail_symbol<L, T>();
 

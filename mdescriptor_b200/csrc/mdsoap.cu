@@ -227,8 +227,8 @@ const Variant kVariants[] = {
             "soap_paired_kernel<" #T ", " #L ", " #PREC ", " #MB ">", &launch::tail<L, T>,                   \
             &launch::tail_symbol<L, T>, &launch::paired_split_symbol<T, L, PREC, MB>,                        \
             &launch::tail_generic<L>, &launch::tail_generic_symbol<L>, &launch::paired_walk<PREC>,           \
-            &launch::paired_walk_symbol<PREC>, &launch::paired_expand<T, L, PREC, MB>,                       \
-            &launch::paired_expand_symbol<T, L, PREC, MB>                                                    \
+            &launch::paired_walk_symbol<PREC>, &launch::paired_expand<(PREC ? 2 : 1), L, PREC, 3>,          \
+            &launch::paired_expand_symbol<(PREC ? 2 : 1), L, PREC, 3>                                        \
     }
 
 // Paired-channel kernels: the default wherever they apply (n_max <= 8,
@@ -419,6 +419,11 @@ struct mdsoap_plan {
     size_t structure_smem = 0;
     size_t tail_smem = 0;      // split tail kernel (tab.split_tail)
     size_t walk_smem = 0;      // edge-list split: walk-only kernel (tab.edge_cap > 0)
+    size_t expand_smem = 0;    // edge-list split: expansion-only kernel
+    int32_t expand_chunk = 0;       // its edge chunk and per-warp shared memory (one species per pass,
+    int32_t expand_warp_bytes = 0;  // raw sums flushed straight to the tail's global scratch)
+    CenterLauncher expand_launch = nullptr;
+    const void* (*expand_symbol)() = nullptr;
     std::string kernel_label;  // the kernel(s) a step launches after binning
     int64_t tail_chunk = 1 << 30; // centres per expansion / tail pair of launches (MDSOAP_TAIL_CHUNK)
     int64_t csize = 0;
@@ -518,9 +523,9 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
         check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, variant->walk_sym(), kWarps * 32, walk_smem),
               "walk kernel occupancy");
         st.walk_grid = (int64_t)std::max(per_sm, 1) * sms;
-        check(cudaFuncSetAttribute(variant->expand_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+        check(cudaFuncSetAttribute(expand_symbol(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
               "expansion kernel smem");
-        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, variant->expand_sym(), kWarps * 32, center_smem),
+        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, expand_symbol(), kWarps * 32, expand_smem),
               "expansion kernel occupancy");
         st.expand_grid = (int64_t)std::max(per_sm, 1) * sms;
     }
@@ -619,8 +624,13 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
                 variant->walk(dim3((unsigned)std::min(one_per_warp, std::max<int64_t>(st.walk_grid, 1))), walk_smem,
                               stream, walk_tab, p);
                 check(cudaGetLastError(), "walk kernel launch");
-                variant->expand(dim3((unsigned)std::min(one_per_warp, std::max<int64_t>(st.expand_grid, 1))),
-                                center_smem, stream, tab, p);
+                SoapTables et = tab;
+                et.chunk = expand_chunk;
+                et.r_global = 1;
+                et.warp_bytes = expand_warp_bytes;
+                et.r_offset = 0;
+                expand_launch(dim3((unsigned)std::min(one_per_warp, std::max<int64_t>(st.expand_grid, 1))),
+                              expand_smem, stream, et, p);
                 check(cudaGetLastError(), "expansion kernel launch");
                 variant->center(dim3((unsigned)grid), center_smem, stream, tab, p);
                 check(cudaGetLastError(), "centre kernel launch");
@@ -1155,11 +1165,28 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                 // redoes the centres whose slot overflowed.  Slots of a
                 // chunk take at most 4 GiB too.  MDSOAP_EDGE_CAP sets the
                 // slot size (0: walk and expansion in one kernel).
-                int64_t cap = 0;
+                int64_t cap = 512;
                 if (const char* cap_env = std::getenv("MDSOAP_EDGE_CAP")) cap = std::max<int64_t>(0, std::atoll(cap_env));
                 if (cap > 0 && v.walk && v.expand) {
                     t.edge_cap = (int32_t)std::min<int64_t>(cap, 1 << 20);
+                    t.parity_group = std::max(1, v.maxt / t.ksplit);
                     plan->walk_smem = 256 + 64 * 8 + (size_t)kWarps * paired::kHeaderBytes;
+                    // The expansion-only kernel: one species per pass (two
+                    // banks of partial sums for float64 rows), so few
+                    // registers (168: 3 CTAs per SM, against 2 for the fused
+                    // kernel); the raw sums go straight to the tail's
+                    // scratch; the largest edge chunk whose shared memory
+                    // fits 3 CTAs per SM.
+                    plan->expand_launch = v.expand;
+                    plan->expand_symbol = v.expand_sym;
+                    const size_t ebudget = 228 * 1024 / 3 - 1024;
+                    int echunk = 32;
+                    auto ewarp = [&](int c) { return align16((size_t)paired::kHeaderBytesExpand + (size_t)c * row * 8); };
+                    const size_t eshared = 256;  // exp table only: no beta table in this kernel
+                    while (echunk > 8 && eshared + kWarps * ewarp(echunk) > ebudget) echunk -= 8;
+                    plan->expand_chunk = echunk;
+                    plan->expand_warp_bytes = (int32_t)ewarp(echunk);
+                    plan->expand_smem = eshared + kWarps * ewarp(echunk);
                     const int64_t slot_bytes = (int64_t)t.edge_cap * (int64_t)(sizeof(double4) + sizeof(int32_t)) + 4;
                     plan->tail_chunk = std::min<int64_t>(plan->tail_chunk,
                                                          std::max<int64_t>(4096, (int64_t)(4ull << 30) / slot_bytes));
@@ -1168,9 +1195,12 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                     plan->tail_chunk = std::max<int64_t>(kWarps, std::atoll(chunk_env));
             }
             plan->kernel_label = v.name;
-            if (t.edge_cap > 0)
-                plan->kernel_label = std::string("soap_paired_kernel<1, 0, ") + (v.precise ? "true" : "false") +
-                                     ", 4, walk> + " + v.name + " (edge lists)";
+            if (t.edge_cap > 0) {
+                const std::string prec = v.precise ? "true" : "false";
+                plan->kernel_label = "soap_paired_kernel<1, 0, " + prec + ", 4, walk> + soap_paired_kernel<" +
+                                     (v.precise ? "2" : "1") + ", " + std::to_string(L) + ", " + prec +
+                                     ", 3, expand> (edge lists; overflowed slots: " + v.name + ")";
+            }
             if (t.split_tail == 1)
                 plan->kernel_label += " + soap_tail_kernel<" + std::to_string(L) + ", " + std::to_string(v.maxt) + ">";
             else if (t.split_tail == 2)

@@ -67,6 +67,8 @@ struct SoapTables {
     int32_t grid_size;    // polynomial basis: quadrature nodes (0 for the GTO basis)
     int32_t ksplit;       // paired kernel: partial sums per species neighbour sum (2 in its float64 instantiations)
     int32_t edge_cap;     // edge-list split of the SPLIT path: accepted edges per centre slot (0: not used)
+    int32_t parity_group; // expansion-only kernel: species per pass of the fused kernel, whose accepted-edge
+                          // order sets the partial sum (of ksplit) each edge goes to
     double eta;           // 1 / (2 sigma^2)
     int32_t weight_fn;    // 0 none, 1 polynomial, 2 power, 3 exponential (soap.cpp:389-420)
     int32_t has_w0;       // the exact self pair takes weight w0

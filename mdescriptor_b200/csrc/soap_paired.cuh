@@ -73,6 +73,12 @@ constexpr int kEdgeBytes = kPendingPaired * (5 * 8 + 4); // dx dy dz r2 weight +
 constexpr int kSortBytes = 32 * 2 * 8;             // r2 and weight of a chunk's edges in bank order
 constexpr int kHeaderBytes = kSegBytes + kSegOffBytes + kPreBytes + kEdgeBytes + kSortBytes;
 static_assert(kHeaderBytes % 16 == 0, "harmonic rows must start 16-byte aligned");
+// The expansion-only kernel (MODE 2) has no walk: its region starts with an
+// edge queue of 64 (below chunk <= 32 entries before a fetch of 32 more).
+constexpr int kPendingExpand = 64;
+constexpr int kHeaderBytesExpand = kPendingExpand * (5 * 8 + 4) + kSortBytes;
+static_assert(kHeaderBytesExpand % 16 == 0, "harmonic rows must start 16-byte aligned");
+__host__ __device__ constexpr int header_bytes(int mode) { return mode == 2 ? kHeaderBytesExpand : kHeaderBytes; }
 
 // Real regular solid harmonics of one displacement into the paired row
 // (soap.cpp:101-216, generic Cartesian recurrence; within a degree, j = l - m
@@ -254,7 +260,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             qwv[i] = nn < n ? p.poly[Q + qq * n + nn] : 0.0;
         }
     }
-    const int kShared = 256 + (L + 1) * 64 * 8 + (POLY ? ((Q * 9 * 8 + 15) & ~15) : 0);
+    // The expansion-only kernel keeps no beta table (its tail runs as a kernel of its own).
+    const int kShared = 256 + (MODE == 2 ? 0 : (L + 1) * 64 * 8) + (POLY ? ((Q * 9 * 8 + 15) & ~15) : 0);
     __syncthreads();
 
     unsigned char* region = smem + kShared + (size_t)warp * tab.warp_bytes;
@@ -265,15 +272,18 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     int* qa = reinterpret_cast<int*>(region + paired::kSegBytes + paired::kSegOffBytes);
     int* qt = qa + paired::kPreQueue;
     int* qs = qt + paired::kPreQueue;
-    double* pdx = reinterpret_cast<double*>(region + paired::kSegBytes + paired::kSegOffBytes + paired::kPreBytes);
-    double* pdy = pdx + paired::kPendingPaired;
-    double* pdz = pdy + paired::kPendingPaired;
-    double* pr2 = pdz + paired::kPendingPaired;
-    double* pw = pr2 + paired::kPendingPaired;
-    int32_t* ptype = reinterpret_cast<int32_t*>(pw + paired::kPendingPaired);
-    double* sr2 = reinterpret_cast<double*>(region + paired::kHeaderBytes - paired::kSortBytes);
+    constexpr int kPend = MODE == 2 ? paired::kPendingExpand : paired::kPendingPaired;
+    constexpr int kHead = paired::header_bytes(MODE);
+    double* pdx = reinterpret_cast<double*>(
+        region + (MODE == 2 ? 0 : paired::kSegBytes + paired::kSegOffBytes + paired::kPreBytes));
+    double* pdy = pdx + kPend;
+    double* pdz = pdy + kPend;
+    double* pr2 = pdz + kPend;
+    double* pw = pr2 + kPend;
+    int32_t* ptype = reinterpret_cast<int32_t*>(pw + kPend);
+    double* sr2 = reinterpret_cast<double*>(region + kHead - paired::kSortBytes);
     double* sw = sr2 + 32;
-    double* ybuf = reinterpret_cast<double*>(region + paired::kHeaderBytes);
+    double* ybuf = reinterpret_cast<double*>(region + kHead);
     // POLY: flir_l(r, q) of the current edge, [L+1][Q], after the harmonic rows.
     double* flir = ybuf + tab.chunk * P::ROW;
     // Centres: CTA b owns the contiguous range [c_lo, c_hi) of this launch
@@ -563,19 +573,27 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             } else if (MODE == 2 && fetched < nedges) {
                 // Next 32 edges of the slot, this pass's species, in order.
                 const int e = fetched + lane;
-                bool ok = false;
+                bool ok = false, in_group = false;
                 const double4 d = next_d;
                 const int info = next_info;
                 const int t = info & 0xffff;
                 const bool self = (info >> 16) != 0;
-                if (e < nedges) ok = pooled || (t >= tb && t < te);
+                if (e < nedges) {
+                    ok = pooled || (t >= tb && t < te);
+                    // The fused kernel's pass holding this species: its
+                    // accepted edges, in order, alternate between the
+                    // partial sums (float64 rows).
+                    in_group = pooled || t / tab.parity_group == tb / tab.parity_group;
+                }
                 if (e + 32 < nedges) {
                     next_d = p.edges[slot * tab.edge_cap + e + 32];
                     next_info = p.edge_info[slot * tab.edge_cap + e + 32];
                 }
                 const unsigned mask = __ballot_sync(0xffffffffu, ok);
+                const unsigned group = ks > 1 ? __ballot_sync(0xffffffffu, in_group) : 0u;
                 if (ok) {
                     const int rank = __popc(mask & ((1u << lane) - 1u));
+                    const int grank = __popc(group & ((1u << lane) - 1u));
                     const int q = pcount + rank;
                     double w = 1.0;
                     if (tab.weighted) {
@@ -587,10 +605,10 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     pdz[q] = d.z;
                     pr2[q] = d.w;
                     pw[q] = w;
-                    ptype[q] = (pooled ? 0 : t - tb) * ks + ((naccepted + rank) & (ks - 1));
+                    ptype[q] = (pooled ? 0 : t - tb) * ks + ((naccepted + grank) & (ks - 1));
                 }
                 pcount += __popc(mask);
-                naccepted += __popc(mask);
+                naccepted += __popc(group);
                 fetched += 32;
                 __syncwarp();
             } else if (MODE != 2 && (qn >= 32 || (walk_done && qn > 0))) {
@@ -891,7 +909,9 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     }
     if (SPLIT || tab.split_tail) {
         // The tail runs as its own kernel (soap_tail_kernel): hand the raw
-        // sums over through global scratch, one contiguous block per centre.
+        // sums over through global scratch, one contiguous block per centre
+        // (already there when the flush wrote them to global memory).
+        if (tab.r_global) return;
         const double2* src = reinterpret_cast<const double2*>(R);
         double2* dst = reinterpret_cast<double2*>(p.rbuf + (center - p.grid_begin) * tab.rsize);
         for (int i = lane; i < tab.rsize / 2; i += 32) dst[i] = src[i];
