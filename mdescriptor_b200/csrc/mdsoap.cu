@@ -1167,7 +1167,9 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                 // slot size (0: walk and expansion in one kernel).
                 int64_t cap = 512;
                 if (const char* cap_env = std::getenv("MDSOAP_EDGE_CAP")) cap = std::max<int64_t>(0, std::atoll(cap_env));
-                if (cap > 0 && v.walk && v.expand) {
+                // (Float32 rows: the expansion kernel pairs radial indices k and
+                // k + n_max / 2, so n_max must be even.)
+                if (cap > 0 && v.walk && v.expand && (v.precise || n % 2 == 0)) {
                     t.edge_cap = (int32_t)std::min<int64_t>(cap, 1 << 20);
                     t.parity_group = std::max(1, v.maxt / t.ksplit);
                     plan->walk_smem = 256 + 64 * 8 + (size_t)kWarps * paired::kHeaderBytes;

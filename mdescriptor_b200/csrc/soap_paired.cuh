@@ -327,20 +327,40 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const bool regs_tail = n == 8 && S * ks <= MAXT && tab.average != 1;
 
     // This lane's channel pair: group g of radial index k.
-    const int g = lane / n, k = lane - (lane / n) * n;
+    // kPair (expansion-only kernel, float32 rows, n_max even): the two half
+    // warps take alternate edges of a run, and lane (g, kp) of a half owns
+    // radial indices kp and kp + n/2 of group g -- each harmonic view it
+    // loads serves two channels, half the shared-memory loads per edge.  The
+    // halves' sums are added at the flush, where half h writes row kp + h n/2.
+    constexpr bool kPair = MODE == 2 && !PRECISE && !POLY && MAXT == 1;
+    const int nh = kPair ? max(n >> 1, 1) : n;
+    const int g = kPair ? (lane & 15) / nh : lane / n;
+    const int kp = kPair ? (lane & 15) - g * nh : lane - g * n;  // first radial index
+    const int k = kPair ? kp + (lane >> 4) * nh : kp;            // radial index of the flushed row
     const bool lane_on = g < P::G;
     const int lA = lane_on ? (g == 0 ? L : L - g) : 0;
     const int lB = (lane_on && g > 0 && g - 1 < L - g) ? g - 1 : -1;
     const int split = 2 * lA + 1;
     double prefA = 0.0, nEA = 0.0, prefB = 0.0, nEB = 0.0;
+    double prefA1 = 0.0, nEA1 = 0.0, prefB1 = 0.0, nEB1 = 0.0;  // kPair: radial index kp + n/2
     if (lane_on) {
-        const RadialItem a = p.items[(L - lA) * n + k];  // items are sorted by l descending
+        const RadialItem a = p.items[(L - lA) * n + kp];  // items are sorted by l descending
         prefA = a.prefactor;
         nEA = -a.exponent;
         if (lB >= 0) {
-            const RadialItem b = p.items[(L - lB) * n + k];
+            const RadialItem b = p.items[(L - lB) * n + kp];
             prefB = b.prefactor;
             nEB = -b.exponent;
+        }
+        if (kPair) {
+            const RadialItem a1 = p.items[(L - lA) * n + kp + nh];
+            prefA1 = a1.prefactor;
+            nEA1 = -a1.exponent;
+            if (lB >= 0) {
+                const RadialItem b1 = p.items[(L - lB) * n + kp + nh];
+                prefB1 = b1.prefactor;
+                nEB1 = -b1.exponent;
+            }
         }
     }
     bool first_above[P::NSEL > 0 ? P::NSEL : 1];
@@ -368,9 +388,10 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     int written = 0;  // MODE 1: accepted edges of this centre so far
     for (int tb = 0; tb < S; tb += pass_species) {
         const int te = min(S, tb + pass_species);
-        double acc[MAXT][P::W];
+        // kPair: acc[0] radial index kp, acc[1] kp + n/2.
+        double acc[kPair ? 2 : MAXT][P::W];
 #pragma unroll
-        for (int t = 0; t < MAXT; ++t)
+        for (int t = 0; t < (kPair ? 2 : MAXT); ++t)
 #pragma unroll
             for (int m = 0; m < P::W; ++m) acc[t][m] = 0.0;
 
@@ -480,6 +501,48 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             }
             __syncwarp();
             const bool weighted = tab.weighted != 0;
+            if constexpr (kPair) {
+                // Two edges per step, one per half warp (one species, one bank).
+                const int half = lane >> 4;
+                for (int ea = 0; ea < count; ea += 2) {
+                    const bool live = ea + half < count;
+                    const int e = live ? ea + half : count - 1;
+                    const double u = sr2[e];
+                    double gA0 = scaled_exp<false>(nEA * u, prefA, etab);
+                    double gB0 = scaled_exp<false>(nEB * u, prefB, etab);
+                    double gA1 = scaled_exp<false>(nEA1 * u, prefA1, etab);
+                    double gB1 = scaled_exp<false>(nEB1 * u, prefB1, etab);
+                    if (weighted) {
+                        const double w = sw[e];
+                        gA0 *= w;
+                        gB0 *= w;
+                        gA1 *= w;
+                        gB1 *= w;
+                    }
+                    if (!live) gA0 = gB0 = gA1 = gB1 = 0.0;
+                    double gs0[P::NSEL > 0 ? P::NSEL : 1], gs1[P::NSEL > 0 ? P::NSEL : 1];
+#pragma unroll
+                    for (int q = 0; q < P::NSEL; ++q) {
+                        gs0[q] = first_above[q] ? gA0 : gB0;
+                        gs1[q] = first_above[q] ? gA1 : gB1;
+                    }
+                    const double2* yv = reinterpret_cast<const double2*>(ybuf + e * P::ROW + view);
+#pragma unroll
+                    for (int mm = 0; mm < (P::W + 1) / 2; ++mm) {
+                        const double2 y = yv[mm];
+                        const int m0 = 2 * mm, m1 = 2 * mm + 1;
+                        const bool a0 = m0 < 2 * P::LAMIN + 1, a1 = m1 < 2 * P::LAMIN + 1;
+                        acc[0][m0] = fma(a0 ? gA0 : gs0[(m0 - 1) / 2 - P::LAMIN], y.x, acc[0][m0]);
+                        acc[1][m0] = fma(a0 ? gA1 : gs1[(m0 - 1) / 2 - P::LAMIN], y.x, acc[1][m0]);
+                        if (m1 < P::W) {
+                            acc[0][m1] = fma(a1 ? gA0 : gs0[(m1 - 1) / 2 - P::LAMIN], y.y, acc[0][m1]);
+                            acc[1][m1] = fma(a1 ? gA1 : gs1[(m1 - 1) / 2 - P::LAMIN], y.y, acc[1][m1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                return;
+            }
             // One edge per step: two independent exp chains per lane are
             // enough to cover their latency, and the shorter loop body (one
             // copy per species bank) stays in the instruction cache.
@@ -868,6 +931,15 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             }
         }
 
+        if constexpr (kPair) {
+            // Both halves' sums of both radial indices; half h keeps index kp + h n/2.
+#pragma unroll
+            for (int m = 0; m < P::W; ++m) {
+                const double v0 = acc[0][m] + __shfl_xor_sync(0xffffffffu, acc[0][m], 16);
+                const double v1 = acc[1][m] + __shfl_xor_sync(0xffffffffu, acc[1][m], 16);
+                acc[0][m] = (lane >> 4) ? v1 : v0;
+            }
+        }
         // Flush the raw sums times the species weight: row (t, k), degree l
         // at columns col_off(l) .. + kpad(l), padding written as 0 where the
         // tail reads it.
@@ -891,8 +963,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                         else if (lB >= 0)
                             row[colB + m] = w * v;
                     }
-                    // The register tail never reads the padding (tail_regs_n8 masks it).
-                    if (!regs_tail) {
+                    // The register tails (tail_regs_n8, soap_tail_kernel) never read the padding.
+                    if (!regs_tail && !(MODE == 2 && tab.split_tail == 1)) {
                         for (int m = split; m < padA; ++m) row[colA + m] = 0.0;
                         if (lB >= 0)
                             for (int m = 2 * lB + 1; m < padB; ++m) row[colB + split + m] = 0.0;

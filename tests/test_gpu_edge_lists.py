@@ -1,17 +1,23 @@
 """The edge-list split of the split-tail path (MDSOAP_EDGE_CAP > 0): a
 walk-only kernel writes each centre's accepted edges to a slot of edge_cap
 edges, an expansion-only kernel reads them back, and the fused kernel redoes
-the centres whose slot overflowed.  The edges reach the expansion in the
-order the fused kernel accepts them, so every row must equal the fused
-kernel's bit for bit: with slots large enough for every centre, with some
-centres overflowing (cap 64, 200) and with every centre overflowing (cap 1),
-in both dtypes, with weighting, pooled species and compression layouts."""
+the centres whose slot overflowed: with slots large enough for every centre,
+with some centres overflowing (cap 64, 200) and with every centre
+overflowing (cap 1), in both dtypes, with weighting, pooled species and
+compression layouts.  The edges reach the expansion in the order the fused
+kernel accepts them and float64 plans add them in that order, so float64
+rows must equal the fused kernel's bit for bit.  For float32 rows the
+expansion kernel lets the two half warps take alternate edges and adds the
+two partial sums at the end, so the fp64 sums may differ from the fused
+kernel's in their last bits: those rows are held to the float32 bound (and
+are mostly identical)."""
 
 from __future__ import annotations
 
 import numpy as np
 import pytest
 
+from _util import assert_features_close
 from mdescriptor_b200 import workloads
 from mdescriptor_b200.basis import basis_gto
 from mdescriptor_b200.soap import Soap
@@ -49,4 +55,7 @@ def test_edge_lists_match_the_fused_kernel_bitwise(cuda_device, monkeypatch, nam
     for cap in ("512", "200", "64", "1"):
         kernel, got = rows(cap)
         assert "edge lists" in kernel
-        assert np.array_equal(got.view(np.uint8), fused.view(np.uint8)), f"cap {cap}: rows differ from the fused kernel"
+        if dtype == "float64":
+            assert np.array_equal(got.view(np.uint8), fused.view(np.uint8)), f"cap {cap}: rows differ from the fused kernel"
+        else:
+            assert_features_close(got, fused, dtype)

@@ -30,6 +30,9 @@ def make(average, dtype, compression="off"):
 @pytest.mark.parametrize("average", ["off", "outer"])
 @pytest.mark.parametrize("dtype", ["float32", "float64"])
 def test_split_fused_and_chunked_tails_agree(oracle, cuda_device, monkeypatch, average, dtype):
+    # Walk and expansion in one kernel throughout (the edge-list split, which
+    # regroups float32 sums, has its own test: test_gpu_edge_lists.py).
+    monkeypatch.setenv("MDSOAP_EDGE_CAP", "0")
     batch = workloads.config2(structures=12, seed=5)
     split = make(average, dtype)
     # float64 plans split each neighbour sum over two register banks, so four
