@@ -467,19 +467,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         };
 
         auto process = [&](int count) {
-            if constexpr (MODE == 1) {
-                // Walk only: the chunk goes to the centre's slot (beyond
-                // edge_cap only counted: the centre is then redone by MODE 0).
-                const int e = written + lane;
-                if (lane < count && e < tab.edge_cap) {
-                    const int64_t at = slot * tab.edge_cap + e;
-                    p.edges[at] = make_double4(pdx[lane], pdy[lane], pdz[lane], pr2[lane]);
-                    p.edge_info[at] = ptype[lane];
-                }
-                written += count;
-                __syncwarp();
-                return;
-            }
+            // (The walk-only kernel never queues: its accepted edges go
+            // straight to the centre's slot, beyond edge_cap only counted.)
             // Stable counting sort of the chunk by species bank; each edge's
             // harmonic row, r^2 and weight go to its rank, so a bank's edges
             // are consecutive rows.
@@ -700,7 +689,14 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     }
                 }
                 const unsigned mask = __ballot_sync(0xffffffffu, ok);
-                if (ok) {
+                if (MODE == 1 && ok) {
+                    // Walk only: straight to the centre's slot.
+                    const int e = written + __popc(mask & ((1u << lane) - 1u));
+                    if (e < tab.edge_cap) {
+                        p.edges[slot * tab.edge_cap + e] = make_double4(dx, dy, dz, d2);
+                        p.edge_info[slot * tab.edge_cap + e] = t;
+                    }
+                } else if (ok) {
                     const int rank = __popc(mask & ((1u << lane) - 1u));
                     const int q = pcount + rank;
                     pdx[q] = dx;
@@ -708,9 +704,12 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     pdz[q] = dz;
                     pr2[q] = d2;
                     pw[q] = w;
-                    ptype[q] = MODE == 1 ? t : (pooled ? 0 : t - tb) * ks + ((naccepted + rank) & (ks - 1));
+                    ptype[q] = (pooled ? 0 : t - tb) * ks + ((naccepted + rank) & (ks - 1));
                 }
-                pcount += __popc(mask);
+                if (MODE == 1)
+                    written += __popc(mask);
+                else
+                    pcount += __popc(mask);
                 naccepted += __popc(mask);
                 // Move the remaining survivors (up to 63) to the queue's front.
                 const int rem = qn - count;
@@ -809,16 +808,30 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                                 if (pooled) w *= tab.species_weight[ty];
                             }
                         }
+                        if constexpr (MODE == 1) {
+                            // Walk only: straight to the centre's slot (the queue
+                            // stays empty, so `at` is the edge's rank among the
+                            // centre's accepted edges after `written`).
+                            const int e = written + at;
+                            if (e < tab.edge_cap) {
+                                p.edges[slot * tab.edge_cap + e] = make_double4(x, y, z, r);
+                                p.edge_info[slot * tab.edge_cap + e] = info;
+                            }
+                            return;
+                        }
                         pdx[at] = x;
                         pdy[at] = y;
                         pdz[at] = z;
                         pr2[at] = r;
                         pw[at] = w;
-                        ptype[at] = MODE == 1 ? info : (pooled ? 0 : ty - tb);
+                        ptype[at] = pooled ? 0 : ty - tb;
                     };
                     if (dirA) push(pcount + __popc(dA & lt), aA, tyA, iA, xA, yA, zA, rA);
                     if (dirB) push(pcount + __popc(dA) + __popc(dB & lt), aB, tyB, iB, xB, yB, zB, rB);
-                    pcount += __popc(dA) + __popc(dB);
+                    if (MODE == 1)
+                        written += __popc(dA) + __popc(dB);
+                    else
+                        pcount += __popc(dA) + __popc(dB);
                     naccepted += __popc(dA) + __popc(dB);
                     passA = passA && !dirA;
                     passB = passB && !dirB;
