@@ -284,6 +284,17 @@ const char* mdsoap_plan_kernel(const mdsoap_plan* plan);
  * reference, whose CPU path calls std::exp, soap.cpp:895-896). */
 int mdsoap_probe_exp(int32_t device, const double* x, int64_t count, double* ours, double* cuda_exp);
 
+/* The radial factors pref * exp(-e u) as the kernels form them, beside
+ * pref * CUDA's exp(-e u), on `device` for `count` host triples (u, e, pref),
+ * written to the host arrays `ours` and `cuda_exp`.  form 0: the float64-row
+ * form; 1: the float32-row form of the one-kernel walk; 2: the float32-row
+ * form of the expansion-only kernel (exponent folded into the reduction,
+ * 64-entry table).  The caller keeps e u in [0, 700] and the result a normal
+ * double, as the plans do (test support; no counterpart in the reference,
+ * whose CPU path calls std::exp, soap.cpp:895-896). */
+int mdsoap_probe_radial(int32_t device, int32_t form, const double* u, const double* e, const double* pref,
+                        int64_t count, double* ours, double* cuda_exp);
+
 /* Failure-detection probe (test support; no counterpart in the reference):
  * launches one thread that arms an mbarrier for a bulk copy it never issues
  * and waits for it with the tail kernel's own bounded wait (limit_ns, at most

@@ -151,6 +151,8 @@ def _load() -> ctypes.CDLL:
     lib.mdsoap_plan_launch_count.restype = ctypes.c_int
     lib.mdsoap_probe_exp.argtypes = [ctypes.c_int32, _P, ctypes.c_int64, _P, _P]
     lib.mdsoap_probe_exp.restype = ctypes.c_int
+    lib.mdsoap_probe_radial.argtypes = [ctypes.c_int32, ctypes.c_int32, _P, _P, _P, ctypes.c_int64, _P, _P]
+    lib.mdsoap_probe_radial.restype = ctypes.c_int
     lib.mdsoap_probe_bounded_wait.argtypes = [ctypes.c_int32, ctypes.c_uint64]
     lib.mdsoap_probe_bounded_wait.restype = ctypes.c_int
     lib.mdsoap_probe_fp64_fma.argtypes = [ctypes.c_int32, _P]
@@ -197,6 +199,7 @@ EXPORTED = (
     "mdsoap_plan_last_timing",
     "mdsoap_plan_launch_count",
     "mdsoap_probe_exp",
+    "mdsoap_probe_radial",
     "mdsoap_probe_fp64_fma",
     "mdsoap_probe_bounded_wait",
     "mdsoap_graph_build",

@@ -335,6 +335,33 @@ __global__ void exp_probe_kernel(const double* __restrict__ x, int64_t count, do
     }
 }
 
+// The radial-factor forms the kernels use, beside pref * CUDA's exp() of the
+// same argument: 0 scaled_exp<true> (float64 rows), 1 scaled_exp<false>
+// (float32 rows, one-kernel walk), 2 scaled_exp_folded<64> (float32 rows,
+// expansion-only kernel).
+__global__ void radial_probe_kernel(int form, const double* __restrict__ u, const double* __restrict__ e,
+                                    const double* __restrict__ pref, int64_t count, double* __restrict__ ours,
+                                    double* __restrict__ cuda_exp) {
+    __shared__ double t32[32], t64[64];
+    for (int i = threadIdx.x; i < 64; i += blockDim.x) {
+        t64[i] = kExp2Table64[i];
+        if (i < 32) t32[i] = kExp2Table[i];
+    }
+    __syncthreads();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x) {
+        const double x = -e[i] * u[i];
+        double v;
+        if (form == 0)
+            v = scaled_exp<true>(x, pref[i], t32);
+        else if (form == 1)
+            v = scaled_exp<false>(x, pref[i], t32);
+        else
+            v = scaled_exp_folded<64>(u[i], -e[i] * folded_scale(64), pref[i], t64);
+        ours[i] = v;
+        cuda_exp[i] = pref[i] * exp(x);
+    }
+}
+
 // The tail kernel's bounded wait made to run out: one thread arms an mbarrier
 // for 16 bytes of copies and issues none, so the phase cannot complete; the
 // wait (bulk::wait, the tail kernel's own) gives up after limit_ns and the
@@ -1184,7 +1211,8 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                     const size_t ebudget = 228 * 1024 / 3 - 1024;
                     int echunk = 32;
                     auto ewarp = [&](int c) { return align16((size_t)paired::kHeaderBytesExpand + (size_t)c * row * 8); };
-                    const size_t eshared = 256;  // exp table only: no beta table in this kernel
+                    // exp table only: no beta table in this kernel
+                    const size_t eshared = (size_t)paired::exp_table_bytes(2, v.precise);
                     while (echunk > 8 && eshared + kWarps * ewarp(echunk) > ebudget) echunk -= 8;
                     plan->expand_chunk = echunk;
                     plan->expand_warp_bytes = (int32_t)ewarp(echunk);
@@ -1803,6 +1831,40 @@ int mdsoap_probe_exp(int32_t device, const double* x, int64_t count, double* our
         return MDSOAP_OK;
     } catch (const Failure& f) {
         return fail(f.status, f.message);
+    }
+}
+
+int mdsoap_probe_radial(int32_t device, int32_t form, const double* u, const double* e, const double* pref,
+                        int64_t count, double* ours, double* cuda_exp) {
+    if (form < 0 || form > 2) return fail(MDSOAP_INVALID_ARGUMENT, "form must be 0, 1 or 2");
+    if (count < 0 || (count > 0 && (!u || !e || !pref || !ours || !cuda_exp)))
+        return fail(MDSOAP_INVALID_ARGUMENT, "null argument");
+    try {
+        int devices = 0;
+        if (cudaGetDeviceCount(&devices) != cudaSuccess || device < 0 || device >= devices)
+            raise(MDSOAP_DEVICE_UNAVAILABLE, "CUDA device unavailable");
+        check(cudaSetDevice(device), "cudaSetDevice");
+        if (count == 0) return MDSOAP_OK;
+        DeviceBytes du, de, dp, d1, d2;
+        const size_t bytes = 8 * (size_t)count;
+        du.reserve(bytes, "probe input");
+        de.reserve(bytes, "probe input");
+        dp.reserve(bytes, "probe input");
+        d1.reserve(bytes, "probe output");
+        d2.reserve(bytes, "probe output");
+        check(cudaMemcpy(du.ptr, u, bytes, cudaMemcpyHostToDevice), "probe upload");
+        check(cudaMemcpy(de.ptr, e, bytes, cudaMemcpyHostToDevice), "probe upload");
+        check(cudaMemcpy(dp.ptr, pref, bytes, cudaMemcpyHostToDevice), "probe upload");
+        radial_probe_kernel<<<256, 256>>>(form, du.as<double>(), de.as<double>(), dp.as<double>(), count,
+                                          d1.as<double>(), d2.as<double>());
+        check(cudaGetLastError(), "probe launch");
+        check(cudaMemcpy(ours, d1.ptr, bytes, cudaMemcpyDeviceToHost), "probe download");
+        check(cudaMemcpy(cuda_exp, d2.ptr, bytes, cudaMemcpyDeviceToHost), "probe download");
+        return MDSOAP_OK;
+    } catch (const Failure& f) {
+        return fail(f.status, f.message);
+    } catch (const std::exception& ex) {
+        return fail(MDSOAP_INTERNAL, ex.what());
     }
 }
 

@@ -79,6 +79,12 @@ constexpr int kPendingExpand = 64;
 constexpr int kHeaderBytesExpand = kPendingExpand * (5 * 8 + 4) + kSortBytes;
 static_assert(kHeaderBytesExpand % 16 == 0, "harmonic rows must start 16-byte aligned");
 __host__ __device__ constexpr int header_bytes(int mode) { return mode == 2 ? kHeaderBytesExpand : kHeaderBytes; }
+// Exp table of the expansion-only kernel's float32 rows (scaled_exp_folded).
+constexpr int kFoldT = 64;
+// CTA shared memory the exp table takes (the kernel's first bytes).
+__host__ __device__ constexpr int exp_table_bytes(int mode, bool precise) {
+    return (mode == 2 && !precise && kFoldT == 64) ? 512 : 256;
+}
 
 // Real regular solid harmonics of one displacement into the paired row
 // (soap.cpp:101-216, generic Cartesian recurrence; within a degree, j = l - m
@@ -241,8 +247,15 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
     const bool pooled = tab.compression == 1;
     // CTA-shared: exp table (32 doubles), then beta as [l][n][k] scaled by
     // pi^{3/2} and zero padded to 8 x 8.
+    // The expansion-only kernel's float32 rows use scaled_exp_folded<kFoldT>
+    // (a table of kFoldT entries); everything else the 32-entry table.
+    constexpr bool kFolded = MODE == 2 && !PRECISE && !POLY;
     double* etab = reinterpret_cast<double*>(smem);
-    if (threadIdx.x < 32) etab[threadIdx.x] = kExp2Table[threadIdx.x];
+    if constexpr (kFolded && paired::kFoldT == 64) {
+        for (int i = threadIdx.x; i < 64; i += blockDim.x) etab[i] = kExp2Table64[i];
+    } else {
+        if (threadIdx.x < 32) etab[threadIdx.x] = kExp2Table[threadIdx.x];
+    }
     double* bt = reinterpret_cast<double*>(smem + 256);
     if (!SPLIT)
         for (int i = threadIdx.x; i < (L + 1) * 64; i += blockDim.x) {
@@ -261,7 +274,8 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         }
     }
     // The expansion-only kernel keeps no beta table (its tail runs as a kernel of its own).
-    const int kShared = 256 + (MODE == 2 ? 0 : (L + 1) * 64 * 8) + (POLY ? ((Q * 9 * 8 + 15) & ~15) : 0);
+    const int kShared = paired::exp_table_bytes(MODE, PRECISE) + (MODE == 2 ? 0 : (L + 1) * 64 * 8) +
+                        (POLY ? ((Q * 9 * 8 + 15) & ~15) : 0);
     __syncthreads();
 
     unsigned char* region = smem + kShared + (size_t)warp * tab.warp_bytes;
@@ -493,14 +507,16 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             if constexpr (kPair) {
                 // Two edges per step, one per half warp (one species, one bank).
                 const int half = lane >> 4;
+                constexpr double fs = folded_scale(paired::kFoldT);
+                const double sA0 = nEA * fs, sB0 = nEB * fs, sA1 = nEA1 * fs, sB1 = nEB1 * fs;
                 for (int ea = 0; ea < count; ea += 2) {
                     const bool live = ea + half < count;
                     const int e = live ? ea + half : count - 1;
                     const double u = sr2[e];
-                    double gA0 = scaled_exp<false>(nEA * u, prefA, etab);
-                    double gB0 = scaled_exp<false>(nEB * u, prefB, etab);
-                    double gA1 = scaled_exp<false>(nEA1 * u, prefA1, etab);
-                    double gB1 = scaled_exp<false>(nEB1 * u, prefB1, etab);
+                    double gA0 = scaled_exp_folded<paired::kFoldT>(u, sA0, prefA, etab);
+                    double gB0 = scaled_exp_folded<paired::kFoldT>(u, sB0, prefB, etab);
+                    double gA1 = scaled_exp_folded<paired::kFoldT>(u, sA1, prefA1, etab);
+                    double gB1 = scaled_exp_folded<paired::kFoldT>(u, sB1, prefB1, etab);
                     if (weighted) {
                         const double w = sw[e];
                         gA0 *= w;

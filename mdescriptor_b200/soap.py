@@ -327,6 +327,18 @@ def probe_exp(x, device: int = 0) -> tuple[np.ndarray, np.ndarray]:
     return ours, cuda
 
 
+def probe_radial(form: int, u, e, pref, device: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """The kernels' radial factor pref * exp(-e u) in form 0 (float64 rows), 1
+    (float32 rows, one-kernel walk) or 2 (float32 rows, expansion-only kernel),
+    and pref * CUDA's exp(-e u), on one device."""
+    u, e, pref = (np.ascontiguousarray(a, dtype=np.float64) for a in np.broadcast_arrays(u, e, pref))
+    ours = np.empty_like(u)
+    cuda = np.empty_like(u)
+    raise_for(lib.mdsoap_probe_radial(int(device), int(form), u.ctypes.data, e.ctypes.data, pref.ctypes.data, u.size,
+                                      ours.ctypes.data, cuda.ctypes.data))
+    return ours, cuda
+
+
 def device_count() -> int:
     return int(lib.mdsoap_device_count())
 

@@ -46,3 +46,38 @@ def test_exp_flushes_below_the_double_range(cuda_device):
     ours, cuda = probe_exp(x, cuda_device)
     assert (ours == 0.0).all()
     assert (cuda <= 3.31e-308).all()
+
+
+def _radial_args(seed):
+    """Arguments spanning what the plans allow: exponents e of the GTO channels
+    (0.01 .. 3 per A^2), r^2 = u up to the padded cutoff^2 and beyond, e u up
+    to 700, prefactors over many decades; results kept normal doubles."""
+    rng = np.random.default_rng(seed)
+    n = 600_000
+    e = np.exp(rng.uniform(np.log(0.01), np.log(3.0), n))
+    u = np.concatenate([rng.uniform(0.0, 100.0, n // 2), rng.uniform(0.0, 700.0, n - n // 2) / e[n // 2:]])
+    u[:1000] = 0.0                                            # the exact self pair
+    pref = np.exp(rng.uniform(np.log(1e-6), np.log(1e6), n))
+    keep = (e * u <= 700.0) & (pref * np.exp(-e * u) >= 1e-300)
+    return u[keep], e[keep], pref[keep]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("form,bound", [(0, 1e-15), (1, 1e-13), (2, 2e-13)],
+                         ids=["float64-rows", "float32-rows-fused", "float32-rows-folded"])
+def test_radial_factor_forms_against_cuda_exp(cuda_device, form, bound):
+    """The kernels' radial factors pref * exp(-e u) (Tang's method with the
+    prefactor folded into the table factor) against pref * CUDA's exp(-e u):
+    the float64-row form within a few ulp; the float32-row forms (one series
+    term and one reduction step fewer; the expansion-only kernel's form also
+    folds e into the reduction and uses a 64-entry table) within a few 1e-14
+    relative, bounded here at 1e-13 and 2e-13 -- far below what a float32
+    row resolves."""
+    from mdescriptor_b200.soap import probe_radial
+
+    u, e, pref = _radial_args(11 + form)
+    ours, cuda = probe_radial(form, u, e, pref, cuda_device)
+    assert np.isfinite(ours).all()
+    rel = np.abs(ours - cuda) / np.abs(cuda)
+    assert rel.max() <= bound, f"max relative error {rel.max():.3e}"
+    assert np.array_equal(ours[u == 0.0], pref[u == 0.0])    # exp(0) exactly: the self pair
