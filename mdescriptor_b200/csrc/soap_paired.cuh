@@ -27,6 +27,11 @@
 //     exponent field); species weights multiply the raw sums once, at the
 //     flush, instead of every edge.
 //
+// Plans whose tail runs as a kernel of its own (SPLIT) take the walk and the
+// expansion as two instantiations (MODE 1 and 2 below) over per-centre edge
+// lists in HBM: the walk needs no accumulators and the expansion no walk
+// state, so each keeps more warps resident than the one-kernel form.
+//
 // The coefficient block layout, the beta transform and the power spectrum on
 // the fp64 tensor cores are dmma.cuh's, as in soap_center_kernel.
 #pragma once
