@@ -860,16 +860,16 @@ soap_paired_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                 const unsigned maskA = __ballot_sync(0xffffffffu, passA);
                 const unsigned maskB = __ballot_sync(0xffffffffu, passB);
                 if (passA) {
-                    const int slot = qn + __popc(maskA & lt);
-                    qa[slot] = aA;
-                    qt[slot] = seg_t[iA];
-                    qs[slot] = tyA;
+                    const int at = qn + __popc(maskA & lt);
+                    qa[at] = aA;
+                    qt[at] = seg_t[iA];
+                    qs[at] = tyA;
                 }
                 if (passB) {
-                    const int slot = qn + __popc(maskA) + __popc(maskB & lt);
-                    qa[slot] = aB;
-                    qt[slot] = seg_t[iB];
-                    qs[slot] = tyB;
+                    const int at = qn + __popc(maskA) + __popc(maskB & lt);
+                    qa[at] = aB;
+                    qt[at] = seg_t[iB];
+                    qs[at] = tyB;
                 }
                 qn += __popc(maskA) + __popc(maskB);
                 q0 += 64;
