@@ -446,6 +446,9 @@ struct mdsoap_plan {
     size_t structure_smem = 0;
     size_t tail_smem = 0;      // split tail kernel (tab.split_tail)
     size_t walk_smem = 0;      // edge-list split: walk-only kernel (tab.edge_cap > 0)
+    CenterLauncher walk_launch = nullptr;   // its launcher and symbol (paired or centre plans)
+    const void* (*walk_symbol)() = nullptr;
+    int64_t edge_chunk = 1 << 30;  // centre plans: centres per walk / centre-kernel pair of launches
     size_t expand_smem = 0;    // edge-list split: expansion-only kernel
     int32_t expand_chunk = 0;       // its edge chunk and per-warp shared memory (one species per pass,
     int32_t expand_warp_bytes = 0;  // raw sums flushed straight to the tail's global scratch)
@@ -545,16 +548,18 @@ void mdsoap_plan::configure_smem(DeviceState& st) {
     if (tab.edge_cap > 0) {
         int per_sm = 0, sms = 0;
         check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, st.device), "SM count");
-        check(cudaFuncSetAttribute(variant->walk_sym(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+        check(cudaFuncSetAttribute(walk_symbol(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
               "walk kernel smem");
-        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, variant->walk_sym(), kWarps * 32, walk_smem),
+        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, walk_symbol(), kWarps * 32, walk_smem),
               "walk kernel occupancy");
         st.walk_grid = (int64_t)std::max(per_sm, 1) * sms;
-        check(cudaFuncSetAttribute(expand_symbol(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
-              "expansion kernel smem");
-        check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, expand_symbol(), kWarps * 32, expand_smem),
-              "expansion kernel occupancy");
-        st.expand_grid = (int64_t)std::max(per_sm, 1) * sms;
+        if (expand_symbol) {
+            check(cudaFuncSetAttribute(expand_symbol(), cudaFuncAttributeMaxDynamicSharedMemorySize, optin),
+                  "expansion kernel smem");
+            check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, expand_symbol(), kWarps * 32, expand_smem),
+                  "expansion kernel occupancy");
+            st.expand_grid = (int64_t)std::max(per_sm, 1) * sms;
+        }
     }
     // The paired kernel runs persistent: as many CTAs as fit on the device,
     // each over a contiguous range of centres.  MDSOAP_PERSISTENT=0 launches
@@ -687,7 +692,37 @@ void mdsoap_plan::run_block(DeviceState& st, const DeviceBatch& b, int64_t s0, i
             st.work.rbuf.reserve(8 * (size_t)std::max<int64_t>(centers, 1) * tab.rsize, "coefficient scratch");
             p.rbuf = st.work.rbuf.as<double>();
         }
-        if (centers > 0) {
+        if (centers > 0 && tab.edge_cap > 0 && !variant->paired) {
+            // Centre kernel on edge lists: per chunk, the walk-only kernel
+            // fills the slots, then the centre kernel reads them.
+            const int64_t chunk = std::min<int64_t>(centers, edge_chunk);
+            const size_t slots = (size_t)std::max<int64_t>(chunk, 1);
+            st.work.edges.reserve(slots * (size_t)tab.edge_cap * sizeof(double4), "edge slots");
+            st.work.edge_info.reserve(slots * (size_t)tab.edge_cap * sizeof(int32_t), "edge slots");
+            st.work.edge_count.reserve(slots * sizeof(int32_t), "edge counts");
+            p.edges = st.work.edges.as<double4>();
+            p.edge_info = st.work.edge_info.as<int32_t>();
+            p.edge_count = st.work.edge_count.as<int32_t>();
+            SoapTables walk_tab = tab;
+            walk_tab.warp_bytes = paired::kHeaderBytes;
+            for (int64_t c0 = a0; c0 < a1; c0 += chunk) {
+                p.grid_begin = c0;
+                p.grid_end = std::min(a1, c0 + chunk);
+                const int64_t one_per_warp = (p.grid_end - c0 + kWarps - 1) / kWarps;
+                NvtxRange range("mdsoap walk + expansion");
+                walk_launch(dim3((unsigned)std::min(one_per_warp, std::max<int64_t>(st.walk_grid, 1))), walk_smem,
+                            stream, walk_tab, p);
+                check(cudaGetLastError(), "walk kernel launch");
+                variant->center(dim3((unsigned)one_per_warp), center_smem, stream, tab, p);
+                check(cudaGetLastError(), "centre kernel launch");
+                launches.fetch_add(2, std::memory_order_relaxed);
+            }
+            p.grid_begin = a0;
+            p.grid_end = a1;
+            p.edges = nullptr;
+            p.edge_info = nullptr;
+            p.edge_count = nullptr;
+        } else if (centers > 0) {
             int64_t grid = (centers + kWarps - 1) / kWarps;
             if (variant->paired && st.center_grid > 0) grid = std::min(grid, st.center_grid);
             NvtxRange range("mdsoap expansion");
@@ -1199,6 +1234,8 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
                 if (cap > 0 && v.walk && v.expand && (v.precise || n % 2 == 0)) {
                     t.edge_cap = (int32_t)std::min<int64_t>(cap, 1 << 20);
                     t.parity_group = std::max(1, v.maxt / t.ksplit);
+                    plan->walk_launch = v.walk;
+                    plan->walk_symbol = v.walk_sym;
                     plan->walk_smem = 256 + 64 * 8 + (size_t)kWarps * paired::kHeaderBytes;
                     // The expansion-only kernel: one species per pass (two
                     // banks of partial sums for float64 rows), so few
@@ -1294,6 +1331,26 @@ int mdsoap_plan_create(const mdsoap_params* params, mdsoap_plan** plan_out) {
         plan->center_smem = beta_smem + kWarps * (size_t)t.warp_bytes;
         plan->structure_smem = q.average == MDSOAP_AVERAGE_INNER ? (size_t)t.csize * 8 : 0;
         plan->csize = t.csize;
+        {
+            // Edge lists: the paired walk-only kernel (prefiltered candidates,
+            // float32 rows with certified pairs) writes each centre's accepted
+            // edges to a slot that the centre kernel reads instead of walking
+            // (centres whose slot overflowed walk themselves).  Slots of a
+            // chunk take at most 4 GiB.  MDSOAP_EDGE_CAP as for the paired plans.
+            int64_t cap = 512;
+            if (const char* cap_env = std::getenv("MDSOAP_EDGE_CAP")) cap = std::max<int64_t>(0, std::atoll(cap_env));
+            if (cap > 0) {
+                const bool f64 = q.output_dtype == MDSOAP_FLOAT64;
+                t.edge_cap = (int32_t)std::min<int64_t>(cap, 1 << 20);
+                plan->walk_launch = f64 ? &launch::paired_walk<true> : &launch::paired_walk<false>;
+                plan->walk_symbol = f64 ? &launch::paired_walk_symbol<true> : &launch::paired_walk_symbol<false>;
+                plan->walk_smem = 256 + 64 * 8 + (size_t)kWarps * paired::kHeaderBytes;
+                const int64_t slot_bytes = (int64_t)t.edge_cap * (int64_t)(sizeof(double4) + sizeof(int32_t)) + 4;
+                plan->edge_chunk = std::max<int64_t>(4096, (int64_t)(4ull << 30) / slot_bytes);
+                plan->kernel_label = std::string("soap_paired_kernel<1, 0, ") + (f64 ? "true" : "false") +
+                                     ", 4, walk> + " + sv.name + " (edge lists)";
+            }
+        }
         if (plan->center_smem > budget1 || plan->structure_smem > budget1)
             return fail(MDSOAP_INVALID_ARGUMENT, "SOAP parameters need more shared memory than the device offers");
         *plan_out = plan.release();

@@ -553,8 +553,9 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
         shared_bytes += (beta_count * 8 + 15) & ~15;
     }
     __syncthreads();
-    const int64_t center = p.center_begin + (int64_t)blockIdx.x * kWarps + warp;
-    if (center >= p.center_end) return;
+    // Centres [grid_begin, grid_end) of this launch (the block's, or a chunk of it).
+    const int64_t center = p.grid_begin + (int64_t)blockIdx.x * kWarps + warp;
+    if (center >= p.grid_end) return;
 
     unsigned char* region = smem + shared_bytes + (size_t)warp * tab.warp_bytes;
     int* seg_prefix = reinterpret_cast<int*>(region);          // 40 ints
@@ -683,23 +684,9 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
             };
 
             int pcount = 0;
-            for_each_candidate_flat(si, bv, center, lane, seg_prefix, seg_start, seg_t,
-                                    [&](bool valid, int j, int tx, int ty, int tz) {
-                int nimg[3];
-                double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0, ew = 1.0;
-                int t = -1;
-                bool ok = false;
-                if (valid) {
-                    t = bv.type[si.atom_begin + j];
-                    if (pooled || (t >= tb && t < te))
-                        ok = accept_candidate(si, bv, p.positions, center, wi, j, tx, ty, tz, tab.cutoff2, nimg,
-                                              dx, dy, dz, d2);
-                    if (ok && weighted) {
-                        ew = soap_edge_weight(tab, d2, si.atom_begin + j == center && nimg[0] == 0 && nimg[1] == 0 &&
-                                                           nimg[2] == 0);
-                        if (pooled) ew *= tab.species_weight[t];
-                    }
-                }
+            // One batch of up to 32 accepted edges (lanes with ok) into the
+            // queue in lane order, whole chunks drained.
+            auto enqueue = [&](bool ok, double dx, double dy, double dz, double d2, double ew, int t) {
                 const unsigned mask = __ballot_sync(0xffffffffu, ok);
                 if (ok) {
                     const int q = pcount + __popc(mask & ((1u << lane) - 1u));
@@ -739,7 +726,55 @@ soap_center_kernel(const __grid_constant__ SoapTables tab, const SoapPointers p)
                     __syncwarp();
                     pcount = rem;
                 }
-            });
+            };
+            // Edge lists (p.edge_count set): the centre's accepted edges from
+            // the walk kernel's slot, unless it overflowed.  The walk visits
+            // the same bin rows in the same order and only drops candidates
+            // beyond the prefilter sphere, so for float64 rows (every edge
+            // through the exact test) the edges arrive in this kernel's own
+            // walk order and the rows are the same bit for bit.
+            const int64_t slot = center - p.grid_begin;
+            const int nedges = p.edge_count ? p.edge_count[slot] : -1;
+            if (nedges >= 0 && nedges <= tab.edge_cap) {
+                for (int f = 0; f < nedges; f += 32) {
+                    const int e = f + lane;
+                    bool ok = false;
+                    double4 d = make_double4(0.0, 0.0, 0.0, 0.0);
+                    double ew = 1.0;
+                    int t = -1;
+                    if (e < nedges) {
+                        d = p.edges[slot * tab.edge_cap + e];
+                        const int info = p.edge_info[slot * tab.edge_cap + e];
+                        t = info & 0xffff;
+                        ok = pooled || (t >= tb && t < te);
+                        if (ok && weighted) {
+                            ew = soap_edge_weight(tab, d.w, (info >> 16) != 0);
+                            if (pooled) ew *= tab.species_weight[t];
+                        }
+                    }
+                    enqueue(ok, d.x, d.y, d.z, d.w, ew, t);
+                }
+            } else {
+                for_each_candidate_flat(si, bv, center, lane, seg_prefix, seg_start, seg_t,
+                                        [&](bool valid, int j, int tx, int ty, int tz) {
+                    int nimg[3];
+                    double dx = 0.0, dy = 0.0, dz = 0.0, d2 = 0.0, ew = 1.0;
+                    int t = -1;
+                    bool ok = false;
+                    if (valid) {
+                        t = bv.type[si.atom_begin + j];
+                        if (pooled || (t >= tb && t < te))
+                            ok = accept_candidate(si, bv, p.positions, center, wi, j, tx, ty, tz, tab.cutoff2, nimg,
+                                                  dx, dy, dz, d2);
+                        if (ok && weighted) {
+                            ew = soap_edge_weight(tab, d2, si.atom_begin + j == center && nimg[0] == 0 &&
+                                                               nimg[1] == 0 && nimg[2] == 0);
+                            if (pooled) ew *= tab.species_weight[t];
+                        }
+                    }
+                    enqueue(ok, dx, dy, dz, d2, ew, t);
+                });
+            }
             __syncwarp();
             if (pcount > 0) process(pcount);
 

@@ -59,3 +59,45 @@ def test_edge_lists_match_the_fused_kernel_bitwise(cuda_device, monkeypatch, nam
             assert np.array_equal(got.view(np.uint8), fused.view(np.uint8)), f"cap {cap}: rows differ from the fused kernel"
         else:
             assert_features_close(got, fused, dtype)
+
+
+CENTER_CASES = {
+    # name: (batch, species, r_cut, n_max, l_max, dtype, average, weighting, compression)
+    "cfg3-l8-f64": ("cfg3", (13, 29), 6.0, 8, 8, "float64", "off", None, "off"),
+    "cfg3-l8-f64-outer-mu1nu1": ("cfg3", (13, 29), 6.0, 8, 8, "float64", "outer", None, "mu1nu1"),
+    "cfg2-l8-f64-inner-poly-mu2": ("cfg2", (1, 6, 7, 8), 5.0, 8, 8, "float64", "inner",
+                                   {"function": "poly", "r0": 7.0, "c": 1.0, "m": 2.0, "w0": 0.5}, "mu2"),
+    "cfg2-n10-f64-w0-crossover": ("cfg2", (1, 6, 7, 8), 5.0, 10, 4, "float64", "off", {"w0": 0.3}, "crossover"),
+    "cfg2-n10-f32-outer": ("cfg2", (1, 6, 7, 8), 5.0, 10, 4, "float32", "outer", None, "off"),
+}
+
+
+@pytest.mark.parametrize("name", sorted(CENTER_CASES))
+def test_centre_kernel_on_edge_lists_matches_its_own_walk(cuda_device, monkeypatch, name):
+    """Shapes outside the paired kernel (l_max > 6, n_max > 8): the walk-only
+    kernel fills the edge slots and the centre kernel reads them instead of
+    walking (a centre whose slot overflowed walks itself).  For float64 rows
+    the accepted edges arrive in the order of the centre kernel's own walk, so
+    the rows equal those of MDSOAP_EDGE_CAP=0 bit for bit; float32 rows take
+    the certified pairs' displacements (last bits) and are held to the float32
+    bound."""
+    bname, species, r_cut, n_max, l_max, dtype, average, weighting, compression = CENTER_CASES[name]
+    batch = workloads.config3(structures=1, reps=(6, 6, 4)) if bname == "cfg3" else workloads.config2(structures=4)
+    alphas, betas = basis_gto(r_cut, n_max, l_max)
+
+    def rows(cap):
+        monkeypatch.setenv("MDSOAP_EDGE_CAP", cap)
+        soap = Soap(species, r_cut=r_cut, n_max=n_max, l_max=l_max, average=average, dtype=dtype, alphas=alphas,
+                    betas=betas, weighting=weighting, compression=compression)
+        return soap.kernel(), soap.compute(batch, devices=[cuda_device])
+
+    own_kernel, own = rows("0")
+    assert "soap_center_kernel" in own_kernel and "edge lists" not in own_kernel
+    for cap in ("512", "64", "1"):
+        kernel, got = rows(cap)
+        assert "soap_center_kernel" in kernel and "edge lists" in kernel
+        if dtype == "float64":
+            assert np.array_equal(got.view(np.uint8), own.view(np.uint8)), f"cap {cap}: rows differ"
+        else:
+            assert_features_close(got, own, dtype)
+
